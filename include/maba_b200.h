@@ -1,0 +1,165 @@
+/*
+ * maba_b200.h -- C ABI of the B200 (sm_100a) Maba v2 hot path.
+ *
+ * Every entry point takes plain device pointers wrapped in `maba_tensor`
+ * descriptors (pointer + dtype + shape + element strides), a caller-owned
+ * CUDA stream (`void*` holding a cudaStream_t) and, where a kernel needs
+ * scratch memory, a caller-owned workspace whose size the matching
+ * `*_workspace_size` call reports.  Nothing here allocates device memory,
+ * synchronises the device or keeps a pointer after it returns.
+ *
+ * Return value: MABA_OK (0) or one of the MABA_ERR_* codes; the message of
+ * the last failure on the calling thread is returned by maba_last_error().
+ *
+ * The reference project (maba_sparse, Python) reaches this path through its
+ * kernel registry; each declaration below names the reference function it
+ * replaces (file:line inside the reference project).
+ */
+#ifndef MABA_B200_H
+#define MABA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MABA_ABI_VERSION 1
+
+/* element types */
+#define MABA_F32  0
+#define MABA_F16  1
+#define MABA_BF16 2
+#define MABA_F64  3
+#define MABA_I64  4
+#define MABA_I32  5
+
+/* status codes */
+#define MABA_OK               0
+#define MABA_ERR_INVALID      1 /* bad shape / stride / argument            */
+#define MABA_ERR_DTYPE        2 /* dtype not supported or mismatched        */
+#define MABA_ERR_UNSUPPORTED  3 /* valid request outside the built kernels */
+#define MABA_ERR_WORKSPACE    4 /* workspace missing or too small           */
+#define MABA_ERR_CUDA         5 /* CUDA launch / runtime error              */
+
+#define MABA_MAX_DIMS 6
+
+#if defined(__GNUC__)
+#define MABA_API __attribute__((visibility("default")))
+#else
+#define MABA_API
+#endif
+
+typedef struct maba_tensor {
+    void*   data;                    /* device address of element [0..0]; NULL = operand absent */
+    int32_t dtype;                   /* MABA_F32 ... MABA_I32 */
+    int32_t ndim;                    /* valid entries in shape / stride */
+    int64_t shape[MABA_MAX_DIMS];
+    int64_t stride[MABA_MAX_DIMS];   /* in elements, may be any non-negative value */
+} maba_tensor;
+
+/* ---- library ---------------------------------------------------------- */
+
+MABA_API int         maba_abi_version(void);
+MABA_API const char* maba_last_error(void);
+
+/* ---- DGDA chunked prefill ---------------------------------------------
+ * Replaces the `dgda_prefill` registry op:
+ *   maba_sparse/kernels/dispatcher.py:258   (dispatch_dgda_prefill)
+ *   maba_sparse/kernels/common.py:229-268   (ref_dgda_prefill, sequential)
+ *   maba_sparse/kernels/cpu_dgda.py:33-197  (cpu_dgda_prefill, chunked WY/UT)
+ *   maba_sparse/kernels/triton_dgda.py:648  (triton_dgda_prefill)
+ * q, k, b, alpha, log_alpha: [B,H,L,dk];  v, w: [B,H,L,dv];
+ * initial_state (optional, NULL data = zeros): [B,H,dk,dv];
+ * out: [B,H,L,dv] (dtype of q);  final_state: [B,H,dk,dv] (dtype of q or F32).
+ * alpha or log_alpha may be absent (not both); when log_alpha is given it is
+ * used (clamped to [-46,0]), otherwise log(clamp(alpha,1e-20,1)).
+ * chunk_size is accepted for API parity; the kernels choose their own chunk
+ * (the recurrence is chunk-invariant).  Workspace: see _workspace_size. */
+MABA_API int maba_dgda_prefill(const maba_tensor* q, const maba_tensor* k, const maba_tensor* v,
+                      const maba_tensor* alpha, const maba_tensor* log_alpha,
+                      const maba_tensor* b, const maba_tensor* w,
+                      const maba_tensor* initial_state,
+                      const maba_tensor* out, const maba_tensor* final_state,
+                      int32_t chunk_size, void* workspace, size_t workspace_bytes,
+                      void* stream);
+MABA_API size_t maba_dgda_prefill_workspace_size(int32_t dtype, int64_t B, int64_t H, int64_t L,
+                                        int64_t dk, int64_t dv);
+
+/* ---- DGDA decode step --------------------------------------------------
+ * Replaces the `dgda_step` registry op:
+ *   maba_sparse/kernels/dispatcher.py:330, common.py:271-309,
+ *   cpu_dgda.py:200-261, triton_dgda.py:668.
+ * q, k, b, alpha, log_alpha: [B,H,dk]; v, w: [B,H,dv];
+ * state (optional): [B,H,dk,dv]; out: [B,H,dv]; new_state: [B,H,dk,dv].
+ * alpha has priority over log_alpha (as in the reference). */
+MABA_API int maba_dgda_step(const maba_tensor* q, const maba_tensor* k, const maba_tensor* v,
+                   const maba_tensor* alpha, const maba_tensor* log_alpha,
+                   const maba_tensor* b, const maba_tensor* w,
+                   const maba_tensor* state,
+                   const maba_tensor* out, const maba_tensor* new_state,
+                   void* stream);
+
+/* ---- DG-Indexer block pooling ------------------------------------------
+ * Replaces `compute_centroids`: dispatcher.py:399, common.py:329-350,
+ * cpu_indexer.py:16-50.  k_idx: [B,L,d] -> out: [B,ceil(L/block),d],
+ * c = 0.5*(sum/block + max) with the tail block zero-padded. */
+MABA_API int maba_compute_centroids(const maba_tensor* k_idx, const maba_tensor* out,
+                           int32_t block_size, void* stream);
+
+/* ---- DG-Indexer scoring + top-k ----------------------------------------
+ * Replaces `index_topk`: dispatcher.py:424, common.py:353-403,
+ * cpu_indexer.py:54-112, and the decode-time inline top-k of
+ * maba_sparse/layers/indexer.py:101-112 (decode != 0).
+ * q_idx: [B,L,d]; centroids: [B,nb,d]; idx_out: [B,L,min(top_k,nb)] int64;
+ * scores_out (optional): [B,L,nb] in q_idx's dtype.
+ * score[t,n] = (q_t*scale).c_n - lambda*log1p(qb(t)-n), scale = 1/sqrt(d),
+ * qb(t) = t/block (prefill) or nb-1 (decode); n > qb(t) is -inf.
+ * Order: score descending, ties to the lower block index; slots past the
+ * number of finite candidates hold the lowest unused (future) indices in
+ * ascending order.  Workspace: see _workspace_size. */
+MABA_API int maba_index_topk(const maba_tensor* q_idx, const maba_tensor* centroids,
+                    float lambda_dist, int32_t top_k, int32_t block_size, int32_t decode,
+                    const maba_tensor* idx_out, const maba_tensor* scores_out,
+                    void* workspace, size_t workspace_bytes, void* stream);
+MABA_API size_t maba_index_topk_workspace_size(int64_t B, int64_t L, int64_t nb, int32_t top_k);
+
+/* ---- Stream superposition ----------------------------------------------
+ * Replaces `stream_superposition`: dispatcher.py:468, common.py:406-438,
+ * cpu_indexer.py:116-150.  o_*: [B,H,L,D]; gate: [B,L,3] or [B,H,L,3];
+ * gate_is_logits != 0 applies a softmax over the last axis first. */
+MABA_API int maba_stream_superposition(const maba_tensor* o_local, const maba_tensor* o_sparse,
+                              const maba_tensor* o_hca, const maba_tensor* gate,
+                              int32_t gate_is_logits, const maba_tensor* out, void* stream);
+
+/* ---- HCA block pooling -------------------------------------------------
+ * The pooled-prefix table of maba_sparse/layers/sparse_attention.py:206:
+ * c_kv: [B,L,d_c] -> out: [B,L/r,d_c] (complete blocks only), mean of r rows. */
+MABA_API int maba_hca_pool(const maba_tensor* c_kv, const maba_tensor* out, int32_t r, void* stream);
+
+/* ---- MABA-SA fused three-stream attention ------------------------------
+ * Replaces MabaSparseAttention._compute_local_attention,
+ * _compute_sparse_attention, _compute_hca_attention and the superposition
+ * call (maba_sparse/layers/sparse_attention.py:79-219, 274-275), computed in
+ * the latent space of the MLA cache (keys/values never up-projected):
+ *   qhat:  [B,Lq,H,d_c]   = scale * W_uk,h^T q_h   (absorbed queries)
+ *   c_kv:  [B,Lkv,d_c]    latent cache, query t sits at pos = Lkv-Lq+t
+ *   hca:   [B,Lkv/r,d_c]  pooled complete blocks (maba_hca_pool)
+ *   top_idx: [B,Lq,K] int64 selected blocks (indices into c_kv blocks)
+ *   gate:  [B,Lq,3] or [B,H,Lq,3] gate logits
+ *   out:   [B,Lq,H,d_c]   sum_s softmax(gate)_s * (attention of stream s),
+ *          still in latent space; the caller applies W_uv and o_proj. */
+MABA_API int maba_sa_attention(const maba_tensor* qhat, const maba_tensor* c_kv,
+                      const maba_tensor* hca, const maba_tensor* top_idx,
+                      const maba_tensor* gate, const maba_tensor* out,
+                      int32_t window, int32_t n_sinks, int32_t block_size, int32_t hca_r,
+                      void* workspace, size_t workspace_bytes, void* stream);
+MABA_API size_t maba_sa_attention_workspace_size(int32_t dtype, int64_t B, int64_t Lq, int64_t Lkv,
+                                        int64_t H, int64_t d_c, int64_t K, int32_t block_size);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MABA_B200_H */

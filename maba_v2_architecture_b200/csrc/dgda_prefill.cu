@@ -1,0 +1,543 @@
+// DGDA chunked prefill (gated delta rule with per-channel decay).
+//
+// Recurrence (maba_sparse/kernels/common.py:256-265):
+//   Sd = diag(alpha_t) S;  delta = w_t*v_t - (b_t*k_t)^T Sd;  S = Sd + k_t delta^T;  o_t = q_t^T S
+// Chunked WY/UT form (maba_sparse/kernels/cpu_dgda.py:101-146), per chunk of C
+// tokens with G = cumsum(log alpha) over the chunk:
+//   L[i,j] = sum_d (b k)_i[d] k_j[d] e^{G_i[d]-G_j[d]}   (j < i)
+//   A[i,j] = sum_d q_i[d]     k_j[d] e^{G_i[d]-G_j[d]}   (j <= i)
+//   (I+L) [W | U] = [(b k) e^{G} | w v]                 (exact blocked solve)
+//   V' = U - W S;   o = (q e^{G}) S + A V';   S <- e^{G_end} S + (k e^{G_end-G})^T V'
+// The solve is exact (16x16 diagonal inverses by forward substitution plus
+// block back-substitution): the Neumann series of cpu_dgda.py:110-114 diverges
+// for large inputs (reference tests/test_dgda_stress.py:169-190).
+//
+// Parallelism.  Columns of S evolve independently, chunks of one (b,h) are a
+// serial chain.  When B*H alone cannot fill the GPU the sequence is cut into
+// segments: pass 1 runs every segment from the augmented state [0 | I] and
+// records its affine transition S_end = P S_start + R (P is dk x dk); a small
+// combine pass chains the transitions; pass 2 reruns each segment from its
+// true starting state and writes the outputs.  This is the same affine-chain
+// that splits a sequence across GPUs.
+//
+// This file is the CUDA-core (FFMA) path: fp32 compute for fp32/fp16/bf16
+// inputs (fp64 compute for fp64 inputs), head dims up to 64.
+#include "common.cuh"
+
+namespace maba {
+namespace {
+
+constexpr int NT = 256;   // threads per CTA
+constexpr int DP = 64;    // padded head dim
+constexpr int SUB = 16;   // diagonal block of the triangular solve
+
+struct PrefillArgs {
+    const void* q; const void* k; const void* v; const void* alpha; const void* log_alpha;
+    const void* b; const void* w; const void* init;
+    void* out; void* fin;
+    int64_t sq[4], sk[4], sv[4], sa[4], sla[4], sb[4], sw[4], si[4], so[4], sf[4];
+    int64_t L;
+    int H, dk, dv;
+    int nseg;
+    int64_t seg_len;      // tokens per segment (multiple of the chunk)
+    float* ws_trans;      // [B*H][nseg][DP][2*DP]   (R | P) per segment
+    float* ws_start;      // [B*H][nseg][DP][DP]     starting state per segment
+};
+
+template <typename ACC> __device__ __forceinline__ ACC fast_exp(ACC x);
+template <> __device__ __forceinline__ float fast_exp<float>(float x) { return __expf(x); }
+template <> __device__ __forceinline__ double fast_exp<double>(double x) { return exp(x); }
+
+template <typename ACC, int C, int MODE>
+struct Smem {
+    static constexpr int RS = DP + 1;
+    static constexpr int XRS = 2 * DP + 1;
+    static constexpr int NCOL = MODE == 1 ? 2 * DP : DP;
+    static constexpr int VRS = NCOL + 1;
+    static constexpr int NB = C / SUB;
+    static constexpr size_t kQ = 0;
+    static constexpr size_t kK = kQ + (size_t)C * RS;
+    static constexpr size_t kB = kK + (size_t)C * RS;
+    static constexpr size_t kG = kB + (size_t)C * RS;
+    static constexpr size_t kX = kG + (size_t)C * RS;
+    static constexpr size_t kL = kX + (size_t)C * XRS;
+    static constexpr size_t kA = kL + (size_t)C * (C + 1);
+    static constexpr size_t kS = kA + (size_t)C * (C + 1);
+    static constexpr size_t kV = kS + (size_t)DP * NCOL;
+    static constexpr size_t kVsz = ((size_t)C * VRS > (size_t)SUB * XRS) ? (size_t)C * VRS : (size_t)SUB * XRS;
+    static constexpr size_t kT = kV + kVsz;
+    static constexpr size_t kD = kT + (size_t)NB * SUB * (SUB + 1);
+    static constexpr size_t kTotal = kD + DP;
+    static constexpr size_t bytes = kTotal * sizeof(ACC);
+};
+
+// MODE 0: single pass from initial_state; MODE 1: transition pass from [0|I];
+// MODE 2: output pass of one segment from its combined starting state.
+template <typename T, typename TS, typename ACC, int C, int MODE>
+__global__ void __launch_bounds__(NT, 1) dgda_chunk_kernel(PrefillArgs a) {
+    using SM = Smem<ACC, C, MODE>;
+    constexpr int RS = SM::RS, XRS = SM::XRS, NCOL = SM::NCOL, VRS = SM::VRS, NB = SM::NB;
+    constexpr int RPT = C / 16;          // rows per thread in the state phase
+    constexpr int CPT = NCOL / 16;       // columns per thread in the state phase
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    ACC* sm = reinterpret_cast<ACC*>(smem_raw);
+    ACC* Qs = sm + SM::kQ;
+    ACC* Ks = sm + SM::kK;
+    ACC* Bs = sm + SM::kB;
+    ACC* Gs = sm + SM::kG;
+    ACC* Xs = sm + SM::kX;
+    ACC* Ls = sm + SM::kL;
+    ACC* As = sm + SM::kA;
+    ACC* Ss = sm + SM::kS;
+    ACC* Vt = sm + SM::kV;
+    ACC* Tb = sm + SM::kT;
+    ACC* dend = sm + SM::kD;
+
+    const int tid = threadIdx.x;
+    const int bh = blockIdx.x;
+    const int seg = blockIdx.y;
+    const int64_t bi = bh / a.H, hi = bh % a.H;
+    const int dk = a.dk, dv = a.dv;
+
+    const T* q = static_cast<const T*>(a.q);
+    const T* k = static_cast<const T*>(a.k);
+    const T* v = static_cast<const T*>(a.v);
+    const T* bb = static_cast<const T*>(a.b);
+    const T* w = static_cast<const T*>(a.w);
+    const T* al = static_cast<const T*>(a.alpha);
+    const T* lal = static_cast<const T*>(a.log_alpha);
+
+    // ---- initial state ----------------------------------------------------
+    for (int e = tid; e < DP * NCOL; e += NT) {
+        const int d = e / NCOL, c = e - (e / NCOL) * NCOL;
+        ACC s = ACC(0);
+        if (MODE == 0) {
+            if (a.init != nullptr && d < dk && c < dv)
+                s = load_as<ACC>(static_cast<const TS*>(a.init) + bi * a.si[0] + hi * a.si[1] +
+                                 (int64_t)d * a.si[2] + (int64_t)c * a.si[3]);
+        } else if (MODE == 1) {
+            s = (c >= DP && c - DP == d) ? ACC(1) : ACC(0);
+        } else {
+            s = (ACC)a.ws_start[(((size_t)bh * a.nseg + seg) * DP + d) * DP + c];
+        }
+        Ss[d * NCOL + c] = s;
+    }
+
+    const int64_t t_begin = (int64_t)seg * a.seg_len;
+    int64_t t_end = t_begin + a.seg_len;
+    if (t_end > a.L) t_end = a.L;
+
+    for (int64_t c0 = t_begin; c0 < t_end; c0 += C) {
+        __syncthreads();
+        // ---- load the chunk (zero rows past the end, zero padded channels) ----
+        for (int e = tid; e < C * DP; e += NT) {
+            const int r = e / DP, d = e - (e / DP) * DP;
+            const int64_t t = c0 + r;
+            ACC qv = 0, kv = 0, bv = 0, gv = 0, wvv = 0;
+            if (t < t_end) {
+                if (d < dk) {
+                    qv = load_as<ACC>(q + bi * a.sq[0] + hi * a.sq[1] + t * a.sq[2] + d * a.sq[3]);
+                    kv = load_as<ACC>(k + bi * a.sk[0] + hi * a.sk[1] + t * a.sk[2] + d * a.sk[3]);
+                    bv = load_as<ACC>(bb + bi * a.sb[0] + hi * a.sb[1] + t * a.sb[2] + d * a.sb[3]);
+                    if (lal != nullptr) {
+                        gv = load_as<ACC>(lal + bi * a.sla[0] + hi * a.sla[1] + t * a.sla[2] + d * a.sla[3]);
+                        gv = gv < ACC(-46) ? ACC(-46) : (gv > ACC(0) ? ACC(0) : gv);
+                    } else {
+                        ACC x = load_as<ACC>(al + bi * a.sa[0] + hi * a.sa[1] + t * a.sa[2] + d * a.sa[3]);
+                        x = x < ACC(1e-20) ? ACC(1e-20) : (x > ACC(1) ? ACC(1) : x);
+                        gv = log_acc<ACC>(x);
+                    }
+                }
+                if (d < dv) {
+                    ACC vv = load_as<ACC>(v + bi * a.sv[0] + hi * a.sv[1] + t * a.sv[2] + d * a.sv[3]);
+                    ACC ww = load_as<ACC>(w + bi * a.sw[0] + hi * a.sw[1] + t * a.sw[2] + d * a.sw[3]);
+                    wvv = ww * vv;
+                }
+            }
+            Qs[r * RS + d] = qv;
+            Ks[r * RS + d] = kv;
+            Bs[r * RS + d] = bv * kv;
+            Gs[r * RS + d] = gv;
+            Xs[r * XRS + DP + d] = wvv;
+        }
+        __syncthreads();
+        // ---- cumulative log decay per channel (sequential, as torch.cumsum) ----
+        if (tid < DP) {
+            ACC run = 0;
+            for (int r = 0; r < C; ++r) {
+                run += Gs[r * RS + tid];
+                Gs[r * RS + tid] = run;
+            }
+        }
+        __syncthreads();
+        // ---- A and L with explicit per-channel decay --------------------------
+        {
+            constexpr int TPR = NT / (C / 2);   // threads per row pair
+            const int rp = tid / TPR, sub = tid - (tid / TPR) * TPR;
+            const int iA = rp, iB = C - 1 - rp;
+            for (int p = sub; p < C + 1; p += TPR) {
+                int i, j;
+                if (p <= iA) { i = iA; j = p; } else { i = iB; j = p - iA - 1; }
+                ACC av = 0, lv = 0;
+                const ACC* gi = Gs + i * RS;
+                const ACC* gj = Gs + j * RS;
+                const ACC* qi = Qs + i * RS;
+                const ACC* bki = Bs + i * RS;
+                const ACC* kj = Ks + j * RS;
+                for (int d = 0; d < dk; ++d) {
+                    const ACC kd = kj[d] * fast_exp<ACC>(gi[d] - gj[d]);
+                    av += qi[d] * kd;
+                    lv += bki[d] * kd;
+                }
+                As[i * (C + 1) + j] = av;
+                Ls[i * (C + 1) + j] = i > j ? lv : ACC(0);
+            }
+        }
+        __syncthreads();
+        // ---- decayed operands; diagonal-block inverses ------------------------
+        for (int e = tid; e < C * DP; e += NT) {
+            const int r = e / DP, d = e - (e / DP) * DP;
+            const ACC g = Gs[r * RS + d];
+            const ACC ge = Gs[(C - 1) * RS + d];
+            const ACC eg = fast_exp<ACC>(g);
+            Xs[r * XRS + d] = Bs[r * RS + d] * eg;          // (b k) e^{G}
+            Qs[r * RS + d] = Qs[r * RS + d] * eg;           // q e^{G}
+            Ks[r * RS + d] = Ks[r * RS + d] * fast_exp<ACC>(ge - g);  // k e^{G_end - G}
+            if (r == 0) dend[d] = fast_exp<ACC>(ge);
+        }
+        if (tid < NB * SUB) {
+            const int blk = tid / SUB, c = tid - (tid / SUB) * SUB;
+            ACC* T_ = Tb + blk * SUB * (SUB + 1);
+            const ACC* Lb = Ls + (blk * SUB) * (C + 1) + blk * SUB;
+            for (int r = 0; r < c; ++r) T_[r * (SUB + 1) + c] = 0;
+            T_[c * (SUB + 1) + c] = 1;
+            for (int r = c + 1; r < SUB; ++r) {
+                ACC s = 0;
+                for (int m = c; m < r; ++m) s += Lb[r * (C + 1) + m] * T_[m * (SUB + 1) + c];
+                T_[r * (SUB + 1) + c] = -s;
+            }
+        }
+        __syncthreads();
+        // ---- blocked forward substitution: (I+L) X = RHS, in place in Xs -------
+        {
+            constexpr int NX = 2 * DP;
+            ACC* Rt = Vt;  // [SUB][XRS] temporary
+            for (int I = 0; I < NB; ++I) {
+                for (int e = tid; e < SUB * NX; e += NT) {
+                    const int r = e / NX, c = e - (e / NX) * NX;
+                    const int row = I * SUB + r;
+                    ACC s = Xs[row * XRS + c];
+                    const ACC* lr = Ls + row * (C + 1);
+                    for (int j = 0; j < I * SUB; ++j) s -= lr[j] * Xs[j * XRS + c];
+                    Rt[r * XRS + c] = s;
+                }
+                __syncthreads();
+                const ACC* T_ = Tb + I * SUB * (SUB + 1);
+                for (int e = tid; e < SUB * NX; e += NT) {
+                    const int r = e / NX, c = e - (e / NX) * NX;
+                    ACC s = 0;
+                    for (int m = 0; m <= r; ++m) s += T_[r * (SUB + 1) + m] * Rt[m * XRS + c];
+                    Xs[(I * SUB + r) * XRS + c] = s;
+                }
+                __syncthreads();
+            }
+        }
+        // ---- state phase ---------------------------------------------------------
+        const int tr = tid >> 4, tc = tid & 15;
+        ACC accq[RPT][DP / 16];
+        {
+            ACC accv[RPT][CPT];
+#pragma unroll
+            for (int m = 0; m < RPT; ++m) {
+#pragma unroll
+                for (int kk = 0; kk < CPT; ++kk) accv[m][kk] = 0;
+#pragma unroll
+                for (int kk = 0; kk < DP / 16; ++kk) accq[m][kk] = 0;
+            }
+            for (int d = 0; d < dk; ++d) {
+                ACC s[CPT];
+#pragma unroll
+                for (int kk = 0; kk < CPT; ++kk) s[kk] = Ss[d * NCOL + tc + 16 * kk];
+#pragma unroll
+                for (int m = 0; m < RPT; ++m) {
+                    const int i = tr + 16 * m;
+                    const ACC wv = Xs[i * XRS + d];
+#pragma unroll
+                    for (int kk = 0; kk < CPT; ++kk) accv[m][kk] += wv * s[kk];
+                    if (MODE != 1) {
+                        const ACC qt = Qs[i * RS + d];
+#pragma unroll
+                        for (int kk = 0; kk < DP / 16; ++kk) accq[m][kk] += qt * s[kk];
+                    }
+                }
+            }
+#pragma unroll
+            for (int m = 0; m < RPT; ++m) {
+                const int i = tr + 16 * m;
+#pragma unroll
+                for (int kk = 0; kk < CPT; ++kk) {
+                    const int c = tc + 16 * kk;
+                    const ACC u = c < DP ? Xs[i * XRS + DP + c] : ACC(0);
+                    Vt[i * VRS + c] = u - accv[m][kk];
+                }
+            }
+        }
+        __syncthreads();
+        if (MODE != 1) {
+            T* o = static_cast<T*>(a.out);
+#pragma unroll
+            for (int m = 0; m < RPT; ++m) {
+                const int i = tr + 16 * m;
+                const int64_t t = c0 + i;
+                const ACC* ar = As + i * (C + 1);
+#pragma unroll
+                for (int kk = 0; kk < DP / 16; ++kk) {
+                    const int c = tc + 16 * kk;
+                    ACC s = accq[m][kk];
+                    for (int j = 0; j <= i; ++j) s += ar[j] * Vt[j * VRS + c];
+                    if (t < t_end && c < dv)
+                        store_from<T, ACC>(o + bi * a.so[0] + hi * a.so[1] + t * a.so[2] + (int64_t)c * a.so[3], s);
+                }
+            }
+        }
+        {
+            ACC acc[DP / 16][CPT];
+#pragma unroll
+            for (int m = 0; m < DP / 16; ++m) {
+                const int d = tr + 16 * m;
+#pragma unroll
+                for (int kk = 0; kk < CPT; ++kk) acc[m][kk] = dend[d] * Ss[d * NCOL + tc + 16 * kk];
+            }
+            for (int i = 0; i < C; ++i) {
+                ACC vv[CPT];
+#pragma unroll
+                for (int kk = 0; kk < CPT; ++kk) vv[kk] = Vt[i * VRS + tc + 16 * kk];
+#pragma unroll
+                for (int m = 0; m < DP / 16; ++m) {
+                    const ACC kt = Ks[i * RS + tr + 16 * m];
+#pragma unroll
+                    for (int kk = 0; kk < CPT; ++kk) acc[m][kk] += kt * vv[kk];
+                }
+            }
+#pragma unroll
+            for (int m = 0; m < DP / 16; ++m) {
+                const int d = tr + 16 * m;
+#pragma unroll
+                for (int kk = 0; kk < CPT; ++kk) Ss[d * NCOL + tc + 16 * kk] = acc[m][kk];
+            }
+        }
+    }
+    __syncthreads();
+    // ---- results ---------------------------------------------------------------
+    if (MODE == 1) {
+        float* dst = a.ws_trans + ((size_t)bh * a.nseg + seg) * DP * (2 * DP);
+        for (int e = tid; e < DP * NCOL; e += NT) dst[e] = (float)Ss[e];
+    } else if (MODE == 0 || seg == a.nseg - 1) {
+        TS* f = static_cast<TS*>(a.fin);
+        for (int e = tid; e < DP * NCOL; e += NT) {
+            const int d = e / NCOL, c = e - (e / NCOL) * NCOL;
+            if (d < dk && c < dv)
+                store_from<TS, ACC>(f + bi * a.sf[0] + hi * a.sf[1] + (int64_t)d * a.sf[2] + (int64_t)c * a.sf[3],
+                                    Ss[e]);
+        }
+    }
+}
+
+// Chains the segment transitions: start[0] = S0, start[s+1] = P_s start[s] + R_s.
+template <typename TS>
+__global__ void __launch_bounds__(NT) dgda_combine_kernel(PrefillArgs a) {
+    __shared__ float S[DP * DP];
+    __shared__ float Tr[DP * 2 * DP];
+    const int tid = threadIdx.x;
+    const int bh = blockIdx.x;
+    const int64_t bi = bh / a.H, hi = bh % a.H;
+    for (int e = tid; e < DP * DP; e += NT) {
+        const int d = e / DP, c = e - (e / DP) * DP;
+        float s = 0.f;
+        if (a.init != nullptr && d < a.dk && c < a.dv)
+            s = load_as<float>(static_cast<const TS*>(a.init) + bi * a.si[0] + hi * a.si[1] + (int64_t)d * a.si[2] +
+                               (int64_t)c * a.si[3]);
+        S[e] = s;
+    }
+    const int tr = tid >> 4, tc = tid & 15;
+    for (int s = 0; s < a.nseg; ++s) {
+        __syncthreads();
+        float* dst = a.ws_start + ((size_t)bh * a.nseg + s) * DP * DP;
+        for (int e = tid; e < DP * DP; e += NT) dst[e] = S[e];
+        if (s == a.nseg - 1) break;
+        const float* src = a.ws_trans + ((size_t)bh * a.nseg + s) * DP * (2 * DP);
+        for (int e = tid; e < DP * 2 * DP; e += NT) Tr[e] = src[e];
+        __syncthreads();
+        float acc[4][4];
+#pragma unroll
+        for (int m = 0; m < 4; ++m)
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) acc[m][kk] = Tr[(tr + 16 * m) * 2 * DP + tc + 16 * kk];  // R
+        for (int e = 0; e < DP; ++e) {
+            float sv[4];
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) sv[kk] = S[e * DP + tc + 16 * kk];
+#pragma unroll
+            for (int m = 0; m < 4; ++m) {
+                const float p = Tr[(tr + 16 * m) * 2 * DP + DP + e];  // P[d][e]
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) acc[m][kk] += p * sv[kk];
+            }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int m = 0; m < 4; ++m)
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) S[(tr + 16 * m) * DP + tc + 16 * kk] = acc[m][kk];
+    }
+}
+
+int choose_segments(int dtype, int64_t BH, int64_t L) {
+    if (dtype == MABA_F64) return 1;
+    const int64_t nchunks = ceil_div(L, 64);
+    const int64_t sms = sm_count();
+    if (BH >= sms || nchunks < 12) return 1;
+    // one CTA per SM (shared-memory bound): segments pay ~2.5x the work, so use
+    // them only to fill a single wave, and only when that is >= 3 segments
+    int64_t nseg = sms / BH;
+    if (nseg > nchunks / 4) nseg = nchunks / 4;
+    if (nseg > 64) nseg = 64;
+    return nseg < 3 ? 1 : (int)nseg;
+}
+
+template <typename K>
+int set_smem(K kern, size_t bytes) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (e != cudaSuccess) return set_error(MABA_ERR_CUDA, "dgda_prefill: smem attribute: %s", cudaGetErrorString(e));
+    return MABA_OK;
+}
+
+template <typename T, typename TS>
+int launch_prefill(PrefillArgs& a, int64_t B, int dtype, cudaStream_t s, void* ws, size_t ws_bytes) {
+    using ACC = typename std::conditional<sizeof(T) == 8, double, float>::type;
+    constexpr int C = sizeof(T) == 8 ? 32 : 64;
+    const int64_t BH = B * a.H;
+    if (BH == 0) return MABA_OK;
+    const int nseg = choose_segments(dtype, BH, a.L);
+    if (nseg <= 1) {
+        a.nseg = 1;
+        a.seg_len = a.L > 0 ? a.L : 1;
+        auto kern = dgda_chunk_kernel<T, TS, ACC, C, 0>;
+        MABA_TRY(set_smem(kern, Smem<ACC, C, 0>::bytes));
+        kern<<<dim3((unsigned)BH, 1), NT, Smem<ACC, C, 0>::bytes, s>>>(a);
+        return check_launch("dgda_prefill");
+    }
+    if constexpr (sizeof(T) == 8) {
+        return set_error(MABA_ERR_UNSUPPORTED, "dgda_prefill: segmented fp64 path not built");
+    } else {
+        const int64_t nchunks = ceil_div(a.L, C);
+        a.nseg = nseg;
+        a.seg_len = ceil_div(nchunks, nseg) * C;
+        a.nseg = (int)ceil_div(a.L, a.seg_len);
+        const size_t need = (size_t)BH * a.nseg * (DP * 2 * DP + DP * DP) * sizeof(float);
+        if (ws == nullptr || ws_bytes < need)
+            return set_error(MABA_ERR_WORKSPACE, "dgda_prefill: workspace of %zu bytes required, got %zu", need, ws_bytes);
+        a.ws_trans = static_cast<float*>(ws);
+        a.ws_start = a.ws_trans + (size_t)BH * a.nseg * DP * 2 * DP;
+        auto k1 = dgda_chunk_kernel<T, TS, ACC, C, 1>;
+        auto k2 = dgda_chunk_kernel<T, TS, ACC, C, 2>;
+        MABA_TRY(set_smem(k1, Smem<ACC, C, 1>::bytes));
+        MABA_TRY(set_smem(k2, Smem<ACC, C, 2>::bytes));
+        k1<<<dim3((unsigned)BH, (unsigned)a.nseg), NT, Smem<ACC, C, 1>::bytes, s>>>(a);
+        MABA_TRY(check_launch("dgda_prefill(transition)"));
+        dgda_combine_kernel<TS><<<(unsigned)BH, NT, 0, s>>>(a);
+        MABA_TRY(check_launch("dgda_prefill(combine)"));
+        k2<<<dim3((unsigned)BH, (unsigned)a.nseg), NT, Smem<ACC, C, 2>::bytes, s>>>(a);
+        return check_launch("dgda_prefill(apply)");
+    }
+}
+
+}  // namespace
+}  // namespace maba
+
+using namespace maba;
+
+extern "C" size_t maba_dgda_prefill_workspace_size(int32_t dtype, int64_t B, int64_t H, int64_t L, int64_t dk,
+                                                   int64_t dv) {
+    (void)dk; (void)dv;
+    const int64_t BH = B * H;
+    const int nseg0 = choose_segments(dtype, BH, L);
+    if (nseg0 <= 1) return 0;
+    const int64_t nchunks = ceil_div(L, 64);
+    const int64_t seg_len = ceil_div(nchunks, nseg0) * 64;
+    const int64_t nseg = ceil_div(L, seg_len);
+    return (size_t)BH * nseg * (DP * 2 * DP + DP * DP) * sizeof(float);
+}
+
+extern "C" int maba_dgda_prefill(const maba_tensor* q, const maba_tensor* k, const maba_tensor* v,
+                                 const maba_tensor* alpha, const maba_tensor* log_alpha, const maba_tensor* b,
+                                 const maba_tensor* w, const maba_tensor* initial_state, const maba_tensor* out,
+                                 const maba_tensor* final_state, int32_t chunk_size, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
+    (void)chunk_size;
+    if (!present(q) || q->ndim != 4) return set_error(MABA_ERR_INVALID, "dgda_prefill: q must be 4D [B, H, L, dk]");
+    const int64_t B = q->shape[0], H = q->shape[1], L = q->shape[2], dk = q->shape[3];
+    if (!present(v) || v->ndim != 4) return set_error(MABA_ERR_INVALID, "dgda_prefill: v must be 4D [B, H, L, dv]");
+    const int64_t dv = v->shape[3];
+    const int64_t s_k[4] = {B, H, L, dk}, s_v[4] = {B, H, L, dv}, s_s[4] = {B, H, dk, dv};
+    MABA_TRY(expect_shape(k, "dgda_prefill: k", 4, s_k));
+    MABA_TRY(expect_shape(v, "dgda_prefill: v", 4, s_v));
+    MABA_TRY(expect_shape(b, "dgda_prefill: b", 4, s_k));
+    MABA_TRY(expect_shape(w, "dgda_prefill: w", 4, s_v));
+    MABA_TRY(expect_shape(out, "dgda_prefill: out", 4, s_v));
+    MABA_TRY(expect_shape(final_state, "dgda_prefill: final_state", 4, s_s));
+    if (!present(alpha) && !present(log_alpha))
+        return set_error(MABA_ERR_INVALID, "dgda_prefill: either alpha or log_alpha must be provided");
+    if (present(alpha)) MABA_TRY(expect_shape(alpha, "dgda_prefill: alpha", 4, s_k));
+    if (present(log_alpha)) MABA_TRY(expect_shape(log_alpha, "dgda_prefill: log_alpha", 4, s_k));
+    if (present(initial_state)) MABA_TRY(expect_shape(initial_state, "dgda_prefill: initial_state", 4, s_s));
+    const int dt = q->dtype;
+    const maba_tensor* same[] = {k, v, b, w, out};
+    const char* names[] = {"k", "v", "b", "w", "out"};
+    for (int i = 0; i < 5; ++i)
+        if (same[i]->dtype != dt)
+            return set_error(MABA_ERR_DTYPE, "dgda_prefill: %s dtype %s differs from q (%s)", names[i],
+                             dtype_name(same[i]->dtype), dtype_name(dt));
+    if (present(alpha) && alpha->dtype != dt) return set_error(MABA_ERR_DTYPE, "dgda_prefill: alpha dtype mismatch");
+    if (present(log_alpha) && log_alpha->dtype != dt)
+        return set_error(MABA_ERR_DTYPE, "dgda_prefill: log_alpha dtype mismatch");
+    const int sdt = final_state->dtype;
+    if (present(initial_state) && initial_state->dtype != sdt)
+        return set_error(MABA_ERR_DTYPE, "dgda_prefill: initial_state and final_state dtypes differ");
+    if (sdt != dt && sdt != MABA_F32)
+        return set_error(MABA_ERR_DTYPE, "dgda_prefill: state dtype must be q's dtype or float32");
+    if (dk > DP || dv > DP || dk <= 0 || dv <= 0)
+        return set_error(MABA_ERR_UNSUPPORTED, "dgda_prefill: head dims dk=%lld dv=%lld outside [1, %d]",
+                         (long long)dk, (long long)dv, DP);
+
+    PrefillArgs a{};
+    a.q = q->data; a.k = k->data; a.v = v->data;
+    a.alpha = present(alpha) ? alpha->data : nullptr;
+    a.log_alpha = present(log_alpha) ? log_alpha->data : nullptr;
+    a.b = b->data; a.w = w->data;
+    a.init = present(initial_state) ? initial_state->data : nullptr;
+    a.out = out->data; a.fin = final_state->data;
+    for (int i = 0; i < 4; ++i) {
+        a.sq[i] = q->stride[i]; a.sk[i] = k->stride[i]; a.sv[i] = v->stride[i];
+        a.sa[i] = present(alpha) ? alpha->stride[i] : 0;
+        a.sla[i] = present(log_alpha) ? log_alpha->stride[i] : 0;
+        a.sb[i] = b->stride[i]; a.sw[i] = w->stride[i];
+        a.si[i] = present(initial_state) ? initial_state->stride[i] : 0;
+        a.so[i] = out->stride[i]; a.sf[i] = final_state->stride[i];
+    }
+    a.L = L; a.H = (int)H; a.dk = (int)dk; a.dv = (int)dv;
+    cudaStream_t s = as_stream(stream);
+    switch (dt) {
+        case MABA_F32: return launch_prefill<float, float>(a, B, dt, s, workspace, workspace_bytes);
+        case MABA_F64:
+            if (sdt != MABA_F64) return set_error(MABA_ERR_DTYPE, "dgda_prefill: float64 needs a float64 state");
+            return launch_prefill<double, double>(a, B, dt, s, workspace, workspace_bytes);
+        case MABA_F16:
+            return sdt == MABA_F32 ? launch_prefill<__half, float>(a, B, dt, s, workspace, workspace_bytes)
+                                   : launch_prefill<__half, __half>(a, B, dt, s, workspace, workspace_bytes);
+        case MABA_BF16:
+            return sdt == MABA_F32 ? launch_prefill<__nv_bfloat16, float>(a, B, dt, s, workspace, workspace_bytes)
+                                   : launch_prefill<__nv_bfloat16, __nv_bfloat16>(a, B, dt, s, workspace, workspace_bytes);
+        default: return set_error(MABA_ERR_DTYPE, "dgda_prefill: unsupported dtype %s", dtype_name(dt));
+    }
+}

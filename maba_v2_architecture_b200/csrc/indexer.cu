@@ -1,0 +1,601 @@
+// DG-Indexer: block pooling (centroids), HCA mean pooling, and fused
+// scoring + top-k block selection.
+//
+// Centroids follow maba_sparse/kernels/common.py:329-350 and
+// cpu_indexer.py:16-50: c = 0.5*(sum/block + max) over 64-token blocks, the
+// tail block zero-padded (so the mean divides by the full block and the max
+// includes 0).
+//
+// Scoring follows cpu_indexer.py:54-112 (the dispatched CPU path: fp32
+// upcast, log1p penalty) and, with decode != 0, the inline decode path of
+// maba_sparse/layers/indexer.py:101-112:
+//   s[t,n] = sum_d (q[t,d]*scale) * c[n,d]  -  lambda*log1p(qb(t)-n)
+// The dot is one sequential fused-multiply-add chain over d (d = 0,1,...),
+// the penalty is fl32(fl32(lambda) * fl32(log1p(delta))) from a table
+// computed once per call; both rules are mirrored by the CPU oracle so the
+// selected indices agree bit for bit.  The score matrix is never
+// materialised: each CTA keeps a running top-k per query token in registers
+// (one entry per lane, warp bitonic sort + merge) and scans candidate blocks
+// from the nearest (largest penalty-free) down, so after the first tile most
+// candidates fail the k-th-best threshold and are rejected by one ballot.
+#include "common.cuh"
+
+#include <climits>
+#include <cmath>
+
+namespace maba {
+namespace {
+
+// ---------------------------------------------------------------------------
+// pooling
+// ---------------------------------------------------------------------------
+struct PoolArgs {
+    const void* in; void* out;
+    int64_t si[3], so[3];
+    int64_t L, nblk;
+    int D, block;
+    int mode;  // 0: centroid 0.5*(mean+max) with zero-padded tail; 1: mean of complete blocks
+};
+
+template <typename TI, typename TO, typename ACC>
+__global__ void pool_kernel(PoolArgs a) {
+    const int64_t n = blockIdx.x;
+    const int64_t bi = blockIdx.y;
+    const TI* in = static_cast<const TI*>(a.in);
+    TO* out = static_cast<TO*>(a.out);
+    const int64_t start = n * a.block;
+    int64_t end = start + a.block;
+    const bool padded = end > a.L;
+    if (padded) end = a.L;
+    for (int d = threadIdx.x; d < a.D; d += blockDim.x) {
+        const TI* p = in + bi * a.si[0] + d * a.si[2];
+        ACC sum = ACC(0);
+        ACC mx = padded ? ACC(0) : -INFINITY;
+        for (int64_t t = start; t < end; ++t) {
+            ACC x = load_as<ACC>(p + t * a.si[1]);
+            sum += x;
+            mx = x > mx ? x : mx;
+        }
+        ACC mean = sum / ACC(a.block);
+        ACC r = a.mode == 0 ? ACC(0.5) * (mean + mx) : mean;
+        store_from<TO, ACC>(out + bi * a.so[0] + n * a.so[1] + d * a.so[2], r);
+    }
+}
+
+template <typename TI, typename TO>
+int launch_pool(PoolArgs& a, int64_t B, cudaStream_t s, const char* what) {
+    using ACC = typename std::conditional<sizeof(TI) == 8, double, float>::type;
+    if (a.nblk == 0 || B == 0) return MABA_OK;
+    dim3 grid((unsigned)a.nblk, (unsigned)B);
+    int threads = a.D >= 128 ? 128 : (a.D >= 64 ? 64 : 32);
+    pool_kernel<TI, TO, ACC><<<grid, threads, 0, s>>>(a);
+    return check_launch(what);
+}
+
+// ---------------------------------------------------------------------------
+// top-k helpers
+// ---------------------------------------------------------------------------
+constexpr unsigned kFull = 0xffffffffu;
+
+template <typename SC>
+__device__ __forceinline__ bool better(SC sa, int ia, SC sb, int ib) {
+    return sa > sb || (sa == sb && ia < ib);
+}
+
+// compare-exchange with the partner lane (lane ^ j); keep_better selects
+// which of the two elements this lane retains.
+template <typename SC>
+__device__ __forceinline__ void cmpx(SC& s, int& i, int j, bool keep_better) {
+    SC os = __shfl_xor_sync(kFull, s, j);
+    int oi = __shfl_xor_sync(kFull, i, j);
+    bool ob = better(os, oi, s, i);
+    if (keep_better == ob) {
+        s = os;
+        i = oi;
+    }
+}
+
+// bitonic sort of one element per lane into descending order (lane 0 best)
+template <typename SC>
+__device__ __forceinline__ void warp_sort_desc(SC& s, int& i, int lane) {
+#pragma unroll
+    for (int k = 2; k <= 32; k <<= 1) {
+#pragma unroll
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            const bool desc = (lane & k) == 0;
+            const bool lower = (lane & j) == 0;
+            cmpx(s, i, j, lower == desc);
+        }
+    }
+}
+
+// list (ls,li) and batch (ns,ni) both sorted descending; leaves the best 32
+// of their union in (ls,li), sorted descending.
+template <typename SC>
+__device__ __forceinline__ void warp_merge(SC& ls, int& li, SC ns, int ni, int lane) {
+    SC rs = __shfl_sync(kFull, ns, 31 - lane);
+    int ri = __shfl_sync(kFull, ni, 31 - lane);
+    if (better(rs, ri, ls, li)) {
+        ls = rs;
+        li = ri;
+    }
+#pragma unroll
+    for (int j = 16; j > 0; j >>= 1) cmpx(ls, li, j, (lane & j) == 0);
+}
+
+// Offer one candidate per lane to the running list; invalid candidates must
+// carry the sentinel (-inf, INT_MAX).
+template <typename SC>
+__device__ __forceinline__ void warp_offer(SC& ls, int& li, SC cs, int ci, int keff, int lane) {
+    SC ts = __shfl_sync(kFull, ls, keff - 1);
+    int ti = __shfl_sync(kFull, li, keff - 1);
+    bool q = better(cs, ci, ts, ti);
+    if (__ballot_sync(kFull, q) == 0u) return;
+    if (!q) {
+        cs = -INFINITY;
+        ci = INT_MAX;
+    }
+    warp_sort_desc(cs, ci, lane);
+    warp_merge(ls, li, cs, ci, lane);
+}
+
+template <typename SC> __device__ __forceinline__ SC fma_sc(SC a, SC b, SC c);
+template <> __device__ __forceinline__ float fma_sc<float>(float a, float b, float c) { return fmaf(a, b, c); }
+template <> __device__ __forceinline__ double fma_sc<double>(double a, double b, double c) { return fma(a, b, c); }
+
+struct TopkArgs {
+    const void* q; const void* c;
+    int64_t* idx; void* scores;
+    const float* pen;  // penalty table, pen[delta]
+    int64_t sq[3], sc[3], si[3], ss[3];
+    int64_t L, nb;
+    int D, block, keff, decode;
+    float scale_f;
+    double scale_d;
+};
+
+__global__ void penalty_table_kernel(float* pen, int64_t n, float lam) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) {
+        // fl32(lambda) * fl32(log1p(delta)), the fp32 arithmetic of cpu_indexer.py:101
+        float l = (float)log1p((double)i);
+        pen[i] = __fmul_rn(lam, l);
+    }
+}
+
+template <typename SC>
+__device__ __forceinline__ SC scale_of(const TopkArgs& a);
+template <> __device__ __forceinline__ float scale_of<float>(const TopkArgs& a) { return a.scale_f; }
+template <> __device__ __forceinline__ double scale_of<double>(const TopkArgs& a) { return a.scale_d; }
+
+__device__ __forceinline__ int64_t query_block(const TopkArgs& a, int64_t t) {
+    return a.decode ? (a.nb - 1) : (t / a.block);
+}
+
+template <typename T, typename SC>
+__device__ __forceinline__ void store_score(const TopkArgs& a, int64_t b, int64_t t, int64_t n, SC v) {
+    T* sp = static_cast<T*>(a.scores);
+    store_from<T, SC>(sp + b * a.ss[0] + t * a.ss[1] + n * a.ss[2], v);
+}
+
+// Write the final list of one token: slots [0, nvalid) from the list,
+// slots [nvalid, keff) with the lowest unused future block indices.
+__device__ __forceinline__ void write_topk_row(const TopkArgs& a, int64_t b, int64_t t, int li, int lane,
+                                               int64_t nmax) {
+    const int64_t ncand = nmax + 1;
+    const int nvalid = (int)(ncand < a.keff ? ncand : a.keff);
+    if (lane < a.keff) {
+        int64_t v = lane < nvalid ? (int64_t)li : (nmax + 1 + (lane - nvalid));
+        a.idx[b * a.si[0] + t * a.si[1] + lane * a.si[2]] = v;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// tile kernel: 64 query tokens x 64 candidate blocks per step (prefill)
+// ---------------------------------------------------------------------------
+constexpr int kTT = 64;   // tokens per CTA
+constexpr int kTN = 64;   // candidates per tile
+constexpr int kTopkThreads = 256;
+
+template <typename T, typename SC>
+__global__ void __launch_bounds__(kTopkThreads) topk_tile_kernel(TopkArgs a) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int D = a.D;
+    SC* Qs = reinterpret_cast<SC*>(smem_raw);   // [D][kTT]
+    SC* Cs = Qs + (size_t)D * kTT;              // [D][kTN]
+    SC* Ss = Cs + (size_t)D * kTN;              // [kTT][kTN+1]
+    const int64_t b = blockIdx.y;
+    const int64_t t0 = (int64_t)blockIdx.x * kTT;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const T* q = static_cast<const T*>(a.q);
+    const T* c = static_cast<const T*>(a.c);
+    const SC scale = scale_of<SC>(a);
+
+    for (int e = tid; e < kTT * D; e += kTopkThreads) {
+        const int tt = e / D, d = e - (e / D) * D;
+        const int64_t t = t0 + tt;
+        SC x = SC(0);
+        if (t < a.L) x = load_as<SC>(q + b * a.sq[0] + t * a.sq[1] + d * a.sq[2]) * scale;
+        Qs[d * kTT + tt] = x;
+    }
+
+    const int64_t tlast = (t0 + kTT - 1 < a.L ? t0 + kTT - 1 : a.L - 1);
+    int64_t n_hi = query_block(a, tlast);
+    if (n_hi > a.nb - 1) n_hi = a.nb - 1;
+
+    SC ls[8];
+    int li[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        ls[j] = -INFINITY;
+        li[j] = INT_MAX;
+    }
+
+    const int ty = tid >> 4, tx = tid & 15;
+    for (int64_t n0 = (n_hi / kTN) * kTN; n0 >= 0; n0 -= kTN) {
+        __syncthreads();
+        for (int e = tid; e < kTN * D; e += kTopkThreads) {
+            const int nn = e / D, d = e - (e / D) * D;
+            const int64_t n = n0 + nn;
+            SC x = SC(0);
+            if (n < a.nb) x = load_as<SC>(c + b * a.sc[0] + n * a.sc[1] + d * a.sc[2]);
+            Cs[d * kTN + nn] = x;
+        }
+        __syncthreads();
+
+        SC acc[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) acc[i][j] = SC(0);
+        for (int d = 0; d < D; ++d) {
+            SC qa[4], cb[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) qa[i] = Qs[d * kTT + 4 * ty + i];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) cb[j] = Cs[d * kTN + 4 * tx + j];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] = fma_sc<SC>(qa[i], cb[j], acc[i][j]);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int tt = 4 * ty + i;
+            const int64_t t = t0 + tt;
+            const int64_t qb = query_block(a, t);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int nn = 4 * tx + j;
+                const int64_t n = n0 + nn;
+                SC v = -INFINITY;
+                if (t < a.L && n <= qb && n < a.nb) v = acc[i][j] - (SC)a.pen[qb - n];
+                Ss[tt * (kTN + 1) + nn] = v;
+            }
+        }
+        __syncthreads();
+
+        if (a.scores != nullptr) {
+            for (int e = tid; e < kTT * kTN; e += kTopkThreads) {
+                const int tt = e / kTN, nn = e - (e / kTN) * kTN;
+                const int64_t t = t0 + tt, n = n0 + nn;
+                if (t < a.L && n < a.nb) store_score<T, SC>(a, b, t, n, Ss[tt * (kTN + 1) + nn]);
+            }
+        }
+
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int tt = warp * 8 + j;
+            const int64_t t = t0 + tt;
+            if (t < a.L) {
+                const int64_t qb = query_block(a, t);
+                const int64_t nmax = qb < a.nb - 1 ? qb : a.nb - 1;
+#pragma unroll
+                for (int half = 0; half < 2; ++half) {
+                    const int nn = half * 32 + lane;
+                    const int64_t n = n0 + nn;
+                    SC s = -INFINITY;
+                    int ci = INT_MAX;
+                    if (n <= nmax) {
+                        s = Ss[tt * (kTN + 1) + nn];
+                        ci = (int)n;
+                    }
+                    warp_offer(ls[j], li[j], s, ci, a.keff, lane);
+                }
+            }
+        }
+    }
+
+    // -inf for candidates past the scanned range
+    if (a.scores != nullptr) {
+        const int64_t nstart = (n_hi / kTN + 1) * kTN;
+        for (int tt = warp; tt < kTT; tt += kTopkThreads / 32) {
+            const int64_t t = t0 + tt;
+            if (t >= a.L) continue;
+            for (int64_t n = nstart + lane; n < a.nb; n += 32) store_score<T, SC>(a, b, t, n, SC(-INFINITY));
+        }
+    }
+
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int tt = warp * 8 + j;
+        const int64_t t = t0 + tt;
+        if (t < a.L) {
+            const int64_t qb = query_block(a, t);
+            const int64_t nmax = qb < a.nb - 1 ? qb : a.nb - 1;
+            write_topk_row(a, b, t, li[j], lane, nmax);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// token kernel: one CTA per query token (decode / single token), 8 warps
+// ---------------------------------------------------------------------------
+template <typename T, typename SC>
+__global__ void __launch_bounds__(kTopkThreads) topk_token_kernel(TopkArgs a) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int D = a.D;
+    SC* qs = reinterpret_cast<SC*>(smem_raw);          // [D]
+    SC* cs_all = qs + D;                                // [8 warps][32][D+1]
+    SC* lists_s = cs_all + (size_t)8 * 32 * (D + 1);    // [8][32]
+    int* lists_i = reinterpret_cast<int*>(lists_s + 8 * 32);
+    const int64_t b = blockIdx.y, t = blockIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const T* q = static_cast<const T*>(a.q);
+    const T* c = static_cast<const T*>(a.c);
+    const SC scale = scale_of<SC>(a);
+    for (int d = tid; d < D; d += kTopkThreads) qs[d] = load_as<SC>(q + b * a.sq[0] + t * a.sq[1] + d * a.sq[2]) * scale;
+    __syncthreads();
+    const int64_t qb = query_block(a, t);
+    const int64_t nmax = qb < a.nb - 1 ? qb : a.nb - 1;
+    SC* cs = cs_all + (size_t)warp * 32 * (D + 1);
+    SC ls = -INFINITY;
+    int li = INT_MAX;
+    // chunk g covers candidates (nmax - 32(g+1), nmax - 32g]
+    const int64_t nchunks = (nmax + 1 + 31) / 32;
+    for (int64_t g = warp; g < nchunks; g += kTopkThreads / 32) {
+        const int64_t nbase = nmax - 32 * g - 31;  // lowest candidate of the chunk (may be < 0)
+        for (int e = lane; e < 32 * D; e += 32) {
+            const int r = e / D, d = e - (e / D) * D;
+            const int64_t n = nbase + r;
+            SC x = SC(0);
+            if (n >= 0) x = load_as<SC>(c + b * a.sc[0] + n * a.sc[1] + d * a.sc[2]);
+            cs[r * (D + 1) + d] = x;
+        }
+        __syncwarp();
+        const int64_t n = nbase + lane;
+        SC acc = SC(0);
+        for (int d = 0; d < D; ++d) acc = fma_sc<SC>(qs[d], cs[lane * (D + 1) + d], acc);
+        SC s = -INFINITY;
+        int ci = INT_MAX;
+        if (n >= 0) {
+            s = acc - (SC)a.pen[qb - n];
+            ci = (int)n;
+            if (a.scores != nullptr) store_score<T, SC>(a, b, t, n, s);
+        }
+        warp_offer(ls, li, s, ci, a.keff, lane);
+        __syncwarp();
+    }
+    if (a.scores != nullptr) {
+        for (int64_t n = nmax + 1 + tid; n < a.nb; n += kTopkThreads) store_score<T, SC>(a, b, t, n, SC(-INFINITY));
+    }
+    lists_s[warp * 32 + lane] = ls;
+    lists_i[warp * 32 + lane] = li;
+    __syncthreads();
+    if (warp == 0) {
+        for (int w = 1; w < kTopkThreads / 32; ++w) {
+            SC ns = lists_s[w * 32 + lane];
+            int ni = lists_i[w * 32 + lane];
+            warp_merge(ls, li, ns, ni, lane);
+        }
+        write_topk_row(a, b, t, li, lane, nmax);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// generic kernel for top_k > 32: full bitonic sort of one token's candidates
+// ---------------------------------------------------------------------------
+template <typename T, typename SC>
+__global__ void __launch_bounds__(kTopkThreads) topk_sort_kernel(TopkArgs a, int p2) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int D = a.D;
+    SC* qs = reinterpret_cast<SC*>(smem_raw);
+    SC* ks = qs + D;
+    int* ki = reinterpret_cast<int*>(ks + p2);
+    const int64_t b = blockIdx.y, t = blockIdx.x;
+    const int tid = threadIdx.x;
+    const T* q = static_cast<const T*>(a.q);
+    const T* c = static_cast<const T*>(a.c);
+    const SC scale = scale_of<SC>(a);
+    for (int d = tid; d < D; d += kTopkThreads) qs[d] = load_as<SC>(q + b * a.sq[0] + t * a.sq[1] + d * a.sq[2]) * scale;
+    __syncthreads();
+    const int64_t qb = query_block(a, t);
+    const int64_t nmax = qb < a.nb - 1 ? qb : a.nb - 1;
+    for (int n = tid; n < p2; n += kTopkThreads) {
+        SC s = -INFINITY;
+        int ci = INT_MAX;
+        if (n <= nmax) {
+            SC acc = SC(0);
+            const T* cr = c + b * a.sc[0] + (int64_t)n * a.sc[1];
+            for (int d = 0; d < D; ++d) acc = fma_sc<SC>(qs[d], load_as<SC>(cr + d * a.sc[2]), acc);
+            s = acc - (SC)a.pen[qb - n];
+            ci = n;
+        }
+        if (a.scores != nullptr && n < a.nb) store_score<T, SC>(a, b, t, n, s);
+        ks[n] = s;
+        ki[n] = ci;
+    }
+    __syncthreads();
+    for (int k = 2; k <= p2; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int i = tid; i < p2; i += kTopkThreads) {
+                const int pj = i ^ j;
+                if (pj > i) {
+                    const bool desc = (i & k) == 0;
+                    SC s0 = ks[i], s1 = ks[pj];
+                    int i0 = ki[i], i1 = ki[pj];
+                    const bool second_better = better(s1, i1, s0, i0);
+                    if (second_better == desc) {
+                        ks[i] = s1; ki[i] = i1;
+                        ks[pj] = s0; ki[pj] = i0;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    }
+    const int64_t ncand = nmax + 1;
+    const int nvalid = (int)(ncand < a.keff ? ncand : a.keff);
+    for (int s = tid; s < a.keff; s += kTopkThreads) {
+        int64_t v = s < nvalid ? (int64_t)ki[s] : (nmax + 1 + (s - nvalid));
+        a.idx[b * a.si[0] + t * a.si[1] + s * a.si[2]] = v;
+    }
+}
+
+template <typename T>
+int launch_topk(TopkArgs& a, int64_t B, cudaStream_t s) {
+    using SC = typename std::conditional<sizeof(T) == 8, double, float>::type;
+    const int D = a.D;
+    if (a.keff > 32) {
+        int p2 = 1;
+        while (p2 < a.nb) p2 <<= 1;
+        const size_t smem = sizeof(SC) * (D + p2) + sizeof(int) * p2;
+        if (smem > 200 * 1024)
+            return set_error(MABA_ERR_UNSUPPORTED, "index_topk: top_k=%d > 32 needs nb <= %d", a.keff,
+                             (int)(200 * 1024 / (sizeof(SC) + sizeof(int))));
+        auto kern = topk_sort_kernel<T, SC>;
+        if (smem > 48 * 1024)
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        dim3 grid((unsigned)a.L, (unsigned)B);
+        kern<<<grid, kTopkThreads, smem, s>>>(a, p2);
+        return check_launch("index_topk(sort)");
+    }
+    if (a.decode || a.L < kTT) {
+        const size_t smem = sizeof(SC) * (D + (size_t)8 * 32 * (D + 1) + 8 * 32) + sizeof(int) * 8 * 32;
+        if (smem > 200 * 1024) return set_error(MABA_ERR_UNSUPPORTED, "index_topk: d_idx=%d too large", D);
+        auto kern = topk_token_kernel<T, SC>;
+        if (smem > 48 * 1024)
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        dim3 grid((unsigned)a.L, (unsigned)B);
+        kern<<<grid, kTopkThreads, smem, s>>>(a);
+        return check_launch("index_topk(token)");
+    }
+    const size_t smem = sizeof(SC) * ((size_t)D * kTT + (size_t)D * kTN + (size_t)kTT * (kTN + 1));
+    if (smem > 200 * 1024) return set_error(MABA_ERR_UNSUPPORTED, "index_topk: d_idx=%d too large", D);
+    auto kern = topk_tile_kernel<T, SC>;
+    if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    dim3 grid((unsigned)ceil_div(a.L, kTT), (unsigned)B);
+    kern<<<grid, kTopkThreads, smem, s>>>(a);
+    return check_launch("index_topk(tile)");
+}
+
+int64_t penalty_len(int64_t L, int64_t nb, int32_t block, int decode) {
+    int64_t n = nb;
+    if (!decode && L > 0 && block > 0) {
+        int64_t qmax = (L - 1) / block + 1;
+        if (qmax > n) n = qmax;
+    }
+    return n > 0 ? n : 1;
+}
+
+}  // namespace
+}  // namespace maba
+
+using namespace maba;
+
+extern "C" int maba_compute_centroids(const maba_tensor* k_idx, const maba_tensor* out, int32_t block_size,
+                                      void* stream) {
+    if (!present(k_idx) || k_idx->ndim != 3)
+        return set_error(MABA_ERR_INVALID, "compute_centroids: k_idx must be 3D [B, L, d_idx]");
+    if (block_size <= 0) return set_error(MABA_ERR_INVALID, "compute_centroids: block_size must be positive");
+    const int64_t B = k_idx->shape[0], L = k_idx->shape[1], D = k_idx->shape[2];
+    const int64_t nb = ceil_div(L, block_size);
+    const int64_t so[3] = {B, nb, D};
+    MABA_TRY(expect_shape(out, "compute_centroids: out", 3, so));
+    MABA_TRY(expect_dtype(out, "compute_centroids: out", k_idx->dtype));
+    PoolArgs a{};
+    a.in = k_idx->data; a.out = out->data;
+    for (int i = 0; i < 3; ++i) { a.si[i] = k_idx->stride[i]; a.so[i] = out->stride[i]; }
+    a.L = L; a.nblk = nb; a.D = (int)D; a.block = block_size; a.mode = 0;
+    cudaStream_t s = as_stream(stream);
+    return MABA_DISPATCH_FLOAT(k_idx->dtype, "compute_centroids", [&] { return launch_pool<T, T>(a, B, s, "compute_centroids"); });
+}
+
+extern "C" int maba_hca_pool(const maba_tensor* c_kv, const maba_tensor* out, int32_t r, void* stream) {
+    if (!present(c_kv) || c_kv->ndim != 3) return set_error(MABA_ERR_INVALID, "hca_pool: c_kv must be [B, L, d_c]");
+    if (r <= 0) return set_error(MABA_ERR_INVALID, "hca_pool: r must be positive");
+    const int64_t B = c_kv->shape[0], L = c_kv->shape[1], D = c_kv->shape[2];
+    const int64_t nc = L / r;
+    const int64_t so[3] = {B, nc, D};
+    MABA_TRY(expect_shape(out, "hca_pool: out", 3, so));
+    PoolArgs a{};
+    a.in = c_kv->data; a.out = out->data;
+    for (int i = 0; i < 3; ++i) { a.si[i] = c_kv->stride[i]; a.so[i] = out->stride[i]; }
+    a.L = L; a.nblk = nc; a.D = (int)D; a.block = r; a.mode = 1;
+    cudaStream_t s = as_stream(stream);
+    const int odt = out->dtype;
+    return MABA_DISPATCH_FLOAT(c_kv->dtype, "hca_pool", [&] {
+        if (odt == MABA_F32) return launch_pool<T, float>(a, B, s, "hca_pool");
+        if (odt == c_kv->dtype) return launch_pool<T, T>(a, B, s, "hca_pool");
+        return set_error(MABA_ERR_DTYPE, "hca_pool: out dtype must be float32 or c_kv's dtype");
+    });
+}
+
+extern "C" size_t maba_index_topk_workspace_size(int64_t B, int64_t L, int64_t nb, int32_t top_k) {
+    (void)B; (void)top_k;
+    // penalty table; the block size is not known here, so size for the
+    // largest query block any block_size >= 1 could produce is not bounded:
+    // callers pass L and nb and the table holds max(nb, L) entries.
+    int64_t n = nb > L ? nb : L;
+    if (n < 1) n = 1;
+    return (size_t)((n * sizeof(float) + 255) / 256 * 256);
+}
+
+extern "C" int maba_index_topk(const maba_tensor* q_idx, const maba_tensor* centroids, float lambda_dist,
+                               int32_t top_k, int32_t block_size, int32_t decode, const maba_tensor* idx_out,
+                               const maba_tensor* scores_out, void* workspace, size_t workspace_bytes,
+                               void* stream) {
+    if (!present(q_idx) || !present(centroids) || q_idx->ndim != 3 || centroids->ndim != 3)
+        return set_error(MABA_ERR_INVALID, "index_topk: q_idx and centroids must be 3D");
+    if (top_k <= 0) return set_error(MABA_ERR_INVALID, "index_topk: top_k must be positive, got %d", top_k);
+    if (block_size <= 0) return set_error(MABA_ERR_INVALID, "index_topk: block_size must be positive");
+    const int64_t B = q_idx->shape[0], L = q_idx->shape[1], D = q_idx->shape[2];
+    const int64_t nb = centroids->shape[1];
+    if (centroids->shape[0] != B || centroids->shape[2] != D)
+        return set_error(MABA_ERR_INVALID, "index_topk: dimension mismatch between q_idx and centroids");
+    MABA_TRY(expect_dtype(centroids, "index_topk: centroids", q_idx->dtype));
+    const int64_t keff = top_k < nb ? top_k : nb;
+    const int64_t si[3] = {B, L, keff};
+    MABA_TRY(expect_shape(idx_out, "index_topk: idx_out", 3, si));
+    MABA_TRY(expect_dtype(idx_out, "index_topk: idx_out", MABA_I64));
+    if (present(scores_out)) {
+        const int64_t ss[3] = {B, L, nb};
+        MABA_TRY(expect_shape(scores_out, "index_topk: scores_out", 3, ss));
+        MABA_TRY(expect_dtype(scores_out, "index_topk: scores_out", q_idx->dtype));
+    }
+    if (L == 0 || nb == 0 || B == 0) return MABA_OK;  // caller fills the empty result
+    if (nb > INT_MAX / 2) return set_error(MABA_ERR_UNSUPPORTED, "index_topk: nb too large");
+    const int64_t plen = penalty_len(L, nb, block_size, decode);
+    const size_t need = (size_t)plen * sizeof(float);
+    if (workspace == nullptr || workspace_bytes < need)
+        return set_error(MABA_ERR_WORKSPACE, "index_topk: workspace of %zu bytes required, got %zu", need,
+                         workspace_bytes);
+    cudaStream_t s = as_stream(stream);
+    float* pen = static_cast<float*>(workspace);
+    penalty_table_kernel<<<(unsigned)ceil_div(plen, 256), 256, 0, s>>>(pen, plen, lambda_dist);
+    MABA_TRY(check_launch("index_topk(penalty)"));
+
+    TopkArgs a{};
+    a.q = q_idx->data; a.c = centroids->data;
+    a.idx = static_cast<int64_t*>(idx_out->data);
+    a.scores = present(scores_out) ? scores_out->data : nullptr;
+    a.pen = pen;
+    for (int i = 0; i < 3; ++i) {
+        a.sq[i] = q_idx->stride[i]; a.sc[i] = centroids->stride[i]; a.si[i] = idx_out->stride[i];
+        a.ss[i] = present(scores_out) ? scores_out->stride[i] : 0;
+    }
+    a.L = L; a.nb = nb; a.D = (int)D; a.block = block_size; a.keff = (int)keff; a.decode = decode ? 1 : 0;
+    a.scale_d = 1.0 / sqrt((double)D);
+    a.scale_f = (float)a.scale_d;
+    return MABA_DISPATCH_FLOAT(q_idx->dtype, "index_topk", [&] { return launch_topk<T>(a, B, s); });
+}

@@ -1,0 +1,38 @@
+// Internal interface shared by the MABA-SA attention kernels.
+#pragma once
+#include "common.cuh"
+
+namespace maba {
+
+struct SaArgs {
+    const void* qhat;        // [B,Lq,H,DC]
+    const void* ckv;         // [B,Lkv,DC]
+    const void* hca;         // [B,NC,DC]  (may be null when NC == 0)
+    const int64_t* top_idx;  // [B,Lq,K]
+    const void* gate;        // [B,Lq,3] or [B,H,Lq,3]
+    void* out;               // [B,Lq,H,DC]
+    int64_t sq[4], sc[3], sh[3], st[3], sg[4], so[4];
+    int64_t Lq, Lkv, NC;
+    int H, DC, K;
+    int window, n_sinks, block, hca_r, gate4d;
+    void* workspace;
+    size_t workspace_bytes;
+};
+
+int sa_attention_simt(SaArgs& a, int64_t B, int dtype, cudaStream_t s);
+int sa_attention_mma(SaArgs& a, int64_t B, int dtype, cudaStream_t s);
+bool sa_attention_mma_supported(const SaArgs& a, int dtype);
+size_t sa_attention_mma_workspace(int dtype, int64_t B, int64_t Lq, int64_t Lkv, int64_t H, int64_t DC, int64_t K,
+                                  int32_t block);
+
+inline size_t sa_attention_workspace_bytes(int dtype, int64_t B, int64_t Lq, int64_t Lkv, int64_t H, int64_t DC,
+                                           int64_t K, int32_t block) {
+    return sa_attention_mma_workspace(dtype, B, Lq, Lkv, H, DC, K, block);
+}
+
+inline int sa_attention_dispatch(SaArgs& a, int64_t B, int dtype, cudaStream_t s) {
+    if (sa_attention_mma_supported(a, dtype)) return sa_attention_mma(a, B, dtype, s);
+    return sa_attention_simt(a, B, dtype, s);
+}
+
+}  // namespace maba

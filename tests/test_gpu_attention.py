@@ -1,0 +1,140 @@
+"""MABA-SA fused latent attention (kernel and layer) vs the CPU oracle and the
+reference's golden layer outputs; DGDA layer vs the reference."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+import maba_v2_architecture_b200 as mb
+from helpers import RTOL_BF16, RTOL_FP32, assert_rel, golden, sub
+from maba_v2_architecture_b200.config import MabaSparseConfig
+from maba_v2_architecture_b200.layers import DGDALayer, MabaSparseAttention
+from maba_v2_architecture_b200.workloads import init_module_, sa_inputs
+from oracle import attention as OA
+from oracle import indexer as OI
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def rand_case(B, Lq, Lkv, H, DC, K, block, seed, gate4d=False):
+    g = torch.Generator().manual_seed(seed)
+    qhat = torch.randn(B, Lq, H, DC, generator=g) * 0.3
+    c = torch.randn(B, Lkv, DC, generator=g)
+    nb = (Lkv + block - 1) // block
+    top = torch.stack([torch.stack([torch.randperm(nb + 2, generator=g)[:K] for _ in range(Lq)]) for _ in range(B)])
+    gate = torch.randn(B, H, Lq, 3, generator=g) if gate4d else torch.randn(B, Lq, 3, generator=g)
+    return qhat, c, top.long(), gate
+
+
+@pytest.mark.parametrize("B,Lq,Lkv,H,DC,K,window,block,r,gate4d", [
+    (2, 300, 300, 3, 128, 5, 48, 16, 32, False),
+    (1, 50, 330, 2, 128, 6, 64, 16, 16, True),     # chunked prefill: queries at the end of a longer cache
+    (1, 1, 700, 10, 128, 8, 128, 64, 64, False),   # decode-shaped
+    (2, 90, 90, 4, 64, 3, 16, 8, 8, False),         # small d_c, window shorter than the prefix
+    (1, 40, 40, 2, 96, 2, 128, 64, 64, False),      # everything inside the window, HCA early path only
+])
+def test_kernel_vs_oracle(B, Lq, Lkv, H, DC, K, window, block, r, gate4d):
+    qhat, c, top, gate = rand_case(B, Lq, Lkv, H, DC, K, block, seed=B * 1000 + Lq, gate4d=gate4d)
+    hca = mb.b200_hca_pool(c.to(DEV), r) if Lkv >= r else None
+    out = mb.b200_sa_attention(qhat.to(DEV), c.to(DEV), hca, top.to(DEV), gate.to(DEV), window_size=window,
+                               n_sinks=4, block_size=block, hca_r=r)
+    ref = OA.sa_attention_latent(qhat.numpy(), c.numpy(), top.numpy(), gate.numpy(), window, 4, block, r)
+    assert_rel(out, ref, RTOL_FP32, "fp32")
+    outb = mb.b200_sa_attention(qhat.to(DEV, torch.bfloat16), c.to(DEV, torch.bfloat16),
+                                None if hca is None else hca.to(torch.bfloat16), top.to(DEV),
+                                gate.to(DEV, torch.bfloat16), window_size=window, n_sinks=4, block_size=block,
+                                hca_r=r)
+    assert outb.dtype == torch.bfloat16
+    assert_rel(outb, ref, RTOL_BF16, "bf16")
+
+
+def load_sa(name):
+    g = sub(golden("sa_layer"), f"{name}.")
+    window, block, top_k, r = (int(v) for v in g["kw"])
+    cfg = MabaSparseConfig(dim=64, n_heads=2, d_head=32, kernel_size=4, chunk_size=16, eps=1e-6, window_size=window,
+                           block_size=block, top_k=top_k, hca_pool_size=r, dist_lambda=float(g["lam"]))
+    layer = MabaSparseAttention(cfg).eval().to(DEV)
+    layer.load_state_dict({k: torch.from_numpy(v) for k, v in sub(g, "w.").items()})
+    return g, layer
+
+
+@pytest.mark.parametrize("name", ["a", "b", "c"])
+def test_layer_vs_reference(name):
+    g, layer = load_sa(name)
+    with torch.no_grad():
+        y, c_full = layer(torch.from_numpy(g["x"]).to(DEV))
+    assert_rel(c_full, g["c_full"], 1e-5, "c_full")
+    assert_rel(y, g["y"], RTOL_FP32, "y")
+
+
+def test_layer_decode_equals_reference_steps():
+    g = sub(golden("sa_layer"), "dec.")
+    window, block, top_k, r = (int(v) for v in g["kw"])
+    cfg = MabaSparseConfig(dim=64, n_heads=2, d_head=32, kernel_size=4, chunk_size=16, eps=1e-6, window_size=window,
+                           block_size=block, top_k=top_k, hca_pool_size=r)
+    layer = MabaSparseAttention(cfg).eval().to(DEV)
+    layer.load_state_dict({k: torch.from_numpy(v) for k, v in sub(g, "w.").items()})
+    x = torch.from_numpy(g["x"]).to(DEV)
+    with torch.no_grad():
+        y_pre, past = layer(x[:, :40])
+        ys = []
+        for t in range(40, 60):
+            yt, past = layer(x[:, t:t + 1], past_c_kv=past)
+            ys.append(yt)
+        layer.reset_cache()
+        y_full, _ = layer(x)
+    assert_rel(y_pre, g["y_pre"], RTOL_FP32, "prefill")
+    assert_rel(torch.cat(ys, 1), g["y_steps"], RTOL_FP32, "decode steps")
+    assert_rel(y_full, g["y_full"], RTOL_FP32, "full")
+    assert_rel(torch.cat(ys, 1), y_full[:, 40:], 1e-4, "decode == prefill")
+
+
+def test_layer_101m_shape():
+    g = sub(golden("sa_layer"), "big.")
+    layer = init_module_(MabaSparseAttention(MabaSparseConfig(dim=640, n_heads=10, d_head=64, dist_lambda=0.1)),
+                         seed=123).eval().to(DEV)
+    x = torch.randn(1, 2304, 640, generator=torch.Generator().manual_seed(124)).to(DEV)
+    with torch.no_grad():
+        y, _ = layer(x)
+    rows = torch.as_tensor(g["rows"], device=DEV)
+    assert_rel(y[0, rows], g["y_rows"], RTOL_FP32, "y rows")
+    assert abs(y.double().sum().item() - float(g["y_sum"])) <= 1e-4 * float(g["y_abs"])
+
+
+def test_config2_attention_sampled_rows():
+    """Config 2 (T=65,536, bf16) through indexer + fused attention; rows checked against the oracle."""
+    wl = sa_inputs()
+    dt = torch.bfloat16
+    c_kv = wl.c_kv.to(DEV, dt)
+    c = mb.b200_compute_centroids(wl.k_idx.to(DEV, dt))
+    idx = mb.b200_index_topk(wl.q_idx.to(DEV, dt), c, lambda_dist=0.1, top_k=32)
+    qhat = mb.ops.absorb_queries(wl.q.to(DEV, dt), wl.w_uk.to(DEV), 10, 0.125)
+    hca = mb.b200_hca_pool(c_kv, 64)
+    out = mb.b200_sa_attention(qhat, c_kv, hca, idx, wl.gate.to(DEV, dt))
+    assert out.shape == (1, 65536, 10, 128) and bool(torch.isfinite(out.float()).all())
+    rows = np.array([0, 5, 62, 63, 64, 127, 128, 2047, 2048, 4095, 33333, 65535])
+    ref = OA.sa_attention_latent(qhat.float().cpu().numpy(), c_kv.float().cpu().numpy(), idx.cpu().numpy(),
+                                 wl.gate.to(dt).float().numpy(), 128, 4, 64, 64, rows=rows)
+    assert_rel(out[:, torch.as_tensor(rows, device=DEV)], ref, RTOL_BF16, "rows")
+
+
+def test_dgda_layer_vs_reference():
+    g = golden("dgda_layer")
+    cfg = MabaSparseConfig(dim=64, n_heads=2, d_head=32, kernel_size=4, chunk_size=16, eps=1e-6)
+    layer = DGDALayer(cfg).eval().to(DEV)
+    layer.load_state_dict({k: torch.from_numpy(v) for k, v in sub(g, "w.").items()})
+    x = torch.from_numpy(g["x"]).to(DEV)
+    with torch.no_grad():
+        y, S, cs = layer(x[:, :40])
+        ys = []
+        for t in range(40, 50):
+            yt, S, cs = layer.step(x[:, t:t + 1], state=S, conv_state=cs)
+            ys.append(yt)
+        yf, Sf, _ = layer(x)
+    assert_rel(y, g["y40"], RTOL_FP32, "prefill")
+    assert_rel(torch.cat(ys, 1), g["y_steps"], RTOL_FP32, "steps")
+    assert_rel(S, g["S_steps"], RTOL_FP32, "state after steps")
+    assert_rel(yf, g["y_full"], RTOL_FP32, "full")
+    assert_rel(Sf, g["S_full"], RTOL_FP32, "full state")

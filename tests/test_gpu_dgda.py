@@ -1,0 +1,218 @@
+"""DGDA prefill / step kernels vs the CPU oracle and the reference's golden outputs."""
+import numpy as np
+import pytest
+import torch
+
+import maba_v2_architecture_b200 as mb
+from helpers import RTOL_BF16, RTOL_FP16, RTOL_FP32, assert_rel, golden, sub
+from maba_v2_architecture_b200.workloads import dgda_inputs
+from oracle import dgda as OD
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def cu(x, dtype=torch.float32):
+    return None if x is None else torch.as_tensor(np.asarray(x)).to(DEV, dtype)
+
+
+def run_prefill(d, dtype=torch.float32, **kw):
+    o, S = mb.b200_dgda_prefill(cu(d["q"], dtype), cu(d["k"], dtype), cu(d["v"], dtype), alpha=cu(d.get("alpha"), dtype),
+                                b=cu(d["b"], dtype), w=cu(d["w"], dtype), initial_state=cu(d.get("s0"), dtype),
+                                log_alpha=cu(d.get("la"), dtype), **kw)
+    torch.cuda.synchronize()
+    return o, S
+
+
+def test_small_with_state():
+    g = sub(golden("dgda_prefill"), "small.")
+    o, S = run_prefill(g)
+    assert o.shape == g["o"].shape and o.dtype == torch.float32 and o.is_contiguous()
+    assert_rel(o, g["o"], RTOL_FP32, "o")
+    assert_rel(S, g["S"], RTOL_FP32, "S")
+
+
+@pytest.mark.parametrize("L", [1, 7, 17, 63, 65, 129])
+def test_lengths_log_alpha_only(L):
+    g = sub(golden("dgda_prefill"), f"len{L}.")
+    o, S = run_prefill(g)
+    assert_rel(o, g["o"], RTOL_FP32, "o")
+    assert_rel(S, g["S"], RTOL_FP32, "S")
+
+
+@pytest.mark.parametrize("i", range(5))
+def test_extreme_decay(i):
+    g = sub(golden("dgda_prefill"), "ext.")
+    d = dict(g)
+    d["alpha"] = np.full_like(g["q"], g["alphas"][i])
+    o, S = run_prefill(d)
+    assert torch.isfinite(o).all() and torch.isfinite(S).all()
+    assert_rel(o, g[f"alpha{i}.o"], RTOL_FP32, "o")
+    assert_rel(S, g[f"alpha{i}.S"], RTOL_FP32, "S")
+
+
+@pytest.mark.parametrize("name", ["b0", "b1", "w0", "w1"])
+def test_extreme_gates(name):
+    g = sub(golden("dgda_prefill"), "ext.")
+    d = dict(g)
+    d["alpha"] = g["alpha_mid"]
+    if name[0] == "b":
+        d["b"] = np.full_like(g["b"], float(name[1]))
+    else:
+        d["w"] = np.full_like(g["w"], float(name[1]))
+    o, S = run_prefill(d)
+    assert_rel(o, g[f"{name}.o"], RTOL_FP32, "o")
+    assert_rel(S, g[f"{name}.S"], RTOL_FP32, "S")
+
+
+def test_stress_inputs():
+    g = sub(golden("dgda_prefill"), "stress.")
+    o, S = run_prefill(g)
+    assert_rel(o, g["o"], RTOL_FP32, "o")
+    assert_rel(S, g["S"], RTOL_FP32, "S")
+
+
+@pytest.mark.parametrize("variant", ["cfg1", "cfg1pc"])
+def test_config1_full(variant):
+    """Config 1 (B=2, T=512, H=10, 64x64, fp32) against the sequential oracle and the reference."""
+    x = dgda_inputs(seed=0 if variant == "cfg1" else 10, per_channel=variant == "cfg1pc")
+    g = sub(golden("dgda_prefill"), f"{variant}.")
+    o, S = mb.b200_dgda_prefill(x["q"].to(DEV), x["k"].to(DEV), x["v"].to(DEV), x["alpha"].to(DEV), x["b"].to(DEV),
+                                x["w"].to(DEV), chunk_size=64, log_alpha=x["log_alpha"].to(DEV))
+    ro, rS = OD.dgda_sequential(*(x[k].numpy() for k in ("q", "k", "v", "alpha", "b", "w")))
+    assert_rel(o, ro, RTOL_FP32, "o vs oracle")
+    assert_rel(S, rS, RTOL_FP32, "S vs oracle")
+    assert_rel(o[:, :, ::8], g["o_sub"], RTOL_FP32, "o vs reference")
+    assert_rel(S, g["S"], RTOL_FP32, "S vs reference")
+
+
+@pytest.mark.parametrize("B,H,L", [(1, 2, 4096), (1, 1, 3000), (2, 3, 2500)])
+def test_segmented_long_sequence(B, H, L):
+    """Few heads, long sequence: the segment-parallel (affine transition) path."""
+    x = dgda_inputs(B=B, T=L, H=H, seed=5, per_channel=True)
+    s0 = torch.randn(B, H, 64, 64, generator=torch.Generator().manual_seed(6)) * 0.1
+    o, S = mb.b200_dgda_prefill(x["q"].to(DEV), x["k"].to(DEV), x["v"].to(DEV), None, x["b"].to(DEV), x["w"].to(DEV),
+                                initial_state=s0.to(DEV), log_alpha=x["log_alpha"].to(DEV))
+    ro, rS = OD.dgda_sequential(*(x[k].numpy() for k in ("q", "k", "v", "alpha", "b", "w")), initial_state=s0.numpy())
+    assert_rel(o, ro, RTOL_FP32, "o")
+    assert_rel(S, rS, RTOL_FP32, "S")
+
+
+def test_token_major_strided_inputs_and_output_layout():
+    B, L, H, d = 2, 150, 3, 64
+    gen = torch.Generator().manual_seed(3)
+    mk = lambda: torch.randn(B, L, H, d, generator=gen)
+    q, v = mk(), mk()
+    k = torch.nn.functional.normalize(mk(), dim=-1)
+    b, w = torch.rand(B, L, H, d, generator=gen), torch.rand(B, L, H, d, generator=gen)
+    la = -torch.nn.functional.softplus(mk())
+    tv = lambda t: t.to(DEV).transpose(1, 2)  # [B,H,L,d] views, non-contiguous
+    o, S = mb.b200_dgda_prefill(tv(q), tv(k), tv(v), None, tv(b), tv(w), log_alpha=tv(la), out_layout="blhd")
+    assert not o.is_contiguous() and o.transpose(1, 2).is_contiguous()
+    tn = lambda t: t.transpose(1, 2).numpy()
+    ro, rS = OD.dgda_sequential(tn(q), tn(k), tn(v), None, tn(b), tn(w), log_alpha=tn(la))
+    assert_rel(o, ro, RTOL_FP32, "o")
+    assert_rel(S, rS, RTOL_FP32, "S")
+
+
+@pytest.mark.parametrize("dtype,rtol", [(torch.bfloat16, RTOL_BF16), (torch.float16, RTOL_FP16)])
+def test_16bit_inputs(dtype, rtol):
+    x = dgda_inputs(B=2, T=300, H=4, seed=8, per_channel=True)
+    args = [x[k].to(DEV, dtype) for k in ("q", "k", "v", "alpha", "b", "w")]
+    o, S = mb.b200_dgda_prefill(*args)
+    assert o.dtype == dtype and S.dtype == dtype
+    ref = {k: x[k].to(dtype).float().numpy() for k in x}
+    ro, rS = OD.dgda_sequential(ref["q"], ref["k"], ref["v"], ref["alpha"], ref["b"], ref["w"])
+    assert_rel(o, ro, rtol, "o")
+    assert_rel(S, rS, rtol, "S")
+    o2, S2 = mb.b200_dgda_prefill(*args, state_dtype=torch.float32)
+    assert S2.dtype == torch.float32
+    assert_rel(S2, rS, rtol, "fp32 state")
+
+
+def test_fp64():
+    g = sub(golden("dgda_prefill"), "small.")
+    o, S = run_prefill(g, torch.float64)
+    assert o.dtype == torch.float64
+    ro, rS = OD.dgda_sequential(g["q"], g["k"], g["v"], g["alpha"], g["b"], g["w"], initial_state=g["s0"])
+    assert_rel(o, ro, 1e-10, "o")
+    assert_rel(S, rS, 1e-10, "S")
+
+
+def test_chaining_through_initial_state():
+    x = {k: v.to(DEV) for k, v in dgda_inputs(B=1, T=700, H=2, seed=9, per_channel=True).items()}
+    cut = 333
+    part = lambda s, e: [x[k][:, :, s:e] for k in ("q", "k", "v", "alpha", "b", "w")]
+    o_full, S_full = mb.b200_dgda_prefill(*part(0, 700))
+    o1, S1 = mb.b200_dgda_prefill(*part(0, cut))
+    o2, S2 = mb.b200_dgda_prefill(*part(cut, 700), initial_state=S1)
+    assert_rel(torch.cat([o1, o2], 2), o_full, RTOL_FP32, "o")
+    assert_rel(S2, S_full, RTOL_FP32, "S")
+
+
+def test_empty_sequence():
+    z = torch.zeros(1, 2, 0, 16, device=DEV)
+    s0 = torch.randn(1, 2, 16, 16, device=DEV)
+    o, S = mb.b200_dgda_prefill(z, z, z, log_alpha=z, b=z, w=z, initial_state=s0)
+    assert o.shape == (1, 2, 0, 16)
+    torch.testing.assert_close(S, s0)
+
+
+def test_step_vs_reference():
+    g = golden("dgda_step")
+    o, S = mb.b200_dgda_step(*(cu(g[k]) for k in ("q", "k", "v", "alpha", "b", "w")), state=cu(g["state"]))
+    assert_rel(o, g["o"], 1e-5, "o")
+    assert_rel(S, g["S"], 1e-5, "S")
+    # 4-D [B,H,1,d] inputs
+    o4, S4 = mb.b200_dgda_step(*(cu(g[k])[:, :, None] for k in ("q", "k", "v", "alpha", "b", "w")),
+                               state=cu(g["state"]))
+    assert o4.shape == (2, 4, 64)
+    torch.testing.assert_close(o4, o)
+
+
+def test_step_alpha_priority_and_log_alpha():
+    g = golden("dgda_step")
+    a = cu(g["alpha"])
+    base = [cu(g[k]) for k in ("q", "k", "v")]
+    o1, _ = mb.b200_dgda_step(*base, alpha=a, b=cu(g["b"]), w=cu(g["w"]), state=cu(g["state"]),
+                              log_alpha=torch.zeros_like(a))
+    o2, _ = mb.b200_dgda_step(*base, b=cu(g["b"]), w=cu(g["w"]), state=cu(g["state"]), log_alpha=torch.log(a))
+    assert_rel(o1, g["o"], 1e-5, "alpha wins")
+    assert_rel(o2, g["o"], 1e-5, "log_alpha")
+
+
+def test_step_unroll_equals_prefill():
+    x = {k: v.to(DEV) for k, v in dgda_inputs(B=2, T=40, H=3, seed=12, per_channel=True).items()}
+    s0 = torch.randn(2, 3, 64, 64, device=DEV) * 0.1
+    o_pre, S_pre = mb.b200_dgda_prefill(*(x[k] for k in ("q", "k", "v", "alpha", "b", "w")), initial_state=s0)
+    S = s0
+    outs = []
+    for t in range(40):
+        ot, S = mb.b200_dgda_step(*(x[k][:, :, t] for k in ("q", "k", "v", "alpha", "b", "w")), state=S)
+        outs.append(ot)
+    assert_rel(torch.stack(outs, 2), o_pre, RTOL_FP32, "o")
+    assert_rel(S, S_pre, RTOL_FP32, "S")
+
+
+def test_prefill_then_steps_continuity():
+    c = sub(golden("dgda_step"), "cont.")
+    t = {k: cu(c[k]) for k in ("q", "k", "v", "alpha", "b", "w")}
+    o1, S = mb.b200_dgda_prefill(*(t[k][:, :, :8] for k in ("q", "k", "v", "alpha", "b", "w")))
+    outs = [o1]
+    for i in range(8, 12):
+        ot, S = mb.b200_dgda_step(*(t[k][:, :, i] for k in ("q", "k", "v", "alpha", "b", "w")), state=S)
+        outs.append(ot[:, :, None])
+    assert_rel(torch.cat(outs, 2), c["o"], RTOL_FP32, "o")
+    assert_rel(S, c["S"], RTOL_FP32, "S")
+
+
+def test_step_bf16_with_fp32_state():
+    x = dgda_inputs(B=4, T=1, H=10, seed=13, per_channel=True)
+    s0 = torch.randn(4, 10, 64, 64) * 0.1
+    args = [x[k][:, :, 0].to(DEV, torch.bfloat16) for k in ("q", "k", "v", "alpha", "b", "w")]
+    o, S = mb.b200_dgda_step(*args, state=s0.to(DEV))
+    assert S.dtype == torch.float32 and o.dtype == torch.bfloat16
+    ref = [a.float().cpu().numpy() for a in args]
+    ro, rS = OD.dgda_step(*ref, state=s0.numpy())
+    assert_rel(o, ro, RTOL_BF16, "o")
+    assert_rel(S, rS, 1e-5, "S")
