@@ -1,0 +1,420 @@
+"""Benchmark of the Maba v2 hot path on B200 (one JSON line on rank 0).
+
+Step (one pass of the hot path over one batch): the configuration-2 workload
+(B=1, T=65,536, H=10, head 64, d_c=128, d_idx=64, lambda=0.1, top-32, window
+128 + 4 sinks, HCA r=64, bf16 I/O, seeded synthetic inputs) through
+  DGDA chunked prefill (one layer op over the same 65,536 tokens) ->
+  DG-Indexer pooling + fused scoring/top-k ->
+  MABA-SA query absorption -> HCA pooling -> fused three-stream attention ->
+  W_uv expansion.
+Metric: prefill tokens/s of that step (DGDA + MABA-SA).  Inputs exceed L2
+(~0.7 GB per step), so no L2 flush is needed between timed steps.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 runs under torchrun, one rank per GPU, each rank processing its own
+sequence (weak scaling, no collective on the data path); time = max over ranks.
+``--impl reference`` times the reference algorithm restated for the CPU
+(oracle/, the checker) on the host cores, on bounded samples of the workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+T_TOK = 65536
+H, DH, DC, DIDX, BLOCK, TOPK, WINDOW, SINKS, HCA_R, LAM = 10, 64, 128, 64, 64, 32, 128, 4, 64, 0.1
+METRIC = "prefill tok/s (DGDA+MABA-SA), config-2 workload T=65536"
+WORKLOAD = ("config2: B=1 T=65536 H=10 dh=64 d_c=128 d_idx=64 lambda=0.1 top32 window128+4sinks HCA64, "
+            "DGDA op (chunked prefill, per-channel gates) + DG-Indexer + MABA-SA fused attention")
+
+
+def peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return {"hbm_gbs": p["hbm_gbs"], "bf16_tflops": p["bf16_tflops"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                smax.append(float(parts[1]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[4:8]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def build_inputs(dev, seed_offset=0):
+    import torch
+    from maba_v2_architecture_b200.workloads import dgda_inputs, sa_inputs
+
+    dt = torch.bfloat16
+    wl = sa_inputs(T=T_TOK, seed=1 + seed_offset)
+    x = dgda_inputs(B=1, T=T_TOK, H=H, D=DH, seed=20 + seed_offset, per_channel=True)
+    host = {
+        # DGDA inputs token-major [B,T,H,d] (the layer's layout), bf16
+        "dq": x["q"].transpose(1, 2).contiguous().to(dt), "dk": x["k"].transpose(1, 2).contiguous().to(dt),
+        "dv": x["v"].transpose(1, 2).contiguous().to(dt), "db": x["b"].transpose(1, 2).contiguous().to(dt),
+        "dw": x["w"].transpose(1, 2).contiguous().to(dt), "dla": x["log_alpha"].transpose(1, 2).contiguous().to(dt),
+        "c_kv": wl.c_kv.to(dt), "q": wl.q.to(dt), "q_idx": wl.q_idx.to(dt), "k_idx": wl.k_idx.to(dt),
+        "gate": wl.gate.to(dt),
+    }
+    weights = {"w_uk": wl.w_uk.to(dev, dt), "w_uv": wl.w_uv.to(dev, dt)}
+    return host, weights
+
+
+def hot_path_step(mb, d, weights, timers=None):
+    """One pass of the hot path; d holds device tensors.  Returns (dgda_out, sa_out)."""
+    import torch
+    from maba_v2_architecture_b200.ops import absorb_queries, expand_values
+
+    def tv(t):  # token-major [B,T,H,d] -> [B,H,T,d] view
+        return t.transpose(1, 2)
+
+    def mark(name):
+        if timers is not None:
+            timers.mark(name)
+
+    mark("dgda_prefill")
+    o_dgda, _ = mb.b200_dgda_prefill(tv(d["dq"]), tv(d["dk"]), tv(d["dv"]), None, tv(d["db"]), tv(d["dw"]),
+                                     log_alpha=tv(d["dla"]), state_dtype=torch.float32, out_layout="blhd")
+    mark("centroids")
+    c = mb.b200_compute_centroids(d["k_idx"], block_size=BLOCK)
+    mark("index_topk")
+    idx = mb.b200_index_topk(d["q_idx"], c, lambda_dist=LAM, top_k=TOPK, block_size=BLOCK)
+    mark("absorb_gemm")
+    qhat = absorb_queries(d["q"], weights["w_uk"], H, 1.0 / (DH ** 0.5))
+    mark("hca_pool")
+    hca = mb.b200_hca_pool(d["c_kv"], HCA_R)
+    mark("sa_attention")
+    o_lat = mb.b200_sa_attention(qhat, d["c_kv"], hca, idx, d["gate"], window_size=WINDOW, n_sinks=SINKS,
+                                 block_size=BLOCK, hca_r=HCA_R)
+    mark("expand_gemm")
+    o = expand_values(o_lat, weights["w_uv"], H)
+    mark(None)
+    return o_dgda, o, idx
+
+
+class OpTimers:
+    """CUDA events between consecutive ops of a step, on the launching stream."""
+
+    def __init__(self, torch):
+        self.torch = torch
+        self.events = []
+
+    def mark(self, name):
+        ev = self.torch.cuda.Event(enable_timing=True)
+        ev.record()
+        self.events.append((name, ev))
+
+    def collect(self):
+        out = {}
+        for (name, ev), (_, nxt) in zip(self.events[:-1], self.events[1:]):
+            if name is not None:
+                out.setdefault(name, []).append(ev.elapsed_time(nxt))
+        return out
+
+
+MY_LAUNCHES_PER_STEP = None  # filled from the op list below
+
+
+def count_launches(mb, L, BH):
+    """Kernels of libmaba_b200 launched per step (cuBLAS GEMMs not counted)."""
+    lib = mb._native.lib()
+    seg = lib.maba_dgda_prefill_workspace_size(2, 1, H, L, DH, DH) > 0
+    dgda = 3 if seg else 1
+    return dgda + 1 + 2 + 1 + 1  # dgda, centroids, penalty table + top-k, hca pool, attention
+
+
+def attention_units(idx, L):
+    """Per-token key counts of the three streams (n_loc, n_sp, n_hca), summed over tokens."""
+    import torch
+
+    pos = torch.arange(L, device=idx.device)
+    lo = torch.clamp(pos - WINDOW + 1, min=0)
+    n_loc = (pos - lo + 1) + torch.clamp(torch.minimum(torch.full_like(lo, SINKS), lo), min=0)
+    qb = pos // BLOCK
+    blk = idx[0]                                    # [L, K]
+    start = blk * BLOCK
+    cnt = torch.clamp(torch.minimum(start + BLOCK - 1, pos[:, None]) - start + 1, min=0)
+    cnt = torch.where(blk <= qb[:, None], cnt, torch.zeros_like(cnt))
+    n_sp = cnt.sum(1)
+    n_hca = torch.where(pos >= HCA_R - 1, (pos + 1) // HCA_R, torch.zeros_like(pos))
+    return int(n_loc.sum()), int(n_sp.sum()), int(n_hca.sum())
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    import maba_v2_architecture_b200 as mb
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+
+    host, weights = build_inputs(dev, seed_offset=rank)
+    d = {k: v.to(dev) for k, v in host.items()}
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    # warm-up
+    for _ in range(args.warmup):
+        hot_path_step(mb, d, weights)
+    torch.cuda.synchronize()
+
+    # device-timed region: inputs resident in HBM
+    timers = OpTimers(torch)
+    clocks = ClockSampler(local)
+    clocks.start()
+    barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        out = hot_path_step(mb, d, weights, timers)
+    end.record()
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    ms = start.elapsed_time(end) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    per_op = {k: sum(v) / len(v) for k, v in timers.collect().items()}
+
+    # end to end through the public API: pinned host inputs -> device -> result back to host
+    pinned = {k: v.pin_memory() for k, v in host.items()}
+    res_host = None
+    h2d = sum(v.numel() * v.element_size() for v in pinned.values())
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2e_steps = max(1, min(args.steps, 5))
+    e0.record()
+    for _ in range(e2e_steps):
+        dd = {k: v.to(dev, non_blocking=True) for k, v in pinned.items()}
+        od, osa, _ = hot_path_step(mb, dd, weights)
+        res_host = (od.to("cpu"), osa.to("cpu"))
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    d2h = sum(r.numel() * r.element_size() for r in res_host)
+
+    if rank == 0:
+        pk = peaks()
+        idx = out[2]
+        n_loc, n_sp, n_hca = attention_units(idx, T_TOK)
+        attn_flops = 4 * DH * H * (n_loc + n_sp + n_hca)                 # per launch, 4*64*(n_loc+n_sp+n_hca) per token-head
+        dgda_bytes = T_TOK * H * (4 * DH + 3 * DH) * 2 + H * 2 * DH * DH * 4  # (4dk+3dv)*s per token-head + state in/out
+        cand = {
+            "sa_attention": ("tensor", attn_flops / (per_op["sa_attention"] * 1e-3) / 1e12, pk["bf16_tflops"],
+                             "TFLOP/s"),
+            "dgda_prefill": ("hbm", dgda_bytes / (per_op["dgda_prefill"] * 1e-3) / 1e9, pk["hbm_gbs"], "GB/s"),
+        }
+        dom = max(("sa_attention", "dgda_prefill"), key=lambda k: per_op[k])
+        bound, achieved, peak, unit = cand[dom]
+        line = {
+            "metric": METRIC,
+            "value": world * T_TOK / (ms * 1e-3),
+            "unit": "tok/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded, configuration-2 distributions; one planted needle block)",
+            "config": {"workload": WORKLOAD, "tokens_per_step_per_gpu": T_TOK, "global_batch": world,
+                       "seq_len": T_TOK, "parallelism": f"replicas x{world} (independent sequences)",
+                       "l2": "inputs > L2 (126 MB) per step; no flush"},
+            "e2e": {"value": world * T_TOK / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+            "roofline": {"kernel": dom, "bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
+                         "frac": achieved / peak, "traffic": None, "peak_source": pk["source"]},
+            "per_op_ms": {k: round(v, 4) for k, v in per_op.items()},
+            "gpu_launches": count_launches(mb, T_TOK, H) * args.steps,
+            "clocks": clk,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(budget_s=args.cpu_budget)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
+# CPU: the reference algorithm restated (oracle/), bounded samples
+# ---------------------------------------------------------------------------
+def cpu_baseline(budget_s: float = 20.0):
+    """Per-token CPU cost of the same step, from bounded samples:
+    DGDA  -- oracle.dgda.dgda_chunked (the reference's chunked CPU algorithm,
+             cpu_dgda.py) on a prefix of the sequence (constant cost per token);
+    index -- oracle.indexer.index_topk on rows sampled uniformly over all positions;
+    attn  -- oracle.attention.sa_attention_latent on the same sampled rows.
+    tok/s = 1 / (sum of the three per-token costs)."""
+    import numpy as np
+    import torch
+
+    from maba_v2_architecture_b200.workloads import dgda_inputs, sa_inputs
+    from oracle import attention as OA
+    from oracle import dgda as OD
+    from oracle import indexer as OI
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    share = budget_s / 3.0
+    # DGDA prefix
+    Ts = 1024
+    x = dgda_inputs(B=1, T=Ts, H=H, seed=20, per_channel=True)
+    xn = {k: v.to(torch.bfloat16).float().numpy() for k, v in x.items()}
+    t0 = time.perf_counter()
+    n_runs = 0
+    while True:
+        OD.dgda_chunked(xn["q"], xn["k"], xn["v"], None, xn["b"], xn["w"], chunk_size=64, log_alpha=xn["log_alpha"])
+        n_runs += 1
+        if time.perf_counter() - t0 > share / 2 or n_runs >= 50:
+            break
+    dgda_tok = (time.perf_counter() - t0) / (n_runs * Ts)
+    # indexer + attention on sampled rows
+    wl = sa_inputs(T=T_TOK)
+    c = OI.compute_centroids(wl.k_idx.to(torch.bfloat16).float().numpy(), BLOCK)
+    rng = np.random.default_rng(0)
+    rows = np.sort(rng.choice(T_TOK, 48, replace=False))
+    t0 = time.perf_counter()
+    idx = OI.index_topk(wl.q_idx.to(torch.bfloat16).float().numpy(), c, lambda_dist=LAM, top_k=TOPK, rows=rows)
+    idx_tok = (time.perf_counter() - t0) / len(rows)
+    full_idx = np.zeros((1, T_TOK, TOPK), np.int64)
+    full_idx[0, rows] = idx[0]
+    qhat = OA.absorb(wl.q.to(torch.bfloat16).float().numpy(), wl.w_uk.numpy(), H, 1.0 / DH ** 0.5)
+    ckv = wl.c_kv.to(torch.bfloat16).float().numpy()
+    arows = rows[:16]
+    t0 = time.perf_counter()
+    OA.sa_attention_latent(qhat, ckv, full_idx, wl.gate.numpy(), WINDOW, SINKS, BLOCK, HCA_R, rows=arows)
+    attn_tok = (time.perf_counter() - t0) / len(arows)
+    per_tok = dgda_tok + idx_tok + attn_tok
+    return {"value": 1.0 / per_tok, "unit": "tok/s", "cores": cores, "kind": "port",
+            "sample": (f"DGDA chunked on a {Ts}-token prefix x{n_runs}; index top-k on {len(rows)} rows and "
+                       f"attention on {len(arows)} rows sampled uniformly over 65,536 positions (numpy oracle)"),
+            "per_token_s": {"dgda": dgda_tok, "index": idx_tok, "attention": attn_tok}}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    vals = []
+    base = None
+    for i in range(args.warmup + args.steps):
+        b = cpu_baseline(budget_s=max(3.0, min(args.cpu_budget, 150.0 / max(1, args.steps + args.warmup))))
+        if i >= args.warmup:
+            vals.append(b["value"])
+            base = b
+    v = statistics.median(vals)
+    line = {
+        "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": int(os.environ.get("WORLD_SIZE", "1")),
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": T_TOK / v * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
+        "config": {"workload": WORKLOAD, "seq_len": T_TOK, "global_batch": 1},
+        "impl": "reference",
+        "cpu_baseline": {"value": v, "unit": "tok/s", "cores": base["cores"], "kind": "port",
+                         "sample": base["sample"]},
+        "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-budget", type=float, default=20.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

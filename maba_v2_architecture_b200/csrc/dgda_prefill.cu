@@ -20,9 +20,11 @@
 // true starting state and writes the outputs.  This is the same affine-chain
 // that splits a sequence across GPUs.
 //
-// This file is the CUDA-core (FFMA) path: fp32 compute for fp32/fp16/bf16
-// inputs (fp64 compute for fp64 inputs), head dims up to 64.
-#include "common.cuh"
+// This file holds the CUDA-core (FFMA) chunk kernel -- exact fp32 compute for
+// fp32 inputs, fp64 for fp64 inputs, head dims up to 64 -- the segment combine
+// kernel and the launcher; 16-bit inputs run the tensor-core chunk kernel of
+// dgda_prefill_mma.cu.
+#include "dgda_prefill.cuh"
 
 namespace maba {
 namespace {
@@ -31,18 +33,7 @@ constexpr int NT = 256;   // threads per CTA
 constexpr int DP = 64;    // padded head dim
 constexpr int SUB = 16;   // diagonal block of the triangular solve
 
-struct PrefillArgs {
-    const void* q; const void* k; const void* v; const void* alpha; const void* log_alpha;
-    const void* b; const void* w; const void* init;
-    void* out; void* fin;
-    int64_t sq[4], sk[4], sv[4], sa[4], sla[4], sb[4], sw[4], si[4], so[4], sf[4];
-    int64_t L;
-    int H, dk, dv;
-    int nseg;
-    int64_t seg_len;      // tokens per segment (multiple of the chunk)
-    float* ws_trans;      // [B*H][nseg][DP][2*DP]   (R | P) per segment
-    float* ws_start;      // [B*H][nseg][DP][DP]     starting state per segment
-};
+
 
 template <typename ACC> __device__ __forceinline__ ACC fast_exp(ACC x);
 template <> __device__ __forceinline__ float fast_exp<float>(float x) { return __expf(x); }
@@ -413,15 +404,17 @@ int set_smem(K kern, size_t bytes) {
 }
 
 template <typename T, typename TS>
-int launch_prefill(PrefillArgs& a, int64_t B, int dtype, cudaStream_t s, void* ws, size_t ws_bytes) {
+int launch_prefill(PrefillArgs& a, int64_t B, int dtype, int sdtype, cudaStream_t s, void* ws, size_t ws_bytes) {
     using ACC = typename std::conditional<sizeof(T) == 8, double, float>::type;
     constexpr int C = sizeof(T) == 8 ? 32 : 64;
+    constexpr bool k16 = sizeof(T) == 2;  // 16-bit inputs: tensor-core chunk kernels
     const int64_t BH = B * a.H;
     if (BH == 0) return MABA_OK;
     const int nseg = choose_segments(dtype, BH, a.L);
     if (nseg <= 1) {
         a.nseg = 1;
         a.seg_len = a.L > 0 ? a.L : 1;
+        if (k16) return dgda_mma_launch(a, dim3((unsigned)BH, 1), 0, dtype, sdtype, s);
         auto kern = dgda_chunk_kernel<T, TS, ACC, C, 0>;
         MABA_TRY(set_smem(kern, Smem<ACC, C, 0>::bytes));
         kern<<<dim3((unsigned)BH, 1), NT, Smem<ACC, C, 0>::bytes, s>>>(a);
@@ -439,17 +432,29 @@ int launch_prefill(PrefillArgs& a, int64_t B, int dtype, cudaStream_t s, void* w
             return set_error(MABA_ERR_WORKSPACE, "dgda_prefill: workspace of %zu bytes required, got %zu", need, ws_bytes);
         a.ws_trans = static_cast<float*>(ws);
         a.ws_start = a.ws_trans + (size_t)BH * a.nseg * DP * 2 * DP;
-        auto k1 = dgda_chunk_kernel<T, TS, ACC, C, 1>;
-        auto k2 = dgda_chunk_kernel<T, TS, ACC, C, 2>;
-        MABA_TRY(set_smem(k1, Smem<ACC, C, 1>::bytes));
-        MABA_TRY(set_smem(k2, Smem<ACC, C, 2>::bytes));
-        k1<<<dim3((unsigned)BH, (unsigned)a.nseg), NT, Smem<ACC, C, 1>::bytes, s>>>(a);
-        MABA_TRY(check_launch("dgda_prefill(transition)"));
+        const dim3 grid((unsigned)BH, (unsigned)a.nseg);
+        if (k16) {
+            MABA_TRY(dgda_mma_launch(a, grid, 1, dtype, sdtype, s));
+        } else {
+            auto k1 = dgda_chunk_kernel<T, TS, ACC, C, 1>;
+            MABA_TRY(set_smem(k1, Smem<ACC, C, 1>::bytes));
+            k1<<<grid, NT, Smem<ACC, C, 1>::bytes, s>>>(a);
+            MABA_TRY(check_launch("dgda_prefill(transition)"));
+        }
         dgda_combine_kernel<TS><<<(unsigned)BH, NT, 0, s>>>(a);
         MABA_TRY(check_launch("dgda_prefill(combine)"));
-        k2<<<dim3((unsigned)BH, (unsigned)a.nseg), NT, Smem<ACC, C, 2>::bytes, s>>>(a);
+        if (k16) return dgda_mma_launch(a, grid, 2, dtype, sdtype, s);
+        auto k2 = dgda_chunk_kernel<T, TS, ACC, C, 2>;
+        MABA_TRY(set_smem(k2, Smem<ACC, C, 2>::bytes));
+        k2<<<grid, NT, Smem<ACC, C, 2>::bytes, s>>>(a);
         return check_launch("dgda_prefill(apply)");
     }
+}
+
+bool vec8_ok(const maba_tensor* t) {
+    if (!present(t)) return true;
+    if (t->stride[3] != 1 || (t->stride[2] % 8) || (t->stride[1] % 8) || (t->stride[0] % 8)) return false;
+    return (reinterpret_cast<uintptr_t>(t->data) & 15u) == 0;
 }
 
 }  // namespace
@@ -526,18 +531,20 @@ extern "C" int maba_dgda_prefill(const maba_tensor* q, const maba_tensor* k, con
         a.so[i] = out->stride[i]; a.sf[i] = final_state->stride[i];
     }
     a.L = L; a.H = (int)H; a.dk = (int)dk; a.dv = (int)dv;
+    a.vec8 = (dk == DP && dv == DP && vec8_ok(q) && vec8_ok(k) && vec8_ok(v) && vec8_ok(b) && vec8_ok(w) &&
+              vec8_ok(log_alpha) && (present(log_alpha) || vec8_ok(alpha))) ? 1 : 0;
     cudaStream_t s = as_stream(stream);
     switch (dt) {
-        case MABA_F32: return launch_prefill<float, float>(a, B, dt, s, workspace, workspace_bytes);
+        case MABA_F32: return launch_prefill<float, float>(a, B, dt, sdt, s, workspace, workspace_bytes);
         case MABA_F64:
             if (sdt != MABA_F64) return set_error(MABA_ERR_DTYPE, "dgda_prefill: float64 needs a float64 state");
-            return launch_prefill<double, double>(a, B, dt, s, workspace, workspace_bytes);
+            return launch_prefill<double, double>(a, B, dt, sdt, s, workspace, workspace_bytes);
         case MABA_F16:
-            return sdt == MABA_F32 ? launch_prefill<__half, float>(a, B, dt, s, workspace, workspace_bytes)
-                                   : launch_prefill<__half, __half>(a, B, dt, s, workspace, workspace_bytes);
+            return sdt == MABA_F32 ? launch_prefill<__half, float>(a, B, dt, sdt, s, workspace, workspace_bytes)
+                                   : launch_prefill<__half, __half>(a, B, dt, sdt, s, workspace, workspace_bytes);
         case MABA_BF16:
-            return sdt == MABA_F32 ? launch_prefill<__nv_bfloat16, float>(a, B, dt, s, workspace, workspace_bytes)
-                                   : launch_prefill<__nv_bfloat16, __nv_bfloat16>(a, B, dt, s, workspace, workspace_bytes);
+            return sdt == MABA_F32 ? launch_prefill<__nv_bfloat16, float>(a, B, dt, sdt, s, workspace, workspace_bytes)
+                                   : launch_prefill<__nv_bfloat16, __nv_bfloat16>(a, B, dt, sdt, s, workspace, workspace_bytes);
         default: return set_error(MABA_ERR_DTYPE, "dgda_prefill: unsupported dtype %s", dtype_name(dt));
     }
 }

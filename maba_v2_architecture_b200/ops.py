@@ -37,6 +37,20 @@ def _check_same(tensors, device, dtype, what="q"):
             raise TypeError(f"Tensor dtypes must match, but got {dtype} for {what} and {t.dtype} for {name}")
 
 
+def _state_check(state, q, name):
+    """A float32 state with 16-bit inputs is accepted (this backend keeps fp32 recurrent
+    state); any other dtype mismatch raises as in the reference."""
+    if state is None:
+        return None
+    if state.dtype == torch.float32 and q.dtype in (torch.float16, torch.bfloat16):
+        if state.device != q.device:
+            raise RuntimeError(
+                f"Expected all tensors to be on the same device, but got {q.device} and {state.device} for {name}"
+            )
+        return None
+    return state
+
+
 def validate_dgda_prefill_inputs(q, k, v, alpha=None, b=None, w=None, initial_state=None, log_alpha=None):
     """Mirrors maba_sparse/kernels/common.py:13-91 (validate_dgda_prefill_inputs)."""
     if alpha is None and log_alpha is None:
@@ -44,7 +58,7 @@ def validate_dgda_prefill_inputs(q, k, v, alpha=None, b=None, w=None, initial_st
     if b is None or w is None:
         raise ValueError("Both b and w gate tensors must be provided")
     _check_same([("k", k), ("v", v), ("b", b), ("w", w), ("alpha", alpha), ("log_alpha", log_alpha),
-                 ("initial_state", initial_state)], q.device, q.dtype)
+                 ("initial_state", _state_check(initial_state, q, "initial_state"))], q.device, q.dtype)
     if q.dim() != 4:
         raise ValueError(f"q must be 4D [B, H, L, dk], got shape {list(q.shape)}")
     B, H, L, dk = q.shape
@@ -72,7 +86,7 @@ def validate_dgda_step_inputs(q, k, v, alpha=None, b=None, w=None, state=None, l
     if b is None or w is None:
         raise ValueError("Both b and w gate tensors must be provided")
     _check_same([("k", k), ("v", v), ("b", b), ("w", w), ("alpha", alpha), ("log_alpha", log_alpha),
-                 ("state", state)], q.device, q.dtype)
+                 ("state", _state_check(state, q, "state"))], q.device, q.dtype)
     q3 = q.squeeze(2) if (q.dim() == 4 and q.shape[2] == 1) else q
     if q3.dim() != 3:
         raise ValueError(f"q must be [B, H, dk] or [B, H, 1, dk], got {list(q.shape)}")
@@ -135,7 +149,11 @@ def b200_dgda_prefill(
     N.require_cuda(q, op="dgda_prefill")
     B, H, L, dk = q.shape
     dv = v.shape[-1]
-    state_dtype = kwargs.get("state_dtype", q.dtype)
+    state_dtype = kwargs.get("state_dtype", initial_state.dtype if initial_state is not None else q.dtype)
+    if L == 0:
+        fin = (initial_state.clone().to(state_dtype) if initial_state is not None
+               else torch.zeros(B, H, dk, dv, dtype=state_dtype, device=q.device))
+        return torch.empty(B, H, 0, dv, dtype=q.dtype, device=q.device), fin
     if kwargs.get("out_layout") == "blhd":
         out = torch.empty(B, L, H, dv, dtype=q.dtype, device=q.device).transpose(1, 2)
     else:

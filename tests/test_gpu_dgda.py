@@ -216,3 +216,73 @@ def test_step_bf16_with_fp32_state():
     ro, rS = OD.dgda_step(*ref, state=s0.numpy())
     assert_rel(o, ro, RTOL_BF16, "o")
     assert_rel(S, rS, 1e-5, "S")
+
+
+# ---------------------------------------------------------------- tensor-core (16-bit) chunk kernel
+@pytest.mark.parametrize("dtype,rtol", [(torch.bfloat16, RTOL_BF16), (torch.float16, RTOL_FP16 * 2)])
+@pytest.mark.parametrize("B,H,L", [(1, 2, 4096), (2, 10, 700), (1, 1, 129)])
+def test_16bit_tensor_core_path_vs_oracle(dtype, rtol, B, H, L):
+    """Token-major strided inputs (vectorised loads), single-pass and segmented launches."""
+    x = dgda_inputs(B=B, T=L, H=H, seed=31 + L, per_channel=True)
+    s0 = torch.randn(B, H, 64, 64, generator=torch.Generator().manual_seed(32)) * 0.1
+    tm = {k: x[k].transpose(1, 2).contiguous().to(DEV, dtype) for k in ("q", "k", "v", "b", "w", "log_alpha")}
+    tv = lambda t: t.transpose(1, 2)
+    o, S = mb.b200_dgda_prefill(tv(tm["q"]), tv(tm["k"]), tv(tm["v"]), None, tv(tm["b"]), tv(tm["w"]),
+                                initial_state=s0.to(DEV), log_alpha=tv(tm["log_alpha"]), state_dtype=torch.float32,
+                                out_layout="blhd")
+    ref = {k: x[k].to(dtype).float().numpy() for k in x}
+    ro, rS = OD.dgda_sequential(ref["q"], ref["k"], ref["v"], None, ref["b"], ref["w"], initial_state=s0.numpy(),
+                                log_alpha=ref["log_alpha"])
+    assert_rel(o, ro, rtol, "o")
+    assert_rel(S, rS, rtol, "S")
+
+
+@pytest.mark.parametrize("i", range(5))
+def test_16bit_extreme_decay(i):
+    g = sub(golden("dgda_prefill"), "ext.")
+    d = dict(g)
+    d["alpha"] = np.full_like(g["q"], g["alphas"][i])
+    o, S = run_prefill(d, torch.bfloat16)
+    assert torch.isfinite(o.float()).all() and torch.isfinite(S.float()).all()
+    ro, rS = OD.dgda_sequential(*(torch.as_tensor(d[k]).to(torch.bfloat16).float().numpy()
+                                  for k in ("q", "k", "v", "alpha", "b", "w")),
+                                initial_state=torch.as_tensor(g["s0"]).to(torch.bfloat16).float().numpy())
+    assert_rel(o, ro, RTOL_BF16, "o")
+    assert_rel(S, rS, RTOL_BF16, "S")
+
+
+def test_16bit_unaligned_and_short_head_dims():
+    """dk=dv=32 and non-unit strides: the scalar-load branch of the tensor-core kernel."""
+    g = sub(golden("dgda_prefill"), "len129.")
+    o, S = run_prefill(g, torch.bfloat16)
+    ro, rS = OD.dgda_sequential(*(torch.as_tensor(g[k]).to(torch.bfloat16).float().numpy()
+                                  for k in ("q", "k", "v")), None,
+                                *(torch.as_tensor(g[k]).to(torch.bfloat16).float().numpy() for k in ("b", "w")),
+                                log_alpha=torch.as_tensor(g["la"]).to(torch.bfloat16).float().numpy())
+    assert_rel(o, ro, RTOL_BF16, "o")
+    assert_rel(S, rS, RTOL_BF16, "S")
+
+
+def test_16bit_long_sequence_full_config2_length():
+    """T = 65,536, H = 10 (the bench's DGDA op): segmented path, property + sampled oracle check."""
+    x = dgda_inputs(B=1, T=65536, H=10, seed=20, per_channel=True)
+    dt = torch.bfloat16
+    tm = {k: x[k].transpose(1, 2).contiguous().to(DEV, dt) for k in ("q", "k", "v", "b", "w", "log_alpha")}
+    tv = lambda t: t.transpose(1, 2)
+    o, S = mb.b200_dgda_prefill(tv(tm["q"]), tv(tm["k"]), tv(tm["v"]), None, tv(tm["b"]), tv(tm["w"]),
+                                log_alpha=tv(tm["log_alpha"]), state_dtype=torch.float32, out_layout="blhd")
+    assert bool(torch.isfinite(o.float()).all()) and bool(torch.isfinite(S).all())
+    # chaining property: the last 4096 tokens from the state at 61,440 equal the tail of the full run
+    cut = 65536 - 4096
+    part = lambda s, e: [tv(tm[k][:, s:e]) for k in ("q", "k", "v")]
+    _, S1 = mb.b200_dgda_prefill(*part(0, cut), None, tv(tm["b"][:, :cut]), tv(tm["w"][:, :cut]),
+                                 log_alpha=tv(tm["log_alpha"][:, :cut]), state_dtype=torch.float32)
+    o2, S2 = mb.b200_dgda_prefill(*part(cut, 65536), None, tv(tm["b"][:, cut:]), tv(tm["w"][:, cut:]),
+                                  initial_state=S1, log_alpha=tv(tm["log_alpha"][:, cut:]),
+                                  state_dtype=torch.float32)
+    assert_rel(o2, o[:, :, cut:], RTOL_BF16, "tail")
+    assert_rel(S2, S, RTOL_BF16, "state")
+    # oracle on heads 0..1 over the first 2048 tokens (sequential fp64)
+    ref = {k: x[k][:, :2, :2048].to(dt).float().numpy() for k in x}
+    ro, _ = OD.dgda_sequential(ref["q"], ref["k"], ref["v"], None, ref["b"], ref["w"], log_alpha=ref["log_alpha"])
+    assert_rel(o[:, :2, :2048], ro, RTOL_BF16, "prefix")
