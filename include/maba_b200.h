@@ -125,6 +125,29 @@ MABA_API int maba_index_topk(const maba_tensor* q_idx, const maba_tensor* centro
                     void* workspace, size_t workspace_bytes, void* stream);
 MABA_API size_t maba_index_topk_workspace_size(int64_t B, int64_t L, int64_t nb, int32_t top_k);
 
+/* ---- DG-Indexer scoring + top-k with no caller workspace ---------------
+ * Has no counterpart in the reference: it exists for callers that cannot
+ * allocate device memory -- an application whose framework owns every byte
+ * of the GPU through its own pool, a latency-critical decode loop that must
+ * not pay cudaMalloc's implicit device synchronisation, or a thin foreign-
+ * language binding that only ever receives device pointers from elsewhere.
+ * Same arguments, results and errors as maba_index_topk minus the workspace.
+ * Its scratch (the penalty table) is one file-scope device array of
+ * MABA_NOALLOC_PENALTY_MAX floats (256 KiB) that every GPU which loads this
+ * library holds until the process exits; requests needing more entries
+ * (max(nb, ceil(L / block_size)) in prefill, nb in decode) are rejected with
+ * MABA_ERR_UNSUPPORTED.  The first call on a device looks the array up (once
+ * per device, with that device current): make that first call before any
+ * stream capture.  All calls share the array and the kernel rewrites every
+ * entry it reads, so nothing needs clearing between calls; calls that overlap
+ * on the GPU (different streams, or different host threads) race on it and
+ * must be serialised by the caller.  Allocates nothing. */
+#define MABA_NOALLOC_PENALTY_MAX 65536
+MABA_API int maba_index_topk_noalloc(const maba_tensor* q_idx, const maba_tensor* centroids,
+                                     float lambda_dist, int32_t top_k, int32_t block_size, int32_t decode,
+                                     const maba_tensor* idx_out, const maba_tensor* scores_out,
+                                     void* stream);
+
 /* ---- Stream superposition ----------------------------------------------
  * Replaces `stream_superposition`: dispatcher.py:468, common.py:406-438,
  * cpu_indexer.py:116-150.  o_*: [B,H,L,D]; gate: [B,L,3] or [B,H,L,3];

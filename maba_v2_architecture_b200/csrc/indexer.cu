@@ -599,3 +599,52 @@ extern "C" int maba_index_topk(const maba_tensor* q_idx, const maba_tensor* cent
     a.scale_f = (float)a.scale_d;
     return MABA_DISPATCH_FLOAT(q_idx->dtype, "index_topk", [&] { return launch_topk<T>(a, B, s); });
 }
+
+// ---------------------------------------------------------------------------
+// Workspace-free variant (maba_index_topk_noalloc): the penalty table lives in
+// a fixed file-scope device array instead of caller memory.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+static __device__ __align__(256) float g_noalloc_penalty[MABA_NOALLOC_PENALTY_MAX];
+
+namespace {
+std::mutex g_noalloc_mutex;
+float* g_noalloc_table[128] = {nullptr};  // device address of g_noalloc_penalty, per device
+
+// Looks the array up once per device (with that device current).  The host
+// symbol g_noalloc_penalty is only a stand-in: kernels get the device address.
+int noalloc_table(float** out) {
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return set_error(MABA_ERR_CUDA, "index_topk_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+    if (dev < 0 || dev >= 128) return set_error(MABA_ERR_UNSUPPORTED, "index_topk_noalloc: device %d out of range", dev);
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (g_noalloc_table[dev] == nullptr) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_penalty);
+        if (e != cudaSuccess || p == nullptr)
+            return set_error(MABA_ERR_CUDA, "index_topk_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+        g_noalloc_table[dev] = static_cast<float*>(p);
+    }
+    *out = g_noalloc_table[dev];
+    return MABA_OK;
+}
+}  // namespace
+
+extern "C" int maba_index_topk_noalloc(const maba_tensor* q_idx, const maba_tensor* centroids, float lambda_dist,
+                                       int32_t top_k, int32_t block_size, int32_t decode, const maba_tensor* idx_out,
+                                       const maba_tensor* scores_out, void* stream) {
+    if (present(q_idx) && present(centroids) && q_idx->ndim == 3 && centroids->ndim == 3 && block_size > 0) {
+        const int64_t need = penalty_len(q_idx->shape[1], centroids->shape[1], block_size, decode);
+        if (need > MABA_NOALLOC_PENALTY_MAX)
+            return set_error(MABA_ERR_UNSUPPORTED,
+                             "index_topk_noalloc: needs %lld penalty entries, the fixed scratch holds %d "
+                             "(use maba_index_topk with a caller workspace)",
+                             (long long)need, MABA_NOALLOC_PENALTY_MAX);
+    }
+    float* table = nullptr;
+    MABA_TRY(noalloc_table(&table));
+    return maba_index_topk(q_idx, centroids, lambda_dist, top_k, block_size, decode, idx_out, scores_out, table,
+                           sizeof(float) * (size_t)MABA_NOALLOC_PENALTY_MAX, stream);
+}
