@@ -50,7 +50,7 @@ def peaks():
 class ClockSampler:
     """nvidia-smi clock / throttle sampling during the timed region."""
 
-    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+    FIELDS = ("timestamp,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
 
@@ -63,7 +63,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
         except OSError:
@@ -71,7 +71,10 @@ class ClockSampler:
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.time(), line.strip()))
+
+    def window(self, t0, t1):
+        self.t0, self.t1 = t0, t1
 
     def stop(self):
         if self.proc is None:
@@ -83,8 +86,11 @@ class ClockSampler:
             self.proc.kill()
         sm, smax, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            parts = [p.strip() for p in ln.split(",")]
+        t0, t1 = getattr(self, "t0", 0.0), getattr(self, "t1", float("inf"))
+        for ts, ln in self.lines:
+            if not (t0 - 0.15 <= ts <= t1 + 0.15):   # samples received during the timed region
+                continue
+            parts = [p.strip() for p in ln.split(",")][1:]
             if len(parts) < 8:
                 continue
             try:
@@ -201,6 +207,113 @@ def attention_units(idx, L):
     return int(n_loc.sum()), int(n_sp.sum()), int(n_hca.sum())
 
 
+def config3_prefill(dev, steps: int = 3, warmup: int = 1):
+    """Config 3: the 101M model (random N(0,0.02) weights, seed 2), bf16, forward over
+    B=8 x T=8,192 uniform ids; prefill tokens/s."""
+    import torch
+
+    from maba_v2_architecture_b200.config import get_101m_config
+    from maba_v2_architecture_b200.model import MabaSparseForCausalLM
+    from maba_v2_architecture_b200.workloads import init_module_
+
+    model = init_module_(MabaSparseForCausalLM(get_101m_config()), seed=2).to(dev, torch.bfloat16).eval()
+    model.set_state_dtype(torch.float32)
+    ids = torch.randint(0, 32768, (8, 8192), generator=torch.Generator().manual_seed(2)).to(dev)
+    with torch.no_grad():
+        for _ in range(warmup):
+            model(ids)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            out = model(ids)
+        e1.record()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    finite = bool(torch.isfinite(out.logits[:, -1].float()).all())
+    del model, out
+    torch.cuda.empty_cache()
+    return {"workload": "config3: 101M model (101,282,319 params) bf16, B=8 T=8192, random-init weights",
+            "value": 8 * 8192 / (ms * 1e-3), "unit": "tok/s", "ms_per_step": ms, "steps": steps,
+            "logits_finite": finite}
+
+
+def config4_decode(dev, ctx: int = 1048576, steps: int = 256, warmup: int = 3):
+    """Config 4: the 101M model (seed 3), bf16 weights and latent cache, fp32 DGDA state;
+    prefill `ctx` uniform ids at B=1 into the decode caches, then `steps` greedy tokens.
+    ms/token over the timed steps and the HBM bytes a step must touch."""
+    import torch
+
+    from maba_v2_architecture_b200.config import get_101m_config
+    from maba_v2_architecture_b200.decode import DecodeSession
+    from maba_v2_architecture_b200.model import MabaSparseForCausalLM
+    from maba_v2_architecture_b200.workloads import init_module_
+
+    model = init_module_(MabaSparseForCausalLM(get_101m_config()), seed=3).to(dev, torch.bfloat16).eval()
+    sess = DecodeSession(model, batch=1, max_len=ctx + steps + warmup + 1, dtype=torch.bfloat16)
+    ids = torch.randint(0, 32768, (1, ctx), generator=torch.Generator().manual_seed(3)).to(dev)
+    torch.cuda.synchronize()
+    t0 = time.time()
+    logits = sess.prefill(ids)
+    torch.cuda.synchronize()
+    prefill_s = time.time() - t0
+    del ids
+    tok = logits[:, -1].argmax(-1, keepdim=True)
+    for _ in range(warmup):
+        tok = sess.step(tok)[:, -1].argmax(-1, keepdim=True)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        tok = sess.step(tok)[:, -1].argmax(-1, keepdim=True)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    L = sess.L
+    nb = L // 64
+    weights = 2 * sum(p.numel() for p in model.parameters())
+    state = 15 * 10 * 64 * 64 * 4 * 2
+    per_sa = (2048 + 132) * 128 * 2 + nb * 128 * 2 + nb * 64 * 2
+    step_bytes = weights + state + 5 * per_sa
+    del sess, model
+    torch.cuda.empty_cache()
+    return {"workload": f"config4: 101M model bf16, B=1, prefill {ctx} ids then {steps} greedy steps",
+            "ms_per_token": ms, "context": L, "prefill_s": prefill_s,
+            "hbm_bytes_per_step": step_bytes, "hbm_gbs": step_bytes / (ms * 1e-3) / 1e9}
+
+
+def run_only(args):
+    """Runs one op of the step (warm-up + steps launches) on the bench workload; used
+    for profiling (ncu) a single kernel on exactly the bench's inputs.  No JSON."""
+    import torch
+
+    import maba_v2_architecture_b200 as mb
+    from maba_v2_architecture_b200.ops import absorb_queries
+
+    dev = torch.device("cuda", 0)
+    host, weights = build_inputs(dev)
+    d = {k: v.to(dev) for k, v in host.items()}
+    tv = lambda t: t.transpose(1, 2)
+    c = mb.b200_compute_centroids(d["k_idx"], block_size=BLOCK)
+    idx = mb.b200_index_topk(d["q_idx"], c, lambda_dist=LAM, top_k=TOPK, block_size=BLOCK)
+    qhat = absorb_queries(d["q"], weights["w_uk"], H, 1.0 / (DH ** 0.5))
+    hca = mb.b200_hca_pool(d["c_kv"], HCA_R)
+    ops = {
+        "sa_attention": lambda: mb.b200_sa_attention(qhat, d["c_kv"], hca, idx, d["gate"], window_size=WINDOW,
+                                                     n_sinks=SINKS, block_size=BLOCK, hca_r=HCA_R),
+        "dgda_prefill": lambda: mb.b200_dgda_prefill(tv(d["dq"]), tv(d["dk"]), tv(d["dv"]), None, tv(d["db"]),
+                                                     tv(d["dw"]), log_alpha=tv(d["dla"]), state_dtype=torch.float32,
+                                                     out_layout="blhd"),
+        "index_topk": lambda: mb.b200_index_topk(d["q_idx"], c, lambda_dist=LAM, top_k=TOPK, block_size=BLOCK),
+    }
+    fn = ops[args.only]
+    torch.cuda.synchronize()
+    for _ in range(args.warmup_only + args.steps):
+        fn()
+    torch.cuda.synchronize()
+    print(f"ran {args.only} x{args.warmup_only + args.steps}")
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -233,15 +346,19 @@ def run_ours(args):
     timers = OpTimers(torch)
     clocks = ClockSampler(local)
     clocks.start()
+    time.sleep(1.0)  # let nvidia-smi start sampling
     barrier()
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    wall0 = time.time()
     start.record()
     for _ in range(args.steps):
         out = hot_path_step(mb, d, weights, timers)
     end.record()
     torch.cuda.synchronize()
+    wall1 = time.time()
     barrier()
+    clocks.window(wall0, wall1)
     clk = clocks.stop()
     ms = start.elapsed_time(end) / args.steps
     if world > 1:
@@ -312,6 +429,11 @@ def run_ours(args):
         }
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(budget_s=args.cpu_budget)
+        if world == 1 and not args.no_extras:
+            del d, dd, out, res_host
+            torch.cuda.empty_cache()
+            line["extras"] = {"config3_prefill": config3_prefill(dev),
+                              "config4_decode": config4_decode(dev, ctx=args.decode_ctx, steps=args.decode_steps)}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier(device_ids=[local])
@@ -402,15 +524,23 @@ def run_reference(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=40)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-budget", type=float, default=20.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true", help="skip the config-3 prefill and config-4 decode fields")
+    ap.add_argument("--decode-ctx", type=int, default=1048576)
+    ap.add_argument("--decode-steps", type=int, default=256)
+    ap.add_argument("--only", default=None, choices=["sa_attention", "dgda_prefill", "index_topk"],
+                    help="profile helper: run one op of the step, print no JSON")
     args = ap.parse_args()
+    args.warmup_only = args.warmup
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.only:
+        run_only(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

@@ -125,6 +125,18 @@ MABA_API int maba_index_topk(const maba_tensor* q_idx, const maba_tensor* centro
                     void* workspace, size_t workspace_bytes, void* stream);
 MABA_API size_t maba_index_topk_workspace_size(int64_t B, int64_t L, int64_t nb, int32_t top_k);
 
+/* Prefill scoring for query rows that sit at absolute positions q_pos0 + t
+ * (qb(t) = (q_pos0 + t) / block): the rows of one sequence segment when a
+ * sequence is split across GPUs.  Same semantics as maba_index_topk with
+ * decode == 0 otherwise (maba_sparse/kernels/cpu_indexer.py:54-112 on the
+ * segment's rows of the full score matrix). */
+MABA_API int maba_index_topk_at(const maba_tensor* q_idx, const maba_tensor* centroids,
+                                float lambda_dist, int32_t top_k, int32_t block_size, int64_t q_pos0,
+                                const maba_tensor* idx_out, const maba_tensor* scores_out,
+                                void* workspace, size_t workspace_bytes, void* stream);
+MABA_API size_t maba_index_topk_at_workspace_size(int64_t B, int64_t L, int64_t nb, int32_t top_k,
+                                                  int32_t block_size, int64_t q_pos0);
+
 /* ---- DG-Indexer scoring + top-k with no caller workspace ---------------
  * Has no counterpart in the reference: it exists for callers that cannot
  * allocate device memory -- an application whose framework owns every byte
@@ -172,14 +184,17 @@ MABA_API int maba_hca_pool(const maba_tensor* c_kv, const maba_tensor* out, int3
  *   top_idx: [B,Lq,K] int64 selected blocks (indices into c_kv blocks)
  *   gate:  [B,Lq,3] or [B,H,Lq,3] gate logits
  *   out:   [B,Lq,H,d_c]   sum_s softmax(gate)_s * (attention of stream s),
- *          still in latent space; the caller applies W_uv and o_proj. */
+ *          still in latent space; the caller applies W_uv and o_proj.
+ * Single-token queries (Lq == 1, decode) run split-K over the keys when the
+ * workspace reported by _workspace_size is supplied. */
 MABA_API int maba_sa_attention(const maba_tensor* qhat, const maba_tensor* c_kv,
                       const maba_tensor* hca, const maba_tensor* top_idx,
                       const maba_tensor* gate, const maba_tensor* out,
                       int32_t window, int32_t n_sinks, int32_t block_size, int32_t hca_r,
                       void* workspace, size_t workspace_bytes, void* stream);
 MABA_API size_t maba_sa_attention_workspace_size(int32_t dtype, int64_t B, int64_t Lq, int64_t Lkv,
-                                        int64_t H, int64_t d_c, int64_t K, int32_t block_size);
+                                                 int64_t H, int64_t d_c, int64_t K, int32_t window,
+                                                 int32_t n_sinks, int32_t block_size, int32_t hca_r);
 
 #ifdef __cplusplus
 }

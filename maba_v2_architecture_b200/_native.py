@@ -54,11 +54,13 @@ SIGNATURES = {
     "maba_compute_centroids": (ctypes.c_int, [T_P, T_P, _i32, _vp]),
     "maba_index_topk": (ctypes.c_int, [T_P, T_P, _f32, _i32, _i32, _i32, T_P, T_P, _vp, _sz, _vp]),
     "maba_index_topk_workspace_size": (_sz, [_i64, _i64, _i64, _i32]),
+    "maba_index_topk_at": (ctypes.c_int, [T_P, T_P, _f32, _i32, _i32, _i64, T_P, T_P, _vp, _sz, _vp]),
+    "maba_index_topk_at_workspace_size": (_sz, [_i64, _i64, _i64, _i32, _i32, _i64]),
     "maba_index_topk_noalloc": (ctypes.c_int, [T_P, T_P, _f32, _i32, _i32, _i32, T_P, T_P, _vp]),
     "maba_stream_superposition": (ctypes.c_int, [T_P, T_P, T_P, T_P, _i32, T_P, _vp]),
     "maba_hca_pool": (ctypes.c_int, [T_P, T_P, _i32, _vp]),
     "maba_sa_attention": (ctypes.c_int, [T_P] * 6 + [_i32, _i32, _i32, _i32, _vp, _sz, _vp]),
-    "maba_sa_attention_workspace_size": (_sz, [_i32, _i64, _i64, _i64, _i64, _i64, _i64, _i32]),
+    "maba_sa_attention_workspace_size": (_sz, [_i32, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _i32, _i32, _i32]),
 }
 
 _lib: Optional[ctypes.CDLL] = None

@@ -9,7 +9,10 @@
 //        reference r_I = G[16I-1], exp(G_i - G_j) = exp(G_i - r_I) exp(r_I - G_j),
 //        both factors <= 1 (G is non-increasing), so the products are tensor-core
 //        GEMMs of pre-scaled operands with no overflow;
-//   A, L diagonal 16x16 blocks      -- explicit per-element decay (fp32, CUDA cores);
+//   A, L diagonal 16x16 blocks      -- the same factorisation around the block's first
+//        row when the block's decay spread is <= 80 (bf16; 8 for fp16) in every
+//        channel (the factors stay inside the 16-bit range), else explicit
+//        per-element decay (fp32);
 //   T = (I + L)^{-1}                -- 16x16 diagonal inverses by forward substitution
 //        (fp32) plus block back-substitution on the tensor cores (exact solve);
 //   per chunk state chain           -- R = w v - (b k e^G) S;  V' = T R;
@@ -51,12 +54,16 @@ struct MS {
     static constexpr size_t TM = SB + (size_t)D * LN * 2;       // [C][LB] T = (I+L)^-1
     static constexpr size_t VP = TM + (size_t)C * LB * 2;       // [C][LN] V'
     static constexpr size_t RB = VP + (size_t)C * LN * 2;       // [C][LN] R
-    static constexpr size_t TOTAL = RB + (size_t)C * LN * 2;
+    static constexpr size_t QD = RB + (size_t)C * LN * 2;       // [C][LB] q e^{G - G_blockstart}
+    static constexpr size_t BD = QD + (size_t)C * LB * 2;       // [C][LB] (b k) e^{G - G_blockstart}
+    static constexpr size_t KD = BD + (size_t)C * LB * 2;       // [C][LB] k e^{G_blockstart - G}
+    static constexpr size_t FLG = KD + (size_t)C * LB * 2;      // int [NB]: block decay too steep to factorise
+    static constexpr size_t TOTAL = FLG + 16;
     // decay-factor operands of the off-diagonal blocks alias TM.. during the A/L phase
     static constexpr size_t QH = TM;                            // [48][LB]
     static constexpr size_t BH = QH + (size_t)48 * LB * 2;      // [48][LB]
     static constexpr size_t KH = BH + (size_t)48 * LB * 2;      // [96][LB]: I=1 rows 0..15, I=2 16..47, I=3 48..95
-    static_assert(KH + (size_t)96 * LB * 2 <= TOTAL, "off-diagonal scratch must fit");
+    static_assert(KH + (size_t)96 * LB * 2 <= QD, "off-diagonal scratch must fit");
 };
 
 __device__ __forceinline__ int kh_off(int I) { return I == 1 ? 0 : (I == 2 ? 16 : 48); }
@@ -91,6 +98,10 @@ __global__ void __launch_bounds__(NTH, 1) dgda_mma_kernel(PrefillArgs a) {
     T* QH = reinterpret_cast<T*>(sm + S_::QH);
     T* BHs = reinterpret_cast<T*>(sm + S_::BH);
     T* KH = reinterpret_cast<T*>(sm + S_::KH);
+    T* QD = reinterpret_cast<T*>(sm + S_::QD);
+    T* BDs = reinterpret_cast<T*>(sm + S_::BD);
+    T* KD = reinterpret_cast<T*>(sm + S_::KD);
+    int* flags = reinterpret_cast<int*>(sm + S_::FLG);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int bh = blockIdx.x, seg = blockIdx.y;
@@ -205,8 +216,9 @@ __global__ void __launch_bounds__(NTH, 1) dgda_mma_kernel(PrefillArgs a) {
                 Gs[r * LF + tid] = run;
             }
         }
+        if (tid < NB) flags[tid] = 0;
         __syncthreads();
-        // ---------------- decayed operands, factor operands, diagonal blocks -------
+        // ---------------- decayed operands, factor operands -----------------------
         for (int e = tid; e < C * D; e += NTH) {
             const int r = e >> 6, d = e & 63;
             const float g = Gs[r * LF + d];
@@ -223,6 +235,14 @@ __global__ void __launch_bounds__(NTH, 1) dgda_mma_kernel(PrefillArgs a) {
                 QH[(r - 16) * LB + d] = to16<T>(qv * f);
                 BHs[(r - 16) * LB + d] = to16<T>(bk * f);
             }
+            const float g0 = Gs[(r & ~15) * LF + d];  // first row of this row's 16-block
+            const float fd = __expf(g - g0);           // <= 1
+            QD[r * LB + d] = to16<T>(qv * fd);
+            BDs[r * LB + d] = to16<T>(bk * fd);
+            KD[r * LB + d] = to16<T>(kv * __expf(g0 - g));  // >= 1, bounded when the block is flat enough
+            // factor range: bf16 keeps e^80 (8-bit exponent), fp16 tops out near 6.5e4
+            constexpr float kFlat = std::is_same<T, __half>::value ? 8.f : 80.f;
+            if ((r & 15) == 15 && g0 - g > kFlat) atomicOr(&flags[r >> 4], 1);
         }
         for (int e = tid; e < 96 * D; e += NTH) {
             const int row = e >> 6, d = e & 63;
@@ -231,8 +251,42 @@ __global__ void __launch_bounds__(NTH, 1) dgda_mma_kernel(PrefillArgs a) {
             const float ref = Gs[(16 * I - 1) * LF + d];
             KH[row * LB + d] = to16<T>(f32(KR[j * LB + d]) * __expf(ref - Gs[j * LF + d]));
         }
-        for (int p = tid; p < NB * 256; p += NTH) {
+        for (int e = tid; e < C * C; e += NTH) {  // strictly-upper off-diagonal blocks
+            const int i = e >> 6, j = e & 63;
+            if ((j >> 4) > (i >> 4)) {
+                AM[i * LB + j] = to16<T>(0.f);
+                LM[i * LB + j] = to16<T>(0.f);
+            }
+        }
+        __syncthreads();
+        // ---------------- A / L blocks: off-diagonal and factorisable diagonal on the tensor cores ----
+        {
+            // diagonal block blk, A (warp even) or L (warp odd): one 16x16 product per warp
+            const int blk = warp >> 1;
+            const bool isL = warp & 1;
+            if (!flags[blk]) {
+                float acc[2][4] = {};
+                warp_mma<T, false, false, 2>(acc, (isL ? BDs : QD) + (16 * blk) * LB, LB, KD + (16 * blk) * LB, LB, D,
+                                             lane);
+#pragma unroll
+                for (int n = 0; n < 2; ++n)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int ii = fr + (e >> 1) * 8, jj = n * 8 + fc + (e & 1);
+                        const float x = isL ? (jj < ii ? acc[n][e] : 0.f) : (jj <= ii ? acc[n][e] : 0.f);
+                        const int i = blk * 16 + ii, j = blk * 16 + jj;
+                        if (isL) {
+                            LM[i * LB + j] = to16<T>(x);
+                            LDs[(blk * 16 + ii) * 17 + jj] = x;
+                        } else {
+                            AM[i * LB + j] = to16<T>(x);
+                        }
+                    }
+            }
+        }
+        for (int p = tid; p < NB * 256; p += NTH) {  // steep blocks: explicit per-element decay
             const int blk = p >> 8, ii = (p >> 4) & 15, jj = p & 15;
+            if (!flags[blk]) continue;
             const int i = blk * 16 + ii, j = blk * 16 + jj;
             float av = 0.f, lv = 0.f;
             if (jj <= ii) {
@@ -250,15 +304,6 @@ __global__ void __launch_bounds__(NTH, 1) dgda_mma_kernel(PrefillArgs a) {
             LM[i * LB + j] = to16<T>(lv);
             LDs[(blk * 16 + ii) * 17 + jj] = lv;
         }
-        for (int e = tid; e < C * C; e += NTH) {  // strictly-upper off-diagonal blocks
-            const int i = e >> 6, j = e & 63;
-            if ((j >> 4) > (i >> 4)) {
-                AM[i * LB + j] = to16<T>(0.f);
-                LM[i * LB + j] = to16<T>(0.f);
-            }
-        }
-        __syncthreads();
-        // ---------------- off-diagonal A / L blocks (tensor cores); diagonal inverses ----
         for (int tile = warp; tile < 12; tile += 8) {
             // I=1: tiles 0,1; I=2: 2..5; I=3: 6..11; within I: first I tiles give A, next I give L
             const int I = tile < 2 ? 1 : (tile < 6 ? 2 : 3);
@@ -271,8 +316,9 @@ __global__ void __launch_bounds__(NTH, 1) dgda_mma_kernel(PrefillArgs a) {
             warp_mma<T, false, false, 2>(acc, Ap, LB, Bp, LB, D, lane);
             store_acc16<T, 2>((isL ? LM : AM) + (16 * I) * LB + 16 * n16, LB, acc, lane);
         }
-        if (tid >= 128 && tid < 192) {
-            const int blk = (tid - 128) >> 4, c = (tid - 128) & 15;
+        __syncthreads();
+        if (tid < 64) {
+            const int blk = tid >> 4, c = tid & 15;
             float tcol[16];
 #pragma unroll
             for (int r = 0; r < 16; ++r) tcol[r] = r == c ? 1.f : 0.f;

@@ -149,6 +149,7 @@ struct TopkArgs {
     const float* pen;  // penalty table, pen[delta]
     int64_t sq[3], sc[3], si[3], ss[3];
     int64_t L, nb;
+    int64_t q_pos0;  // absolute position of query row 0 (prefill)
     int D, block, keff, decode;
     float scale_f;
     double scale_d;
@@ -169,7 +170,7 @@ template <> __device__ __forceinline__ float scale_of<float>(const TopkArgs& a) 
 template <> __device__ __forceinline__ double scale_of<double>(const TopkArgs& a) { return a.scale_d; }
 
 __device__ __forceinline__ int64_t query_block(const TopkArgs& a, int64_t t) {
-    return a.decode ? (a.nb - 1) : (t / a.block);
+    return a.decode ? (a.nb - 1) : ((a.q_pos0 + t) / a.block);
 }
 
 template <typename T, typename SC>
@@ -452,6 +453,83 @@ __global__ void __launch_bounds__(kTopkThreads) topk_sort_kernel(TopkArgs a, int
     }
 }
 
+// ---------------------------------------------------------------------------
+// decode split: one token, many candidates -> partial sorted lists per CTA, then
+// a warp merge.  The final order is the same total order (score desc, index
+// asc) on the same per-candidate scores, so the result equals the token kernel.
+// ---------------------------------------------------------------------------
+constexpr int kSplitCand = 512;  // candidates per CTA (8 warps x 64)
+
+template <typename T>
+__global__ void __launch_bounds__(kTopkThreads) topk_decode_partial_kernel(TopkArgs a, float* part_s, int* part_i,
+                                                                           int nsplit) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int D = a.D;
+    float* qs = reinterpret_cast<float*>(smem_raw);           // [D]
+    float* cs_all = qs + D;                                     // [8][32][D+1]
+    float* lists_s = cs_all + (size_t)8 * 32 * (D + 1);         // [8][32]
+    int* lists_i = reinterpret_cast<int*>(lists_s + 8 * 32);
+    const int split = blockIdx.x;
+    const int64_t t = blockIdx.y, b = blockIdx.z;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const T* q = static_cast<const T*>(a.q);
+    const T* c = static_cast<const T*>(a.c);
+    for (int d = tid; d < D; d += kTopkThreads) qs[d] = load_as<float>(q + b * a.sq[0] + t * a.sq[1] + d * a.sq[2]) * a.scale_f;
+    __syncthreads();
+    const int64_t qb = a.nb - 1;
+    float* cs = cs_all + (size_t)warp * 32 * (D + 1);
+    float ls = -INFINITY;
+    int li = INT_MAX;
+    for (int ch = 0; ch < 2; ++ch) {
+        const int64_t nbase = (int64_t)split * kSplitCand + warp * 64 + ch * 32;
+        for (int e = lane; e < 32 * D; e += 32) {
+            const int r = e / D, d = e - (e / D) * D;
+            const int64_t n = nbase + r;
+            cs[r * (D + 1) + d] = n < a.nb ? load_as<float>(c + b * a.sc[0] + n * a.sc[1] + d * a.sc[2]) : 0.f;
+        }
+        __syncwarp();
+        const int64_t n = nbase + lane;
+        float sc = -INFINITY;
+        int ci = INT_MAX;
+        if (n < a.nb) {
+            float acc = 0.f;
+            for (int d = 0; d < D; ++d) acc = fmaf(qs[d], cs[lane * (D + 1) + d], acc);
+            sc = acc - a.pen[qb - n];
+            ci = (int)n;
+        }
+        warp_offer(ls, li, sc, ci, a.keff, lane);
+        __syncwarp();
+    }
+    lists_s[warp * 32 + lane] = ls;
+    lists_i[warp * 32 + lane] = li;
+    __syncthreads();
+    if (warp == 0) {
+        for (int w = 1; w < kTopkThreads / 32; ++w) warp_merge(ls, li, lists_s[w * 32 + lane], lists_i[w * 32 + lane], lane);
+        const size_t o = ((size_t)(b * a.L + t) * nsplit + split) * 32 + lane;
+        part_s[o] = ls;
+        part_i[o] = li;
+    }
+}
+
+__global__ void topk_decode_merge_kernel(TopkArgs a, const float* part_s, const int* part_i, int nsplit, int64_t B) {
+    const int lane = threadIdx.x & 31;
+    const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+    if (row >= B * a.L) return;
+    const int64_t b = row / a.L, t = row - (row / a.L) * a.L;
+    const size_t base = (size_t)row * nsplit * 32;
+    float ls = part_s[base + lane];
+    int li = part_i[base + lane];
+    for (int sp = 1; sp < nsplit; ++sp) warp_merge(ls, li, part_s[base + sp * 32 + lane], part_i[base + sp * 32 + lane], lane);
+    write_topk_row(a, b, t, li, lane, a.nb - 1);
+}
+
+int64_t decode_split_count(int64_t nb) { return (nb + kSplitCand - 1) / kSplitCand; }
+
+bool decode_split_wanted(const TopkArgs& a, int64_t B, int dtype) {
+    return a.decode && dtype != MABA_F64 && a.keff <= 32 && a.nb >= 4 * kSplitCand && B * a.L <= 256 &&
+           a.scores == nullptr;
+}
+
 template <typename T>
 int launch_topk(TopkArgs& a, int64_t B, cudaStream_t s) {
     using SC = typename std::conditional<sizeof(T) == 8, double, float>::type;
@@ -489,10 +567,10 @@ int launch_topk(TopkArgs& a, int64_t B, cudaStream_t s) {
     return check_launch("index_topk(tile)");
 }
 
-int64_t penalty_len(int64_t L, int64_t nb, int32_t block, int decode) {
+int64_t penalty_len(int64_t L, int64_t nb, int32_t block, int decode, int64_t q_pos0 = 0) {
     int64_t n = nb;
     if (!decode && L > 0 && block > 0) {
-        int64_t qmax = (L - 1) / block + 1;
+        int64_t qmax = (q_pos0 + L - 1) / block + 1;
         if (qmax > n) n = qmax;
     }
     return n > 0 ? n : 1;
@@ -548,13 +626,16 @@ extern "C" size_t maba_index_topk_workspace_size(int64_t B, int64_t L, int64_t n
     // callers pass L and nb and the table holds max(nb, L) entries.
     int64_t n = nb > L ? nb : L;
     if (n < 1) n = 1;
-    return (size_t)((n * sizeof(float) + 255) / 256 * 256);
+    size_t bytes = (size_t)((n * sizeof(float) + 255) / 256 * 256);
+    if (B * L <= 256 && nb >= 4 * kSplitCand && top_k <= 32)  // room for the decode split partial lists
+        bytes += (size_t)B * L * decode_split_count(nb) * 32 * 8;
+    return bytes;
 }
 
-extern "C" int maba_index_topk(const maba_tensor* q_idx, const maba_tensor* centroids, float lambda_dist,
-                               int32_t top_k, int32_t block_size, int32_t decode, const maba_tensor* idx_out,
-                               const maba_tensor* scores_out, void* workspace, size_t workspace_bytes,
-                               void* stream) {
+static int index_topk_impl(const maba_tensor* q_idx, const maba_tensor* centroids, float lambda_dist,
+                           int32_t top_k, int32_t block_size, int32_t decode, int64_t q_pos0,
+                           const maba_tensor* idx_out, const maba_tensor* scores_out, void* workspace,
+                           size_t workspace_bytes, void* stream) {
     if (!present(q_idx) || !present(centroids) || q_idx->ndim != 3 || centroids->ndim != 3)
         return set_error(MABA_ERR_INVALID, "index_topk: q_idx and centroids must be 3D");
     if (top_k <= 0) return set_error(MABA_ERR_INVALID, "index_topk: top_k must be positive, got %d", top_k);
@@ -575,7 +656,8 @@ extern "C" int maba_index_topk(const maba_tensor* q_idx, const maba_tensor* cent
     }
     if (L == 0 || nb == 0 || B == 0) return MABA_OK;  // caller fills the empty result
     if (nb > INT_MAX / 2) return set_error(MABA_ERR_UNSUPPORTED, "index_topk: nb too large");
-    const int64_t plen = penalty_len(L, nb, block_size, decode);
+    if (q_pos0 < 0) return set_error(MABA_ERR_INVALID, "index_topk: negative query offset");
+    const int64_t plen = penalty_len(L, nb, block_size, decode, q_pos0);
     const size_t need = (size_t)plen * sizeof(float);
     if (workspace == nullptr || workspace_bytes < need)
         return set_error(MABA_ERR_WORKSPACE, "index_topk: workspace of %zu bytes required, got %zu", need,
@@ -595,9 +677,60 @@ extern "C" int maba_index_topk(const maba_tensor* q_idx, const maba_tensor* cent
         a.ss[i] = present(scores_out) ? scores_out->stride[i] : 0;
     }
     a.L = L; a.nb = nb; a.D = (int)D; a.block = block_size; a.keff = (int)keff; a.decode = decode ? 1 : 0;
+    a.q_pos0 = decode ? 0 : q_pos0;
     a.scale_d = 1.0 / sqrt((double)D);
     a.scale_f = (float)a.scale_d;
+    if (decode_split_wanted(a, B, q_idx->dtype)) {
+        const int64_t nsplit = decode_split_count(nb);
+        const size_t off = (need + 255) / 256 * 256;
+        const size_t part = (size_t)B * L * nsplit * 32;
+        if (workspace_bytes >= off + part * 8) {
+            float* ps = reinterpret_cast<float*>(static_cast<char*>(workspace) + off);
+            int* pi = reinterpret_cast<int*>(ps + part);
+            const size_t smem = sizeof(float) * ((size_t)D + (size_t)8 * 32 * (D + 1) + 8 * 32) + sizeof(int) * 8 * 32;
+            if (smem <= 200 * 1024) {
+                return MABA_DISPATCH_FLOAT(q_idx->dtype, "index_topk", [&] {
+                    if constexpr (sizeof(T) == 8) {
+                        return launch_topk<T>(a, B, s);
+                    } else {
+                        auto kern = topk_decode_partial_kernel<T>;
+                        if (smem > 48 * 1024)
+                            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+                        kern<<<dim3((unsigned)nsplit, (unsigned)L, (unsigned)B), kTopkThreads, smem, s>>>(a, ps, pi,
+                                                                                                        (int)nsplit);
+                        MABA_TRY(check_launch("index_topk(decode partial)"));
+                        const int64_t rows = B * L;
+                        topk_decode_merge_kernel<<<(unsigned)ceil_div(rows, 4), 128, 0, s>>>(a, ps, pi, (int)nsplit, B);
+                        return check_launch("index_topk(decode merge)");
+                    }
+                });
+            }
+        }
+    }
     return MABA_DISPATCH_FLOAT(q_idx->dtype, "index_topk", [&] { return launch_topk<T>(a, B, s); });
+}
+
+extern "C" int maba_index_topk(const maba_tensor* q_idx, const maba_tensor* centroids, float lambda_dist,
+                               int32_t top_k, int32_t block_size, int32_t decode, const maba_tensor* idx_out,
+                               const maba_tensor* scores_out, void* workspace, size_t workspace_bytes,
+                               void* stream) {
+    return index_topk_impl(q_idx, centroids, lambda_dist, top_k, block_size, decode, 0, idx_out, scores_out,
+                           workspace, workspace_bytes, stream);
+}
+
+extern "C" int maba_index_topk_at(const maba_tensor* q_idx, const maba_tensor* centroids, float lambda_dist,
+                                  int32_t top_k, int32_t block_size, int64_t q_pos0, const maba_tensor* idx_out,
+                                  const maba_tensor* scores_out, void* workspace, size_t workspace_bytes,
+                                  void* stream) {
+    return index_topk_impl(q_idx, centroids, lambda_dist, top_k, block_size, 0, q_pos0, idx_out, scores_out,
+                           workspace, workspace_bytes, stream);
+}
+
+extern "C" size_t maba_index_topk_at_workspace_size(int64_t B, int64_t L, int64_t nb, int32_t top_k, int32_t block_size,
+                                                    int64_t q_pos0) {
+    (void)B; (void)top_k;
+    const int64_t n = penalty_len(L, nb, block_size > 0 ? block_size : 1, 0, q_pos0 > 0 ? q_pos0 : 0);
+    return (size_t)((n * sizeof(float) + 255) / 256 * 256);
 }
 
 // ---------------------------------------------------------------------------

@@ -234,8 +234,9 @@ int sa_attention_simt(SaArgs& a, int64_t B, int dtype, cudaStream_t s) {
 using namespace maba;
 
 extern "C" size_t maba_sa_attention_workspace_size(int32_t dtype, int64_t B, int64_t Lq, int64_t Lkv, int64_t H,
-                                                   int64_t d_c, int64_t K, int32_t block_size) {
-    return sa_attention_workspace_bytes(dtype, B, Lq, Lkv, H, d_c, K, block_size);
+                                                   int64_t d_c, int64_t K, int32_t window, int32_t n_sinks,
+                                                   int32_t block_size, int32_t hca_r) {
+    return sa_attention_workspace_bytes(dtype, B, Lq, Lkv, H, d_c, K, block_size, window, n_sinks, hca_r);
 }
 
 extern "C" int maba_sa_attention(const maba_tensor* qhat, const maba_tensor* c_kv, const maba_tensor* hca,

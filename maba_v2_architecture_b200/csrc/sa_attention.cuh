@@ -25,12 +25,27 @@ bool sa_attention_mma_supported(const SaArgs& a, int dtype);
 size_t sa_attention_mma_workspace(int dtype, int64_t B, int64_t Lq, int64_t Lkv, int64_t H, int64_t DC, int64_t K,
                                   int32_t block);
 
+bool sa_attention_decode_supported(const SaArgs& a);
+size_t sa_attention_decode_workspace(int64_t B, int64_t Lq, int64_t Lkv, int64_t H, int64_t DC, int64_t K,
+                                     int32_t block, int32_t window, int32_t n_sinks, int32_t hca_r);
+int sa_attention_decode(SaArgs& a, int64_t B, int dtype, cudaStream_t s);
+
 inline size_t sa_attention_workspace_bytes(int dtype, int64_t B, int64_t Lq, int64_t Lkv, int64_t H, int64_t DC,
-                                           int64_t K, int32_t block) {
-    return sa_attention_mma_workspace(dtype, B, Lq, Lkv, H, DC, K, block);
+                                           int64_t K, int32_t block, int32_t window, int32_t n_sinks,
+                                           int32_t hca_r) {
+    size_t a = sa_attention_mma_workspace(dtype, B, Lq, Lkv, H, DC, K, block);
+    size_t b = sa_attention_decode_workspace(B, Lq, Lkv, H, DC, K, block, window, n_sinks, hca_r);
+    return a > b ? a : b;
 }
 
+// Single-token queries take the split-K decode kernels when the caller gave
+// the workspace they need; 16-bit prefill tiles take the tensor-core kernel;
+// everything else the exact CUDA-core kernel.
 inline int sa_attention_dispatch(SaArgs& a, int64_t B, int dtype, cudaStream_t s) {
+    if (dtype != MABA_F64 && sa_attention_decode_supported(a) &&
+        a.workspace_bytes >= sa_attention_decode_workspace(B, a.Lq, a.Lkv, a.H, a.DC, a.K, a.block, a.window,
+                                                           a.n_sinks, a.hca_r))
+        return sa_attention_decode(a, B, dtype, s);
     if (sa_attention_mma_supported(a, dtype)) return sa_attention_mma(a, B, dtype, s);
     return sa_attention_simt(a, B, dtype, s);
 }

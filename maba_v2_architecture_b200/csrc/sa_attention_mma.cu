@@ -52,6 +52,13 @@ struct MmaSmem {
     }
 };
 
+// 2^x on the SFU (ex2.approx: relative error ~2^-22, flushes subnormals; exp2(-inf) = 0)
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
@@ -381,25 +388,49 @@ __global__ void __launch_bounds__(NTHR, 1) sa_attention_mma_kernel(SaArgs a, int
                         MmaOp<T>::run(s[2 * jp + 1], af, b2, b3);
                     }
                 }
-                // masks (per stream) and scaling to log2 units
-                const int t0 = t_r0, t1 = t_r1;
-                const bool row0_ok = t0 < nt, row1_ok = t1 < nt;
-                const bool sel0 = ti.stream != 1 || ((tmask >> t0) & 1ull);
-                const bool sel1 = ti.stream != 1 || ((tmask >> t1) & 1ull);
+                // masks (per stream) and scaling to log2 units.  Each of the thread's two
+                // rows is classified once per tile: every key of the tile valid, none valid,
+                // or mixed (only then the per-key test runs, in 32-bit arithmetic).
+                const int kb = (int)ti.row0;
+                int cls[2];
+#pragma unroll
+                for (int rr = 0; rr < 2; ++rr) {
+                    const int t = rr == 0 ? t_r0 : t_r1;
+                    const int pos = (int)(rr == 0 ? pos_r0 : pos_r1);
+                    const bool sel = ti.stream != 1 || ((tmask >> t) & 1ull);
+                    int c;  // 0 none, 1 all, 2 mixed
+                    if (t >= nt || !sel) {
+                        c = 0;
+                    } else if (ti.stream == 0) {
+                        const bool all = kb + KT - 1 <= pos && kb + KT - 1 < a.Lkv && pos - kb < a.window;
+                        const bool none = kb > pos || (pos - (kb + KT - 1) >= a.window && kb >= a.n_sinks);
+                        c = all ? 1 : (none ? 0 : 2);
+                    } else if (ti.stream == 1) {
+                        const bool all = kb + KT - 1 <= pos && kb + KT - 1 < a.Lkv && a.block >= KT;
+                        c = all ? 1 : (kb > pos ? 0 : 2);
+                    } else {
+                        const bool all = (kb + KT) * a.hca_r - 1 <= pos && kb + KT - 1 < a.NC;
+                        c = all ? 1 : ((kb + 1) * a.hca_r - 1 > pos ? 0 : 2);
+                    }
+                    cls[rr] = c;
+                }
                 float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
-                        const int64_t key = ti.row0 + j * 8 + qd + (e & 1);
-                        const int64_t pos = e < 2 ? pos_r0 : pos_r1;
-                        bool ok = e < 2 ? (row0_ok && sel0) : (row1_ok && sel1);
-                        if (ti.stream == 0) {
-                            ok = ok && key < a.Lkv && key <= pos && ((pos - key) < a.window || key < a.n_sinks);
-                        } else if (ti.stream == 1) {
-                            ok = ok && key < a.Lkv && key <= pos && (key - ti.row0) < a.block;
-                        } else {
-                            ok = ok && key < a.NC && (key + 1) * a.hca_r - 1 <= pos;
+                        const int rr = e >> 1;
+                        bool ok = cls[rr] == 1;
+                        if (cls[rr] == 2) {
+                            const int key = kb + j * 8 + qd + (e & 1);
+                            const int pos = (int)(rr == 0 ? pos_r0 : pos_r1);
+                            if (ti.stream == 0) {
+                                ok = key < a.Lkv && key <= pos && ((pos - key) < a.window || key < a.n_sinks);
+                            } else if (ti.stream == 1) {
+                                ok = key < a.Lkv && key <= pos && (key - kb) < a.block;
+                            } else {
+                                ok = key < a.NC && (key + 1) * a.hca_r - 1 <= pos;
+                            }
                         }
                         const float v = ok ? s[j][e] * LOG2E : -INFINITY;
                         s[j][e] = v;
@@ -414,27 +445,29 @@ __global__ void __launch_bounds__(NTHR, 1) sa_attention_mma_kernel(SaArgs a, int
                 const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
                 const float mu0 = mn0 == -INFINITY ? 0.f : mn0;
                 const float mu1 = mn1 == -INFINITY ? 0.f : mn1;
-                const float c0 = exp2f(m0 - mu0), c1 = exp2f(m1 - mu1);
+                const float c0 = ex2(m0 - mu0), c1 = ex2(m1 - mu1);
                 m0 = mn0;
                 m1 = mn1;
                 float ps0 = 0.f, ps1 = 0.f;
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
-                    s[j][0] = exp2f(s[j][0] - mu0);
-                    s[j][1] = exp2f(s[j][1] - mu0);
-                    s[j][2] = exp2f(s[j][2] - mu1);
-                    s[j][3] = exp2f(s[j][3] - mu1);
+                    s[j][0] = ex2(s[j][0] - mu0);
+                    s[j][1] = ex2(s[j][1] - mu0);
+                    s[j][2] = ex2(s[j][2] - mu1);
+                    s[j][3] = ex2(s[j][3] - mu1);
                     ps0 += s[j][0] + s[j][1];
                     ps1 += s[j][2] + s[j][3];
                 }
                 l0 = l0 * c0 + ps0;
                 l1 = l1 * c1 + ps1;
+                if (c0 != 1.f || c1 != 1.f) {
 #pragma unroll
-                for (int n = 0; n < 16; ++n) {
-                    oacc[n][0] *= c0;
-                    oacc[n][1] *= c0;
-                    oacc[n][2] *= c1;
-                    oacc[n][3] *= c1;
+                    for (int n = 0; n < 16; ++n) {
+                        oacc[n][0] *= c0;
+                        oacc[n][1] *= c0;
+                        oacc[n][2] *= c1;
+                        oacc[n][3] *= c1;
+                    }
                 }
                 // O += P V  (V = the same latent tile, read transposed)
 #pragma unroll

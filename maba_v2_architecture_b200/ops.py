@@ -262,6 +262,7 @@ def b200_index_topk(
     """
     lam = kwargs.get("dist_lambda", lambda_dist)
     decode = bool(kwargs.get("decode", False))
+    q_pos0 = int(kwargs.get("q_pos0", 0))  # absolute position of row 0 (a sequence segment); prefill only
     if q_idx.device != centroids.device:
         raise RuntimeError(
             f"Expected all tensors to be on the same device, got {q_idx.device} and {centroids.device}"
@@ -290,12 +291,20 @@ def b200_index_topk(
     idx = torch.empty(B, L, ak, dtype=torch.long, device=q_idx.device)
     scores = torch.empty(B, L, nb, dtype=q_idx.dtype, device=q_idx.device) if return_scores else None
     lib = N.lib()
-    nbytes = lib.maba_index_topk_workspace_size(B, L, nb, int(top_k))
-    ws = N.workspace(nbytes, q_idx.device)
-    rc = lib.maba_index_topk(
-        N.ref(N.desc(q_idx)), N.ref(N.desc(centroids)), float(lam), int(top_k), int(block_size), int(decode),
-        N.ref(N.desc(idx)), N.ref(N.desc(scores)), ws.data_ptr(), int(nbytes), N.stream_of(q_idx),
-    )
+    if q_pos0 and not decode:
+        nbytes = lib.maba_index_topk_at_workspace_size(B, L, nb, int(top_k), int(block_size), q_pos0)
+        ws = N.workspace(nbytes, q_idx.device)
+        rc = lib.maba_index_topk_at(
+            N.ref(N.desc(q_idx)), N.ref(N.desc(centroids)), float(lam), int(top_k), int(block_size), q_pos0,
+            N.ref(N.desc(idx)), N.ref(N.desc(scores)), ws.data_ptr(), int(nbytes), N.stream_of(q_idx),
+        )
+    else:
+        nbytes = lib.maba_index_topk_workspace_size(B, L, nb, int(top_k))
+        ws = N.workspace(nbytes, q_idx.device)
+        rc = lib.maba_index_topk(
+            N.ref(N.desc(q_idx)), N.ref(N.desc(centroids)), float(lam), int(top_k), int(block_size), int(decode),
+            N.ref(N.desc(idx)), N.ref(N.desc(scores)), ws.data_ptr(), int(nbytes), N.stream_of(q_idx),
+        )
     N.check(rc, "maba_index_topk")
     if return_scores:
         return idx, scores
@@ -394,7 +403,8 @@ def b200_sa_attention(
         return out
     lib = N.lib()
     K = top_idx.shape[-1]
-    nbytes = lib.maba_sa_attention_workspace_size(N.DTYPE_CODES[qhat.dtype], B, Lq, Lkv, H, dc, K, int(block_size))
+    nbytes = lib.maba_sa_attention_workspace_size(N.DTYPE_CODES[qhat.dtype], B, Lq, Lkv, H, dc, K, int(window_size),
+                                                  int(n_sinks), int(block_size), int(hca_r))
     ws = N.workspace(nbytes, qhat.device)
     rc = lib.maba_sa_attention(
         N.ref(N.desc(qhat)), N.ref(N.desc(c_kv)), N.ref(N.desc(hca)), N.ref(N.desc(top_idx)),
