@@ -250,7 +250,7 @@ def config4_decode(dev, ctx: int = 1048576, steps: int = 256, warmup: int = 3):
     from maba_v2_architecture_b200.workloads import init_module_
 
     model = init_module_(MabaSparseForCausalLM(get_101m_config()), seed=3).to(dev, torch.bfloat16).eval()
-    sess = DecodeSession(model, batch=1, max_len=ctx + steps + warmup + 1, dtype=torch.bfloat16)
+    sess = DecodeSession(model, batch=1, max_len=ctx + steps + 2 * warmup + 16, dtype=torch.bfloat16)
     ids = torch.randint(0, 32768, (1, ctx), generator=torch.Generator().manual_seed(3)).to(dev)
     torch.cuda.synchronize()
     t0 = time.time()
@@ -259,13 +259,24 @@ def config4_decode(dev, ctx: int = 1048576, steps: int = 256, warmup: int = 3):
     prefill_s = time.time() - t0
     del ids
     tok = logits[:, -1].argmax(-1, keepdim=True)
+    # eager steps (one host call per op) for reference, then the captured CUDA-graph step
     for _ in range(warmup):
         tok = sess.step(tok)[:, -1].argmax(-1, keepdim=True)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for _ in range(steps):
+    for _ in range(8):
         tok = sess.step(tok)[:, -1].argmax(-1, keepdim=True)
+    e1.record()
+    torch.cuda.synchronize()
+    eager_ms = e0.elapsed_time(e1) / 8
+    sess.capture(tok)
+    for _ in range(warmup):
+        sess.replay()
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(steps):
+        sess.replay()
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / steps
@@ -277,8 +288,9 @@ def config4_decode(dev, ctx: int = 1048576, steps: int = 256, warmup: int = 3):
     step_bytes = weights + state + 5 * per_sa
     del sess, model
     torch.cuda.empty_cache()
-    return {"workload": f"config4: 101M model bf16, B=1, prefill {ctx} ids then {steps} greedy steps",
-            "ms_per_token": ms, "context": L, "prefill_s": prefill_s,
+    return {"workload": f"config4: 101M model bf16, B=1, prefill {ctx} ids then {steps} greedy steps "
+                        "(captured CUDA-graph decode step)",
+            "ms_per_token": ms, "eager_ms_per_token": eager_ms, "context": L, "prefill_s": prefill_s,
             "hbm_bytes_per_step": step_bytes, "hbm_gbs": step_bytes / (ms * 1e-3) / 1e9}
 
 

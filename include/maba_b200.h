@@ -87,6 +87,19 @@ MABA_API int maba_dgda_prefill(const maba_tensor* q, const maba_tensor* k, const
 MABA_API size_t maba_dgda_prefill_workspace_size(int32_t dtype, int64_t B, int64_t H, int64_t L,
                                         int64_t dk, int64_t dv);
 
+/* ---- DGDA segment transition -------------------------------------------
+ * The affine map of a whole sequence segment on the recurrent state:
+ * S_end = P S_start + R, written as trans_out [B,H,64,128] fp32 = [R | P]
+ * (R: 64 x 64 padded dk x dv, P: 64 x 64 padded dk x dk).  Lets GPUs that hold
+ * consecutive segments of one sequence chain their states with one small
+ * all-gather (same recurrence as maba_sparse/kernels/common.py:256-265).
+ * Inputs as for maba_dgda_prefill; fp32 / fp16 / bf16. */
+MABA_API int maba_dgda_transition(const maba_tensor* q, const maba_tensor* k, const maba_tensor* v,
+                                  const maba_tensor* alpha, const maba_tensor* log_alpha,
+                                  const maba_tensor* b, const maba_tensor* w, const maba_tensor* trans_out,
+                                  void* workspace, size_t workspace_bytes, void* stream);
+MABA_API size_t maba_dgda_transition_workspace_size(int32_t dtype, int64_t B, int64_t H, int64_t L);
+
 /* ---- DGDA decode step --------------------------------------------------
  * Replaces the `dgda_step` registry op:
  *   maba_sparse/kernels/dispatcher.py:330, common.py:271-309,
@@ -195,6 +208,41 @@ MABA_API int maba_sa_attention(const maba_tensor* qhat, const maba_tensor* c_kv,
 MABA_API size_t maba_sa_attention_workspace_size(int32_t dtype, int64_t B, int64_t Lq, int64_t Lkv,
                                                  int64_t H, int64_t d_c, int64_t K, int32_t window,
                                                  int32_t n_sinks, int32_t block_size, int32_t hca_r);
+
+/* ---- Decode at a device-held position ------------------------------------
+ * Single-token decode over preallocated caches whose visible length lives in
+ * device memory (*pos_dev = position of the new token), so that a whole decode
+ * step can be captured once in a CUDA graph and replayed.  Same results as the
+ * host-length entry points above (the reference's decode:
+ * maba_sparse/layers/sparse_attention.py:228-261, layers/indexer.py:62-112).
+ *
+ * maba_decode_cache_append: writes the new latent row c_new [B,1,d_c] and
+ *   index-key row k_new [B,1,d_idx] at pos into c_cache [B,Lcap,d_c] /
+ *   kidx_cache [B,Lcap,d_idx], refreshes the centroid of pos's block in
+ *   cent_table [B,nbcap,d_idx] (zero-padded tail, as compute_centroids) and,
+ *   when pos closes an r-row group, its pooled mean in hca_table [B,NCcap,d_c]. */
+MABA_API int maba_decode_cache_append(const maba_tensor* c_new, const maba_tensor* k_new,
+                                      const maba_tensor* c_cache, const maba_tensor* kidx_cache,
+                                      const maba_tensor* cent_table, const maba_tensor* hca_table,
+                                      const int64_t* pos_dev, int32_t block_size, int32_t hca_r, void* stream);
+/* Decode top-k over the first pos/block + 1 rows of cent_table; idx_out is
+ * [B,1,min(top_k,nbcap)], slots past the visible blocks hold future indices. */
+MABA_API int maba_index_topk_decode_at(const maba_tensor* q_idx, const maba_tensor* cent_table,
+                                       float lambda_dist, int32_t top_k, int32_t block_size,
+                                       const int64_t* pos_dev, const maba_tensor* idx_out,
+                                       void* workspace, size_t workspace_bytes, void* stream);
+MABA_API size_t maba_index_topk_decode_at_workspace_size(int64_t B, int64_t nbcap, int32_t top_k);
+/* Split-K three-stream decode attention over c_cache[:, :pos+1] and the
+ * complete rows of hca_table; qhat [B,1,H,d_c], top_idx [B,1,K], out [B,1,H,d_c]. */
+MABA_API int maba_sa_attention_decode_at(const maba_tensor* qhat, const maba_tensor* c_cache,
+                                         const maba_tensor* hca_table, const maba_tensor* top_idx,
+                                         const maba_tensor* gate, const maba_tensor* out,
+                                         const int64_t* pos_dev, int32_t window, int32_t n_sinks,
+                                         int32_t block_size, int32_t hca_r, void* workspace,
+                                         size_t workspace_bytes, void* stream);
+MABA_API size_t maba_sa_attention_decode_at_workspace_size(int64_t B, int64_t Lcap, int64_t NCcap,
+                                                           int64_t H, int64_t d_c, int64_t K, int32_t window,
+                                                           int32_t n_sinks, int32_t block_size, int32_t hca_r);
 
 #ifdef __cplusplus
 }

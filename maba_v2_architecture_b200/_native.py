@@ -51,6 +51,8 @@ SIGNATURES = {
     "maba_dgda_prefill": (ctypes.c_int, [T_P] * 10 + [_i32, _vp, _sz, _vp]),
     "maba_dgda_prefill_workspace_size": (_sz, [_i32, _i64, _i64, _i64, _i64, _i64]),
     "maba_dgda_step": (ctypes.c_int, [T_P] * 10 + [_vp]),
+    "maba_dgda_transition": (ctypes.c_int, [T_P] * 8 + [_vp, _sz, _vp]),
+    "maba_dgda_transition_workspace_size": (_sz, [_i32, _i64, _i64, _i64]),
     "maba_compute_centroids": (ctypes.c_int, [T_P, T_P, _i32, _vp]),
     "maba_index_topk": (ctypes.c_int, [T_P, T_P, _f32, _i32, _i32, _i32, T_P, T_P, _vp, _sz, _vp]),
     "maba_index_topk_workspace_size": (_sz, [_i64, _i64, _i64, _i32]),
@@ -61,6 +63,11 @@ SIGNATURES = {
     "maba_hca_pool": (ctypes.c_int, [T_P, T_P, _i32, _vp]),
     "maba_sa_attention": (ctypes.c_int, [T_P] * 6 + [_i32, _i32, _i32, _i32, _vp, _sz, _vp]),
     "maba_sa_attention_workspace_size": (_sz, [_i32, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _i32, _i32, _i32]),
+    "maba_decode_cache_append": (ctypes.c_int, [T_P] * 6 + [_vp, _i32, _i32, _vp]),
+    "maba_index_topk_decode_at": (ctypes.c_int, [T_P, T_P, _f32, _i32, _i32, _vp, T_P, _vp, _sz, _vp]),
+    "maba_index_topk_decode_at_workspace_size": (_sz, [_i64, _i64, _i32]),
+    "maba_sa_attention_decode_at": (ctypes.c_int, [T_P] * 6 + [_vp, _i32, _i32, _i32, _i32, _vp, _sz, _vp]),
+    "maba_sa_attention_decode_at_workspace_size": (_sz, [_i64, _i64, _i64, _i64, _i64, _i64, _i32, _i32, _i32, _i32]),
 }
 
 _lib: Optional[ctypes.CDLL] = None

@@ -383,6 +383,52 @@ __global__ void __launch_bounds__(NT) dgda_combine_kernel(PrefillArgs a) {
     }
 }
 
+// Composes the per-segment transitions of one (b,h) into the transition of the
+// whole range: X = [R | P] starts at [0 | I]; X <- P_s X + [R_s | 0].
+__global__ void __launch_bounds__(NT) dgda_compose_kernel(const float* ws_trans, float* out, int nseg, int64_t out_bh_stride) {
+    __shared__ float X[DP * 2 * DP];
+    __shared__ float Pm[DP * DP];
+    const int tid = threadIdx.x;
+    const int bh = blockIdx.x;
+    for (int e = tid; e < DP * 2 * DP; e += NT) {
+        const int d = e / (2 * DP), c = e - (e / (2 * DP)) * (2 * DP);
+        X[e] = (c >= DP && c - DP == d) ? 1.f : 0.f;
+    }
+    const int tr = tid >> 4, tc = tid & 15;
+    for (int sg = 0; sg < nseg; ++sg) {
+        const float* T = ws_trans + ((size_t)bh * nseg + sg) * DP * 2 * DP;
+        __syncthreads();
+        for (int e = tid; e < DP * DP; e += NT) Pm[e] = T[(e / DP) * 2 * DP + DP + (e % DP)];
+        __syncthreads();
+        float acc[4][8];
+#pragma unroll
+        for (int m = 0; m < 4; ++m)
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+                const int d = tr + 16 * m, c = tc + 16 * kk;
+                acc[m][kk] = c < DP ? T[d * 2 * DP + c] : 0.f;  // + [R_s | 0]
+            }
+        for (int e = 0; e < DP; ++e) {
+            float xv[8];
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) xv[kk] = X[e * 2 * DP + tc + 16 * kk];
+#pragma unroll
+            for (int m = 0; m < 4; ++m) {
+                const float p = Pm[(tr + 16 * m) * DP + e];
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk) acc[m][kk] += p * xv[kk];
+            }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int m = 0; m < 4; ++m)
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) X[(tr + 16 * m) * 2 * DP + tc + 16 * kk] = acc[m][kk];
+    }
+    __syncthreads();
+    for (int e = tid; e < DP * 2 * DP; e += NT) out[(size_t)bh * out_bh_stride + e] = X[e];
+}
+
 int choose_segments(int dtype, int64_t BH, int64_t L) {
     if (dtype == MABA_F64) return 1;
     const int64_t nchunks = ceil_div(L, 64);
@@ -547,4 +593,75 @@ extern "C" int maba_dgda_prefill(const maba_tensor* q, const maba_tensor* k, con
                                    : launch_prefill<__nv_bfloat16, __nv_bfloat16>(a, B, dt, sdt, s, workspace, workspace_bytes);
         default: return set_error(MABA_ERR_DTYPE, "dgda_prefill: unsupported dtype %s", dtype_name(dt));
     }
+}
+
+extern "C" size_t maba_dgda_transition_workspace_size(int32_t dtype, int64_t B, int64_t H, int64_t L) {
+    const int64_t BH = B * H;
+    int nseg = choose_segments(dtype, BH, L);
+    if (nseg < 1) nseg = 1;
+    const int64_t nchunks = ceil_div(L > 0 ? L : 1, 64);
+    const int64_t seg_len = ceil_div(nchunks, nseg) * 64;
+    const int64_t ns = ceil_div(L > 0 ? L : 1, seg_len);
+    return (size_t)BH * ns * DP * 2 * DP * sizeof(float);
+}
+
+extern "C" int maba_dgda_transition(const maba_tensor* q, const maba_tensor* k, const maba_tensor* v,
+                                    const maba_tensor* alpha, const maba_tensor* log_alpha, const maba_tensor* b,
+                                    const maba_tensor* w, const maba_tensor* trans_out, void* workspace,
+                                    size_t workspace_bytes, void* stream) {
+    if (!present(q) || q->ndim != 4 || !present(v) || v->ndim != 4)
+        return set_error(MABA_ERR_INVALID, "dgda_transition: q, v must be 4D [B, H, L, d]");
+    const int64_t B = q->shape[0], H = q->shape[1], L = q->shape[2], dk = q->shape[3], dv = v->shape[3];
+    const int64_t s_k[4] = {B, H, L, dk}, s_v[4] = {B, H, L, dv}, s_t[4] = {B, H, DP, 2 * DP};
+    MABA_TRY(expect_shape(k, "dgda_transition: k", 4, s_k));
+    MABA_TRY(expect_shape(b, "dgda_transition: b", 4, s_k));
+    MABA_TRY(expect_shape(w, "dgda_transition: w", 4, s_v));
+    MABA_TRY(expect_shape(trans_out, "dgda_transition: trans_out", 4, s_t));
+    MABA_TRY(expect_dtype(trans_out, "dgda_transition: trans_out", MABA_F32));
+    if (!present(alpha) && !present(log_alpha))
+        return set_error(MABA_ERR_INVALID, "dgda_transition: either alpha or log_alpha must be provided");
+    if (dk > DP || dv > DP) return set_error(MABA_ERR_UNSUPPORTED, "dgda_transition: head dims <= %d", DP);
+    const int64_t tst[4] = {H * DP * 2 * DP, DP * 2 * DP, 2 * DP, 1};
+    for (int i = 0; i < 4; ++i)
+        if (trans_out->stride[i] != tst[i]) return set_error(MABA_ERR_INVALID, "dgda_transition: trans_out must be contiguous");
+    const int dt = q->dtype;
+    if (dt != MABA_F32 && dt != MABA_F16 && dt != MABA_BF16)
+        return set_error(MABA_ERR_DTYPE, "dgda_transition: float32 / float16 / bfloat16 inputs");
+    const size_t need = maba_dgda_transition_workspace_size(dt, B, H, L);
+    if (workspace == nullptr || workspace_bytes < need)
+        return set_error(MABA_ERR_WORKSPACE, "dgda_transition: workspace of %zu bytes required", need);
+    PrefillArgs a{};
+    a.q = q->data; a.k = k->data; a.v = v->data;
+    a.alpha = present(alpha) ? alpha->data : nullptr;
+    a.log_alpha = present(log_alpha) ? log_alpha->data : nullptr;
+    a.b = b->data; a.w = w->data; a.init = nullptr; a.out = nullptr; a.fin = nullptr;
+    for (int i = 0; i < 4; ++i) {
+        a.sq[i] = q->stride[i]; a.sk[i] = k->stride[i]; a.sv[i] = v->stride[i];
+        a.sa[i] = present(alpha) ? alpha->stride[i] : 0;
+        a.sla[i] = present(log_alpha) ? log_alpha->stride[i] : 0;
+        a.sb[i] = b->stride[i]; a.sw[i] = w->stride[i];
+    }
+    a.L = L; a.H = (int)H; a.dk = (int)dk; a.dv = (int)dv;
+    a.vec8 = (dk == DP && dv == DP && vec8_ok(q) && vec8_ok(k) && vec8_ok(v) && vec8_ok(b) && vec8_ok(w) &&
+              vec8_ok(log_alpha) && (present(log_alpha) || vec8_ok(alpha))) ? 1 : 0;
+    const int64_t BH = B * H;
+    int nseg = choose_segments(dt, BH, L);
+    if (nseg < 1) nseg = 1;
+    const int64_t nchunks = ceil_div(L > 0 ? L : 1, 64);
+    a.seg_len = ceil_div(nchunks, nseg) * 64;
+    a.nseg = (int)ceil_div(L > 0 ? L : 1, a.seg_len);
+    a.ws_trans = static_cast<float*>(workspace);
+    cudaStream_t s = as_stream(stream);
+    const dim3 grid((unsigned)BH, (unsigned)a.nseg);
+    if (dt == MABA_F32) {
+        auto k1 = dgda_chunk_kernel<float, float, float, 64, 1>;
+        MABA_TRY(set_smem(k1, Smem<float, 64, 1>::bytes));
+        k1<<<grid, NT, Smem<float, 64, 1>::bytes, s>>>(a);
+        MABA_TRY(check_launch("dgda_transition"));
+    } else {
+        MABA_TRY(dgda_mma_launch(a, grid, 1, dt, MABA_F32, s));
+    }
+    dgda_compose_kernel<<<(unsigned)BH, NT, 0, s>>>(a.ws_trans, static_cast<float*>(trans_out->data), a.nseg,
+                                                   DP * 2 * DP);
+    return check_launch("dgda_transition(compose)");
 }

@@ -150,6 +150,7 @@ struct TopkArgs {
     int64_t sq[3], sc[3], si[3], ss[3];
     int64_t L, nb;
     int64_t q_pos0;  // absolute position of query row 0 (prefill)
+    const int64_t* pos_dev;  // decode at a device-held position: nb = *pos_dev / block + 1 (<= nb)
     int D, block, keff, decode;
     float scale_f;
     double scale_d;
@@ -474,9 +475,15 @@ __global__ void __launch_bounds__(kTopkThreads) topk_decode_partial_kernel(TopkA
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const T* q = static_cast<const T*>(a.q);
     const T* c = static_cast<const T*>(a.c);
+    int64_t nb = a.nb;
+    if (a.pos_dev != nullptr) {
+        const int64_t v = *a.pos_dev / a.block + 1;
+        nb = v < a.nb ? v : a.nb;
+    }
+    if ((int64_t)split * kSplitCand >= nb) return;  // capacity-sized grid: nothing to score here
     for (int d = tid; d < D; d += kTopkThreads) qs[d] = load_as<float>(q + b * a.sq[0] + t * a.sq[1] + d * a.sq[2]) * a.scale_f;
     __syncthreads();
-    const int64_t qb = a.nb - 1;
+    const int64_t qb = nb - 1;
     float* cs = cs_all + (size_t)warp * 32 * (D + 1);
     float ls = -INFINITY;
     int li = INT_MAX;
@@ -485,13 +492,13 @@ __global__ void __launch_bounds__(kTopkThreads) topk_decode_partial_kernel(TopkA
         for (int e = lane; e < 32 * D; e += 32) {
             const int r = e / D, d = e - (e / D) * D;
             const int64_t n = nbase + r;
-            cs[r * (D + 1) + d] = n < a.nb ? load_as<float>(c + b * a.sc[0] + n * a.sc[1] + d * a.sc[2]) : 0.f;
+            cs[r * (D + 1) + d] = n < nb ? load_as<float>(c + b * a.sc[0] + n * a.sc[1] + d * a.sc[2]) : 0.f;
         }
         __syncwarp();
         const int64_t n = nbase + lane;
         float sc = -INFINITY;
         int ci = INT_MAX;
-        if (n < a.nb) {
+        if (n < nb) {
             float acc = 0.f;
             for (int d = 0; d < D; ++d) acc = fmaf(qs[d], cs[lane * (D + 1) + d], acc);
             sc = acc - a.pen[qb - n];
@@ -516,11 +523,18 @@ __global__ void topk_decode_merge_kernel(TopkArgs a, const float* part_s, const 
     const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
     if (row >= B * a.L) return;
     const int64_t b = row / a.L, t = row - (row / a.L) * a.L;
+    int64_t nb = a.nb;
+    if (a.pos_dev != nullptr) {
+        const int64_t v = *a.pos_dev / a.block + 1;
+        nb = v < a.nb ? v : a.nb;
+    }
+    const int used = (int)((nb + kSplitCand - 1) / kSplitCand);
     const size_t base = (size_t)row * nsplit * 32;
     float ls = part_s[base + lane];
     int li = part_i[base + lane];
-    for (int sp = 1; sp < nsplit; ++sp) warp_merge(ls, li, part_s[base + sp * 32 + lane], part_i[base + sp * 32 + lane], lane);
-    write_topk_row(a, b, t, li, lane, a.nb - 1);
+    for (int sp = 1; sp < used && sp < nsplit; ++sp)
+        warp_merge(ls, li, part_s[base + sp * 32 + lane], part_i[base + sp * 32 + lane], lane);
+    write_topk_row(a, b, t, li, lane, nb - 1);
 }
 
 int64_t decode_split_count(int64_t nb) { return (nb + kSplitCand - 1) / kSplitCand; }
@@ -780,4 +794,159 @@ extern "C" int maba_index_topk_noalloc(const maba_tensor* q_idx, const maba_tens
     MABA_TRY(noalloc_table(&table));
     return maba_index_topk(q_idx, centroids, lambda_dist, top_k, block_size, decode, idx_out, scores_out, table,
                            sizeof(float) * (size_t)MABA_NOALLOC_PENALTY_MAX, stream);
+}
+
+// ---------------------------------------------------------------------------
+// Decode at a device-held position (CUDA-graph friendly): cache append + top-k
+// ---------------------------------------------------------------------------
+namespace maba {
+namespace {
+
+struct AppendArgs {
+    const void* c_new; const void* k_new;
+    void* c; void* kidx; void* cent; void* hca;
+    int64_t s_cn[3], s_kn[3], s_c[3], s_k[3], s_ce[3], s_h[3];
+    int64_t Lcap, nbcap, nccap;
+    int DC, DI, block, r;
+    const int64_t* pos_dev;
+};
+
+// Writes the new latent / index-key rows at `pos`, refreshes the centroid of
+// pos's block (zero-padded tail, as compute_centroids) and, when pos closes an
+// r-row group, writes its pooled HCA mean.
+template <typename T>
+__global__ void decode_append_kernel(AppendArgs a) {
+    const int64_t b = blockIdx.x;
+    const int64_t pos = *a.pos_dev;
+    if (pos < 0 || pos >= a.Lcap) return;
+    T* c = static_cast<T*>(a.c);
+    T* kidx = static_cast<T*>(a.kidx);
+    const T* cn = static_cast<const T*>(a.c_new);
+    const T* kn = static_cast<const T*>(a.k_new);
+    for (int d = threadIdx.x; d < a.DC; d += blockDim.x)
+        c[b * a.s_c[0] + pos * a.s_c[1] + d * a.s_c[2]] = cn[b * a.s_cn[0] + d * a.s_cn[2]];
+    for (int d = threadIdx.x; d < a.DI; d += blockDim.x)
+        kidx[b * a.s_k[0] + pos * a.s_k[1] + d * a.s_k[2]] = kn[b * a.s_kn[0] + d * a.s_kn[2]];
+    __syncthreads();
+    const int64_t blk = pos / a.block, start = blk * a.block;
+    if (blk < a.nbcap) {
+        T* cent = static_cast<T*>(a.cent);
+        const bool padded = pos + 1 < start + a.block;
+        for (int d = threadIdx.x; d < a.DI; d += blockDim.x) {
+            float sum = 0.f, mx = padded ? 0.f : -INFINITY;
+            for (int64_t t = start; t <= pos; ++t) {
+                const float x = load_as<float>(kidx + b * a.s_k[0] + t * a.s_k[1] + d * a.s_k[2]);
+                sum += x;
+                mx = x > mx ? x : mx;
+            }
+            store_from<T, float>(cent + b * a.s_ce[0] + blk * a.s_ce[1] + d * a.s_ce[2],
+                                 0.5f * (sum / float(a.block) + mx));
+        }
+    }
+    if ((pos + 1) % a.r == 0) {
+        const int64_t g = (pos + 1) / a.r - 1;
+        if (g < a.nccap) {
+            T* hca = static_cast<T*>(a.hca);
+            for (int d = threadIdx.x; d < a.DC; d += blockDim.x) {
+                float sum = 0.f;
+                for (int64_t t = pos + 1 - a.r; t <= pos; ++t) sum += load_as<float>(c + b * a.s_c[0] + t * a.s_c[1] + d * a.s_c[2]);
+                store_from<T, float>(hca + b * a.s_h[0] + g * a.s_h[1] + d * a.s_h[2], sum / float(a.r));
+            }
+        }
+    }
+}
+
+}  // namespace
+}  // namespace maba
+
+extern "C" int maba_decode_cache_append(const maba_tensor* c_new, const maba_tensor* k_new, const maba_tensor* c_cache,
+                                        const maba_tensor* kidx_cache, const maba_tensor* cent_table,
+                                        const maba_tensor* hca_table, const int64_t* pos_dev, int32_t block_size,
+                                        int32_t hca_r, void* stream) {
+    if (!present(c_cache) || c_cache->ndim != 3 || !present(kidx_cache) || kidx_cache->ndim != 3)
+        return set_error(MABA_ERR_INVALID, "decode_cache_append: caches must be [B, Lcap, d]");
+    if (pos_dev == nullptr) return set_error(MABA_ERR_INVALID, "decode_cache_append: device position required");
+    if (block_size <= 0 || hca_r <= 0) return set_error(MABA_ERR_INVALID, "decode_cache_append: block/r must be positive");
+    const int64_t B = c_cache->shape[0], Lcap = c_cache->shape[1], DC = c_cache->shape[2], DI = kidx_cache->shape[2];
+    const int64_t scn[3] = {B, 1, DC}, skn[3] = {B, 1, DI}, sk[3] = {B, Lcap, DI};
+    MABA_TRY(expect_shape(c_new, "decode_cache_append: c_new", 3, scn));
+    MABA_TRY(expect_shape(k_new, "decode_cache_append: k_new", 3, skn));
+    MABA_TRY(expect_shape(kidx_cache, "decode_cache_append: kidx_cache", 3, sk));
+    const int64_t sce[3] = {B, -1, DI}, sh[3] = {B, -1, DC};
+    MABA_TRY(expect_shape(cent_table, "decode_cache_append: cent_table", 3, sce));
+    MABA_TRY(expect_shape(hca_table, "decode_cache_append: hca_table", 3, sh));
+    const int dt = c_cache->dtype;
+    const maba_tensor* all[] = {c_new, k_new, kidx_cache, cent_table, hca_table};
+    for (const maba_tensor* t : all) MABA_TRY(expect_dtype(t, "decode_cache_append", dt));
+    AppendArgs a{};
+    a.c_new = c_new->data; a.k_new = k_new->data; a.c = c_cache->data; a.kidx = kidx_cache->data;
+    a.cent = cent_table->data; a.hca = hca_table->data;
+    for (int i = 0; i < 3; ++i) {
+        a.s_cn[i] = c_new->stride[i]; a.s_kn[i] = k_new->stride[i]; a.s_c[i] = c_cache->stride[i];
+        a.s_k[i] = kidx_cache->stride[i]; a.s_ce[i] = cent_table->stride[i]; a.s_h[i] = hca_table->stride[i];
+    }
+    a.Lcap = Lcap; a.nbcap = cent_table->shape[1]; a.nccap = hca_table->shape[1];
+    a.DC = (int)DC; a.DI = (int)DI; a.block = block_size; a.r = hca_r; a.pos_dev = pos_dev;
+    cudaStream_t s = as_stream(stream);
+    return MABA_DISPATCH_FLOAT(dt, "decode_cache_append", [&] {
+        decode_append_kernel<T><<<(unsigned)B, 128, 0, s>>>(a);
+        return check_launch("decode_cache_append");
+    });
+}
+
+extern "C" size_t maba_index_topk_decode_at_workspace_size(int64_t B, int64_t nbcap, int32_t top_k) {
+    (void)top_k;
+    const size_t pen = (size_t)(((nbcap > 0 ? nbcap : 1) * sizeof(float) + 255) / 256 * 256);
+    return pen + (size_t)B * decode_split_count(nbcap) * 32 * 8;
+}
+
+extern "C" int maba_index_topk_decode_at(const maba_tensor* q_idx, const maba_tensor* cent_table, float lambda_dist,
+                                         int32_t top_k, int32_t block_size, const int64_t* pos_dev,
+                                         const maba_tensor* idx_out, void* workspace, size_t workspace_bytes,
+                                         void* stream) {
+    if (!present(q_idx) || !present(cent_table) || q_idx->ndim != 3 || cent_table->ndim != 3 || q_idx->shape[1] != 1)
+        return set_error(MABA_ERR_INVALID, "index_topk_decode_at: q_idx [B,1,d] and cent_table [B,nbcap,d] required");
+    if (pos_dev == nullptr) return set_error(MABA_ERR_INVALID, "index_topk_decode_at: device position required");
+    if (top_k <= 0 || top_k > 32) return set_error(MABA_ERR_UNSUPPORTED, "index_topk_decode_at: top_k in [1, 32]");
+    if (block_size <= 0) return set_error(MABA_ERR_INVALID, "index_topk_decode_at: block_size must be positive");
+    const int64_t B = q_idx->shape[0], D = q_idx->shape[2], nbcap = cent_table->shape[1];
+    if (cent_table->shape[0] != B || cent_table->shape[2] != D)
+        return set_error(MABA_ERR_INVALID, "index_topk_decode_at: dimension mismatch");
+    MABA_TRY(expect_dtype(cent_table, "index_topk_decode_at: cent_table", q_idx->dtype));
+    if (q_idx->dtype == MABA_F64) return set_error(MABA_ERR_UNSUPPORTED, "index_topk_decode_at: float64");
+    const int64_t kout = top_k < nbcap ? top_k : nbcap;
+    const int64_t si[3] = {B, 1, kout};
+    MABA_TRY(expect_shape(idx_out, "index_topk_decode_at: idx_out", 3, si));
+    MABA_TRY(expect_dtype(idx_out, "index_topk_decode_at: idx_out", MABA_I64));
+    const size_t need = maba_index_topk_decode_at_workspace_size(B, nbcap, top_k);
+    if (workspace == nullptr || workspace_bytes < need)
+        return set_error(MABA_ERR_WORKSPACE, "index_topk_decode_at: workspace of %zu bytes required", need);
+    cudaStream_t s = as_stream(stream);
+    float* pen = static_cast<float*>(workspace);
+    penalty_table_kernel<<<(unsigned)ceil_div(nbcap, 256), 256, 0, s>>>(pen, nbcap, lambda_dist);
+    MABA_TRY(check_launch("index_topk_decode_at(penalty)"));
+    const int64_t nsplit = decode_split_count(nbcap);
+    const size_t off = (nbcap * sizeof(float) + 255) / 256 * 256;
+    float* ps = reinterpret_cast<float*>(static_cast<char*>(workspace) + off);
+    int* pi = reinterpret_cast<int*>(ps + (size_t)B * nsplit * 32);
+    TopkArgs a{};
+    a.q = q_idx->data; a.c = cent_table->data; a.idx = static_cast<int64_t*>(idx_out->data); a.scores = nullptr;
+    a.pen = pen;
+    for (int i = 0; i < 3; ++i) { a.sq[i] = q_idx->stride[i]; a.sc[i] = cent_table->stride[i]; a.si[i] = idx_out->stride[i]; }
+    a.L = 1; a.nb = nbcap; a.D = (int)D; a.block = block_size; a.keff = (int)kout; a.decode = 1;
+    a.scale_d = 1.0 / sqrt((double)D); a.scale_f = (float)a.scale_d; a.pos_dev = pos_dev;
+    const size_t smem = sizeof(float) * ((size_t)D + (size_t)8 * 32 * (D + 1) + 8 * 32) + sizeof(int) * 8 * 32;
+    if (smem > 200 * 1024) return set_error(MABA_ERR_UNSUPPORTED, "index_topk_decode_at: d_idx too large");
+    return MABA_DISPATCH_FLOAT(q_idx->dtype, "index_topk_decode_at", [&] {
+        if constexpr (sizeof(T) == 8) {
+            return set_error(MABA_ERR_UNSUPPORTED, "index_topk_decode_at: float64");
+        } else {
+            auto kern = topk_decode_partial_kernel<T>;
+            if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            kern<<<dim3((unsigned)nsplit, 1, (unsigned)B), kTopkThreads, smem, s>>>(a, ps, pi, (int)nsplit);
+            MABA_TRY(check_launch("index_topk_decode_at(partial)"));
+            topk_decode_merge_kernel<<<(unsigned)ceil_div(B, 4), 128, 0, s>>>(a, ps, pi, (int)nsplit, B);
+            return check_launch("index_topk_decode_at(merge)");
+        }
+    });
 }

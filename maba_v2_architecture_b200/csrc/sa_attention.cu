@@ -295,3 +295,48 @@ extern "C" int maba_sa_attention(const maba_tensor* qhat, const maba_tensor* c_k
     if (B == 0 || Lq == 0) return MABA_OK;
     return sa_attention_dispatch(a, B, qhat->dtype, as_stream(stream));
 }
+
+extern "C" size_t maba_sa_attention_decode_at_workspace_size(int64_t B, int64_t Lcap, int64_t NCcap, int64_t H,
+                                                             int64_t d_c, int64_t K, int32_t window, int32_t n_sinks,
+                                                             int32_t block_size, int32_t hca_r) {
+    return sa_attention_decode_at_workspace(B, Lcap, NCcap, H, d_c, K, block_size, window, n_sinks, hca_r);
+}
+
+extern "C" int maba_sa_attention_decode_at(const maba_tensor* qhat, const maba_tensor* c_cache,
+                                           const maba_tensor* hca_table, const maba_tensor* top_idx,
+                                           const maba_tensor* gate, const maba_tensor* out, const int64_t* pos_dev,
+                                           int32_t window, int32_t n_sinks, int32_t block_size, int32_t hca_r,
+                                           void* workspace, size_t workspace_bytes, void* stream) {
+    if (pos_dev == nullptr) return set_error(MABA_ERR_INVALID, "sa_attention_decode_at: device position required");
+    if (!present(qhat) || qhat->ndim != 4 || qhat->shape[1] != 1)
+        return set_error(MABA_ERR_INVALID, "sa_attention_decode_at: qhat must be [B, 1, H, d_c]");
+    if (!present(c_cache) || c_cache->ndim != 3 || !present(hca_table) || hca_table->ndim != 3)
+        return set_error(MABA_ERR_INVALID, "sa_attention_decode_at: c_cache / hca_table must be 3D");
+    const int64_t B = qhat->shape[0], H = qhat->shape[2], DC = qhat->shape[3];
+    if (c_cache->shape[0] != B || c_cache->shape[2] != DC || hca_table->shape[0] != B || hca_table->shape[2] != DC)
+        return set_error(MABA_ERR_INVALID, "sa_attention_decode_at: shape mismatch");
+    if (!present(top_idx) || top_idx->ndim != 3 || top_idx->shape[0] != B || top_idx->shape[1] != 1)
+        return set_error(MABA_ERR_INVALID, "sa_attention_decode_at: top_idx must be [B, 1, K]");
+    if (H > 16 || DC > 256) return set_error(MABA_ERR_UNSUPPORTED, "sa_attention_decode_at: H <= 16, d_c <= 256");
+    const int dt = qhat->dtype;
+    if (dt == MABA_F64) return set_error(MABA_ERR_UNSUPPORTED, "sa_attention_decode_at: float64");
+    MABA_TRY(expect_dtype(c_cache, "sa_attention_decode_at: c_cache", dt));
+    MABA_TRY(expect_dtype(hca_table, "sa_attention_decode_at: hca_table", dt));
+    MABA_TRY(expect_dtype(gate, "sa_attention_decode_at: gate", dt));
+    MABA_TRY(expect_dtype(top_idx, "sa_attention_decode_at: top_idx", MABA_I64));
+    const int64_t so[4] = {B, 1, H, DC};
+    MABA_TRY(expect_shape(out, "sa_attention_decode_at: out", 4, so));
+    MABA_TRY(expect_dtype(out, "sa_attention_decode_at: out", dt));
+    int gate4d = gate->ndim == 4 ? 1 : 0;
+    SaArgs a{};
+    a.qhat = qhat->data; a.ckv = c_cache->data; a.hca = hca_table->data;
+    a.top_idx = static_cast<const int64_t*>(top_idx->data); a.gate = gate->data; a.out = out->data;
+    for (int i = 0; i < 4; ++i) { a.sq[i] = qhat->stride[i]; a.so[i] = out->stride[i]; a.sg[i] = i < gate->ndim ? gate->stride[i] : 0; }
+    for (int i = 0; i < 3; ++i) { a.sc[i] = c_cache->stride[i]; a.st[i] = top_idx->stride[i]; a.sh[i] = hca_table->stride[i]; }
+    a.Lq = 1; a.Lkv = c_cache->shape[1]; a.NC = hca_table->shape[1]; a.H = (int)H; a.DC = (int)DC;
+    a.K = (int)top_idx->shape[2]; a.window = window; a.n_sinks = n_sinks; a.block = block_size; a.hca_r = hca_r;
+    a.gate4d = gate4d; a.workspace = workspace; a.workspace_bytes = workspace_bytes; a.pos_dev = pos_dev;
+    if (window <= 0 || n_sinks < 0 || block_size <= 0 || hca_r <= 0)
+        return set_error(MABA_ERR_INVALID, "sa_attention_decode_at: window/block/hca_r must be positive");
+    return sa_attention_decode(a, B, dt, as_stream(stream));
+}

@@ -17,6 +17,7 @@ struct SaArgs {
     int window, n_sinks, block, hca_r, gate4d;
     void* workspace;
     size_t workspace_bytes;
+    const int64_t* pos_dev;  // decode at a device-held position (c_kv / hca are capacity-sized buffers)
 };
 
 int sa_attention_simt(SaArgs& a, int64_t B, int dtype, cudaStream_t s);
@@ -29,6 +30,8 @@ bool sa_attention_decode_supported(const SaArgs& a);
 size_t sa_attention_decode_workspace(int64_t B, int64_t Lq, int64_t Lkv, int64_t H, int64_t DC, int64_t K,
                                      int32_t block, int32_t window, int32_t n_sinks, int32_t hca_r);
 int sa_attention_decode(SaArgs& a, int64_t B, int dtype, cudaStream_t s);
+size_t sa_attention_decode_at_workspace(int64_t B, int64_t Lcap, int64_t NCcap, int64_t H, int64_t DC, int64_t K,
+                                        int32_t block, int32_t window, int32_t n_sinks, int32_t hca_r);
 
 inline size_t sa_attention_workspace_bytes(int dtype, int64_t B, int64_t Lq, int64_t Lkv, int64_t H, int64_t DC,
                                            int64_t K, int32_t block, int32_t window, int32_t n_sinks,

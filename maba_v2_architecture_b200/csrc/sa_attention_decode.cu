@@ -26,14 +26,15 @@ struct DecodePlan {
     int blocks_per_split;          // sparse: selected blocks per split
     int64_t nhca;                  // pooled keys visible to the query
     int64_t lo, nsink_extra, nlocal;
-    int total() const { return n_local + n_sparse + n_hca; }
+    __host__ __device__ int total() const { return n_local + n_sparse + n_hca; }
 };
 
-__host__ __device__ inline DecodePlan make_plan(const SaArgs& a) {
+// Plan for a query at position Lkv-1 (Lkv = the visible cache length).
+__host__ __device__ inline DecodePlan make_plan(const SaArgs& a, int64_t Lkv) {
     DecodePlan p;
-    const int64_t pos = a.Lkv - 1;
+    const int64_t pos = Lkv - 1;
     p.lo = pos - a.window + 1 > 0 ? pos - a.window + 1 : 0;
-    const int64_t nsink = a.n_sinks < a.Lkv ? a.n_sinks : a.Lkv;
+    const int64_t nsink = a.n_sinks < Lkv ? a.n_sinks : Lkv;
     p.nsink_extra = nsink < p.lo ? nsink : p.lo;
     p.nlocal = p.nsink_extra + (pos - p.lo + 1);
     p.n_local = 1;
@@ -53,8 +54,10 @@ __device__ __forceinline__ float* part_ptr(float* ws, int64_t b, int split, int 
     return ws + (((size_t)b * nsplit + split) * H + h) * (size_t)(DC + 2);
 }
 
+__device__ __forceinline__ int64_t visible_len(const SaArgs& a) { return a.pos_dev ? *a.pos_dev + 1 : a.Lkv; }
+
 template <typename T>
-__global__ void sa_decode_partial_kernel_t(SaArgs a, DecodePlan p, float* ws, int nsplit) {
+__global__ void sa_decode_partial_kernel_t(SaArgs a, float* ws, int nsplit) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const int DC = a.DC, H = a.H;
     int64_t* rows = reinterpret_cast<int64_t*>(smem_raw);
@@ -65,8 +68,11 @@ __global__ void sa_decode_partial_kernel_t(SaArgs a, DecodePlan p, float* ws, in
     const int64_t b = blockIdx.y;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int nwarps = blockDim.x >> 5;
-    const int64_t pos = a.Lkv - 1;
-    const int64_t nb_kv = (a.Lkv + a.block - 1) / a.block;
+    const int64_t Lkv = visible_len(a);
+    const DecodePlan p = make_plan(a, Lkv);
+    if (split >= p.total()) return;  // capacity-sized grid: HCA splits past the visible table
+    const int64_t pos = Lkv - 1;
+    const int64_t nb_kv = (Lkv + a.block - 1) / a.block;
     const T* qh = static_cast<const T*>(a.qhat);
     const T* ckv = static_cast<const T*>(a.ckv);
     const T* hca = static_cast<const T*>(a.hca);
@@ -111,7 +117,7 @@ __global__ void sa_decode_partial_kernel_t(SaArgs a, DecodePlan p, float* ws, in
                     const int64_t slot = n / a.block, off = n - (n / a.block) * a.block;
                     const int64_t blk = a.top_idx[b * a.st[0] + slot * a.st[2]];
                     const int64_t tok = blk * a.block + off;
-                    if (blk >= 0 && blk < nb_kv && tok < a.Lkv && tok <= pos) row = tok;
+                    if (blk >= 0 && blk < nb_kv && tok < Lkv && tok <= pos) row = tok;
                 } else {
                     row = n;
                 }
@@ -181,12 +187,14 @@ __global__ void sa_decode_partial_kernel_t(SaArgs a, DecodePlan p, float* ws, in
 }
 
 template <typename T>
-__global__ void sa_decode_combine_kernel(SaArgs a, DecodePlan p, const float* ws, int nsplit) {
+__global__ void sa_decode_combine_kernel(SaArgs a, const float* ws, int nsplit) {
     const int DC = a.DC, H = a.H;
     const int64_t b = blockIdx.x;
     const int lane = threadIdx.x & 31, h = threadIdx.x >> 5;
     if (h >= H) return;
-    const int64_t pos = a.Lkv - 1;
+    const int64_t Lkv = visible_len(a);
+    const DecodePlan p = make_plan(a, Lkv);
+    const int64_t pos = Lkv - 1;
     constexpr int NPL = MAXDC / 32;
     float res[NPL];
 #pragma unroll
@@ -247,10 +255,19 @@ __global__ void sa_decode_combine_kernel(SaArgs a, DecodePlan p, const float* ws
     }
 }
 
+// Splits of the launch: exact for a host-known length, capacity-sized (every
+// split the largest visible table could need) for a device-held position.
+int decode_splits(const SaArgs& a) {
+    if (a.pos_dev == nullptr) return make_plan(a, a.Lkv).total();
+    DecodePlan p = make_plan(a, a.Lkv);  // a.Lkv = cache capacity
+    const int64_t ncap = a.NC;
+    p.n_hca = (int)((ncap + SPLIT_KEYS - 1) / SPLIT_KEYS);
+    return p.n_local + p.n_sparse + p.n_hca;
+}
+
 template <typename T>
 int launch_decode(SaArgs& a, int64_t B, cudaStream_t s) {
-    const DecodePlan p = make_plan(a);
-    const int nsplit = p.total();
+    const int nsplit = decode_splits(a);
     const size_t need = (size_t)B * nsplit * a.H * (a.DC + 2) * sizeof(float);
     if (a.workspace == nullptr || a.workspace_bytes < need)
         return set_error(MABA_ERR_WORKSPACE, "sa_attention(decode): workspace of %zu bytes required, got %zu", need,
@@ -259,9 +276,9 @@ int launch_decode(SaArgs& a, int64_t B, cudaStream_t s) {
     const size_t smem = KT * (sizeof(int64_t) + sizeof(int)) + sizeof(float) * ((size_t)a.H * a.DC + (size_t)KT * (a.DC + 1));
     auto k1 = sa_decode_partial_kernel_t<T>;
     if (smem > 48 * 1024) cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    k1<<<dim3((unsigned)nsplit, (unsigned)B), 32 * a.H, smem, s>>>(a, p, ws, nsplit);
+    k1<<<dim3((unsigned)nsplit, (unsigned)B), 32 * a.H, smem, s>>>(a, ws, nsplit);
     MABA_TRY(check_launch("sa_attention(decode partial)"));
-    sa_decode_combine_kernel<T><<<(unsigned)B, 32 * a.H, 0, s>>>(a, p, ws, nsplit);
+    sa_decode_combine_kernel<T><<<(unsigned)B, 32 * a.H, 0, s>>>(a, ws, nsplit);
     return check_launch("sa_attention(decode combine)");
 }
 
@@ -277,8 +294,17 @@ size_t sa_attention_decode_workspace(int64_t B, int64_t Lq, int64_t Lkv, int64_t
     SaArgs a{};
     a.Lq = 1; a.Lkv = Lkv; a.NC = Lkv / hca_r; a.H = (int)H; a.DC = (int)DC; a.K = (int)K;
     a.window = window; a.n_sinks = n_sinks; a.block = block; a.hca_r = hca_r;
-    const DecodePlan p = make_plan(a);
-    return (size_t)B * p.total() * H * (DC + 2) * sizeof(float);
+    return (size_t)B * decode_splits(a) * H * (DC + 2) * sizeof(float);
+}
+
+size_t sa_attention_decode_at_workspace(int64_t B, int64_t Lcap, int64_t NCcap, int64_t H, int64_t DC, int64_t K,
+                                        int32_t block, int32_t window, int32_t n_sinks, int32_t hca_r) {
+    SaArgs a{};
+    a.Lq = 1; a.Lkv = Lcap; a.NC = NCcap; a.H = (int)H; a.DC = (int)DC; a.K = (int)K;
+    a.window = window; a.n_sinks = n_sinks; a.block = block; a.hca_r = hca_r;
+    int64_t one = 0;
+    a.pos_dev = &one;  // any non-null: capacity-sized plan
+    return (size_t)B * decode_splits(a) * H * (DC + 2) * sizeof(float);
 }
 
 int sa_attention_decode(SaArgs& a, int64_t B, int dtype, cudaStream_t s) {

@@ -26,7 +26,8 @@ from typing import List, Optional
 
 import torch
 
-from .ops import absorb_queries, b200_compute_centroids, b200_hca_pool, b200_index_topk, b200_sa_attention, expand_values
+from .ops import (absorb_queries, b200_compute_centroids, b200_decode_cache_append, b200_hca_pool, b200_index_topk,
+                  b200_index_topk_decode_at, b200_sa_attention, b200_sa_attention_decode_at, expand_values)
 
 
 @dataclass
@@ -122,6 +123,85 @@ class DecodeSession:
             x = x + torch.sigmoid(layer.res_gate2) * layer.ffn(layer.norm2(x))
         self.L = Ln
         return model.lm_head(model.head_proj(model.final_norm(x)))
+
+    # -------------------------------------------------------------- CUDA-graph decode
+    def _sa_step_dev(self, m, cache: _SACache, h: torch.Tensor) -> torch.Tensor:
+        """One MABA-SA decode step at the device-held position (no host-side length)."""
+        B = h.shape[0]
+        b200_decode_cache_append(m.kv_down_proj(h), m.indexer.k_idx_proj(h), cache.c, cache.kidx, cache.cent,
+                                 cache.hca, self.pos_dev, self.block, m.hca_pool_size)
+        idx = b200_index_topk_decode_at(m.indexer.q_idx_proj(h), cache.cent, self.pos_dev,
+                                        lambda_dist=m.indexer.dist_lambda, top_k=m.indexer.top_k,
+                                        block_size=self.block)
+        q = m.q_proj(h).view(B, 1, m.n_heads, m.d_head)
+        qhat = absorb_queries(q, m.k_up_proj.weight, m.n_heads, m.scale)
+        o_lat = b200_sa_attention_decode_at(qhat, cache.c, cache.hca, idx, m.stream_gate(h), self.pos_dev,
+                                            window_size=m.window_size, n_sinks=m.n_sink_tokens,
+                                            block_size=self.block, hca_r=m.hca_pool_size)
+        o = expand_values(o_lat, m.v_up_proj.weight, m.n_heads).reshape(B, 1, m.n_heads * m.d_head)
+        return m.o_proj(o.to(h.dtype))
+
+    def _step_dev(self) -> None:
+        """Greedy decode step on static buffers: ids_buf -> logits_buf, argmax back into ids_buf."""
+        model = self.model
+        x = model.embeddings(self.ids_buf)
+        for i, layer in enumerate(model.layers):
+            h = layer.norm1(x)
+            if layer.is_attention:
+                mo = self._sa_step_dev(layer.mixer, self.sa[i], h)
+            else:
+                mo, st, cv = layer.mixer.step(h, state=self.states[i], conv_state=self.convs[i])
+                self.states[i].copy_(st)
+                for dst, src in zip(self.convs[i], cv):
+                    dst.copy_(src)
+            x = x + torch.sigmoid(layer.res_gate1) * mo
+            x = x + torch.sigmoid(layer.res_gate2) * layer.ffn(layer.norm2(x))
+        self.logits_buf.copy_(model.lm_head(model.head_proj(model.final_norm(x))))
+        self.ids_buf.copy_(self.logits_buf[:, -1].argmax(-1, keepdim=True))
+        self.pos_dev.add_(1)
+
+    @torch.no_grad()
+    def capture(self, first_ids: torch.Tensor) -> None:
+        """Captures one greedy decode step in a CUDA graph (call after prefill).
+        ``first_ids`` [B,1] is the token fed to the first replayed step."""
+        V = self.model.config.vocab_size
+        self.ids_buf = first_ids.clone()
+        self.logits_buf = torch.empty(self.B, 1, V, dtype=self.dtype, device=self.device)
+        self.pos_dev = torch.full((), self.L, dtype=torch.int64, device=self.device)
+        self.states = [s.clone() if s is not None else None for s in self.states]
+        self.convs = [tuple(c.clone() for c in cv) if cv is not None else None for cv in self.convs]
+        saved = (self.ids_buf.clone(), self.pos_dev.clone(), [s.clone() if s is not None else None for s in self.states],
+                 [tuple(c.clone() for c in cv) if cv is not None else None for cv in self.convs],
+                 [(c.c.clone(), c.kidx.clone(), c.cent.clone(), c.hca.clone()) if c is not None else None
+                  for c in self.sa] if self.L < 4096 else None)
+        side = torch.cuda.Stream(device=self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(side):
+            self._step_dev()  # warm-up on a side stream (cuBLAS handles, allocator pools)
+        torch.cuda.current_stream(self.device).wait_stream(side)
+        # undo the warm-up step (it advanced the position and touched the caches at that row)
+        self.ids_buf.copy_(saved[0])
+        self.pos_dev.copy_(saved[1])
+        for dst, src in zip(self.states, saved[2]):
+            if dst is not None:
+                dst.copy_(src)
+        for dst, src in zip(self.convs, saved[3]):
+            if dst is not None:
+                for d_, s_ in zip(dst, src):
+                    d_.copy_(s_)
+        if saved[4] is not None:
+            for c, sv in zip(self.sa, saved[4]):
+                if c is not None:
+                    c.c.copy_(sv[0]); c.kidx.copy_(sv[1]); c.cent.copy_(sv[2]); c.hca.copy_(sv[3])
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self._step_dev()
+
+    def replay(self) -> torch.Tensor:
+        """Runs the captured step once; returns the logits buffer [B,1,V] (ids_buf holds the argmax)."""
+        self.graph.replay()
+        self.L += 1
+        return self.logits_buf
 
     def _sa_step(self, m, cache: _SACache, h: torch.Tensor, pos: int) -> torch.Tensor:
         B = h.shape[0]

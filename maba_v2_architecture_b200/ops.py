@@ -177,6 +177,21 @@ def b200_dgda_prefill(
     return out, fin
 
 
+def b200_dgda_transition(q, k, v, alpha=None, b=None, w=None, log_alpha=None) -> torch.Tensor:
+    """Affine transition [R | P] ([B,H,64,128] fp32) of the segment on the state: S_end = P S_start + R."""
+    validate_dgda_prefill_inputs(q, k, v, alpha, b, w, None, log_alpha)
+    N.require_cuda(q, op="dgda_transition")
+    B, H, L, _ = q.shape
+    out = torch.empty(B, H, 64, 128, dtype=torch.float32, device=q.device)
+    lib = N.lib()
+    nbytes = lib.maba_dgda_transition_workspace_size(N.DTYPE_CODES[q.dtype], B, H, L)
+    ws = N.workspace(nbytes, q.device)
+    ds = [N.desc(t) for t in (q, k, v, alpha, log_alpha, b, w, out)]
+    rc = lib.maba_dgda_transition(*[N.ref(d) for d in ds], ws.data_ptr(), int(nbytes), N.stream_of(q))
+    N.check(rc, "maba_dgda_transition")
+    return out
+
+
 def _squeeze_step(t: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
     if t is not None and t.dim() == 4 and t.shape[2] == 1:
         return t.squeeze(2)
@@ -412,6 +427,53 @@ def b200_sa_attention(
         ws.data_ptr() if ws is not None else None, int(nbytes), N.stream_of(qhat),
     )
     N.check(rc, "maba_sa_attention")
+    return out
+
+
+# ---------------------------------------------------------------------------
+# decode at a device-held position (CUDA-graph friendly)
+# ---------------------------------------------------------------------------
+def b200_decode_cache_append(c_new, k_new, c_cache, kidx_cache, cent_table, hca_table, pos_dev, block_size=64,
+                             hca_r=64) -> None:
+    """Append one latent / index-key row at *pos_dev and refresh the block centroid / pooled row in place."""
+    N.require_cuda(c_new, c_cache, op="decode_cache_append")
+    rc = N.lib().maba_decode_cache_append(
+        N.ref(N.desc(c_new)), N.ref(N.desc(k_new)), N.ref(N.desc(c_cache)), N.ref(N.desc(kidx_cache)),
+        N.ref(N.desc(cent_table)), N.ref(N.desc(hca_table)), pos_dev.data_ptr(), int(block_size), int(hca_r),
+        N.stream_of(c_cache))
+    N.check(rc, "maba_decode_cache_append")
+
+
+def b200_index_topk_decode_at(q_idx, cent_table, pos_dev, lambda_dist=0.5, top_k=32, block_size=64):
+    N.require_cuda(q_idx, cent_table, op="index_topk_decode_at")
+    B, _, _ = q_idx.shape
+    nbcap = cent_table.shape[1]
+    idx = torch.empty(B, 1, min(top_k, nbcap), dtype=torch.long, device=q_idx.device)
+    lib = N.lib()
+    nbytes = lib.maba_index_topk_decode_at_workspace_size(B, nbcap, int(top_k))
+    ws = N.workspace(nbytes, q_idx.device)
+    rc = lib.maba_index_topk_decode_at(N.ref(N.desc(q_idx)), N.ref(N.desc(cent_table)), float(lambda_dist),
+                                       int(top_k), int(block_size), pos_dev.data_ptr(), N.ref(N.desc(idx)),
+                                       ws.data_ptr(), int(nbytes), N.stream_of(q_idx))
+    N.check(rc, "maba_index_topk_decode_at")
+    return idx
+
+
+def b200_sa_attention_decode_at(qhat, c_cache, hca_table, top_idx, gate_logits, pos_dev, window_size=128,
+                                n_sinks=4, block_size=64, hca_r=64):
+    N.require_cuda(qhat, c_cache, op="sa_attention_decode_at")
+    B, _, H, dc = qhat.shape
+    out = torch.empty(B, 1, H, dc, dtype=qhat.dtype, device=qhat.device)
+    lib = N.lib()
+    nbytes = lib.maba_sa_attention_decode_at_workspace_size(B, c_cache.shape[1], hca_table.shape[1], H, dc,
+                                                            top_idx.shape[-1], int(window_size), int(n_sinks),
+                                                            int(block_size), int(hca_r))
+    ws = N.workspace(nbytes, qhat.device)
+    rc = lib.maba_sa_attention_decode_at(
+        N.ref(N.desc(qhat)), N.ref(N.desc(c_cache)), N.ref(N.desc(hca_table)), N.ref(N.desc(top_idx)),
+        N.ref(N.desc(gate_logits)), N.ref(N.desc(out)), pos_dev.data_ptr(), int(window_size), int(n_sinks),
+        int(block_size), int(hca_r), ws.data_ptr() if ws is not None else None, int(nbytes), N.stream_of(qhat))
+    N.check(rc, "maba_sa_attention_decode_at")
     return out
 
 

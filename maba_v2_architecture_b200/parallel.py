@@ -1,0 +1,149 @@
+"""Multi-GPU execution of the hot path: one process per GPU, torch.distributed.
+
+Two layouts:
+
+* **batch sharding** -- independent sequences per rank; nothing crosses GPUs on
+  the data path (``bench.py --gpus N`` runs it).
+* **sequence split** -- one long sequence cut into P contiguous segments, rank r
+  holding tokens [r*Ls, (r+1)*Ls) with Ls a multiple of the block size.  The
+  reference never splits a sequence; this layout adds one small exchange per
+  layer and keeps every result equal to the single-GPU computation:
+
+  - DGDA: the recurrence is affine in the state, so each rank computes its
+    segment's transition S_end = P S_start + R (``b200_dgda_transition``), the
+    ranks all-gather the [B,H,64,128] fp32 transitions (320 KB per rank at
+    H=10), each folds the preceding ones into its starting state and runs the
+    output pass from it;
+  - MABA-SA: a query may attend any earlier token (sparse blocks anywhere in the
+    prefix, HCA over all complete blocks, the window and sinks), so the ranks
+    all-gather the latent rows, the block centroids and the pooled HCA rows
+    (d_c=128 / d_idx=64 per token or block); each rank then scores and attends
+    its own queries at their absolute positions (``q_pos0``; the attention's
+    queries sit at the end of the gathered prefix).
+
+Each layout is written as local phases around one exchange so the same code
+runs with NCCL (one process per GPU), with gloo on CPU (tests inject a CPU
+backend), or as an emulation of the ranks inside one process.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Callable, List, Optional, Sequence
+
+import torch
+import torch.distributed as dist
+
+from . import ops as _ops
+
+DP = 64  # padded head dim of the transition
+
+
+class B200Backend:
+    """The sm_100a kernels."""
+
+    def dgda_transition(self, q, k, v, b, w, la):
+        return _ops.b200_dgda_transition(q, k, v, None, b, w, log_alpha=la)
+
+    def dgda_prefill(self, q, k, v, b, w, la, initial_state):
+        return _ops.b200_dgda_prefill(q, k, v, None, b, w, initial_state=initial_state, log_alpha=la,
+                                      state_dtype=torch.float32)
+
+    def compute_centroids(self, k_idx, block):
+        return _ops.b200_compute_centroids(k_idx, block_size=block)
+
+    def hca_pool(self, c, r):
+        return _ops.b200_hca_pool(c, r)
+
+    def index_topk_at(self, q_idx, cent, lam, top_k, block, q_pos0):
+        return _ops.b200_index_topk(q_idx, cent, lambda_dist=lam, top_k=top_k, block_size=block, q_pos0=q_pos0)
+
+    def sa_attention(self, qhat, c, hca, idx, gate, window, sinks, block, r):
+        return _ops.b200_sa_attention(qhat, c, hca, idx, gate, window_size=window, n_sinks=sinks, block_size=block,
+                                      hca_r=r)
+
+
+def fold_transitions(trans: Sequence[torch.Tensor], upto: int, s0: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Starting state of segment `upto` from the transitions [R | P] of segments 0..upto-1."""
+    t0 = trans[0]
+    B, H = t0.shape[:2]
+    S = torch.zeros(B, H, DP, DP, dtype=torch.float32, device=t0.device) if s0 is None else s0.float()
+    for j in range(upto):
+        R, P = trans[j][..., :DP].float(), trans[j][..., DP:].float()
+        S = torch.matmul(P, S) + R
+    return S
+
+
+def _gather(t: torch.Tensor, group) -> List[torch.Tensor]:
+    world = dist.get_world_size(group)
+    out = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(out, t.contiguous(), group=group)
+    return out
+
+
+# ------------------------------------------------------------------ DGDA
+def dgda_segment_phase_a(q, k, v, b, w, la, backend=None):
+    """Local: the segment's transition."""
+    backend = backend or B200Backend()
+    return backend.dgda_transition(q, k, v, b, w, la)
+
+
+def dgda_segment_phase_b(q, k, v, b, w, la, trans: Sequence[torch.Tensor], rank: int, backend=None):
+    """Local: output pass of segment `rank` from the state folded out of the preceding transitions."""
+    backend = backend or B200Backend()
+    dk, dv = q.shape[-1], v.shape[-1]
+    S = fold_transitions(trans, rank)[..., :dk, :dv].contiguous()
+    return backend.dgda_prefill(q, k, v, b, w, la, S)
+
+
+def sp_dgda_prefill(q, k, v, b, w, la, group=None, backend=None):
+    """Sequence-split DGDA prefill: this rank's segment of q..la ([B,H,Ls,d] views).
+    Returns (o of the segment, state at the end of the segment)."""
+    rank = dist.get_rank(group)
+    trans = _gather(dgda_segment_phase_a(q, k, v, b, w, la, backend), group)
+    return dgda_segment_phase_b(q, k, v, b, w, la, trans, rank, backend)
+
+
+# ------------------------------------------------------------------ MABA-SA
+@dataclass
+class SAParams:
+    window: int = 128
+    sinks: int = 4
+    block: int = 64
+    hca_r: int = 64
+    top_k: int = 32
+    lam: float = 0.1
+
+
+def sa_segment_phase_a(c_local, k_idx_local, p: SAParams, backend=None):
+    """Local: the segment's latent rows, block centroids and pooled HCA rows (to be exchanged)."""
+    backend = backend or B200Backend()
+    return c_local, backend.compute_centroids(k_idx_local, p.block), backend.hca_pool(c_local, p.hca_r)
+
+
+def sa_segment_phase_b(qhat_local, q_idx_local, gate_local, c_all: Sequence[torch.Tensor],
+                       cent_all: Sequence[torch.Tensor], hca_all: Sequence[torch.Tensor], rank: int, p: SAParams,
+                       backend=None):
+    """Local: indexer + three-stream attention of this segment's queries over the gathered prefix."""
+    backend = backend or B200Backend()
+    Ls = qhat_local.shape[1]
+    end = (rank + 1) * Ls
+    c_prefix = torch.cat(list(c_all[: rank + 1]), dim=1)
+    cent = torch.cat(list(cent_all[: rank + 1]), dim=1)
+    hca = torch.cat(list(hca_all[: rank + 1]), dim=1)
+    idx = backend.index_topk_at(q_idx_local, cent, p.lam, p.top_k, p.block, rank * Ls)
+    o = backend.sa_attention(qhat_local, c_prefix, hca if hca.shape[1] else None, idx, gate_local, p.window,
+                             p.sinks, p.block, p.hca_r)
+    assert c_prefix.shape[1] == end
+    return o, idx
+
+
+def sp_sa_prefill(qhat_local, c_local, q_idx_local, k_idx_local, gate_local, p: SAParams, group=None,
+                  backend=None):
+    """Sequence-split DG-Indexer + MABA-SA prefill of this rank's segment."""
+    rank = dist.get_rank(group)
+    Ls = c_local.shape[1]
+    if Ls % p.block or Ls % p.hca_r:
+        raise ValueError(f"segment length {Ls} must be a multiple of block {p.block} and r {p.hca_r}")
+    c, cent, hca = sa_segment_phase_a(c_local, k_idx_local, p, backend)
+    return sa_segment_phase_b(qhat_local, q_idx_local, gate_local, _gather(c, group), _gather(cent, group),
+                              _gather(hca, group), rank, p, backend)

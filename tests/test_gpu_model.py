@@ -102,3 +102,25 @@ def test_decode_kernels_long_context_vs_oracle():
     ref = OA.sa_attention_latent(qhat.float().cpu().numpy(), c.float().cpu().numpy(), idx.cpu().numpy(),
                                  gate.float().cpu().numpy(), 128, 4, 64, 64)
     assert_rel(out, ref, 2e-2, "decode attention")
+
+
+def test_graph_decode_matches_eager_session():
+    """The captured decode step (device-held position) replays the eager session's results."""
+    from maba_v2_architecture_b200.decode import DecodeSession
+    from maba_v2_architecture_b200.workloads import init_module_
+
+    cfg = tiny_config()
+    model = init_module_(MabaSparseForCausalLM(cfg), seed=21).to(DEV).eval()
+    ids = torch.randint(0, cfg.vocab_size, (2, 70), generator=torch.Generator().manual_seed(22)).to(DEV)
+    eager = DecodeSession(model, batch=2, max_len=200, dtype=torch.float32)
+    eager.prefill(ids)
+    graph = DecodeSession(model, batch=2, max_len=200, dtype=torch.float32)
+    first = graph.prefill(ids)[:, -1].argmax(-1, keepdim=True)
+    graph.capture(first)
+    tok = first
+    for _ in range(60):  # crosses block (16) and pooling (16) boundaries several times
+        le = eager.step(tok)
+        tok = le[:, -1].argmax(-1, keepdim=True)
+        lg = graph.replay()
+        assert_rel(lg, le, 1e-5, "graph vs eager logits")
+        assert torch.equal(graph.ids_buf, tok)
