@@ -27,11 +27,15 @@ from .layers import ConvState, DGDALayer, DGIndexer, DecoupledGatedDeltaAttentio
 from .layers import MABASALayer, MabaSparseAttention
 from .ops import (
     b200_compute_centroids,
+    b200_decode_cache_append,
     b200_dgda_prefill,
     b200_dgda_step,
+    b200_dgda_transition,
     b200_hca_pool,
     b200_index_topk,
+    b200_index_topk_decode_at,
     b200_sa_attention,
+    b200_sa_attention_decode_at,
     b200_stream_superposition,
 )
 

@@ -499,6 +499,10 @@ __all__ = [
     "b200_stream_superposition",
     "b200_hca_pool",
     "b200_sa_attention",
+    "b200_dgda_transition",
+    "b200_decode_cache_append",
+    "b200_index_topk_decode_at",
+    "b200_sa_attention_decode_at",
     "absorb_queries",
     "expand_values",
     "validate_dgda_prefill_inputs",

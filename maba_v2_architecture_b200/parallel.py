@@ -28,7 +28,7 @@ backend), or as an emulation of the ranks inside one process.
 from __future__ import annotations
 
 from dataclasses import dataclass
-from typing import Callable, List, Optional, Sequence
+from typing import List, Optional, Sequence
 
 import torch
 import torch.distributed as dist
@@ -123,12 +123,17 @@ def sa_segment_phase_a(c_local, k_idx_local, p: SAParams, backend=None):
 def sa_segment_phase_b(qhat_local, q_idx_local, gate_local, c_all: Sequence[torch.Tensor],
                        cent_all: Sequence[torch.Tensor], hca_all: Sequence[torch.Tensor], rank: int, p: SAParams,
                        backend=None):
-    """Local: indexer + three-stream attention of this segment's queries over the gathered prefix."""
+    """Local: indexer + three-stream attention of this segment's queries over the gathered prefix.
+    Block indices past the prefix (fillers) are dropped by the attention; every token they
+    name lies after the query, which the reference's causal mask of the gathered tokens
+    removes as well (maba_sparse/layers/sparse_attention.py:117-164)."""
     backend = backend or B200Backend()
     Ls = qhat_local.shape[1]
     end = (rank + 1) * Ls
     c_prefix = torch.cat(list(c_all[: rank + 1]), dim=1)
-    cent = torch.cat(list(cent_all[: rank + 1]), dim=1)
+    # The whole centroid table: future blocks score -inf, but the table's length sets
+    # min(top_k, nb) and the filler indices, which then match the single-GPU indexer.
+    cent = torch.cat(list(cent_all), dim=1)
     hca = torch.cat(list(hca_all[: rank + 1]), dim=1)
     idx = backend.index_topk_at(q_idx_local, cent, p.lam, p.top_k, p.block, rank * Ls)
     o = backend.sa_attention(qhat_local, c_prefix, hca if hca.shape[1] else None, idx, gate_local, p.window,
@@ -140,10 +145,10 @@ def sa_segment_phase_b(qhat_local, q_idx_local, gate_local, c_all: Sequence[torc
 def sp_sa_prefill(qhat_local, c_local, q_idx_local, k_idx_local, gate_local, p: SAParams, group=None,
                   backend=None):
     """Sequence-split DG-Indexer + MABA-SA prefill of this rank's segment."""
-    rank = dist.get_rank(group)
     Ls = c_local.shape[1]
     if Ls % p.block or Ls % p.hca_r:
         raise ValueError(f"segment length {Ls} must be a multiple of block {p.block} and r {p.hca_r}")
+    rank = dist.get_rank(group)
     c, cent, hca = sa_segment_phase_a(c_local, k_idx_local, p, backend)
     return sa_segment_phase_b(qhat_local, q_idx_local, gate_local, _gather(c, group), _gather(cent, group),
                               _gather(hca, group), rank, p, backend)

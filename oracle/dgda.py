@@ -3,6 +3,8 @@
 * ``dgda_sequential``   -- maba_sparse/kernels/common.py:229-268 (ref_dgda_prefill):
   the token-by-token recurrence, the ground truth.
 * ``dgda_step``         -- maba_sparse/kernels/common.py:271-309 (ref_dgda_step).
+* ``dgda_transition``   -- the segment's affine map [R | P], derived from
+  ``dgda_sequential`` (checks the sequence-split chain of this build).
 * ``dgda_chunked``      -- maba_sparse/kernels/cpu_dgda.py:33-197 (cpu_dgda_prefill),
   the reference's chunked WY/UT CPU algorithm with the exact triangular solve;
   used as the timed CPU baseline.
@@ -58,6 +60,27 @@ def dgda_step(q, k, v, alpha=None, b=None, w=None, state=None, log_alpha=None, d
     S2 = Sd + k[..., None] * delta[:, :, None, :]
     o = np.einsum("bhi,bhij->bhj", q, S2)
     return o, S2
+
+
+def dgda_transition(q, k, v, alpha=None, b=None, w=None, log_alpha=None, pad: int = 64,
+                    dtype=np.float64) -> np.ndarray:
+    """Affine map of a segment on the state, S_end = P S_start + R, as [B,H,pad,2*pad] = [R | P].
+
+    The recurrence of ``dgda_sequential`` is affine in S (common.py:256-265), so R is its
+    final state from S_start = 0 and P its final state from S_start = I with v = 0.  Head dims
+    below ``pad`` are padded: R with zeros, P with the identity (padded rows of a state stay 0)."""
+    q, k, v = (_as(t, dtype) for t in (q, k, v))
+    B, H, L, dk = q.shape
+    dv = v.shape[-1]
+    _, R = dgda_sequential(q, k, v, alpha, b, w, log_alpha=log_alpha, dtype=dtype)
+    eye = np.broadcast_to(np.eye(dk, dtype=dtype), (B, H, dk, dk)).copy()
+    _, P = dgda_sequential(q, k, np.zeros((B, H, L, dk), dtype), alpha, b, np.ones((B, H, L, 1), dtype),
+                           initial_state=eye, log_alpha=log_alpha, dtype=dtype)
+    out = np.zeros((B, H, pad, 2 * pad), dtype)
+    out[..., :dk, :dv] = R
+    out[..., :, pad:] = np.eye(pad, dtype=dtype)
+    out[..., :dk, pad:pad + dk] = P
+    return out
 
 
 def _log_decay(alpha, log_alpha, dtype):

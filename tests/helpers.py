@@ -86,3 +86,48 @@ def check_topk_rule(idx, scores, qb, top_k, ulp_slack: int = 2):
             assert np.all(gap <= tol), f"row ({b},{r}): {got.tolist()} vs {want.tolist()}"
             ties += 1
     return ties
+
+
+class OracleBackend:
+    """Compute backend of ``maba_v2_architecture_b200.parallel`` on the CPU oracle, so the
+    sequence-split plumbing (phases, exchange, folding) runs under gloo without a GPU."""
+
+    def __init__(self):
+        import oracle.attention as oa
+        import oracle.dgda as od
+        import oracle.indexer as oi
+        self.oa, self.od, self.oi = oa, od, oi
+
+    @staticmethod
+    def _t(x, like):
+        return torch.from_numpy(np.ascontiguousarray(x)).to(like.dtype)
+
+    def dgda_transition(self, q, k, v, b, w, la):
+        return torch.from_numpy(self.od.dgda_transition(to_np(q), to_np(k), to_np(v), b=to_np(b), w=to_np(w),
+                                                        log_alpha=to_np(la))).float()
+
+    def dgda_prefill(self, q, k, v, b, w, la, initial_state):
+        o, S = self.od.dgda_sequential(to_np(q), to_np(k), to_np(v), b=to_np(b), w=to_np(w),
+                                       initial_state=to_np(initial_state), log_alpha=to_np(la))
+        return self._t(o, q), torch.from_numpy(S).float()
+
+    def compute_centroids(self, k_idx, block):
+        return self._t(self.oi.compute_centroids(to_np(k_idx), block), k_idx)
+
+    def hca_pool(self, c, r):
+        return self._t(self.oi.hca_pool(to_np(c), r), c)
+
+    def index_topk_at(self, q_idx, cent, lam, top_k, block, q_pos0):
+        B, Ls, D = q_idx.shape
+        qf = np.zeros((B, q_pos0 + Ls, D), np.float32)
+        qf[:, q_pos0:] = to_np(q_idx)
+        return torch.from_numpy(self.oi.index_topk(qf, to_np(cent), lam, top_k, block,
+                                                   rows=np.arange(q_pos0, q_pos0 + Ls)))
+
+    def sa_attention(self, qhat, c, hca, idx, gate, window, sinks, block, r):
+        nc = c.shape[1] // r
+        pooled = self.oi.hca_pool(to_np(c), r)[:, :nc]
+        got = np.zeros_like(pooled) if hca is None else to_np(hca)
+        assert got.shape == pooled.shape and np.allclose(got, pooled, rtol=1e-6, atol=1e-6), "pooled HCA rows"
+        o = self.oa.sa_attention_latent(to_np(qhat), to_np(c), to_np(idx), to_np(gate), window, sinks, block, r)
+        return self._t(o, qhat)
