@@ -64,6 +64,12 @@ typedef struct maba_tensor {
 MABA_API int         maba_abi_version(void);
 MABA_API const char* maba_last_error(void);
 
+/* Reads and clears the device error word (synchronises `stream`): 0, or 1 when
+ * a kernel gave up on a bounded wait (a pipeline barrier that never completed)
+ * and returned early; its outputs are then not valid.  No reference
+ * counterpart (the reference's kernels do not wait on barriers). */
+MABA_API int maba_device_error(int32_t* out, void* stream);
+
 /* ---- DGDA chunked prefill ---------------------------------------------
  * Replaces the `dgda_prefill` registry op:
  *   maba_sparse/kernels/dispatcher.py:258   (dispatch_dgda_prefill)

@@ -48,6 +48,7 @@ _i32, _i64, _f32, _vp, _sz = ctypes.c_int32, ctypes.c_int64, ctypes.c_float, cty
 SIGNATURES = {
     "maba_abi_version": (ctypes.c_int, []),
     "maba_last_error": (ctypes.c_char_p, []),
+    "maba_device_error": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int32), _vp]),
     "maba_dgda_prefill": (ctypes.c_int, [T_P] * 10 + [_i32, _vp, _sz, _vp]),
     "maba_dgda_prefill_workspace_size": (_sz, [_i32, _i64, _i64, _i64, _i64, _i64]),
     "maba_dgda_step": (ctypes.c_int, [T_P] * 10 + [_vp]),
@@ -155,3 +156,11 @@ def workspace(nbytes: int, device: torch.device) -> Optional[torch.Tensor]:
     if nbytes <= 0:
         return None
     return torch.empty(int(nbytes), dtype=torch.uint8, device=device)
+
+
+def device_error(device: Optional[torch.device] = None) -> int:
+    """Reads and clears the device error word of the current device (0 = no kernel gave up on a wait)."""
+    out = ctypes.c_int32(0)
+    stream = torch.cuda.current_stream(device).cuda_stream
+    check(lib().maba_device_error(ctypes.byref(out), ctypes.c_void_p(stream)), "maba_device_error")
+    return int(out.value)

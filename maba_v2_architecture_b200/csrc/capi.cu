@@ -1,6 +1,7 @@
 // Library-wide pieces of the C ABI: version, per-thread error message,
 // descriptor validation helpers.
 #include "common.cuh"
+#include "sa_attention.cuh"
 
 #include <string.h>
 
@@ -65,3 +66,11 @@ int sm_count() {
 extern "C" int maba_abi_version(void) { return MABA_ABI_VERSION; }
 
 extern "C" const char* maba_last_error(void) { return maba::g_last_error; }
+
+extern "C" int maba_device_error(int32_t* out, void* stream) {
+    if (out == nullptr) return maba::set_error(MABA_ERR_INVALID, "device_error: out is null");
+    int v = 0;
+    MABA_TRY(maba::device_error_take(static_cast<cudaStream_t>(stream), &v));
+    *out = v;
+    return MABA_OK;
+}

@@ -22,6 +22,9 @@ struct SaArgs {
 
 int sa_attention_simt(SaArgs& a, int64_t B, int dtype, cudaStream_t s);
 int sa_attention_mma(SaArgs& a, int64_t B, int dtype, cudaStream_t s);
+int sa_attention_tc(SaArgs& a, int64_t B, int dtype, cudaStream_t s);
+bool sa_attention_tc_supported(const SaArgs& a, int dtype);
+int device_error_take(cudaStream_t s, int* out);
 bool sa_attention_mma_supported(const SaArgs& a, int dtype);
 size_t sa_attention_mma_workspace(int dtype, int64_t B, int64_t Lq, int64_t Lkv, int64_t H, int64_t DC, int64_t K,
                                   int32_t block);
@@ -42,13 +45,15 @@ inline size_t sa_attention_workspace_bytes(int dtype, int64_t B, int64_t Lq, int
 }
 
 // Single-token queries take the split-K decode kernels when the caller gave
-// the workspace they need; 16-bit prefill tiles take the tensor-core kernel;
-// everything else the exact CUDA-core kernel.
+// the workspace they need; 16-bit prefill tiles take the tcgen05 kernel (block
+// 64, K <= 32, TMA-compatible strides), else the mma.sync kernel; everything
+// else the exact CUDA-core kernel.
 inline int sa_attention_dispatch(SaArgs& a, int64_t B, int dtype, cudaStream_t s) {
     if (dtype != MABA_F64 && sa_attention_decode_supported(a) &&
         a.workspace_bytes >= sa_attention_decode_workspace(B, a.Lq, a.Lkv, a.H, a.DC, a.K, a.block, a.window,
                                                            a.n_sinks, a.hca_r))
         return sa_attention_decode(a, B, dtype, s);
+    if (sa_attention_tc_supported(a, dtype)) return sa_attention_tc(a, B, dtype, s);
     if (sa_attention_mma_supported(a, dtype)) return sa_attention_mma(a, B, dtype, s);
     return sa_attention_simt(a, B, dtype, s);
 }

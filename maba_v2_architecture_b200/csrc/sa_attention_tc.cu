@@ -1,0 +1,636 @@
+// MABA-SA attention on the 5th-generation tensor cores (tcgen05 + TMEM + TMA),
+// 16-bit inputs, latent dim 128, block size 64.
+//
+// Same math as sa_attention.cu / sa_attention_mma.cu (maba_sparse/layers/
+// sparse_attention.py:79-219 and 274-275 in the MLA-absorbed latent space):
+// three streams (window + sinks, the selected blocks, the pooled HCA rows),
+// one softmax per stream and row, superposed by the softmax of the gate.
+//
+// One CTA per (pair of heads, 64 query tokens): 128 MMA rows, row m = 2 t + h.
+//  * warp 0 (one lane): TMA producer -- the Q tile once (box 64 x 2 heads x 64
+//    tokens, two 64-wide halves of d_c), then every latent key tile of the
+//    three streams into a 4-stage ring (box 64 rows x 64 columns, twice); all
+//    with 128-byte swizzle;
+//  * warp 1: allocates the 512 TMEM columns; one lane issues the MMAs:
+//    S = Q K^T (M=128, N=64, K=128; K-major A and B) into one of two TMEM S
+//    buffers, and O_s += P V (M=128, N=128, K=64; A = P from shared memory,
+//    B = the same key tile read MN-major) into the TMEM accumulator of the
+//    tile's stream;
+//  * warps 2..5 (128 threads, thread = TMEM lane = MMA row): masked online
+//    softmax of the S tile (ex2), P to shared memory, lazy rescaling of O in
+//    TMEM (only when a row's running maximum grows by more than 2^8), and the
+//    epilogue: O_local / l, O_sparse / l, O_hca / l weighted by the gate.
+// TMEM: S buffers in columns [0,128), O of stream s in [128+128s, 256+128s).
+// The sparse stream runs over the union of the blocks the 64 tokens selected
+// (bitmap + popcount ranks + 64-bit token masks), as in the mma kernel.
+//
+// Every mbarrier wait is bounded: a wait that runs out raises a shared abort
+// flag, all roles leave their loops, the MMA issuer drains its MMAs and the
+// producer its copies (bounded again), TMEM is freed and the device error word
+// read by maba_device_error() is set.
+#include "sa_attention.cuh"
+#include "tcgen05.cuh"
+
+#include <cudaTypedefs.h>
+#include <type_traits>
+
+namespace maba {
+
+__device__ int g_device_error = 0;
+
+namespace {
+using namespace tc;
+
+constexpr int QT = 64;            // query tokens per CTA
+constexpr int KT = 64;            // keys per tile (= block size)
+constexpr int DCX = 128;          // latent dim
+constexpr int HPG = 2;            // heads per CTA
+constexpr int ROWS = QT * HPG;    // MMA rows
+constexpr int NS = 4;             // key-tile stages
+constexpr int KMAX = 32;          // selected blocks per token
+constexpr int UMAX = QT * KMAX;   // union capacity
+constexpr int NTHR = 192;         // 6 warps
+constexpr int TMEM_COLS = 512;
+constexpr int COL_S = 0;
+constexpr int COL_O = 128;
+constexpr float LOG2E = 1.4426950408889634f;
+constexpr float RESCALE_T = 8.f;
+
+constexpr uint32_t Q_HALF = ROWS * 128;     // 16 KB: 128 rows x 64 elements
+constexpr uint32_t Q_BYTES = 2 * Q_HALF;
+constexpr uint32_t KV_HALF = KT * 128;      // 8 KB: 64 rows x 64 elements
+constexpr uint32_t KV_BYTES = 2 * KV_HALF;
+constexpr uint32_t P_BYTES = ROWS * 128;    // 128 rows x 64 keys
+
+enum { B_QFULL = 0, B_KVFULL = 1, B_KVEMPTY = B_KVFULL + NS, B_SFULL = B_KVEMPTY + NS, B_SFREE = B_SFULL + 2,
+       B_PFULL = B_SFREE + 2, B_ODONE = B_PFULL + 2, B_DRAIN = B_ODONE + 1, N_BARS = B_DRAIN + 1 };
+
+struct TcLayout {
+    uint32_t q, kv, p, bars, misc, gate, umask, ulist, bitmap, wpref, scan, total;
+    __host__ __device__ explicit TcLayout(int nwords) {
+        q = 0;
+        kv = q + Q_BYTES;
+        p = kv + NS * KV_BYTES;
+        bars = p + 2 * P_BYTES;
+        misc = bars + 32 * 8;
+        gate = misc + 16;
+        umask = gate + ROWS * 3 * 4;
+        ulist = umask + UMAX * 8;
+        bitmap = ulist + UMAX * 4;
+        wpref = bitmap + nwords * 4;
+        scan = wpref + nwords * 4;
+        total = scan + (NTHR + 16) * 4;
+    }
+};
+
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+template <typename T> __device__ __forceinline__ uint32_t pack2(float lo, float hi);
+template <> __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float lo, float hi) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+}
+template <> __device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__device__ __forceinline__ int clamp64(int64_t x) { return x < 0 ? 0 : (x > KT ? KT : (int)x); }
+
+struct TcTile {
+    int stream;    // 0 local, 1 sparse, 2 hca
+    int64_t row0;  // first row in the source table
+    int u;         // union slot (sparse)
+    bool first;    // first tile of its stream
+};
+
+template <typename T>
+__global__ void __launch_bounds__(NTHR, 1)
+    sa_attention_tc_kernel(const SaArgs a, const __grid_constant__ CUtensorMap tm_q,
+                           const __grid_constant__ CUtensorMap tm_c, const __grid_constant__ CUtensorMap tm_h,
+                           int nwords) {
+    extern __shared__ unsigned char smem_dyn[];
+    unsigned char* base =
+        reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
+    const TcLayout LY(nwords);
+    unsigned char* Qs = base + LY.q;
+    unsigned char* KVs = base + LY.kv;
+    unsigned char* Ps = base + LY.p;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(base + LY.bars);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + LY.misc);
+    volatile int* abort_f = reinterpret_cast<volatile int*>(base + LY.misc + 4);
+    float* gsm = reinterpret_cast<float*>(base + LY.gate);
+    unsigned long long* umask = reinterpret_cast<unsigned long long*>(base + LY.umask);
+    int* ulist = reinterpret_cast<int*>(base + LY.ulist);
+    unsigned* bitmap = reinterpret_cast<unsigned*>(base + LY.bitmap);
+    int* wpref = reinterpret_cast<int*>(base + LY.wpref);
+    int* scan = reinterpret_cast<int*>(base + LY.scan);
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int h0 = blockIdx.x * HPG;
+    const int64_t q0 = (int64_t)blockIdx.y * QT;
+    const int64_t b = blockIdx.z;
+    const int nt = (int)((a.Lq - q0) < QT ? (a.Lq - q0) : QT);
+    const int64_t P0 = a.Lkv - a.Lq + q0;  // absolute position of query row 0 of the tile
+    const int64_t Plast = P0 + nt - 1;
+    const int64_t nb_kv = (a.Lkv + KT - 1) / KT;
+    const int K = a.K;
+    const int64_t* tix = a.top_idx + b * a.st[0];
+
+    if (tid == 0) {
+        for (int i = 0; i < N_BARS; ++i) {
+            uint32_t cnt = 1;
+            if (i == B_SFREE || i == B_SFREE + 1 || i == B_PFULL || i == B_PFULL + 1) cnt = 128;
+            mbar_init(&bars[i], cnt);
+        }
+        *abort_f = 0;
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        prefetch_tmap(&tm_q);
+        prefetch_tmap(&tm_c);
+        prefetch_tmap(&tm_h);
+    }
+    if (warp == 1) tmem_alloc<TMEM_COLS>(tmem_slot);
+
+    // ---------------- union of the selected blocks -------------------------
+    for (int i = tid; i < nwords; i += NTHR) bitmap[i] = 0u;
+    __syncthreads();
+    for (int e = tid; e < nt * K; e += NTHR) {
+        const int t = e / K, sl = e - t * K;
+        const int64_t n = tix[(q0 + t) * a.st[1] + sl * a.st[2]];
+        if (n >= 0 && n < nb_kv && n * KT <= P0 + t) atomicOr(&bitmap[n >> 5], 1u << (n & 31));
+    }
+    __syncthreads();
+    {
+        const int per = (nwords + NTHR - 1) / NTHR;
+        const int w0 = tid * per;
+        int s = 0;
+        for (int i = 0; i < per; ++i)
+            if (w0 + i < nwords) s += __popc(bitmap[w0 + i]);
+        scan[tid] = s;
+        __syncthreads();
+        if (warp == 0) {
+            constexpr int PL = NTHR / 32;
+            int v[PL];
+            int tot = 0;
+#pragma unroll
+            for (int i = 0; i < PL; ++i) {
+                v[i] = scan[lane * PL + i];
+                tot += v[i];
+            }
+            int inc = tot;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, inc, o);
+                if (lane >= o) inc += y;
+            }
+            int run = inc - tot;
+#pragma unroll
+            for (int i = 0; i < PL; ++i) {
+                scan[lane * PL + i] = run;
+                run += v[i];
+            }
+            if (lane == 31) scan[NTHR] = inc;
+        }
+        __syncthreads();
+        int run = scan[tid];
+        for (int i = 0; i < per; ++i) {
+            const int wi = w0 + i;
+            if (wi < nwords) {
+                wpref[wi] = run;
+                unsigned bits = bitmap[wi];
+                int r = run;
+                while (bits) {
+                    const int bit = __ffs(bits) - 1;
+                    bits &= bits - 1;
+                    ulist[r] = wi * 32 + bit;
+                    umask[r] = 0ull;
+                    ++r;
+                }
+                run += __popc(bitmap[wi]);
+            }
+        }
+    }
+    __syncthreads();
+    const int U = scan[NTHR];
+    for (int e = tid; e < nt * K; e += NTHR) {
+        const int t = e / K, sl = e - t * K;
+        const int64_t n = tix[(q0 + t) * a.st[1] + sl * a.st[2]];
+        if (n >= 0 && n < nb_kv && n * KT <= P0 + t) {
+            const int wi = (int)(n >> 5);
+            const int r = wpref[wi] + __popc(bitmap[wi] & ((1u << (n & 31)) - 1u));
+            atomicOr(&umask[r], 1ull << t);
+        }
+    }
+    // gate weights of the 128 rows (row m = 2 t + h)
+    for (int row = tid; row < ROWS; row += NTHR) {
+        const int t = row >> 1, h = h0 + (row & 1);
+        float g0 = 0.f, g1 = 0.f, g2 = 0.f;
+        if (t < nt) {
+            const T* gp = static_cast<const T*>(a.gate);
+            const T* gr = a.gate4d ? gp + b * a.sg[0] + h * a.sg[1] + (q0 + t) * a.sg[2]
+                                   : gp + b * a.sg[0] + (q0 + t) * a.sg[1];
+            const int64_t gs = a.gate4d ? a.sg[3] : a.sg[2];
+            g0 = Cvt<T>::to_f(gr[0]);
+            g1 = Cvt<T>::to_f(gr[gs]);
+            g2 = Cvt<T>::to_f(gr[2 * gs]);
+            const float m = fmaxf(g0, fmaxf(g1, g2));
+            const float e0 = expf(g0 - m), e1 = expf(g1 - m), e2 = expf(g2 - m);
+            const float inv = 1.f / (e0 + e1 + e2);
+            g0 = e0 * inv;
+            g1 = e1 * inv;
+            g2 = e2 * inv;
+        }
+        gsm[row * 3 + 0] = g0;
+        gsm[row * 3 + 1] = g1;
+        gsm[row * 3 + 2] = g2;
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    // ---------------- tile schedule -----------------------------------------
+    const int64_t lo_min = P0 - a.window + 1 > 0 ? P0 - a.window + 1 : 0;
+    const int64_t ws = (lo_min / KT) * KT;
+    const int n_win = (int)((Plast - ws) / KT + 1);
+    const bool sink_tile = ws > 0 && a.n_sinks > 0;
+    const int n_local = n_win + (sink_tile ? 1 : 0);
+    int64_t nhca_max = 0;
+    if (Plast >= a.hca_r - 1) {
+        nhca_max = (Plast + 1) / a.hca_r;
+        if (nhca_max > a.NC) nhca_max = a.NC;
+    }
+    const int n_hca = (int)((nhca_max + KT - 1) / KT);
+    const int n_tiles = n_local + U + n_hca;
+    auto tile_at = [&](int i) {
+        TcTile ti;
+        if (i < n_local) {
+            ti.stream = 0;
+            ti.row0 = sink_tile ? (i == 0 ? 0 : ws + (int64_t)(i - 1) * KT) : ws + (int64_t)i * KT;
+            ti.u = -1;
+            ti.first = i == 0;
+        } else if (i < n_local + U) {
+            ti.stream = 1;
+            ti.u = i - n_local;
+            ti.row0 = (int64_t)ulist[ti.u] * KT;
+            ti.first = ti.u == 0;
+        } else {
+            ti.stream = 2;
+            ti.row0 = (int64_t)(i - n_local - U) * KT;
+            ti.u = -1;
+            ti.first = i == n_local + U;
+        }
+        return ti;
+    };
+    constexpr bool BF = std::is_same<T, __nv_bfloat16>::value;
+
+    if (warp == 0) {
+        // ============================ TMA producer ============================
+        if (lane == 0) {
+            mbar_arrive_expect_tx(&bars[B_QFULL], Q_BYTES);
+            tma_load_4d(Qs, &tm_q, &bars[B_QFULL], 0, h0, (int)q0, (int)b);
+            tma_load_4d(Qs + Q_HALF, &tm_q, &bars[B_QFULL], 64, h0, (int)q0, (int)b);
+            int j = 0;
+            for (; j < n_tiles; ++j) {
+                const int st = j % NS;
+                if (j >= NS && !mbar_wait(&bars[B_KVEMPTY + st], ((j / NS) - 1) & 1, abort_f)) break;
+                const TcTile ti = tile_at(j);
+                const CUtensorMap* m = ti.stream == 2 ? &tm_h : &tm_c;
+                unsigned char* dst = KVs + st * KV_BYTES;
+                mbar_arrive_expect_tx(&bars[B_KVFULL + st], KV_BYTES);
+                tma_load_3d(dst, m, &bars[B_KVFULL + st], 0, (int)ti.row0, (int)b);
+                tma_load_3d(dst + KV_HALF, m, &bars[B_KVFULL + st], 64, (int)ti.row0, (int)b);
+            }
+            // every copy issued has landed before the CTA may exit
+            mbar_wait(&bars[B_QFULL], 0, nullptr);
+            for (int s = 0; s < NS && s < j; ++s) {
+                const int last = ((j - 1 - s) / NS) * NS + s;
+                mbar_wait(&bars[B_KVFULL + s], (last / NS) & 1, nullptr);
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ============================ MMA issuer ==============================
+        if (lane == 0) {
+            constexpr uint32_t ID_QK = idesc_f16(ROWS, KT, BF, false, false);
+            constexpr uint32_t ID_PV = idesc_f16(ROWS, DCX, BF, false, true);
+            const uint32_t qa = smem_addr(Qs), kva = smem_addr(KVs), pa = smem_addr(Ps);
+            if (mbar_wait(&bars[B_QFULL], 0, abort_f)) {
+                tc_fence_after();
+                for (int j = 0; j <= n_tiles; ++j) {
+                    if (j < n_tiles) {
+                        const int st = j % NS, sb = j & 1;
+                        if (!mbar_wait(&bars[B_KVFULL + st], (j / NS) & 1, abort_f)) break;
+                        if (j >= 2 && !mbar_wait(&bars[B_SFREE + sb], ((j >> 1) - 1) & 1, abort_f)) break;
+                        tc_fence_after();
+#pragma unroll
+                        for (int k = 0; k < DCX / 16; ++k) {
+                            const uint64_t ad = sdesc_sw128(qa + (k >> 2) * Q_HALF + (k & 3) * 32, 16, 1024);
+                            const uint64_t bd =
+                                sdesc_sw128(kva + st * KV_BYTES + (k >> 2) * KV_HALF + (k & 3) * 32, 16, 1024);
+                            umma_f16_ss(tmem + COL_S + sb * KT, ad, bd, ID_QK, k > 0 ? 1u : 0u);
+                        }
+                        umma_commit(&bars[B_SFULL + sb]);
+                    }
+                    if (j >= 1) {
+                        const int i = j - 1, st = i % NS, sb = i & 1;
+                        if (!mbar_wait(&bars[B_PFULL + sb], (i >> 1) & 1, abort_f)) break;
+                        tc_fence_after();
+                        const TcTile ti = tile_at(i);
+                        const uint32_t dst = tmem + COL_O + ti.stream * DCX;
+#pragma unroll
+                        for (int k = 0; k < KT / 16; ++k) {
+                            const uint64_t ad = sdesc_sw128(pa + sb * P_BYTES + k * 32, 16, 1024);
+                            const uint64_t bd = sdesc_sw128(kva + st * KV_BYTES + k * 2048, KV_HALF, 1024);
+                            umma_f16_ss(dst, ad, bd, ID_PV, (k > 0 || !ti.first) ? 1u : 0u);
+                        }
+                        umma_commit(&bars[B_KVEMPTY + st]);
+                        umma_commit(&bars[B_ODONE]);
+                    }
+                }
+            }
+            // every MMA issued has completed before TMEM is freed
+            umma_commit(&bars[B_DRAIN]);
+            mbar_wait(&bars[B_DRAIN], 0, nullptr);
+        }
+        __syncwarp();
+    } else {
+        // ===================== softmax + epilogue (128 threads) ===============
+        const int q4 = warp & 3;
+        const int rid = q4 * 32 + lane;
+        const int t = rid >> 1, hh = rid & 1;
+        const bool rvalid = t < nt;
+        const int64_t pos = P0 + t;
+        const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
+        unsigned char* prow = Ps + (rid >> 3) * 1024 + (rid & 7) * 128;
+        const int sw = rid & 7;
+        const int64_t lo_p = pos - a.window + 1 > 0 ? pos - a.window + 1 : 0;
+        const int64_t sink_end = a.n_sinks < lo_p ? a.n_sinks : lo_p;
+        int64_t nv_hca = 0;
+        if (pos >= a.hca_r - 1) {
+            nv_hca = (pos + 1) / a.hca_r;
+            if (nv_hca > a.NC) nv_hca = a.NC;
+        }
+        float lsum0 = 0.f, lsum1 = 0.f, lsum2 = 0.f;
+        float m_cur = -INFINITY, l_cur = 0.f;
+        int cur = -1;
+        bool ok = true;
+        for (int j = 0; j < n_tiles; ++j) {
+            const int sb = j & 1;
+            const TcTile ti = tile_at(j);
+            if (ti.stream != cur) {
+                if (cur == 0) lsum0 = l_cur;
+                else if (cur == 1) lsum1 = l_cur;
+                m_cur = -INFINITY;
+                l_cur = 0.f;
+                cur = ti.stream;
+            }
+            // valid columns of this row: [a1, b1) and the sinks [0, b2)
+            int a1 = 0, b1 = 0, b2 = 0;
+            if (rvalid) {
+                if (ti.stream == 0) {
+                    a1 = clamp64(lo_p - ti.row0);
+                    b1 = clamp64(pos - ti.row0 + 1);
+                    b2 = clamp64(sink_end - ti.row0);
+                } else if (ti.stream == 1) {
+                    if ((umask[ti.u] >> t) & 1ull) b1 = clamp64((pos + 1 < a.Lkv ? pos + 1 : a.Lkv) - ti.row0);
+                } else {
+                    b1 = clamp64(nv_hca - ti.row0);
+                }
+            }
+            ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_SFULL + sb], (j >> 1) & 1, abort_f));
+            if (!ok) break;
+            tc_fence_after();
+            uint32_t s[64];
+            tmem_ld32(tmem + lane_base + COL_S + sb * KT, s);
+            tmem_ld32(tmem + lane_base + COL_S + sb * KT + 32, s + 32);
+            tmem_wait_ld();
+            tc_fence_before();
+            mbar_arrive(&bars[B_SFREE + sb]);
+            float mx = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < KT; ++c) {
+                const bool v = (c >= a1 && c < b1) || c < b2;
+                const float x = v ? __uint_as_float(s[c]) * LOG2E : -INFINITY;
+                s[c] = __float_as_uint(x);
+                mx = fmaxf(mx, x);
+            }
+            float fac = 1.f;
+            bool resc = false;
+            if (mx != -INFINITY) {
+                if (m_cur == -INFINITY) {
+                    m_cur = mx;
+                } else if (mx > m_cur + RESCALE_T) {
+                    fac = ex2(m_cur - mx);
+                    m_cur = mx;
+                    resc = true;
+                }
+            }
+            const float mu = m_cur == -INFINITY ? 0.f : m_cur;
+            float psum = 0.f;
+            uint32_t pk[32];
+#pragma unroll
+            for (int c = 0; c < KT; c += 2) {
+                const float p0 = ex2(__uint_as_float(s[c]) - mu);
+                const float p1 = ex2(__uint_as_float(s[c + 1]) - mu);
+                psum += p0 + p1;
+                pk[c >> 1] = pack2<T>(p0, p1);
+            }
+            l_cur = l_cur * fac + psum;
+            // PV of the previous tile done: its P buffer and O are free to touch
+            if (j >= 1) {
+                ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_ODONE], (j - 1) & 1, abort_f));
+                if (!ok) break;
+            }
+            unsigned char* pdst = prow + sb * P_BYTES;
+#pragma unroll
+            for (int cc = 0; cc < 8; ++cc) {
+                *reinterpret_cast<uint4*>(pdst + ((cc ^ sw) << 4)) =
+                    make_uint4(pk[4 * cc], pk[4 * cc + 1], pk[4 * cc + 2], pk[4 * cc + 3]);
+            }
+            if (__any_sync(0xffffffffu, resc)) {
+                tc_fence_after();
+                const uint32_t to = tmem + lane_base + COL_O + ti.stream * DCX;
+#pragma unroll
+                for (int cc = 0; cc < DCX / 32; ++cc) {
+                    uint32_t o[32];
+                    tmem_ld32(to + cc * 32, o);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * fac);
+                    tmem_st32(to + cc * 32, o);
+                }
+                tmem_wait_st();
+            }
+            fence_proxy_async_smem();
+            tc_fence_before();
+            mbar_arrive(&bars[B_PFULL + sb]);
+        }
+        if (cur == 0) lsum0 = l_cur;
+        else if (cur == 1) lsum1 = l_cur;
+        else if (cur == 2) lsum2 = l_cur;
+        if (ok && n_tiles > 0) ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_ODONE], (n_tiles - 1) & 1, abort_f));
+        if (ok) {
+            tc_fence_after();
+            const float g0 = gsm[rid * 3 + 0], g1 = gsm[rid * 3 + 1], g2 = gsm[rid * 3 + 2];
+            const bool u0 = lsum0 > 0.f, u1 = lsum1 > 0.f, u2 = lsum2 > 0.f;
+            const float f0 = u0 ? g0 / lsum0 : 0.f, f1 = u1 ? g1 / lsum1 : 0.f, f2 = u2 ? g2 / lsum2 : 0.f;
+            const bool early = rvalid && pos < a.hca_r - 1;  // HCA: mean of the latent prefix
+            const T* ckv = static_cast<const T*>(a.ckv) + b * a.sc[0];
+            T* orow = static_cast<T*>(a.out) + b * a.so[0] + (q0 + (rvalid ? t : 0)) * a.so[1] +
+                      (int64_t)(h0 + hh) * a.so[2];
+            const uint32_t to = tmem + lane_base + COL_O;
+#pragma unroll 1
+            for (int cc = 0; cc < DCX / 32; ++cc) {
+                uint32_t o0[32], o1[32], o2[32];
+                tmem_ld32(to + cc * 32, o0);
+                tmem_ld32(to + DCX + cc * 32, o1);
+                tmem_ld32(to + 2 * DCX + cc * 32, o2);
+                tmem_wait_ld();
+                float v[32];
+#pragma unroll
+                for (int e = 0; e < 32; ++e) {
+                    float x = u0 ? f0 * __uint_as_float(o0[e]) : 0.f;
+                    x += u1 ? f1 * __uint_as_float(o1[e]) : 0.f;
+                    x += u2 ? f2 * __uint_as_float(o2[e]) : 0.f;
+                    v[e] = x;
+                }
+                if (early) {
+                    const float w = g2 / float(pos + 1);
+                    for (int64_t jj = 0; jj <= pos; ++jj) {
+                        const T* cr = ckv + jj * a.sc[1] + cc * 32;
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) v[e] += w * Cvt<T>::to_f(cr[e]);
+                    }
+                }
+                if (rvalid) {
+#pragma unroll
+                    for (int e8 = 0; e8 < 4; ++e8) {
+                        uint4 w4 = make_uint4(pack2<T>(v[8 * e8 + 0], v[8 * e8 + 1]), pack2<T>(v[8 * e8 + 2], v[8 * e8 + 3]),
+                                              pack2<T>(v[8 * e8 + 4], v[8 * e8 + 5]), pack2<T>(v[8 * e8 + 6], v[8 * e8 + 7]));
+                        *reinterpret_cast<uint4*>(orow + cc * 32 + 8 * e8) = w4;
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc<TMEM_COLS>(tmem);
+    }
+    if (tid == 0 && *abort_f) atomicExch(&g_device_error, 1);
+}
+
+// ------------------------------------------------------------------ host side
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encode_fn() {
+    static EncodeTiled fn = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) !=
+                cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            p = nullptr;
+        return reinterpret_cast<EncodeTiled>(p);
+    }();
+    return fn;
+}
+
+// rank-R tiled map of 16-bit elements, 128-byte swizzle; strides in elements (R-1 of them)
+bool make_map(CUtensorMap* m, int dtype, const void* ptr, int rank, const int64_t* dims, const int64_t* strides,
+              const uint32_t* box) {
+    EncodeTiled fn = encode_fn();
+    if (fn == nullptr) return false;
+    cuuint64_t gd[5], gs[4];
+    cuuint32_t bx[5], es[5];
+    for (int i = 0; i < rank; ++i) {
+        gd[i] = (cuuint64_t)dims[i];
+        bx[i] = box[i];
+        es[i] = 1;
+        if (i + 1 < rank) gs[i] = (cuuint64_t)strides[i] * 2;
+    }
+    const CUresult r =
+        fn(m, dtype == MABA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, (cuuint32_t)rank,
+           const_cast<void*>(ptr), gd, gs, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+inline bool a16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+inline bool s16(int64_t stride_elems) { return ((stride_elems * 2) % 16) == 0 && stride_elems > 0; }
+
+int tc_nwords(const SaArgs& a) { return (int)(((a.Lkv + KT - 1) / KT + 31) / 32) + 1; }
+
+}  // namespace
+
+bool sa_attention_tc_supported(const SaArgs& a, int dtype) {
+    if (dtype != MABA_BF16 && dtype != MABA_F16) return false;
+    if (a.pos_dev != nullptr) return false;
+    if (a.DC != DCX || a.block != KT || a.K <= 0 || a.K > KMAX) return false;
+    if (a.H % HPG != 0 || a.Lq < 16 || a.n_sinks > KT || a.window <= 0) return false;
+    if (a.Lkv >= (int64_t(1) << 31) || a.Lq >= (int64_t(1) << 31)) return false;
+    if (a.sq[3] != 1 || a.sc[2] != 1 || a.so[3] != 1 || (a.NC > 0 && a.sh[2] != 1)) return false;
+    if (!s16(a.sq[2]) || !s16(a.sq[1]) || !s16(a.sq[0]) || !s16(a.sc[1]) || !s16(a.sc[0])) return false;
+    if (a.NC > 0 && (!s16(a.sh[1]) || !s16(a.sh[0]) || !a16(a.hca))) return false;
+    if (!a16(a.qhat) || !a16(a.ckv) || !a16(a.out) || (a.so[1] % 8) || (a.so[2] % 8)) return false;
+    if (TcLayout(tc_nwords(a)).total + 1024 > 227 * 1024) return false;
+    return encode_fn() != nullptr;
+}
+
+int sa_attention_tc(SaArgs& a, int64_t B, int dtype, cudaStream_t s) {
+    const int nwords = tc_nwords(a);
+    const size_t smem = TcLayout(nwords).total + 1024;
+    CUtensorMap mq, mc, mh;
+    {
+        const int64_t dq[4] = {a.DC, a.H, a.Lq, B};
+        const int64_t sq[3] = {a.sq[2], a.sq[1], a.sq[0]};
+        const uint32_t bq[4] = {64, (uint32_t)HPG, (uint32_t)QT, 1};
+        const int64_t dc[3] = {a.DC, a.Lkv, B};
+        const int64_t sc[2] = {a.sc[1], a.sc[0]};
+        const uint32_t bc[3] = {64, (uint32_t)KT, 1};
+        if (!make_map(&mq, dtype, a.qhat, 4, dq, sq, bq) || !make_map(&mc, dtype, a.ckv, 3, dc, sc, bc))
+            return sa_attention_mma(a, B, dtype, s);
+        if (a.NC > 0) {
+            const int64_t dh[3] = {a.DC, a.NC, B};
+            const int64_t sh[2] = {a.sh[1], a.sh[0]};
+            if (!make_map(&mh, dtype, a.hca, 3, dh, sh, bc)) return sa_attention_mma(a, B, dtype, s);
+        } else {
+            mh = mc;  // no HCA tiles are scheduled
+        }
+    }
+    dim3 grid((unsigned)(a.H / HPG), (unsigned)ceil_div(a.Lq, QT), (unsigned)B);
+    if (dtype == MABA_BF16) {
+        auto kern = sa_attention_tc_kernel<__nv_bfloat16>;
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        kern<<<grid, NTHR, smem, s>>>(a, mq, mc, mh, nwords);
+    } else {
+        auto kern = sa_attention_tc_kernel<__half>;
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        kern<<<grid, NTHR, smem, s>>>(a, mq, mc, mh, nwords);
+    }
+    return check_launch("sa_attention(tcgen05)");
+}
+
+int device_error_take(cudaStream_t s, int* out) {
+    int v = 0;
+    cudaError_t e = cudaMemcpyFromSymbolAsync(&v, g_device_error, sizeof(int), 0, cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return set_error(MABA_ERR_CUDA, "device_error: %s", cudaGetErrorString(e));
+    const int zero = 0;
+    if (v != 0) cudaMemcpyToSymbolAsync(g_device_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, s);
+    *out = v;
+    return MABA_OK;
+}
+
+}  // namespace maba

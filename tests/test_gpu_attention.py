@@ -50,6 +50,29 @@ def test_kernel_vs_oracle(B, Lq, Lkv, H, DC, K, window, block, r, gate4d):
     assert_rel(outb, ref, RTOL_BF16, "bf16")
 
 
+@pytest.mark.parametrize("B,Lq,Lkv,H,K,window,sinks,gate4d,dt", [
+    (1, 256, 256, 2, 4, 128, 4, False, torch.bfloat16),    # whole tiles, HCA early rows
+    (2, 200, 200, 4, 6, 100, 4, False, torch.bfloat16),    # batch 2, ragged last tile, window % 64 != 0
+    (1, 130, 1000, 2, 8, 128, 4, True, torch.bfloat16),    # queries at offset 870 of the cache, per-head gate
+    (1, 64, 64, 2, 1, 1, 0, False, torch.bfloat16),        # window 1, no sinks, one selected block
+    (1, 300, 300, 2, 32, 4096, 4, False, torch.float16),   # window covering everything, top-32, fp16
+    (1, 1024, 1024, 10, 32, 128, 4, False, torch.bfloat16),  # config-2 shape, longer HCA stream
+])
+def test_tc_kernel_vs_oracle(B, Lq, Lkv, H, K, window, sinks, gate4d, dt):
+    """The tcgen05 path (block 64, d_c 128, even H): every stream, mask and tile edge vs the oracle."""
+    qhat, c, top, gate = rand_case(B, Lq, Lkv, H, 128, K, 64, seed=7 * Lq + K, gate4d=gate4d)
+    cd = c.to(DEV, dt)
+    hca = mb.b200_hca_pool(cd, 64) if Lkv >= 64 else None
+    out = mb.b200_sa_attention(qhat.to(DEV, dt), cd, hca, top.to(DEV), gate.to(DEV, dt), window_size=window,
+                               n_sinks=sinks, block_size=64, hca_r=64)
+    torch.cuda.synchronize()
+    assert mb._native.device_error() == 0
+    ref = OA.sa_attention_latent(qhat.to(dt).float().numpy(), c.to(dt).float().numpy(), top.numpy(),
+                                 gate.to(dt).float().numpy(), window, sinks, 64, 64)
+    assert out.dtype == dt
+    assert_rel(out, ref, RTOL_BF16, str(dt))
+
+
 def load_sa(name):
     g = sub(golden("sa_layer"), f"{name}.")
     window, block, top_k, r = (int(v) for v in g["kw"])
