@@ -6,21 +6,27 @@
 // three streams (window + sinks, the selected blocks, the pooled HCA rows),
 // one softmax per stream and row, superposed by the softmax of the gate.
 //
-// One CTA per (pair of heads, 64 query tokens): 128 MMA rows, row m = 2 t + h.
-//  * warp 0 (one lane): TMA producer -- the Q tile once (box 64 x 2 heads x 64
-//    tokens, two 64-wide halves of d_c), then every latent key tile of the
-//    three streams into a 4-stage ring (box 64 rows x 64 columns, twice); all
-//    with 128-byte swizzle;
+// One CTA per 64 query tokens; it runs the heads two at a time (128 MMA rows,
+// row m = 2 t + h) over one tile schedule built once per CTA.  The tiles of
+// all head pairs form one sequence g = hp * n_tiles + j, so every pipeline
+// barrier's phases simply count g.
+//  * warp 0 (one lane): TMA producer -- the Q tile of each head pair into one
+//    of two buffers (box 64 x 2 heads x 64 tokens, two 64-wide halves of d_c),
+//    and every latent key tile into a 4-stage ring (box 64 rows x 64 columns,
+//    twice); all with 128-byte swizzle;
 //  * warp 1: allocates the 512 TMEM columns; one lane issues the MMAs:
 //    S = Q K^T (M=128, N=64, K=128; K-major A and B) into one of two TMEM S
-//    buffers, and O_s += P V (M=128, N=128, K=64; A = P from shared memory,
+//    buffers, and O_s += P V (M=128, N=128, K=64; A = P read from TMEM,
 //    B = the same key tile read MN-major) into the TMEM accumulator of the
 //    tile's stream;
 //  * warps 2..5 (128 threads, thread = TMEM lane = MMA row): masked online
-//    softmax of the S tile (ex2), P to shared memory, lazy rescaling of O in
-//    TMEM (only when a row's running maximum grows by more than 2^8), and the
-//    epilogue: O_local / l, O_sparse / l, O_hca / l weighted by the gate.
-// TMEM: S buffers in columns [0,128), O of stream s in [128+128s, 256+128s).
+//    softmax of the S tile (ex2), P (16-bit) written back over the first 32
+//    columns of its S buffer, lazy rescaling of O in TMEM (only when a row's
+//    running maximum grows by more than 2^8), and the epilogue of each head
+//    pair: O_local / l, O_sparse / l, O_hca / l weighted by the gate.
+// TMEM: S/P buffers in columns [0,128), O of stream s in [128+128s, 256+128s).
+// The MMAs of one thread run in issue order, so QK of tile g+2 (which
+// overwrites S/P buffer g&1) is issued only after PV of tile g read P.
 // The sparse stream runs over the union of the blocks the 64 tokens selected
 // (bitmap + popcount ranks + 64-bit token masks), as in the mma kernel.
 //
@@ -44,7 +50,7 @@ using namespace tc;
 constexpr int QT = 64;            // query tokens per CTA
 constexpr int KT = 64;            // keys per tile (= block size)
 constexpr int DCX = 128;          // latent dim
-constexpr int HPG = 2;            // heads per CTA
+constexpr int HPG = 2;            // heads per MMA tile
 constexpr int ROWS = QT * HPG;    // MMA rows
 constexpr int NS = 4;             // key-tile stages
 constexpr int KMAX = 32;          // selected blocks per token
@@ -60,21 +66,18 @@ constexpr uint32_t Q_HALF = ROWS * 128;     // 16 KB: 128 rows x 64 elements
 constexpr uint32_t Q_BYTES = 2 * Q_HALF;
 constexpr uint32_t KV_HALF = KT * 128;      // 8 KB: 64 rows x 64 elements
 constexpr uint32_t KV_BYTES = 2 * KV_HALF;
-constexpr uint32_t P_BYTES = ROWS * 128;    // 128 rows x 64 keys
 
-enum { B_QFULL = 0, B_KVFULL = 1, B_KVEMPTY = B_KVFULL + NS, B_SFULL = B_KVEMPTY + NS, B_SFREE = B_SFULL + 2,
-       B_PFULL = B_SFREE + 2, B_ODONE = B_PFULL + 2, B_DRAIN = B_ODONE + 1, N_BARS = B_DRAIN + 1 };
+enum { B_QFULL = 0, B_QEMPTY = 2, B_KVFULL = 4, B_KVEMPTY = B_KVFULL + NS, B_SFULL = B_KVEMPTY + NS,
+       B_PFULL = B_SFULL + 2, B_ODONE = B_PFULL + 2, B_DRAIN = B_ODONE + 2, N_BARS = B_DRAIN + 1 };
 
 struct TcLayout {
-    uint32_t q, kv, p, bars, misc, gate, umask, ulist, bitmap, wpref, scan, total;
+    uint32_t q, kv, bars, misc, umask, ulist, bitmap, wpref, scan, total;
     __host__ __device__ explicit TcLayout(int nwords) {
         q = 0;
-        kv = q + Q_BYTES;
-        p = kv + NS * KV_BYTES;
-        bars = p + 2 * P_BYTES;
+        kv = q + 2 * Q_BYTES;
+        bars = kv + NS * KV_BYTES;
         misc = bars + 32 * 8;
-        gate = misc + 16;
-        umask = gate + ROWS * 3 * 4;
+        umask = misc + 16;
         ulist = umask + UMAX * 8;
         bitmap = ulist + UMAX * 4;
         wpref = bitmap + nwords * 4;
@@ -99,8 +102,6 @@ template <> __device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi
     return *reinterpret_cast<uint32_t*>(&v);
 }
 
-__device__ __forceinline__ int clamp64(int64_t x) { return x < 0 ? 0 : (x > KT ? KT : (int)x); }
-
 struct TcTile {
     int stream;    // 0 local, 1 sparse, 2 hca
     int64_t row0;  // first row in the source table
@@ -119,11 +120,9 @@ __global__ void __launch_bounds__(NTHR, 1)
     const TcLayout LY(nwords);
     unsigned char* Qs = base + LY.q;
     unsigned char* KVs = base + LY.kv;
-    unsigned char* Ps = base + LY.p;
     uint64_t* bars = reinterpret_cast<uint64_t*>(base + LY.bars);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + LY.misc);
     volatile int* abort_f = reinterpret_cast<volatile int*>(base + LY.misc + 4);
-    float* gsm = reinterpret_cast<float*>(base + LY.gate);
     unsigned long long* umask = reinterpret_cast<unsigned long long*>(base + LY.umask);
     int* ulist = reinterpret_cast<int*>(base + LY.ulist);
     unsigned* bitmap = reinterpret_cast<unsigned*>(base + LY.bitmap);
@@ -131,9 +130,9 @@ __global__ void __launch_bounds__(NTHR, 1)
     int* scan = reinterpret_cast<int*>(base + LY.scan);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int h0 = blockIdx.x * HPG;
-    const int64_t q0 = (int64_t)blockIdx.y * QT;
-    const int64_t b = blockIdx.z;
+    const int64_t q0 = (int64_t)blockIdx.x * QT;
+    const int64_t b = blockIdx.y;
+    const int NH = a.H / HPG;
     const int nt = (int)((a.Lq - q0) < QT ? (a.Lq - q0) : QT);
     const int64_t P0 = a.Lkv - a.Lq + q0;  // absolute position of query row 0 of the tile
     const int64_t Plast = P0 + nt - 1;
@@ -144,7 +143,7 @@ __global__ void __launch_bounds__(NTHR, 1)
     if (tid == 0) {
         for (int i = 0; i < N_BARS; ++i) {
             uint32_t cnt = 1;
-            if (i == B_SFREE || i == B_SFREE + 1 || i == B_PFULL || i == B_PFULL + 1) cnt = 128;
+            if (i == B_PFULL || i == B_PFULL + 1) cnt = 128;
             mbar_init(&bars[i], cnt);
         }
         *abort_f = 0;
@@ -227,35 +226,12 @@ __global__ void __launch_bounds__(NTHR, 1)
             atomicOr(&umask[r], 1ull << t);
         }
     }
-    // gate weights of the 128 rows (row m = 2 t + h)
-    for (int row = tid; row < ROWS; row += NTHR) {
-        const int t = row >> 1, h = h0 + (row & 1);
-        float g0 = 0.f, g1 = 0.f, g2 = 0.f;
-        if (t < nt) {
-            const T* gp = static_cast<const T*>(a.gate);
-            const T* gr = a.gate4d ? gp + b * a.sg[0] + h * a.sg[1] + (q0 + t) * a.sg[2]
-                                   : gp + b * a.sg[0] + (q0 + t) * a.sg[1];
-            const int64_t gs = a.gate4d ? a.sg[3] : a.sg[2];
-            g0 = Cvt<T>::to_f(gr[0]);
-            g1 = Cvt<T>::to_f(gr[gs]);
-            g2 = Cvt<T>::to_f(gr[2 * gs]);
-            const float m = fmaxf(g0, fmaxf(g1, g2));
-            const float e0 = expf(g0 - m), e1 = expf(g1 - m), e2 = expf(g2 - m);
-            const float inv = 1.f / (e0 + e1 + e2);
-            g0 = e0 * inv;
-            g1 = e1 * inv;
-            g2 = e2 * inv;
-        }
-        gsm[row * 3 + 0] = g0;
-        gsm[row * 3 + 1] = g1;
-        gsm[row * 3 + 2] = g2;
-    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    // ---------------- tile schedule -----------------------------------------
+    // ---------------- tile schedule (the same for every head pair) ----------
     const int64_t lo_min = P0 - a.window + 1 > 0 ? P0 - a.window + 1 : 0;
     const int64_t ws = (lo_min / KT) * KT;
     const int n_win = (int)((Plast - ws) / KT + 1);
@@ -268,6 +244,7 @@ __global__ void __launch_bounds__(NTHR, 1)
     }
     const int n_hca = (int)((nhca_max + KT - 1) / KT);
     const int n_tiles = n_local + U + n_hca;
+    const int G = NH * n_tiles;
     auto tile_at = [&](int i) {
         TcTile ti;
         if (i < n_local) {
@@ -293,24 +270,37 @@ __global__ void __launch_bounds__(NTHR, 1)
     if (warp == 0) {
         // ============================ TMA producer ============================
         if (lane == 0) {
-            mbar_arrive_expect_tx(&bars[B_QFULL], Q_BYTES);
-            tma_load_4d(Qs, &tm_q, &bars[B_QFULL], 0, h0, (int)q0, (int)b);
-            tma_load_4d(Qs + Q_HALF, &tm_q, &bars[B_QFULL], 64, h0, (int)q0, (int)b);
-            int j = 0;
-            for (; j < n_tiles; ++j) {
-                const int st = j % NS;
-                if (j >= NS && !mbar_wait(&bars[B_KVEMPTY + st], ((j / NS) - 1) & 1, abort_f)) break;
-                const TcTile ti = tile_at(j);
-                const CUtensorMap* m = ti.stream == 2 ? &tm_h : &tm_c;
-                unsigned char* dst = KVs + st * KV_BYTES;
-                mbar_arrive_expect_tx(&bars[B_KVFULL + st], KV_BYTES);
-                tma_load_3d(dst, m, &bars[B_KVFULL + st], 0, (int)ti.row0, (int)b);
-                tma_load_3d(dst + KV_HALF, m, &bars[B_KVFULL + st], 64, (int)ti.row0, (int)b);
+            int g = 0, nq = 0;
+            for (int hp = 0; hp < NH && g >= 0; ++hp) {
+                const int qb = hp & 1;
+                if (hp >= 2 && !mbar_wait(&bars[B_QEMPTY + qb], ((hp >> 1) - 1) & 1, abort_f)) break;
+                mbar_arrive_expect_tx(&bars[B_QFULL + qb], Q_BYTES);
+                tma_load_4d(Qs + qb * Q_BYTES, &tm_q, &bars[B_QFULL + qb], 0, hp * HPG, (int)q0, (int)b);
+                tma_load_4d(Qs + qb * Q_BYTES + Q_HALF, &tm_q, &bars[B_QFULL + qb], 64, hp * HPG, (int)q0, (int)b);
+                ++nq;
+                bool stop = false;
+                for (int j = 0; j < n_tiles; ++j, ++g) {
+                    const int st = g % NS;
+                    if (g >= NS && !mbar_wait(&bars[B_KVEMPTY + st], ((g / NS) - 1) & 1, abort_f)) {
+                        stop = true;
+                        break;
+                    }
+                    const TcTile ti = tile_at(j);
+                    const CUtensorMap* m = ti.stream == 2 ? &tm_h : &tm_c;
+                    unsigned char* dst = KVs + st * KV_BYTES;
+                    mbar_arrive_expect_tx(&bars[B_KVFULL + st], KV_BYTES);
+                    tma_load_3d(dst, m, &bars[B_KVFULL + st], 0, (int)ti.row0, (int)b);
+                    tma_load_3d(dst + KV_HALF, m, &bars[B_KVFULL + st], 64, (int)ti.row0, (int)b);
+                }
+                if (stop) break;
             }
             // every copy issued has landed before the CTA may exit
-            mbar_wait(&bars[B_QFULL], 0, nullptr);
-            for (int s = 0; s < NS && s < j; ++s) {
-                const int last = ((j - 1 - s) / NS) * NS + s;
+            for (int qb = 0; qb < 2 && qb < nq; ++qb) {
+                const int last = ((nq - 1 - qb) / 2) * 2 + qb;
+                mbar_wait(&bars[B_QFULL + qb], (last >> 1) & 1, nullptr);
+            }
+            for (int s = 0; s < NS && s < g; ++s) {
+                const int last = ((g - 1 - s) / NS) * NS + s;
                 mbar_wait(&bars[B_KVFULL + s], (last / NS) & 1, nullptr);
             }
         }
@@ -320,39 +310,45 @@ __global__ void __launch_bounds__(NTHR, 1)
         if (lane == 0) {
             constexpr uint32_t ID_QK = idesc_f16(ROWS, KT, BF, false, false);
             constexpr uint32_t ID_PV = idesc_f16(ROWS, DCX, BF, false, true);
-            const uint32_t qa = smem_addr(Qs), kva = smem_addr(KVs), pa = smem_addr(Ps);
-            if (mbar_wait(&bars[B_QFULL], 0, abort_f)) {
-                tc_fence_after();
-                for (int j = 0; j <= n_tiles; ++j) {
-                    if (j < n_tiles) {
-                        const int st = j % NS, sb = j & 1;
-                        if (!mbar_wait(&bars[B_KVFULL + st], (j / NS) & 1, abort_f)) break;
-                        if (j >= 2 && !mbar_wait(&bars[B_SFREE + sb], ((j >> 1) - 1) & 1, abort_f)) break;
-                        tc_fence_after();
+            const uint32_t qa0 = smem_addr(Qs), kva = smem_addr(KVs);
+            int hp = 0, j = 0;          // coordinates of tile g (QK)
+            int ihp = 0, ij = 0;        // coordinates of tile g - 1 (PV)
+            (void)ihp;
+            for (int g = 0; g <= G; ++g) {
+                if (g < G) {
+                    const int st = g % NS, sb = g & 1, qb = hp & 1;
+                    if (j == 0 && !mbar_wait(&bars[B_QFULL + qb], (hp >> 1) & 1, abort_f)) break;
+                    if (!mbar_wait(&bars[B_KVFULL + st], (g / NS) & 1, abort_f)) break;
+                    tc_fence_after();
+                    const uint32_t qa = qa0 + qb * Q_BYTES;
 #pragma unroll
-                        for (int k = 0; k < DCX / 16; ++k) {
-                            const uint64_t ad = sdesc_sw128(qa + (k >> 2) * Q_HALF + (k & 3) * 32, 16, 1024);
-                            const uint64_t bd =
-                                sdesc_sw128(kva + st * KV_BYTES + (k >> 2) * KV_HALF + (k & 3) * 32, 16, 1024);
-                            umma_f16_ss(tmem + COL_S + sb * KT, ad, bd, ID_QK, k > 0 ? 1u : 0u);
-                        }
-                        umma_commit(&bars[B_SFULL + sb]);
+                    for (int k = 0; k < DCX / 16; ++k) {
+                        const uint64_t ad = sdesc_sw128(qa + (k >> 2) * Q_HALF + (k & 3) * 32, 16, 1024);
+                        const uint64_t bd =
+                            sdesc_sw128(kva + st * KV_BYTES + (k >> 2) * KV_HALF + (k & 3) * 32, 16, 1024);
+                        umma_f16_ss(tmem + COL_S + sb * KT, ad, bd, ID_QK, k > 0 ? 1u : 0u);
                     }
-                    if (j >= 1) {
-                        const int i = j - 1, st = i % NS, sb = i & 1;
-                        if (!mbar_wait(&bars[B_PFULL + sb], (i >> 1) & 1, abort_f)) break;
-                        tc_fence_after();
-                        const TcTile ti = tile_at(i);
-                        const uint32_t dst = tmem + COL_O + ti.stream * DCX;
+                    umma_commit(&bars[B_SFULL + sb]);
+                    if (j == n_tiles - 1) umma_commit(&bars[B_QEMPTY + qb]);
+                }
+                if (g >= 1) {
+                    const int i = g - 1, st = i % NS, sb = i & 1;
+                    if (!mbar_wait(&bars[B_PFULL + sb], (i >> 1) & 1, abort_f)) break;
+                    tc_fence_after();
+                    const TcTile ti = tile_at(ij);
+                    const uint32_t dst = tmem + COL_O + ti.stream * DCX;
 #pragma unroll
-                        for (int k = 0; k < KT / 16; ++k) {
-                            const uint64_t ad = sdesc_sw128(pa + sb * P_BYTES + k * 32, 16, 1024);
-                            const uint64_t bd = sdesc_sw128(kva + st * KV_BYTES + k * 2048, KV_HALF, 1024);
-                            umma_f16_ss(dst, ad, bd, ID_PV, (k > 0 || !ti.first) ? 1u : 0u);
-                        }
-                        umma_commit(&bars[B_KVEMPTY + st]);
-                        umma_commit(&bars[B_ODONE]);
+                    for (int k = 0; k < KT / 16; ++k) {
+                        const uint64_t bd = sdesc_sw128(kva + st * KV_BYTES + k * 2048, KV_HALF, 1024);
+                        umma_f16_ts(dst, tmem + COL_S + sb * KT + k * 8, bd, ID_PV, (k > 0 || !ti.first) ? 1u : 0u);
                     }
+                    umma_commit(&bars[B_KVEMPTY + st]);
+                    umma_commit(&bars[B_ODONE + sb]);
+                    if (++ij == n_tiles) ij = 0;
+                }
+                if (g < G && ++j == n_tiles) {
+                    j = 0;
+                    ++hp;
                 }
             }
             // every MMA issued has completed before TMEM is freed
@@ -366,125 +362,167 @@ __global__ void __launch_bounds__(NTHR, 1)
         const int rid = q4 * 32 + lane;
         const int t = rid >> 1, hh = rid & 1;
         const bool rvalid = t < nt;
-        const int64_t pos = P0 + t;
+        // positions fit in 32 bits (Lkv < 2^31 on this path)
+        const int pos = (int)(P0 + t);
+        const int lkv = (int)a.Lkv;
         const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
-        unsigned char* prow = Ps + (rid >> 3) * 1024 + (rid & 7) * 128;
-        const int sw = rid & 7;
-        const int64_t lo_p = pos - a.window + 1 > 0 ? pos - a.window + 1 : 0;
-        const int64_t sink_end = a.n_sinks < lo_p ? a.n_sinks : lo_p;
-        int64_t nv_hca = 0;
+        const int lo_p = pos - a.window + 1 > 0 ? pos - a.window + 1 : 0;
+        const int sink_end = a.n_sinks < lo_p ? a.n_sinks : lo_p;
+        const int sp_end = pos + 1 < lkv ? pos + 1 : lkv;
+        int nv_hca = 0;
         if (pos >= a.hca_r - 1) {
             nv_hca = (pos + 1) / a.hca_r;
-            if (nv_hca > a.NC) nv_hca = a.NC;
+            if (nv_hca > a.NC) nv_hca = (int)a.NC;
         }
-        float lsum0 = 0.f, lsum1 = 0.f, lsum2 = 0.f;
-        float m_cur = -INFINITY, l_cur = 0.f;
-        int cur = -1;
+        const unsigned long long tbit = 1ull << t;
+        const T* ckv = static_cast<const T*>(a.ckv) + b * a.sc[0];
+        auto clampk = [](int x) { return x < 0 ? 0 : (x > KT ? KT : x); };
         bool ok = true;
-        for (int j = 0; j < n_tiles; ++j) {
-            const int sb = j & 1;
-            const TcTile ti = tile_at(j);
-            if (ti.stream != cur) {
-                if (cur == 0) lsum0 = l_cur;
-                else if (cur == 1) lsum1 = l_cur;
-                m_cur = -INFINITY;
-                l_cur = 0.f;
-                cur = ti.stream;
-            }
-            // valid columns of this row: [a1, b1) and the sinks [0, b2)
-            int a1 = 0, b1 = 0, b2 = 0;
-            if (rvalid) {
-                if (ti.stream == 0) {
-                    a1 = clamp64(lo_p - ti.row0);
-                    b1 = clamp64(pos - ti.row0 + 1);
-                    b2 = clamp64(sink_end - ti.row0);
-                } else if (ti.stream == 1) {
-                    if ((umask[ti.u] >> t) & 1ull) b1 = clamp64((pos + 1 < a.Lkv ? pos + 1 : a.Lkv) - ti.row0);
+        int g = 0;
+        for (int hp = 0; hp < NH && ok; ++hp) {
+            float lsum0 = 0.f, lsum1 = 0.f, lsum2 = 0.f;
+            float m_cur = -INFINITY, l_cur = 0.f;
+            int cur = -1;
+            for (int j = 0; j < n_tiles; ++j, ++g) {
+                const int sb = g & 1;
+                // tile j: stream and first row (int32)
+                int stream, row0;
+                if (j < n_local) {
+                    stream = 0;
+                    row0 = sink_tile ? (j == 0 ? 0 : (int)ws + (j - 1) * KT) : (int)ws + j * KT;
+                } else if (j < n_local + U) {
+                    stream = 1;
+                    row0 = ulist[j - n_local] * KT;
                 } else {
-                    b1 = clamp64(nv_hca - ti.row0);
+                    stream = 2;
+                    row0 = (j - n_local - U) * KT;
                 }
-            }
-            ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_SFULL + sb], (j >> 1) & 1, abort_f));
-            if (!ok) break;
-            tc_fence_after();
-            uint32_t s[64];
-            tmem_ld32(tmem + lane_base + COL_S + sb * KT, s);
-            tmem_ld32(tmem + lane_base + COL_S + sb * KT + 32, s + 32);
-            tmem_wait_ld();
-            tc_fence_before();
-            mbar_arrive(&bars[B_SFREE + sb]);
-            float mx = -INFINITY;
-#pragma unroll
-            for (int c = 0; c < KT; ++c) {
-                const bool v = (c >= a1 && c < b1) || c < b2;
-                const float x = v ? __uint_as_float(s[c]) * LOG2E : -INFINITY;
-                s[c] = __float_as_uint(x);
-                mx = fmaxf(mx, x);
-            }
-            float fac = 1.f;
-            bool resc = false;
-            if (mx != -INFINITY) {
-                if (m_cur == -INFINITY) {
-                    m_cur = mx;
-                } else if (mx > m_cur + RESCALE_T) {
-                    fac = ex2(m_cur - mx);
-                    m_cur = mx;
-                    resc = true;
+                if (stream != cur) {
+                    if (cur == 0) lsum0 = l_cur;
+                    else if (cur == 1) lsum1 = l_cur;
+                    m_cur = -INFINITY;
+                    l_cur = 0.f;
+                    cur = stream;
                 }
-            }
-            const float mu = m_cur == -INFINITY ? 0.f : m_cur;
-            float psum = 0.f;
-            uint32_t pk[32];
-#pragma unroll
-            for (int c = 0; c < KT; c += 2) {
-                const float p0 = ex2(__uint_as_float(s[c]) - mu);
-                const float p1 = ex2(__uint_as_float(s[c + 1]) - mu);
-                psum += p0 + p1;
-                pk[c >> 1] = pack2<T>(p0, p1);
-            }
-            l_cur = l_cur * fac + psum;
-            // PV of the previous tile done: its P buffer and O are free to touch
-            if (j >= 1) {
-                ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_ODONE], (j - 1) & 1, abort_f));
+                // valid columns of this row: [a1, b1) and the sinks [0, b2)
+                int a1 = 0, b1 = 0, b2 = 0;
+                if (rvalid) {
+                    if (stream == 0) {
+                        a1 = clampk(lo_p - row0);
+                        b1 = clampk(pos - row0 + 1);
+                        b2 = clampk(sink_end - row0);
+                    } else if (stream == 1) {
+                        if (umask[j - n_local] & tbit) b1 = clampk(sp_end - row0);
+                    } else {
+                        b1 = clampk(nv_hca - row0);
+                    }
+                }
+                const bool full = a1 == 0 && b1 == KT;
+                ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_SFULL + sb], (g >> 1) & 1, abort_f));
                 if (!ok) break;
-            }
-            unsigned char* pdst = prow + sb * P_BYTES;
-#pragma unroll
-            for (int cc = 0; cc < 8; ++cc) {
-                *reinterpret_cast<uint4*>(pdst + ((cc ^ sw) << 4)) =
-                    make_uint4(pk[4 * cc], pk[4 * cc + 1], pk[4 * cc + 2], pk[4 * cc + 3]);
-            }
-            if (__any_sync(0xffffffffu, resc)) {
                 tc_fence_after();
-                const uint32_t to = tmem + lane_base + COL_O + ti.stream * DCX;
+                const uint32_t ts = tmem + lane_base + COL_S + sb * KT;
+                uint32_t s[64];
+                tmem_ld32(ts, s);
+                tmem_ld32(ts + 32, s + 32);
+                tmem_wait_ld();
+                // raw-score maximum of the valid columns (8 independent chains)
+                float m8[8];
 #pragma unroll
-                for (int cc = 0; cc < DCX / 32; ++cc) {
-                    uint32_t o[32];
-                    tmem_ld32(to + cc * 32, o);
-                    tmem_wait_ld();
+                for (int i = 0; i < 8; ++i) m8[i] = -INFINITY;
+                if (__all_sync(0xffffffffu, full)) {
 #pragma unroll
-                    for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * fac);
-                    tmem_st32(to + cc * 32, o);
+                    for (int c = 0; c < KT; ++c) m8[c & 7] = fmaxf(m8[c & 7], __uint_as_float(s[c]));
+                } else {
+#pragma unroll
+                    for (int c = 0; c < KT; ++c) {
+                        const bool v = (c >= a1 && c < b1) || c < b2;
+                        const float x = v ? __uint_as_float(s[c]) : -INFINITY;
+                        s[c] = __float_as_uint(x);
+                        m8[c & 7] = fmaxf(m8[c & 7], x);
+                    }
+                }
+                const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                                       fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7]))) * LOG2E;
+                float fac = 1.f;
+                bool resc = false;
+                if (mx != -INFINITY) {
+                    if (m_cur == -INFINITY) {
+                        m_cur = mx;
+                    } else if (mx > m_cur + RESCALE_T) {
+                        fac = ex2(m_cur - mx);
+                        m_cur = mx;
+                        resc = true;
+                    }
+                }
+                const float nmu = m_cur == -INFINITY ? 0.f : -m_cur;
+                float ps[4] = {0.f, 0.f, 0.f, 0.f};
+                uint32_t pk[32];
+#pragma unroll
+                for (int c = 0; c < KT; c += 2) {
+                    const float p0 = ex2(fmaf(__uint_as_float(s[c]), LOG2E, nmu));
+                    const float p1 = ex2(fmaf(__uint_as_float(s[c + 1]), LOG2E, nmu));
+                    ps[(c >> 1) & 3] += p0 + p1;
+                    pk[c >> 1] = pack2<T>(p0, p1);
+                }
+                l_cur = l_cur * fac + ((ps[0] + ps[1]) + (ps[2] + ps[3]));
+                tmem_st32(ts, pk);  // P over the first 32 columns of the S buffer
+                if (__any_sync(0xffffffffu, resc)) {
+                    // every PV so far (the latest: tile g-1) has completed before O is rescaled
+                    if (g >= 1) {
+                        ok = __all_sync(0xffffffffu,
+                                        mbar_wait(&bars[B_ODONE + ((g - 1) & 1)], ((g - 1) >> 1) & 1, abort_f));
+                        if (!ok) break;
+                    }
+                    tc_fence_after();
+                    const uint32_t to = tmem + lane_base + COL_O + stream * DCX;
+#pragma unroll
+                    for (int cc = 0; cc < DCX / 32; ++cc) {
+                        uint32_t o[32];
+                        tmem_ld32(to + cc * 32, o);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * fac);
+                        tmem_st32(to + cc * 32, o);
+                    }
                 }
                 tmem_wait_st();
+                tc_fence_before();
+                mbar_arrive(&bars[B_PFULL + sb]);
             }
-            fence_proxy_async_smem();
-            tc_fence_before();
-            mbar_arrive(&bars[B_PFULL + sb]);
-        }
-        if (cur == 0) lsum0 = l_cur;
-        else if (cur == 1) lsum1 = l_cur;
-        else if (cur == 2) lsum2 = l_cur;
-        if (ok && n_tiles > 0) ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_ODONE], (n_tiles - 1) & 1, abort_f));
-        if (ok) {
+            if (!ok) break;
+            if (cur == 0) lsum0 = l_cur;
+            else if (cur == 1) lsum1 = l_cur;
+            else if (cur == 2) lsum2 = l_cur;
+            // ------------------------- epilogue of head pair hp ------------------
+            // the last two PVs of the head pair (tiles g-2, g-1) have completed
+            if (g >= 2)
+                ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_ODONE + (g & 1)], ((g - 2) >> 1) & 1, abort_f));
+            if (ok)
+                ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_ODONE + ((g - 1) & 1)], ((g - 1) >> 1) & 1, abort_f));
+            if (!ok) break;
             tc_fence_after();
-            const float g0 = gsm[rid * 3 + 0], g1 = gsm[rid * 3 + 1], g2 = gsm[rid * 3 + 2];
+            const int h = hp * HPG + hh;
+            float g0 = 0.f, g1 = 0.f, g2 = 0.f;
+            if (rvalid) {
+                const T* gp = static_cast<const T*>(a.gate);
+                const T* gr = a.gate4d ? gp + b * a.sg[0] + h * a.sg[1] + (q0 + t) * a.sg[2]
+                                       : gp + b * a.sg[0] + (q0 + t) * a.sg[1];
+                const int64_t gs = a.gate4d ? a.sg[3] : a.sg[2];
+                g0 = Cvt<T>::to_f(gr[0]);
+                g1 = Cvt<T>::to_f(gr[gs]);
+                g2 = Cvt<T>::to_f(gr[2 * gs]);
+                const float m = fmaxf(g0, fmaxf(g1, g2));
+                const float e0 = expf(g0 - m), e1 = expf(g1 - m), e2 = expf(g2 - m);
+                const float inv = 1.f / (e0 + e1 + e2);
+                g0 = e0 * inv;
+                g1 = e1 * inv;
+                g2 = e2 * inv;
+            }
             const bool u0 = lsum0 > 0.f, u1 = lsum1 > 0.f, u2 = lsum2 > 0.f;
             const float f0 = u0 ? g0 / lsum0 : 0.f, f1 = u1 ? g1 / lsum1 : 0.f, f2 = u2 ? g2 / lsum2 : 0.f;
             const bool early = rvalid && pos < a.hca_r - 1;  // HCA: mean of the latent prefix
-            const T* ckv = static_cast<const T*>(a.ckv) + b * a.sc[0];
-            T* orow = static_cast<T*>(a.out) + b * a.so[0] + (q0 + (rvalid ? t : 0)) * a.so[1] +
-                      (int64_t)(h0 + hh) * a.so[2];
+            T* orow = static_cast<T*>(a.out) + b * a.so[0] + (q0 + (rvalid ? t : 0)) * a.so[1] + (int64_t)h * a.so[2];
             const uint32_t to = tmem + lane_base + COL_O;
 #pragma unroll 1
             for (int cc = 0; cc < DCX / 32; ++cc) {
@@ -512,12 +550,16 @@ __global__ void __launch_bounds__(NTHR, 1)
                 if (rvalid) {
 #pragma unroll
                     for (int e8 = 0; e8 < 4; ++e8) {
-                        uint4 w4 = make_uint4(pack2<T>(v[8 * e8 + 0], v[8 * e8 + 1]), pack2<T>(v[8 * e8 + 2], v[8 * e8 + 3]),
-                                              pack2<T>(v[8 * e8 + 4], v[8 * e8 + 5]), pack2<T>(v[8 * e8 + 6], v[8 * e8 + 7]));
+                        uint4 w4 = make_uint4(pack2<T>(v[8 * e8 + 0], v[8 * e8 + 1]),
+                                              pack2<T>(v[8 * e8 + 2], v[8 * e8 + 3]),
+                                              pack2<T>(v[8 * e8 + 4], v[8 * e8 + 5]),
+                                              pack2<T>(v[8 * e8 + 6], v[8 * e8 + 7]));
                         *reinterpret_cast<uint4*>(orow + cc * 32 + 8 * e8) = w4;
                     }
                 }
             }
+            // the next head pair's PVs overwrite O: every TMEM read above is complete
+            tc_fence_before();
         }
     }
     tc_fence_before();
@@ -609,7 +651,7 @@ int sa_attention_tc(SaArgs& a, int64_t B, int dtype, cudaStream_t s) {
             mh = mc;  // no HCA tiles are scheduled
         }
     }
-    dim3 grid((unsigned)(a.H / HPG), (unsigned)ceil_div(a.Lq, QT), (unsigned)B);
+    dim3 grid((unsigned)ceil_div(a.Lq, QT), (unsigned)B);
     if (dtype == MABA_BF16) {
         auto kern = sa_attention_tc_kernel<__nv_bfloat16>;
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

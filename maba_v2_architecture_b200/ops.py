@@ -478,10 +478,15 @@ def b200_sa_attention_decode_at(qhat, c_cache, hca_table, top_idx, gate_logits, 
 
 
 def absorb_queries(q: torch.Tensor, w_uk: torch.Tensor, n_heads: int, scale: float) -> torch.Tensor:
-    """qhat[b,t,h,:] = scale * W_uk,h^T q[b,t,h,:] with W_uk = k_up_proj.weight [H*dh, d_c]."""
+    """qhat[b,t,h,:] = scale * W_uk,h^T q[b,t,h,:] with W_uk = k_up_proj.weight [H*dh, d_c].
+
+    One batched GEMM over the heads with the scale folded into the (small) weight;
+    the result is a [B, L, H, d_c] view of an [H, B*L, d_c] buffer (the attention
+    kernels take strided queries), so no layout copy follows the GEMM."""
     B, L, H, dh = q.shape
-    w = w_uk.view(n_heads, dh, -1).to(q.dtype)
-    return torch.einsum("blhd,hdc->blhc", q, w) * scale
+    w = (w_uk.view(n_heads, dh, -1).float() * scale).to(q.dtype)
+    qh = torch.bmm(q.reshape(B * L, H, dh).transpose(0, 1), w)
+    return qh.view(H, B, L, -1).permute(1, 2, 0, 3)
 
 
 def expand_values(o_lat: torch.Tensor, w_uv: torch.Tensor, n_heads: int) -> torch.Tensor:
