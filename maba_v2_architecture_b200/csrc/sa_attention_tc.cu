@@ -10,11 +10,12 @@
 // row m = 2 t + h) over one tile schedule built once per CTA.  The tiles of
 // all head pairs form one sequence g = hp * n_tiles + j, so every pipeline
 // barrier's phases simply count g.
-//  * warp 0 (one lane): TMA producer -- the Q tile of each head pair into one
+//  * warp 0: TMA producer -- the Q tile of each head pair into one
 //    of two buffers (box 64 x 2 heads x 64 tokens, two 64-wide halves of d_c),
 //    and every latent key tile into a 4-stage ring (box 64 rows x 64 columns,
 //    twice); all with 128-byte swizzle;
-//  * warp 1: allocates the 512 TMEM columns; one lane issues the MMAs:
+//  * warp 1: allocates the 512 TMEM columns and issues the MMAs (whole warp
+//    runs the loop, one elected lane issues):
 //    S = Q K^T (M=128, N=64, K=128; K-major A and B) into one of two TMEM S
 //    buffers, and O_s += P V (M=128, N=128, K=64; A = P read from TMEM,
 //    B = the same key tile read MN-major) into the TMEM accumulator of the
@@ -101,13 +102,6 @@ template <> __device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi
     __half2 v = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&v);
 }
-
-struct TcTile {
-    int stream;    // 0 local, 1 sparse, 2 hca
-    int64_t row0;  // first row in the source table
-    int u;         // union slot (sparse)
-    bool first;    // first tile of its stream
-};
 
 template <typename T>
 __global__ void __launch_bounds__(NTHR, 1)
@@ -245,117 +239,114 @@ __global__ void __launch_bounds__(NTHR, 1)
     const int n_hca = (int)((nhca_max + KT - 1) / KT);
     const int n_tiles = n_local + U + n_hca;
     const int G = NH * n_tiles;
-    auto tile_at = [&](int i) {
-        TcTile ti;
-        if (i < n_local) {
-            ti.stream = 0;
-            ti.row0 = sink_tile ? (i == 0 ? 0 : ws + (int64_t)(i - 1) * KT) : ws + (int64_t)i * KT;
-            ti.u = -1;
-            ti.first = i == 0;
-        } else if (i < n_local + U) {
-            ti.stream = 1;
-            ti.u = i - n_local;
-            ti.row0 = (int64_t)ulist[ti.u] * KT;
-            ti.first = ti.u == 0;
-        } else {
-            ti.stream = 2;
-            ti.row0 = (int64_t)(i - n_local - U) * KT;
-            ti.u = -1;
-            ti.first = i == n_local + U;
-        }
-        return ti;
-    };
     constexpr bool BF = std::is_same<T, __nv_bfloat16>::value;
 
     if (warp == 0) {
         // ============================ TMA producer ============================
-        if (lane == 0) {
-            int g = 0, nq = 0;
-            for (int hp = 0; hp < NH && g >= 0; ++hp) {
-                const int qb = hp & 1;
-                if (hp >= 2 && !mbar_wait(&bars[B_QEMPTY + qb], ((hp >> 1) - 1) & 1, abort_f)) break;
+        // The whole warp runs the loop (warp-uniform coordinates and waits); one
+        // elected lane issues the copies.
+        int g = 0, nq = 0;
+        bool okp = true;
+        for (int hp = 0; hp < NH && okp; ++hp) {
+            const int qb = hp & 1;
+            if (hp >= 2) okp = mbar_wait_warp(&bars[B_QEMPTY + qb], ((hp >> 1) - 1) & 1, abort_f);
+            if (!okp) break;
+            if (elect_one()) {
                 mbar_arrive_expect_tx(&bars[B_QFULL + qb], Q_BYTES);
                 tma_load_4d(Qs + qb * Q_BYTES, &tm_q, &bars[B_QFULL + qb], 0, hp * HPG, (int)q0, (int)b);
                 tma_load_4d(Qs + qb * Q_BYTES + Q_HALF, &tm_q, &bars[B_QFULL + qb], 64, hp * HPG, (int)q0, (int)b);
-                ++nq;
-                bool stop = false;
-                for (int j = 0; j < n_tiles; ++j, ++g) {
-                    const int st = g % NS;
-                    if (g >= NS && !mbar_wait(&bars[B_KVEMPTY + st], ((g / NS) - 1) & 1, abort_f)) {
-                        stop = true;
-                        break;
-                    }
-                    const TcTile ti = tile_at(j);
-                    const CUtensorMap* m = ti.stream == 2 ? &tm_h : &tm_c;
-                    unsigned char* dst = KVs + st * KV_BYTES;
-                    mbar_arrive_expect_tx(&bars[B_KVFULL + st], KV_BYTES);
-                    tma_load_3d(dst, m, &bars[B_KVFULL + st], 0, (int)ti.row0, (int)b);
-                    tma_load_3d(dst + KV_HALF, m, &bars[B_KVFULL + st], 64, (int)ti.row0, (int)b);
+            }
+            __syncwarp();
+            ++nq;
+            for (int j = 0; j < n_tiles; ++j, ++g) {
+                const int st = g % NS;
+                if (g >= NS) okp = mbar_wait_warp(&bars[B_KVEMPTY + st], ((g / NS) - 1) & 1, abort_f);
+                if (!okp) break;
+                int row0, hcat;
+                if (j < n_local) {
+                    hcat = 0;
+                    row0 = sink_tile ? (j == 0 ? 0 : (int)ws + (j - 1) * KT) : (int)ws + j * KT;
+                } else if (j < n_local + U) {
+                    hcat = 0;
+                    row0 = ulist[j - n_local] * KT;
+                } else {
+                    hcat = 1;
+                    row0 = (j - n_local - U) * KT;
                 }
-                if (stop) break;
-            }
-            // every copy issued has landed before the CTA may exit
-            for (int qb = 0; qb < 2 && qb < nq; ++qb) {
-                const int last = ((nq - 1 - qb) / 2) * 2 + qb;
-                mbar_wait(&bars[B_QFULL + qb], (last >> 1) & 1, nullptr);
-            }
-            for (int s = 0; s < NS && s < g; ++s) {
-                const int last = ((g - 1 - s) / NS) * NS + s;
-                mbar_wait(&bars[B_KVFULL + s], (last / NS) & 1, nullptr);
+                const CUtensorMap* m = hcat ? &tm_h : &tm_c;
+                unsigned char* dst = KVs + st * KV_BYTES;
+                if (elect_one()) {
+                    mbar_arrive_expect_tx(&bars[B_KVFULL + st], KV_BYTES);
+                    tma_load_3d(dst, m, &bars[B_KVFULL + st], 0, row0, (int)b);
+                    tma_load_3d(dst + KV_HALF, m, &bars[B_KVFULL + st], 64, row0, (int)b);
+                }
+                __syncwarp();
             }
         }
-        __syncwarp();
+        // every copy issued has landed before the CTA may exit
+        for (int qb = 0; qb < 2 && qb < nq; ++qb) {
+            const int last = ((nq - 1 - qb) / 2) * 2 + qb;
+            mbar_wait_warp(&bars[B_QFULL + qb], (last >> 1) & 1, nullptr);
+        }
+        for (int s = 0; s < NS && s < g; ++s) {
+            const int last = ((g - 1 - s) / NS) * NS + s;
+            mbar_wait_warp(&bars[B_KVFULL + s], (last / NS) & 1, nullptr);
+        }
     } else if (warp == 1) {
         // ============================ MMA issuer ==============================
-        if (lane == 0) {
-            constexpr uint32_t ID_QK = idesc_f16(ROWS, KT, BF, false, false);
-            constexpr uint32_t ID_PV = idesc_f16(ROWS, DCX, BF, false, true);
-            const uint32_t qa0 = smem_addr(Qs), kva = smem_addr(KVs);
-            int hp = 0, j = 0;          // coordinates of tile g (QK)
-            int ihp = 0, ij = 0;        // coordinates of tile g - 1 (PV)
-            (void)ihp;
-            for (int g = 0; g <= G; ++g) {
-                if (g < G) {
-                    const int st = g % NS, sb = g & 1, qb = hp & 1;
-                    if (j == 0 && !mbar_wait(&bars[B_QFULL + qb], (hp >> 1) & 1, abort_f)) break;
-                    if (!mbar_wait(&bars[B_KVFULL + st], (g / NS) & 1, abort_f)) break;
-                    tc_fence_after();
-                    const uint32_t qa = qa0 + qb * Q_BYTES;
+        // The whole warp runs the loop; the descriptors are warp-uniform and one
+        // elected lane issues each MMA / commit.  Descriptor bases are built once:
+        // a start address moves by adding (bytes >> 4) to the descriptor.
+        constexpr uint32_t ID_QK = idesc_f16(ROWS, KT, BF, false, false);
+        constexpr uint32_t ID_PV = idesc_f16(ROWS, DCX, BF, false, true);
+        const uint64_t qd0 = sdesc_sw128(smem_addr(Qs), 16, 1024);
+        const uint64_t kd0 = sdesc_sw128(smem_addr(KVs), 16, 1024);
+        const uint64_t vd0 = sdesc_sw128(smem_addr(KVs), KV_HALF, 1024);
+        int hp = 0, j = 0, ij = 0;
+        bool okm = true;
+        for (int g = 0; g <= G; ++g) {
+            if (g < G) {
+                const int st = g % NS, sb = g & 1, qb = hp & 1;
+                if (j == 0) okm = mbar_wait_warp(&bars[B_QFULL + qb], (hp >> 1) & 1, abort_f);
+                if (okm) okm = mbar_wait_warp(&bars[B_KVFULL + st], (g / NS) & 1, abort_f);
+                if (!okm) break;
+                tc_fence_after();
+                const uint64_t qd = qd0 + (uint64_t)(qb * (Q_BYTES >> 4));
+                const uint64_t kd = kd0 + (uint64_t)(st * (KV_BYTES >> 4));
 #pragma unroll
-                    for (int k = 0; k < DCX / 16; ++k) {
-                        const uint64_t ad = sdesc_sw128(qa + (k >> 2) * Q_HALF + (k & 3) * 32, 16, 1024);
-                        const uint64_t bd =
-                            sdesc_sw128(kva + st * KV_BYTES + (k >> 2) * KV_HALF + (k & 3) * 32, 16, 1024);
-                        umma_f16_ss(tmem + COL_S + sb * KT, ad, bd, ID_QK, k > 0 ? 1u : 0u);
-                    }
-                    umma_commit(&bars[B_SFULL + sb]);
-                    if (j == n_tiles - 1) umma_commit(&bars[B_QEMPTY + qb]);
+                for (int k = 0; k < DCX / 16; ++k) {
+                    const uint32_t off_q = (k >> 2) * (Q_HALF >> 4) + (k & 3) * 2;
+                    const uint32_t off_k = (k >> 2) * (KV_HALF >> 4) + (k & 3) * 2;
+                    umma_f16_ss_elect(tmem + COL_S + sb * KT, qd + off_q, kd + off_k, ID_QK, k > 0 ? 1u : 0u);
                 }
-                if (g >= 1) {
-                    const int i = g - 1, st = i % NS, sb = i & 1;
-                    if (!mbar_wait(&bars[B_PFULL + sb], (i >> 1) & 1, abort_f)) break;
-                    tc_fence_after();
-                    const TcTile ti = tile_at(ij);
-                    const uint32_t dst = tmem + COL_O + ti.stream * DCX;
-#pragma unroll
-                    for (int k = 0; k < KT / 16; ++k) {
-                        const uint64_t bd = sdesc_sw128(kva + st * KV_BYTES + k * 2048, KV_HALF, 1024);
-                        umma_f16_ts(dst, tmem + COL_S + sb * KT + k * 8, bd, ID_PV, (k > 0 || !ti.first) ? 1u : 0u);
-                    }
-                    umma_commit(&bars[B_KVEMPTY + st]);
-                    umma_commit(&bars[B_ODONE + sb]);
-                    if (++ij == n_tiles) ij = 0;
-                }
-                if (g < G && ++j == n_tiles) {
-                    j = 0;
-                    ++hp;
-                }
+                umma_commit_elect(&bars[B_SFULL + sb]);
+                if (j == n_tiles - 1) umma_commit_elect(&bars[B_QEMPTY + qb]);
             }
-            // every MMA issued has completed before TMEM is freed
-            umma_commit(&bars[B_DRAIN]);
-            mbar_wait(&bars[B_DRAIN], 0, nullptr);
+            if (g >= 1) {
+                const int i = g - 1, st = i % NS, sb = i & 1;
+                okm = mbar_wait_warp(&bars[B_PFULL + sb], (i >> 1) & 1, abort_f);
+                if (!okm) break;
+                tc_fence_after();
+                const int stream = ij < n_local ? 0 : (ij < n_local + U ? 1 : 2);
+                const bool first = ij == 0 || ij == n_local || ij == n_local + U;
+                const uint32_t dst = tmem + COL_O + stream * DCX;
+                const uint64_t vd = vd0 + (uint64_t)(st * (KV_BYTES >> 4));
+#pragma unroll
+                for (int k = 0; k < KT / 16; ++k)
+                    umma_f16_ts_elect(dst, tmem + COL_S + sb * KT + k * 8, vd + (uint64_t)(k * (2048 >> 4)), ID_PV,
+                                      (k > 0 || !first) ? 1u : 0u);
+                umma_commit_elect(&bars[B_KVEMPTY + st]);
+                umma_commit_elect(&bars[B_ODONE + sb]);
+                if (++ij == n_tiles) ij = 0;
+            }
+            if (g < G && ++j == n_tiles) {
+                j = 0;
+                ++hp;
+            }
         }
-        __syncwarp();
+        // every MMA issued has completed before TMEM is freed
+        umma_commit_elect(&bars[B_DRAIN]);
+        mbar_wait_warp(&bars[B_DRAIN], 0, nullptr);
     } else {
         // ===================== softmax + epilogue (128 threads) ===============
         const int q4 = warp & 3;
@@ -377,6 +368,31 @@ __global__ void __launch_bounds__(NTHR, 1)
         const unsigned long long tbit = 1ull << t;
         const T* ckv = static_cast<const T*>(a.ckv) + b * a.sc[0];
         auto clampk = [](int x) { return x < 0 ? 0 : (x > KT ? KT : x); };
+        // stream of tile j and the valid columns of this row: [a1, b1) and the sinks [0, b2)
+        auto bounds = [&](int j, int& stream, int& a1, int& b1, int& b2) {
+            a1 = 0;
+            b1 = 0;
+            b2 = 0;
+            if (j < n_local) {
+                stream = 0;
+                const int row0 = sink_tile ? (j == 0 ? 0 : (int)ws + (j - 1) * KT) : (int)ws + j * KT;
+                if (rvalid) {
+                    a1 = clampk(lo_p - row0);
+                    b1 = clampk(pos - row0 + 1);
+                    b2 = clampk(sink_end - row0);
+                }
+            } else if (j < n_local + U) {
+                stream = 1;
+                const int u = j - n_local;
+                const int row0 = ulist[u] * KT;
+                if (rvalid && (umask[u] & tbit)) b1 = clampk(sp_end - row0);
+            } else {
+                stream = 2;
+                if (rvalid) b1 = clampk(nv_hca - (j - n_local - U) * KT);
+            }
+        };
+        int nstream = 0, na1 = 0, nb1 = 0, nb2 = 0;
+        bounds(0, nstream, na1, nb1, nb2);
         bool ok = true;
         int g = 0;
         for (int hp = 0; hp < NH && ok; ++hp) {
@@ -385,18 +401,7 @@ __global__ void __launch_bounds__(NTHR, 1)
             int cur = -1;
             for (int j = 0; j < n_tiles; ++j, ++g) {
                 const int sb = g & 1;
-                // tile j: stream and first row (int32)
-                int stream, row0;
-                if (j < n_local) {
-                    stream = 0;
-                    row0 = sink_tile ? (j == 0 ? 0 : (int)ws + (j - 1) * KT) : (int)ws + j * KT;
-                } else if (j < n_local + U) {
-                    stream = 1;
-                    row0 = ulist[j - n_local] * KT;
-                } else {
-                    stream = 2;
-                    row0 = (j - n_local - U) * KT;
-                }
+                const int stream = nstream, a1 = na1, b1 = nb1, b2 = nb2;
                 if (stream != cur) {
                     if (cur == 0) lsum0 = l_cur;
                     else if (cur == 1) lsum1 = l_cur;
@@ -404,46 +409,41 @@ __global__ void __launch_bounds__(NTHR, 1)
                     l_cur = 0.f;
                     cur = stream;
                 }
-                // valid columns of this row: [a1, b1) and the sinks [0, b2)
-                int a1 = 0, b1 = 0, b2 = 0;
-                if (rvalid) {
-                    if (stream == 0) {
-                        a1 = clampk(lo_p - row0);
-                        b1 = clampk(pos - row0 + 1);
-                        b2 = clampk(sink_end - row0);
-                    } else if (stream == 1) {
-                        if (umask[j - n_local] & tbit) b1 = clampk(sp_end - row0);
-                    } else {
-                        b1 = clampk(nv_hca - row0);
-                    }
-                }
-                const bool full = a1 == 0 && b1 == KT;
-                ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_SFULL + sb], (g >> 1) & 1, abort_f));
+                ok = mbar_wait_warp(&bars[B_SFULL + sb], (g >> 1) & 1, abort_f);
                 if (!ok) break;
                 tc_fence_after();
                 const uint32_t ts = tmem + lane_base + COL_S + sb * KT;
                 uint32_t s[64];
                 tmem_ld32(ts, s);
                 tmem_ld32(ts + 32, s + 32);
-                tmem_wait_ld();
-                // raw-score maximum of the valid columns (8 independent chains)
+                // next tile's bounds while the load is in flight
+                bounds(j + 1 < n_tiles ? j + 1 : 0, nstream, na1, nb1, nb2);
+                tmem_wait_ld_pin64(s);
+                // row class: none (no valid column), full (all 64), or partial
+                const bool none = b1 <= a1 && b2 == 0;
+                const bool full = a1 == 0 && b1 == KT;
                 float m8[8];
 #pragma unroll
                 for (int i = 0; i < 8; ++i) m8[i] = -INFINITY;
-                if (__all_sync(0xffffffffu, full)) {
-#pragma unroll
-                    for (int c = 0; c < KT; ++c) m8[c & 7] = fmaxf(m8[c & 7], __uint_as_float(s[c]));
-                } else {
+                if (__any_sync(0xffffffffu, !none && !full)) {
+                    unsigned long long vm = 0ull;
+                    if (b1 > a1) vm = (b1 >= 64 ? ~0ull : ((1ull << b1) - 1ull)) & ~((1ull << a1) - 1ull);
+                    if (b2 > 0) vm |= b2 >= 64 ? ~0ull : ((1ull << b2) - 1ull);
+                    const uint32_t vlo = (uint32_t)vm, vhi = (uint32_t)(vm >> 32);
 #pragma unroll
                     for (int c = 0; c < KT; ++c) {
-                        const bool v = (c >= a1 && c < b1) || c < b2;
+                        const bool v = ((c < 32 ? vlo : vhi) >> (c & 31)) & 1u;
                         const float x = v ? __uint_as_float(s[c]) : -INFINITY;
                         s[c] = __float_as_uint(x);
                         m8[c & 7] = fmaxf(m8[c & 7], x);
                     }
+                } else {
+#pragma unroll
+                    for (int c = 0; c < KT; ++c) m8[c & 7] = fmaxf(m8[c & 7], __uint_as_float(s[c]));
                 }
-                const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                                       fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7]))) * LOG2E;
+                float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                                 fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7]))) * LOG2E;
+                if (none) mx = -INFINITY;
                 float fac = 1.f;
                 bool resc = false;
                 if (mx != -INFINITY) {
@@ -455,7 +455,8 @@ __global__ void __launch_bounds__(NTHR, 1)
                         resc = true;
                     }
                 }
-                const float nmu = m_cur == -INFINITY ? 0.f : -m_cur;
+                // rows without a valid column give p = 0 (ex2(-inf)); scores are finite
+                const float nmu = none ? -INFINITY : (m_cur == -INFINITY ? 0.f : -m_cur);
                 float ps[4] = {0.f, 0.f, 0.f, 0.f};
                 uint32_t pk[32];
 #pragma unroll
@@ -470,8 +471,7 @@ __global__ void __launch_bounds__(NTHR, 1)
                 if (__any_sync(0xffffffffu, resc)) {
                     // every PV so far (the latest: tile g-1) has completed before O is rescaled
                     if (g >= 1) {
-                        ok = __all_sync(0xffffffffu,
-                                        mbar_wait(&bars[B_ODONE + ((g - 1) & 1)], ((g - 1) >> 1) & 1, abort_f));
+                        ok = mbar_wait_warp(&bars[B_ODONE + ((g - 1) & 1)], ((g - 1) >> 1) & 1, abort_f);
                         if (!ok) break;
                     }
                     tc_fence_after();
@@ -497,9 +497,8 @@ __global__ void __launch_bounds__(NTHR, 1)
             // ------------------------- epilogue of head pair hp ------------------
             // the last two PVs of the head pair (tiles g-2, g-1) have completed
             if (g >= 2)
-                ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_ODONE + (g & 1)], ((g - 2) >> 1) & 1, abort_f));
-            if (ok)
-                ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_ODONE + ((g - 1) & 1)], ((g - 1) >> 1) & 1, abort_f));
+                ok = mbar_wait_warp(&bars[B_ODONE + (g & 1)], ((g - 2) >> 1) & 1, abort_f);
+            if (ok) ok = mbar_wait_warp(&bars[B_ODONE + ((g - 1) & 1)], ((g - 1) >> 1) & 1, abort_f);
             if (!ok) break;
             tc_fence_after();
             const int h = hp * HPG + hh;

@@ -490,10 +490,15 @@ def absorb_queries(q: torch.Tensor, w_uk: torch.Tensor, n_heads: int, scale: flo
 
 
 def expand_values(o_lat: torch.Tensor, w_uv: torch.Tensor, n_heads: int) -> torch.Tensor:
-    """o[b,t,h,:] = W_uv,h o_lat[b,t,h,:] with W_uv = v_up_proj.weight [H*dh, d_c]."""
+    """o[b,t,h,:] = W_uv,h o_lat[b,t,h,:] with W_uv = v_up_proj.weight [H*dh, d_c].
+
+    One batched GEMM over the heads; the result is a [B, L, H, dh] view of an
+    [H, B*L, dh] buffer."""
+    B, L, H, dc = o_lat.shape
     dh = w_uv.shape[0] // n_heads
-    w = w_uv.view(n_heads, dh, -1).to(o_lat.dtype)
-    return torch.einsum("blhc,hdc->blhd", o_lat, w)
+    w = w_uv.view(n_heads, dh, dc).transpose(1, 2).to(o_lat.dtype)
+    o = torch.bmm(o_lat.reshape(B * L, H, dc).transpose(0, 1), w)
+    return o.view(H, B, L, dh).permute(1, 2, 0, 3)
 
 
 __all__ = [
