@@ -26,6 +26,8 @@
 // dgda_prefill_mma.cu.
 #include "dgda_prefill.cuh"
 
+#include <cstdlib>
+
 namespace maba {
 namespace {
 
@@ -442,10 +444,106 @@ int choose_segments(int dtype, int64_t BH, int64_t L) {
     return nseg < 3 ? 1 : (int)nseg;
 }
 
+// Chunk-parallel path (16-bit inputs): chunk records for a window of `win`
+// chunks (the sequence is processed in windows so the records stay within a
+// fixed budget), `nseg` scan segments per window, and the fp32 state carried
+// between windows.
+struct ChunkPlan {
+    int64_t nch, win, nwin;
+    int nseg;
+    size_t rec_bytes, bytes;
+};
+
+constexpr size_t kChunkWsBudget = size_t(2) << 30;
+
+// MABA_DGDA_WINDOW_CHUNKS (> 0) caps the window length in chunks; it exists so
+// the multi-window path can be exercised on short sequences.
+int64_t window_cap() {
+    const char* e = getenv("MABA_DGDA_WINDOW_CHUNKS");
+    if (e == nullptr) return 0;
+    const long long v = atoll(e);
+    return v > 0 ? (int64_t)v : 0;
+}
+
+ChunkPlan chunk_plan(int64_t BH, int64_t L) {
+    ChunkPlan p{};
+    p.nch = ceil_div(L, 64);
+    int64_t win = (int64_t)(kChunkWsBudget / ((size_t)BH * CHUNK_REC));
+    if (win < 64) win = 64;
+    const int64_t cap = window_cap();
+    if (cap > 0 && win > cap) win = cap;
+    if (win > p.nch) win = p.nch;
+    p.win = win > 0 ? win : 1;
+    p.nwin = ceil_div(p.nch, p.win);
+    const int64_t sms = sm_count();
+    int64_t nseg = BH >= sms ? 1 : (2 * sms) / BH;  // two scan CTAs per SM
+    if (nseg > p.win / 8) nseg = p.win / 8;
+    if (nseg > 32) nseg = 32;
+    p.nseg = nseg < 2 ? 1 : (int)nseg;
+    p.rec_bytes = (size_t)BH * p.win * CHUNK_REC;
+    p.bytes = p.rec_bytes + (size_t)BH * p.nseg * (DP * 2 * DP + DP * DP) * sizeof(float) +
+              (size_t)BH * DP * DP * sizeof(float);
+    return p;
+}
+
 template <typename K>
 int set_smem(K kern, size_t bytes) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
     if (e != cudaSuccess) return set_error(MABA_ERR_CUDA, "dgda_prefill: smem attribute: %s", cudaGetErrorString(e));
+    return MABA_OK;
+}
+
+// Chunk-parallel prefill (16-bit): per window, the preparation pass over all
+// chunks, the segmented state scan, and the output pass.
+template <typename T>
+int launch_chunked(const PrefillArgs& a0, int64_t BH, const ChunkPlan& p, int dtype, int sdtype, cudaStream_t s,
+                   void* ws) {
+    unsigned char* base = static_cast<unsigned char*>(ws);
+    float* trans = reinterpret_cast<float*>(base + p.rec_bytes);
+    float* start = trans + (size_t)BH * p.nseg * DP * 2 * DP;
+    float* carry = start + (size_t)BH * p.nseg * DP * DP;  // fp32 [B][H][64][64] between windows
+    for (int64_t w = 0; w < p.nwin; ++w) {
+        PrefillArgs a = a0;
+        const int64_t t0 = w * p.win * 64;
+        const int64_t len = (a0.L - t0) < p.win * 64 ? (a0.L - t0) : p.win * 64;
+        auto shift = [&](const void* ptr, const int64_t* st) -> const void* {
+            return ptr ? static_cast<const void*>(static_cast<const T*>(ptr) + t0 * st[2]) : nullptr;
+        };
+        a.q = shift(a0.q, a0.sq); a.k = shift(a0.k, a0.sk); a.v = shift(a0.v, a0.sv);
+        a.alpha = shift(a0.alpha, a0.sa); a.log_alpha = shift(a0.log_alpha, a0.sla);
+        a.b = shift(a0.b, a0.sb); a.w = shift(a0.w, a0.sw);
+        a.out = static_cast<T*>(a0.out) + t0 * a0.so[2];
+        a.L = len;
+        a.nch = ceil_div(len, 64);
+        a.ws_chunk = base;
+        const int64_t carry_st[4] = {(int64_t)a0.H * DP * DP, DP * DP, DP, 1};
+        if (w > 0) {
+            a.init = carry;
+            for (int i = 0; i < 4; ++i) a.si[i] = carry_st[i];
+        }
+        if (w + 1 < p.nwin) {
+            a.fin = carry;
+            for (int i = 0; i < 4; ++i) a.sf[i] = carry_st[i];
+        }
+        MABA_TRY(dgda_mma_launch(a, dim3((unsigned)BH, (unsigned)a.nch), 3, dtype, sdtype, s));
+        const int64_t seg_chunks = ceil_div(a.nch, (int64_t)p.nseg);
+        a.seg_len = seg_chunks * 64;
+        a.nseg = (int)ceil_div(a.nch, seg_chunks);
+        if (a.nseg <= 1) {
+            a.nseg = 1;
+            MABA_TRY(dgda_scan_launch(a, dim3((unsigned)BH, 1), 0, dtype, sdtype, s));
+        } else {
+            a.ws_trans = trans;
+            a.ws_start = start;
+            const dim3 grid((unsigned)BH, (unsigned)a.nseg);
+            MABA_TRY(dgda_scan_launch(a, grid, 1, dtype, sdtype, s));
+            if (sdtype == MABA_F32) dgda_combine_kernel<float><<<(unsigned)BH, NT, 0, s>>>(a);
+            else dgda_combine_kernel<T><<<(unsigned)BH, NT, 0, s>>>(a);
+            MABA_TRY(check_launch("dgda_prefill(combine)"));
+            MABA_TRY(dgda_scan_launch(a, grid, 2, dtype, sdtype, s));
+        }
+        MABA_TRY(dgda_out_launch(a, BH, dtype, s));
+    }
     return MABA_OK;
 }
 
@@ -456,6 +554,15 @@ int launch_prefill(PrefillArgs& a, int64_t B, int dtype, int sdtype, cudaStream_
     constexpr bool k16 = sizeof(T) == 2;  // 16-bit inputs: tensor-core chunk kernels
     const int64_t BH = B * a.H;
     if (BH == 0) return MABA_OK;
+    if constexpr (k16) {
+        // chunk-parallel path when the caller's workspace holds its plan (windows
+        // after the first carry an fp32 state, so they need an fp32 state dtype)
+        if (a.L >= 2 * 64) {
+            const ChunkPlan p = chunk_plan(BH, a.L);
+            if (ws != nullptr && ws_bytes >= p.bytes && (p.nwin == 1 || sdtype == MABA_F32))
+                return launch_chunked<T>(a, BH, p, dtype, sdtype, s, ws);
+        }
+    }
     const int nseg = choose_segments(dtype, BH, a.L);
     if (nseg <= 1) {
         a.nseg = 1;
@@ -512,12 +619,19 @@ extern "C" size_t maba_dgda_prefill_workspace_size(int32_t dtype, int64_t B, int
                                                    int64_t dv) {
     (void)dk; (void)dv;
     const int64_t BH = B * H;
+    size_t need = 0;
     const int nseg0 = choose_segments(dtype, BH, L);
-    if (nseg0 <= 1) return 0;
-    const int64_t nchunks = ceil_div(L, 64);
-    const int64_t seg_len = ceil_div(nchunks, nseg0) * 64;
-    const int64_t nseg = ceil_div(L, seg_len);
-    return (size_t)BH * nseg * (DP * 2 * DP + DP * DP) * sizeof(float);
+    if (nseg0 > 1) {
+        const int64_t nchunks = ceil_div(L, 64);
+        const int64_t seg_len = ceil_div(nchunks, nseg0) * 64;
+        const int64_t nseg = ceil_div(L, seg_len);
+        need = (size_t)BH * nseg * (DP * 2 * DP + DP * DP) * sizeof(float);
+    }
+    if ((dtype == MABA_BF16 || dtype == MABA_F16) && BH > 0 && L >= 2 * 64) {
+        const size_t c = chunk_plan(BH, L).bytes;
+        if (c > need) need = c;
+    }
+    return need;
 }
 
 extern "C" int maba_dgda_prefill(const maba_tensor* q, const maba_tensor* k, const maba_tensor* v,

@@ -16,11 +16,32 @@ struct PrefillArgs {
     float* ws_trans;      // [B*H][nseg][64][128]   (R | P) per segment
     float* ws_start;      // [B*H][nseg][64][64]    starting state per segment
     int vec8;             // all inputs: unit stride on d, 16-byte aligned rows (8 x 16-bit loads)
+    // chunk-parallel path (16-bit inputs): one record per (b*h, chunk)
+    unsigned char* ws_chunk;  // [B*H][nch] records of CHUNK_REC bytes
+    int64_t nch;              // chunks per (b, h)
 };
 
+// Chunk record of the chunk-parallel path: 16-bit 64x64 tiles (row = token of
+// the chunk) and the chunk's total decay.
+//   W  = T (b k e^G)      U  = T (w v)       KT = k e^{G_end - G}
+//   QT = q e^G            A  = tril(q . decay . k)   (row = query, col = key)
+//   S  = state at the chunk start (written by the scan)
+//   dend = e^{G_end}  (fp32 [64])
+constexpr size_t CH_TILE = 64 * 64 * 2;
+constexpr size_t CH_W = 0, CH_U = CH_TILE, CH_KT = 2 * CH_TILE, CH_QT = 3 * CH_TILE, CH_A = 4 * CH_TILE,
+                 CH_S = 5 * CH_TILE, CH_DEND = 6 * CH_TILE;
+constexpr size_t CHUNK_REC = 6 * CH_TILE + 64 * 4;
+
 // Tensor-core chunk kernels for 16-bit inputs (dk, dv <= 64).
-// mode 0: single pass; 1: segment transition pass; 2: segment output pass.
+// mode 0: single pass; 1: segment transition pass; 2: segment output pass;
+// 3: chunk preparation of the chunk-parallel path (grid = (B*H, nch)).
 size_t dgda_mma_smem_bytes(int mode);
 int dgda_mma_launch(const PrefillArgs& a, dim3 grid, int mode, int dtype, int state_dtype, cudaStream_t s);
+
+// Chunk-parallel path (16-bit): the state scan over chunk records
+// (mode 0: one segment from the initial state; 1: segment transitions;
+// 2: segments from their start states) and the output pass.
+int dgda_scan_launch(const PrefillArgs& a, dim3 grid, int mode, int dtype, int state_dtype, cudaStream_t s);
+int dgda_out_launch(const PrefillArgs& a, int64_t BH, int dtype, cudaStream_t s);
 
 }  // namespace maba

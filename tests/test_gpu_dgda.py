@@ -286,3 +286,27 @@ def test_16bit_long_sequence_full_config2_length():
     ref = {k: x[k][:, :2, :2048].to(dt).float().numpy() for k in x}
     ro, _ = OD.dgda_sequential(ref["q"], ref["k"], ref["v"], None, ref["b"], ref["w"], log_alpha=ref["log_alpha"])
     assert_rel(o[:, :2, :2048], ro, RTOL_BF16, "prefix")
+
+
+@pytest.mark.parametrize("state", ["fp32", "bf16"])
+def test_16bit_chunk_parallel_windows(monkeypatch, state):
+    """Chunk-parallel path over several windows (window capped at 16 chunks): the fp32
+    state carried between windows reproduces the unwindowed result; a 16-bit state
+    takes the segmented path instead (windows need an fp32 carry)."""
+    x = dgda_inputs(B=1, T=4096, H=2, seed=11, per_channel=True)
+    dt = torch.bfloat16
+    args = [x[k].to(DEV, dt) for k in ("q", "k", "v")]
+    kw = dict(b=x["b"].to(DEV, dt), w=x["w"].to(DEV, dt), log_alpha=x["log_alpha"].to(DEV, dt))
+    sd = torch.float32 if state == "fp32" else dt
+    s0 = (torch.randn(1, 2, 64, 64, generator=torch.Generator().manual_seed(3)) * 0.1).to(DEV, sd)
+    o_ref, S_ref = mb.b200_dgda_prefill(*args, None, initial_state=s0, state_dtype=sd, **kw)
+    monkeypatch.setenv("MABA_DGDA_WINDOW_CHUNKS", "16")
+    o, S = mb.b200_dgda_prefill(*args, None, initial_state=s0, state_dtype=sd, **kw)
+    torch.cuda.synchronize()
+    assert_rel(o, o_ref, RTOL_BF16, "o")
+    assert_rel(S, S_ref, RTOL_BF16, "S")
+    ro, rS = OD.dgda_sequential(*(t.float().cpu().numpy() for t in args), b=kw["b"].float().cpu().numpy(),
+                                w=kw["w"].float().cpu().numpy(), initial_state=s0.float().cpu().numpy(),
+                                log_alpha=kw["log_alpha"].float().cpu().numpy())
+    assert_rel(o, ro, RTOL_BF16, "o vs oracle")
+    assert_rel(S, rS, RTOL_BF16, "S vs oracle")
