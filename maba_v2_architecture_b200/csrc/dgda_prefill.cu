@@ -525,7 +525,7 @@ int launch_chunked(const PrefillArgs& a0, int64_t BH, const ChunkPlan& p, int dt
             a.fin = carry;
             for (int i = 0; i < 4; ++i) a.sf[i] = carry_st[i];
         }
-        MABA_TRY(dgda_mma_launch(a, dim3((unsigned)BH, (unsigned)a.nch), 3, dtype, sdtype, s));
+        MABA_TRY(dgda_prep_launch(a, BH, dtype, s));
         const int64_t seg_chunks = ceil_div(a.nch, (int64_t)p.nseg);
         a.seg_len = seg_chunks * 64;
         a.nseg = (int)ceil_div(a.nch, seg_chunks);
@@ -557,7 +557,7 @@ int launch_prefill(PrefillArgs& a, int64_t B, int dtype, int sdtype, cudaStream_
     if constexpr (k16) {
         // chunk-parallel path when the caller's workspace holds its plan (windows
         // after the first carry an fp32 state, so they need an fp32 state dtype)
-        if (a.L >= 2 * 64) {
+        if (a.L >= 2 * 64 && a.vec8) {
             const ChunkPlan p = chunk_plan(BH, a.L);
             if (ws != nullptr && ws_bytes >= p.bytes && (p.nwin == 1 || sdtype == MABA_F32))
                 return launch_chunked<T>(a, BH, p, dtype, sdtype, s, ws);

@@ -43,5 +43,6 @@ int dgda_mma_launch(const PrefillArgs& a, dim3 grid, int mode, int dtype, int st
 // 2: segments from their start states) and the output pass.
 int dgda_scan_launch(const PrefillArgs& a, dim3 grid, int mode, int dtype, int state_dtype, cudaStream_t s);
 int dgda_out_launch(const PrefillArgs& a, int64_t BH, int dtype, cudaStream_t s);
+int dgda_prep_launch(const PrefillArgs& a, int64_t BH, int dtype, cudaStream_t s);
 
 }  // namespace maba
