@@ -3,20 +3,21 @@
 //
 // Same recurrence as dgda_prefill_mma.cu (reference maba_sparse/kernels/
 // common.py:256-265, chunked form cpu_dgda.py:101-146) with the per-chunk WY/UT
-// quantities precomputed in parallel over all chunks:
-//   u  = U - W S                 (U = T w v, W = T (b k e^G))
-//   o  = (q e^G) S + A u
-//   S' = e^{G_end} S + (k e^{G_end - G})^T u
-// so the sequential part per chunk is two 64x64x64 products (scan), and the
-// output is three products per chunk, independent across chunks (out pass).
+// quantities precomputed in parallel over all chunks (record: dgda_prefill.cuh):
+//   S' = e^{G_end} S + (k e^{G_end-G})^T (U - W S) = e^{G_end} S + N - M S
+//   o  = (q e^G) S + A (U - W S)                   = QW S + AU
+// so the sequential part per chunk is one 64x64x64 product (scan) and the output
+// one product per chunk, independent across chunks (out pass).  The decay term
+// e^{G_end} S stays in fp32; only the correction M S and the increment N pass
+// through 16-bit operands, as in the single-pass kernel.
 //
-// Scan (grid = (B*H, segments), 8 warps): the chunk records of the next chunk
-// are fetched by cp.async while the current chunk's products run; the state is
-// held in fp32 accumulator registers (a 16-bit copy in shared memory feeds the
-// MMAs, and is what the output pass reads as the chunk's start state).  Modes:
-// 0 -- one segment from the initial state; 1 -- the affine transition [R | P]
-// of each segment (the augmented state starts at [0 | I] and u = [U | 0] - W X);
-// 2 -- each segment from its start state (folded from the transitions).
+// Scan (grid = (B*H, segments), 8 warps): the next chunk's M, N are fetched by
+// cp.async while the current product runs; the state is held in fp32
+// accumulator registers, with a double-buffered 16-bit copy in shared memory
+// that feeds the MMA and is what the output pass reads as the chunk's start
+// state.  Modes: 0 -- one segment from the initial state; 1 -- the affine
+// transition [R | P] of each segment (the augmented state starts at [0 | I]:
+// X' = e^{G_end} X + [N | 0] - M X); 2 -- each segment from its start state.
 #include "dgda_prefill.cuh"
 #include "mma_util.cuh"
 
@@ -49,10 +50,10 @@ template <int NCOL>
 struct ScanSmem {
     static constexpr int LN = NCOL + 8;
     static constexpr size_t TILE = (size_t)C * LB * 2;
-    static constexpr size_t REC = 3 * TILE + 64 * 4;               // W, U, KT, dend
-    static constexpr size_t SB = 2 * REC;                          // [D][LN] 16-bit state
-    static constexpr size_t UB = SB + (size_t)D * LN * 2;          // [C][LN] 16-bit u
-    static constexpr size_t TOTAL = UB + (size_t)C * LN * 2;
+    static constexpr size_t REC = 2 * TILE + 64 * 4;               // M, N, dend
+    static constexpr size_t SB = 2 * REC;                          // 2 x [D][LN] 16-bit state
+    static constexpr size_t SBSZ = (size_t)D * LN * 2;
+    static constexpr size_t TOTAL = SB + 2 * SBSZ;
 };
 
 template <typename T, typename TS, int MODE>
@@ -63,7 +64,6 @@ __global__ void __launch_bounds__(NTH, 2) dgda_scan_kernel(PrefillArgs a) {
     constexpr int NTW = NCOL / 16;
     extern __shared__ __align__(16) unsigned char sm[];
     T* SB = reinterpret_cast<T*>(sm + SM::SB);
-    T* UB = reinterpret_cast<T*>(sm + SM::UB);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int bh = blockIdx.x, seg = blockIdx.y;
@@ -81,10 +81,9 @@ __global__ void __launch_bounds__(NTH, 2) dgda_scan_kernel(PrefillArgs a) {
     auto fetch = [&](int64_t c, int buf) {
         unsigned char* base = sm + buf * SM::REC;
         const unsigned char* r = recs + (size_t)c * CHUNK_REC;
-        fetch_tile<T>(reinterpret_cast<T*>(base), r + CH_W, tid);
-        fetch_tile<T>(reinterpret_cast<T*>(base + SM::TILE), r + CH_U, tid);
-        fetch_tile<T>(reinterpret_cast<T*>(base + 2 * SM::TILE), r + CH_KT, tid);
-        if (tid < 16) cp_async16(base + 3 * SM::TILE + tid * 16, r + CH_DEND + tid * 16);
+        fetch_tile<T>(reinterpret_cast<T*>(base), r + CH_M, tid);
+        fetch_tile<T>(reinterpret_cast<T*>(base + SM::TILE), r + CH_N, tid);
+        if (tid < 16) cp_async16(base + 2 * SM::TILE + tid * 16, r + CH_DEND + tid * 16);
         cp_async_commit();
     };
     if (c_begin < c_end) fetch(c_begin, 0);
@@ -114,42 +113,35 @@ __global__ void __launch_bounds__(NTH, 2) dgda_scan_kernel(PrefillArgs a) {
     int buf = 0;
     for (int64_t c = c_begin; c < c_end; ++c, buf ^= 1) {
         cp_async_wait_all();
-        __syncthreads();  // this chunk's record and the state copy are visible
+        __syncthreads();  // this chunk's record and the current state copy are visible
         if (c + 1 < c_end) fetch(c + 1, buf ^ 1);
-        const T* Wt = reinterpret_cast<const T*>(sm + buf * SM::REC);
-        const T* Ut = reinterpret_cast<const T*>(sm + buf * SM::REC + SM::TILE);
-        const T* KTt = reinterpret_cast<const T*>(sm + buf * SM::REC + 2 * SM::TILE);
-        const float* dend = reinterpret_cast<const float*>(sm + buf * SM::REC + 3 * SM::TILE);
+        const T* Mt = reinterpret_cast<const T*>(sm + buf * SM::REC);
+        const T* Nt = reinterpret_cast<const T*>(sm + buf * SM::REC + SM::TILE);
+        const float* dend = reinterpret_cast<const float*>(sm + buf * SM::REC + 2 * SM::TILE);
+        const T* Sc = SB + buf * (SM::SBSZ / 2);        // state at the chunk start (16-bit)
+        T* Sn = SB + (buf ^ 1) * (SM::SBSZ / 2);        // state after the chunk
         if (MODE != 1) {
             // the chunk's start state, for the output pass
             unsigned char* dst = const_cast<unsigned char*>(recs) + (size_t)c * CHUNK_REC + CH_S;
             for (int e = tid; e < 64 * 8; e += NTH) {
                 const int r = e >> 3, c8 = (e & 7) * 8;
                 *reinterpret_cast<uint4*>(dst + (size_t)(r * 64 + c8) * 2) =
-                    *reinterpret_cast<const uint4*>(SB + r * LN + c8);
+                    *reinterpret_cast<const uint4*>(Sc + r * LN + c8);
             }
         }
-        // u = [U | 0] - W S
-        float racc[NTW][4] = {};
-        warp_mma<T, false, true, NTW>(racc, Wt + wr * LB, LB, SB + wc, LN, D, lane);
+        // S' = e^{G_end} S + [N | 0] - M S
+        float macc[NTW][4] = {};
+        warp_mma<T, false, true, NTW>(macc, Mt + wr * LB, LB, Sc + wc, LN, D, lane);
 #pragma unroll
         for (int n = 0; n < NTW; ++n)
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
                 const int r = wr + fr + (e >> 1) * 8;
                 const int col = wc + n * 8 + fc + (e & 1);
-                const float u = col < D ? Cvt<T>::to_f(Ut[r * LB + col]) : 0.f;
-                racc[n][e] = u - racc[n][e];
+                const float nv = col < D ? Cvt<T>::to_f(Nt[r * LB + col]) : 0.f;
+                sacc[n][e] = fmaf(sacc[n][e], dend[r], nv - macc[n][e]);
             }
-        store_acc16<T, NTW>(UB + wr * LN + wc, LN, racc, lane);
-        __syncthreads();
-        // S = e^{G_end} S + KT^T u
-#pragma unroll
-        for (int n = 0; n < NTW; ++n)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) sacc[n][e] *= dend[wr + fr + (e >> 1) * 8];
-        warp_mma<T, true, true, NTW>(sacc, KTt + wr, LB, UB + wc, LN, C, lane);
-        store_acc16<T, NTW>(SB + wr * LN + wc, LN, sacc, lane);
+        store_acc16<T, NTW>(Sn + wr * LN + wc, LN, sacc, lane);
     }
     cp_async_wait_all();
     // ---- results -------------------------------------------------------------
@@ -199,8 +191,10 @@ constexpr size_t QH = KD + TILE;                        // [48][LB]
 constexpr size_t BH = QH + (size_t)48 * LB * 2;         // [48][LB]
 constexpr size_t KH = BH + (size_t)48 * LB * 2;         // [96][LB]
 constexpr size_t TOTAL = KH + (size_t)96 * LB * 2;
-// aliases of the dead A/L region during the solve
+// aliases of the dead A/L region during the solve and the epilogue
 constexpr size_t TM = R1, SCR = R1 + TILE;
+constexpr size_t EP_KT = SCR + (size_t)16 * LB * 2, EP_QT = EP_KT + TILE, EP_W = EP_QT + TILE, EP_U = EP_W + TILE;
+static_assert(EP_U + TILE <= TOTAL, "epilogue tiles fit in the A/L region");
 static_assert(TOTAL <= 113 * 1024, "two CTAs per SM");
 }  // namespace prep
 
@@ -347,8 +341,9 @@ __global__ void __launch_bounds__(NTH, 2) dgda_prep_kernel(PrefillArgs a) {
     const float pr1 = blk == 0 ? 0.f : (blk == 1 ? bend1[0] : (blk == 2 ? bend1[1] : bend1[2]));
 
     // ---------------- decayed operands ----------------------------------------------
-    T* QTg = reinterpret_cast<T*>(rec + CH_QT);
-    T* KTg = reinterpret_cast<T*>(rec + CH_KT);
+    // QT and KT wait in the record (slots of N and S) until the epilogue needs them
+    T* QTg = reinterpret_cast<T*>(rec + CH_QT_TMP);
+    T* KTg = reinterpret_cast<T*>(rec + CH_KT_TMP);
     auto st2 = [](T* p, float x, float y) {
         T2 v2;
         v2.x = to16<T>(x);
@@ -393,6 +388,7 @@ __global__ void __launch_bounds__(NTH, 2) dgda_prep_kernel(PrefillArgs a) {
         for (int I = 1; I < 4; ++I)
             if (I > blk) st2(KHs + (kh_off(I) + r) * LB + d0, k0 * (ck0[I - 1] * r0), k1 * (ck1[I - 1] * r1));
     }
+    __threadfence();  // QT, KT reach L2 before this CTA reads them back (cp.async.cg)
     for (int e = tid; e < C * C; e += NTH) {  // strictly-upper off-diagonal blocks
         const int i = e >> 6, j = e & 63;
         if ((j >> 4) > (i >> 4)) {
@@ -507,51 +503,76 @@ __global__ void __launch_bounds__(NTH, 2) dgda_prep_kernel(PrefillArgs a) {
         }
         __syncthreads();
     }
-    // ---------------- W = T BT, U = T WV, A, e^{G_end} -> chunk record ------------------
+    // ---------------- W = T BT, U = T WV; M, N, QW, AU -> chunk record --------------------
     {
         constexpr int NTW = D / 16;
         const int wr = (warp & 3) * 16, wc = (warp >> 2) * (D / 2);
-        float wacc[NTW][4] = {};
-        float uacc[NTW][4] = {};
-        warp_mma<T, false, true, NTW>(wacc, TMs + wr * LB, LB, BTs + wc, LB, C, lane);
-        warp_mma<T, false, true, NTW>(uacc, TMs + wr * LB, LB, WVs + wc, LB, C, lane);
-        T* Wg = reinterpret_cast<T*>(rec + CH_W);
-        T* Ug = reinterpret_cast<T*>(rec + CH_U);
+        T* KTs = reinterpret_cast<T*>(sm + EP_KT);
+        T* QTs = reinterpret_cast<T*>(sm + EP_QT);
+        T* W16 = reinterpret_cast<T*>(sm + EP_W);
+        T* U16 = reinterpret_cast<T*>(sm + EP_U);
+        fetch_tile<T>(KTs, rec + CH_KT_TMP, tid);  // written by this CTA above (fenced)
+        fetch_tile<T>(QTs, rec + CH_QT_TMP, tid);
+        cp_async_commit();
+        {
+            float wacc[NTW][4] = {};
+            float uacc[NTW][4] = {};
+            warp_mma<T, false, true, NTW>(wacc, TMs + wr * LB, LB, BTs + wc, LB, C, lane);
+            warp_mma<T, false, true, NTW>(uacc, TMs + wr * LB, LB, WVs + wc, LB, C, lane);
+            store_acc16<T, NTW>(W16 + wr * LB + wc, LB, wacc, lane);
+            store_acc16<T, NTW>(U16 + wr * LB + wc, LB, uacc, lane);
+        }
+        cp_async_wait_all();
+        __syncthreads();  // W, U, KT, QT in shared memory; the temporary slots are free
+        auto put = [&](size_t off, const float (&acc)[NTW][4], const T* sub) {
+            T* g = reinterpret_cast<T*>(rec + off);
 #pragma unroll
-        for (int n = 0; n < NTW; ++n)
+            for (int n = 0; n < NTW; ++n)
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const int r = wr + fr + h * 8, c = wc + n * 8 + fc;
-                T w2[2] = {to16<T>(wacc[n][2 * h]), to16<T>(wacc[n][2 * h + 1])};
-                T u2[2] = {to16<T>(uacc[n][2 * h]), to16<T>(uacc[n][2 * h + 1])};
-                *reinterpret_cast<uint32_t*>(Wg + r * 64 + c) = *reinterpret_cast<uint32_t*>(w2);
-                *reinterpret_cast<uint32_t*>(Ug + r * 64 + c) = *reinterpret_cast<uint32_t*>(u2);
-            }
-    }
-    for (int e = tid; e < C * 8; e += NTH) {
-        const int r = e >> 3, c8 = (e & 7) * 8;
-        *reinterpret_cast<uint4*>(rec + CH_A + (size_t)(r * 64 + c8) * 2) =
-            *reinterpret_cast<const uint4*>(AMs + r * LB + c8);
+                for (int h = 0; h < 2; ++h) {
+                    const int r = wr + fr + h * 8, c = wc + n * 8 + fc;
+                    float x0 = acc[n][2 * h], x1 = acc[n][2 * h + 1];
+                    if (sub != nullptr) {
+                        x0 = Cvt<T>::to_f(sub[r * LB + c]) - x0;
+                        x1 = Cvt<T>::to_f(sub[r * LB + c + 1]) - x1;
+                    }
+                    T p2[2] = {to16<T>(x0), to16<T>(x1)};
+                    *reinterpret_cast<uint32_t*>(g + r * 64 + c) = *reinterpret_cast<uint32_t*>(p2);
+                }
+        };
+        {
+            float macc[NTW][4] = {};
+            float nacc[NTW][4] = {};
+            warp_mma<T, true, true, NTW>(macc, KTs + wr, LB, W16 + wc, LB, C, lane);  // KT^T W
+            warp_mma<T, true, true, NTW>(nacc, KTs + wr, LB, U16 + wc, LB, C, lane);  // KT^T U
+            put(CH_M, macc, nullptr);
+            put(CH_N, nacc, nullptr);
+        }
+        {
+            float qacc[NTW][4] = {};
+            float aacc[NTW][4] = {};
+            warp_mma<T, false, true, NTW>(qacc, AMs + wr * LB, LB, W16 + wc, LB, C, lane);  // A W
+            warp_mma<T, false, true, NTW>(aacc, AMs + wr * LB, LB, U16 + wc, LB, C, lane);  // A U
+            put(CH_QW, qacc, QTs);  // QT - A W
+            put(CH_AU, aacc, nullptr);
+        }
     }
     if (tid < D) reinterpret_cast<float*>(rec + CH_DEND)[tid] = dend[tid];
 }
 
-// Output pass: o = QT S + A (U - W S) per chunk, independent across chunks.
+// Output pass: o = QW S + AU per chunk, independent across chunks.
 struct OutSmem {
     static constexpr size_t TILE = (size_t)C * LB * 2;
-    static constexpr size_t QT = 0, S = TILE, W = 2 * TILE, U = 3 * TILE, A = 4 * TILE, UB = 5 * TILE;
-    static constexpr size_t TOTAL = 6 * TILE;
+    static constexpr size_t QW = 0, S = TILE, AU = 2 * TILE;
+    static constexpr size_t TOTAL = 3 * TILE;
 };
 
 template <typename T>
 __global__ void __launch_bounds__(NTH) dgda_out_kernel(PrefillArgs a) {
     extern __shared__ __align__(16) unsigned char sm[];
-    T* QTt = reinterpret_cast<T*>(sm + OutSmem::QT);
+    T* QWt = reinterpret_cast<T*>(sm + OutSmem::QW);
     T* St = reinterpret_cast<T*>(sm + OutSmem::S);
-    T* Wt = reinterpret_cast<T*>(sm + OutSmem::W);
-    T* Ut = reinterpret_cast<T*>(sm + OutSmem::U);
-    T* At = reinterpret_cast<T*>(sm + OutSmem::A);
-    T* UB = reinterpret_cast<T*>(sm + OutSmem::UB);
+    T* AUt = reinterpret_cast<T*>(sm + OutSmem::AU);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int64_t ci = blockIdx.x;  // chunk over (b*h, chunk)
     const int bh = (int)(ci / a.nch);
@@ -561,29 +582,14 @@ __global__ void __launch_bounds__(NTH) dgda_out_kernel(PrefillArgs a) {
     const int wr = (warp & 3) * 16, wc = (warp >> 2) * (D / 2);
     const int fr = lane >> 2, fc = (lane & 3) * 2;
     const unsigned char* rec = a.ws_chunk + (size_t)ci * CHUNK_REC;
-    fetch_tile<T>(QTt, rec + CH_QT, tid);
+    fetch_tile<T>(QWt, rec + CH_QW, tid);
     fetch_tile<T>(St, rec + CH_S, tid);
-    fetch_tile<T>(Wt, rec + CH_W, tid);
-    fetch_tile<T>(Ut, rec + CH_U, tid);
-    fetch_tile<T>(At, rec + CH_A, tid);
+    fetch_tile<T>(AUt, rec + CH_AU, tid);
     cp_async_commit();
     cp_async_wait_all();
     __syncthreads();
     float qacc[NTW][4] = {};
-    float racc[NTW][4] = {};
-    warp_mma<T, false, true, NTW>(qacc, QTt + wr * LB, LB, St + wc, LB, D, lane);
-    warp_mma<T, false, true, NTW>(racc, Wt + wr * LB, LB, St + wc, LB, D, lane);
-#pragma unroll
-    for (int n = 0; n < NTW; ++n)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const int r = wr + fr + (e >> 1) * 8;
-            const int col = wc + n * 8 + fc + (e & 1);
-            racc[n][e] = Cvt<T>::to_f(Ut[r * LB + col]) - racc[n][e];
-        }
-    store_acc16<T, NTW>(UB + wr * LB + wc, LB, racc, lane);
-    __syncthreads();
-    warp_mma<T, false, true, NTW>(qacc, At + wr * LB, LB, UB + wc, LB, C, lane);
+    warp_mma<T, false, true, NTW>(qacc, QWt + wr * LB, LB, St + wc, LB, D, lane);
     T* o = static_cast<T*>(a.out);
     const int64_t t0 = c * C;
 #pragma unroll
@@ -594,7 +600,8 @@ __global__ void __launch_bounds__(NTH) dgda_out_kernel(PrefillArgs a) {
             const int col = wc + n * 8 + fc + (e & 1);
             const int64_t t = t0 + r;
             if (t < a.L && col < a.dv)
-                o[bi * a.so[0] + hi * a.so[1] + t * a.so[2] + (int64_t)col * a.so[3]] = to16<T>(qacc[n][e]);
+                o[bi * a.so[0] + hi * a.so[1] + t * a.so[2] + (int64_t)col * a.so[3]] =
+                    to16<T>(qacc[n][e] + Cvt<T>::to_f(AUt[r * LB + col]));
         }
 }
 

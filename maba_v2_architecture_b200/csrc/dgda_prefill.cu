@@ -337,10 +337,13 @@ __global__ void __launch_bounds__(NT, 1) dgda_chunk_kernel(PrefillArgs a) {
 }
 
 // Chains the segment transitions: start[0] = S0, start[s+1] = P_s start[s] + R_s.
+// One CTA per (b,h).  P is kept in a padded tile (row stride 65: the rows a warp
+// reads at one column fall in distinct banks); the next segment's P and R are
+// loaded into registers while the current product runs.
 template <typename TS>
 __global__ void __launch_bounds__(NT) dgda_combine_kernel(PrefillArgs a) {
     __shared__ float S[DP * DP];
-    __shared__ float Tr[DP * 2 * DP];
+    __shared__ float Pm[DP * (DP + 1)];
     const int tid = threadIdx.x;
     const int bh = blockIdx.x;
     const int64_t bi = bh / a.H, hi = bh % a.H;
@@ -353,28 +356,60 @@ __global__ void __launch_bounds__(NT) dgda_combine_kernel(PrefillArgs a) {
         S[e] = s;
     }
     const int tr = tid >> 4, tc = tid & 15;
-    for (int s = 0; s < a.nseg; ++s) {
+    const float* trans = a.ws_trans + (size_t)bh * a.nseg * DP * (2 * DP);
+    // this thread's share of a transition: 16 elements of P (4 float4) and its 16 outputs' R
+    float4 pp[4];
+    float rr[4][4];
+    auto fetch = [&](int sg) {
+        const float* src = trans + (size_t)sg * DP * (2 * DP);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int q = (tid * 4 + j) * 4;  // element of the 64x64 P
+            const int d = q >> 6, e = q & 63;
+            pp[j] = *reinterpret_cast<const float4*>(src + d * (2 * DP) + DP + e);
+        }
+#pragma unroll
+        for (int m = 0; m < 4; ++m)
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) rr[m][kk] = src[(tr + 16 * m) * (2 * DP) + tc + 16 * kk];
+    };
+    auto stash = [&]() {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int q = (tid * 4 + j) * 4;
+            const int d = q >> 6, e = q & 63;
+            float* dst = Pm + d * (DP + 1) + e;
+            dst[0] = pp[j].x;
+            dst[1] = pp[j].y;
+            dst[2] = pp[j].z;
+            dst[3] = pp[j].w;
+        }
+    };
+    if (a.nseg > 1) {
+        fetch(0);
+        stash();
+    }
+    for (int sg = 0; sg < a.nseg; ++sg) {
         __syncthreads();
-        float* dst = a.ws_start + ((size_t)bh * a.nseg + s) * DP * DP;
-        for (int e = tid; e < DP * DP; e += NT) dst[e] = S[e];
-        if (s == a.nseg - 1) break;
-        const float* src = a.ws_trans + ((size_t)bh * a.nseg + s) * DP * (2 * DP);
-        for (int e = tid; e < DP * 2 * DP; e += NT) Tr[e] = src[e];
-        __syncthreads();
+        float* dst = a.ws_start + ((size_t)bh * a.nseg + sg) * DP * DP;
+        for (int e = tid * 4; e < DP * DP; e += NT * 4)
+            *reinterpret_cast<float4*>(dst + e) = *reinterpret_cast<const float4*>(S + e);
+        if (sg == a.nseg - 1) break;
         float acc[4][4];
 #pragma unroll
         for (int m = 0; m < 4; ++m)
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk) acc[m][kk] = Tr[(tr + 16 * m) * 2 * DP + tc + 16 * kk];  // R
+            for (int kk = 0; kk < 4; ++kk) acc[m][kk] = rr[m][kk];
+        if (sg + 2 < a.nseg) fetch(sg + 1);  // next P, R in flight during the product
         for (int e = 0; e < DP; ++e) {
             float sv[4];
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) sv[kk] = S[e * DP + tc + 16 * kk];
 #pragma unroll
             for (int m = 0; m < 4; ++m) {
-                const float p = Tr[(tr + 16 * m) * 2 * DP + DP + e];  // P[d][e]
+                const float p = Pm[(tr + 16 * m) * (DP + 1) + e];  // P[d][e]
 #pragma unroll
-                for (int kk = 0; kk < 4; ++kk) acc[m][kk] += p * sv[kk];
+                for (int kk = 0; kk < 4; ++kk) acc[m][kk] = fmaf(p, sv[kk], acc[m][kk]);
             }
         }
         __syncthreads();
@@ -382,6 +417,7 @@ __global__ void __launch_bounds__(NT) dgda_combine_kernel(PrefillArgs a) {
         for (int m = 0; m < 4; ++m)
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) S[(tr + 16 * m) * DP + tc + 16 * kk] = acc[m][kk];
+        if (sg + 2 < a.nseg) stash();
     }
 }
 

@@ -21,20 +21,22 @@ struct PrefillArgs {
     int64_t nch;              // chunks per (b, h)
 };
 
-// Chunk record of the chunk-parallel path: 16-bit 64x64 tiles (row = token of
-// the chunk) and the chunk's total decay.
-//   W  = T (b k e^G)      U  = T (w v)       KT = k e^{G_end - G}
-//   QT = q e^G            A  = tril(q . decay . k)   (row = query, col = key)
+// Chunk record of the chunk-parallel path: 16-bit 64x64 tiles and the chunk's
+// total decay.  With T = (I + L)^{-1}, W = T (b k e^G), U = T (w v),
+// KT = k e^{G_end - G}, QT = q e^G and A = tril(q . decay . k):
+//   M  = KT^T W    N  = KT^T U      (state update: S' = e^{G_end} S + N - M S)
+//   QW = QT - A W  AU = A U         (output: o = QW S + AU)
 //   S  = state at the chunk start (written by the scan)
 //   dend = e^{G_end}  (fp32 [64])
+// While the preparation pass runs, the N and S slots hold KT and QT.
 constexpr size_t CH_TILE = 64 * 64 * 2;
-constexpr size_t CH_W = 0, CH_U = CH_TILE, CH_KT = 2 * CH_TILE, CH_QT = 3 * CH_TILE, CH_A = 4 * CH_TILE,
-                 CH_S = 5 * CH_TILE, CH_DEND = 6 * CH_TILE;
-constexpr size_t CHUNK_REC = 6 * CH_TILE + 64 * 4;
+constexpr size_t CH_M = 0, CH_N = CH_TILE, CH_QW = 2 * CH_TILE, CH_AU = 3 * CH_TILE, CH_S = 4 * CH_TILE,
+                 CH_DEND = 5 * CH_TILE;
+constexpr size_t CH_KT_TMP = CH_N, CH_QT_TMP = CH_S;
+constexpr size_t CHUNK_REC = 5 * CH_TILE + 64 * 4;
 
 // Tensor-core chunk kernels for 16-bit inputs (dk, dv <= 64).
-// mode 0: single pass; 1: segment transition pass; 2: segment output pass;
-// 3: chunk preparation of the chunk-parallel path (grid = (B*H, nch)).
+// mode 0: single pass; 1: segment transition pass; 2: segment output pass.
 size_t dgda_mma_smem_bytes(int mode);
 int dgda_mma_launch(const PrefillArgs& a, dim3 grid, int mode, int dtype, int state_dtype, cudaStream_t s);
 

@@ -74,7 +74,6 @@ __device__ __forceinline__ float f32(T x) { return Cvt<T>::to_f(x); }
 template <typename T, typename TS, int MODE>
 __global__ void __launch_bounds__(NTH, 1) dgda_mma_kernel(PrefillArgs a) {
     constexpr int NCOL = MODE == 1 ? 2 * D : D;
-    constexpr bool PREP = MODE == 3;
     using S_ = MS<NCOL>;
     constexpr int LN = S_::LN;
     constexpr int NTW = NCOL / 16;  // n8 tiles per warp: warp tile = 16 rows x NCOL/2 columns
@@ -105,7 +104,7 @@ __global__ void __launch_bounds__(NTH, 1) dgda_mma_kernel(PrefillArgs a) {
     int* flags = reinterpret_cast<int*>(sm + S_::FLG);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int bh = blockIdx.x, seg = PREP ? 0 : (int)blockIdx.y;
+    const int bh = blockIdx.x, seg = blockIdx.y;
     const int64_t bi = bh / a.H, hi = bh % a.H;
     const int dk = a.dk, dv = a.dv;
     const int wr = (warp & 3) * 16;           // warp rows in [64 x NCOL] products
@@ -126,10 +125,6 @@ __global__ void __launch_bounds__(NTH, 1) dgda_mma_kernel(PrefillArgs a) {
     for (int n = 0; n < NTW; ++n)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-            if (PREP) {
-                sacc[n][e] = 0.f;
-                continue;
-            }
             const int d = wr + fr + (e >> 1) * 8;
             const int c = wc + n * 8 + fc + (e & 1);
             float s = 0.f;
@@ -146,8 +141,8 @@ __global__ void __launch_bounds__(NTH, 1) dgda_mma_kernel(PrefillArgs a) {
             SB[d * LN + c] = to16<T>(s);
         }
 
-    const int64_t t_begin = PREP ? (int64_t)blockIdx.y * C : (int64_t)seg * a.seg_len;
-    int64_t t_end = t_begin + (PREP ? C : a.seg_len);
+    const int64_t t_begin = (int64_t)seg * a.seg_len;
+    int64_t t_end = t_begin + a.seg_len;
     if (t_end > a.L) t_end = a.L;
 
     for (int64_t c0 = t_begin; c0 < t_end; c0 += C) {
@@ -368,40 +363,6 @@ __global__ void __launch_bounds__(NTH, 1) dgda_mma_kernel(PrefillArgs a) {
             }
             __syncthreads();
         }
-        if constexpr (PREP) {
-            // ---------------- chunk record: W = T (b k e^G), U = T (w v), QT, KT, A, e^{G_end} ----
-            unsigned char* rec = a.ws_chunk + ((size_t)bh * a.nch + blockIdx.y) * CHUNK_REC;
-            for (int e = tid; e < C * D; e += NTH) {
-                const int r = e >> 6, c = e & 63;
-                RB[r * LN + c] = to16<T>(WVs[r * LF + c]);
-            }
-            __syncthreads();
-            float wacc[NTW][4] = {};
-            float uacc[NTW][4] = {};
-            warp_mma<T, false, true, NTW>(wacc, TM + wr * LB, LB, BTs + wc, LB, C, lane);
-            warp_mma<T, false, true, NTW>(uacc, TM + wr * LB, LB, RB + wc, LN, C, lane);
-            T* Wg = reinterpret_cast<T*>(rec + CH_W);
-            T* Ug = reinterpret_cast<T*>(rec + CH_U);
-#pragma unroll
-            for (int n = 0; n < NTW; ++n)
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int r = wr + fr + h * 8, c = wc + n * 8 + fc;
-                    T w2[2] = {to16<T>(wacc[n][2 * h]), to16<T>(wacc[n][2 * h + 1])};
-                    T u2[2] = {to16<T>(uacc[n][2 * h]), to16<T>(uacc[n][2 * h + 1])};
-                    *reinterpret_cast<uint32_t*>(Wg + r * 64 + c) = *reinterpret_cast<uint32_t*>(w2);
-                    *reinterpret_cast<uint32_t*>(Ug + r * 64 + c) = *reinterpret_cast<uint32_t*>(u2);
-                }
-            for (int e = tid; e < 3 * C * 8; e += NTH) {  // QT, KT, A: 16-byte rows pieces
-                const int tile = e / (C * 8), rem = e - tile * (C * 8), r = rem >> 3, c8 = (rem & 7) * 8;
-                const T* src = tile == 0 ? QTs : (tile == 1 ? KTs : AM);
-                const size_t off = tile == 0 ? CH_QT : (tile == 1 ? CH_KT : CH_A);
-                *reinterpret_cast<uint4*>(rec + off + (size_t)(r * 64 + c8) * 2) =
-                    *reinterpret_cast<const uint4*>(src + r * LB + c8);
-            }
-            if (tid < D) reinterpret_cast<float*>(rec + CH_DEND)[tid] = dend[tid];
-            continue;
-        }
         // ---------------- state chain ---------------------------------------------------
         float racc[NTW][4] = {};
         float qacc[NTW][4] = {};
@@ -445,7 +406,6 @@ __global__ void __launch_bounds__(NTH, 1) dgda_mma_kernel(PrefillArgs a) {
         warp_mma<T, true, true, NTW>(sacc, KTs + wr, LB, VP + wc, LN, C, lane);
         store_acc16<T, NTW>(SB + wr * LN + wc, LN, sacc, lane);
     }
-    if constexpr (PREP) return;
     __syncthreads();
     // ---------------- results -----------------------------------------------------------
 #pragma unroll
@@ -480,7 +440,6 @@ int launch_mode(const PrefillArgs& a, dim3 grid, int mode, cudaStream_t s) {
     switch (mode) {
         case 0: return launch_one<T, TS, 0>(a, grid, s);
         case 1: return launch_one<T, TS, 1>(a, grid, s);
-        case 3: return launch_one<T, TS, 3>(a, grid, s);
         default: return launch_one<T, TS, 2>(a, grid, s);
     }
 }

@@ -52,8 +52,16 @@ def test_transition_chains_prefill():
     outs = [par.dgda_segment_phase_b(*segs[r], trans, r) for r in range(P)]
     torch.cuda.synchronize()
     assert_rel(torch.cat([o for o, _ in outs], dim=2), o_full, RTOL_BF16, "o")
-    assert_rel(outs[-1][1], S_full, RTOL_FP32 * 10, "final state")
-    assert_rel(par.fold_transitions(trans, P)[..., :64, :64], S_full, RTOL_FP32 * 10, "folded state")
+    folded = par.fold_transitions(trans, P)[..., :64, :64]
+    # two 16-bit paths (segment transitions vs the whole-sequence prefill) agree closely ...
+    assert_rel(outs[-1][1], S_full, RTOL_BF16 / 4, "final state")
+    assert_rel(folded, S_full, RTOL_BF16 / 4, "folded state")
+    # ... and both match the fp64 recurrence on the 16-bit inputs
+    ro, rS = OD.dgda_sequential(*(x.double().cpu().numpy() for x in (q, k, v)), b=b.double().cpu().numpy(),
+                                w=w.double().cpu().numpy(), log_alpha=la.double().cpu().numpy())
+    assert_rel(o_full, ro, RTOL_BF16, "o vs oracle")
+    assert_rel(S_full, rS, RTOL_BF16, "S vs oracle")
+    assert_rel(folded, rS, RTOL_BF16, "folded S vs oracle")
 
 
 def _sa_parts(T, seed=5):
