@@ -70,6 +70,11 @@ MABA_API const char* maba_last_error(void);
  * counterpart (the reference's kernels do not wait on barriers). */
 MABA_API int maba_device_error(int32_t* out, void* stream);
 
+/* Self-test of the bounded waits: launches one warp that waits on a barrier
+ * nothing arrives on; after ~limit_cycles the wait gives up, the device error
+ * word becomes 2 and the kernel returns (the context stays usable). */
+MABA_API int maba_selftest_wait_timeout(int64_t limit_cycles, void* stream);
+
 /* ---- DGDA chunked prefill ---------------------------------------------
  * Replaces the `dgda_prefill` registry op:
  *   maba_sparse/kernels/dispatcher.py:258   (dispatch_dgda_prefill)

@@ -49,6 +49,7 @@ SIGNATURES = {
     "maba_abi_version": (ctypes.c_int, []),
     "maba_last_error": (ctypes.c_char_p, []),
     "maba_device_error": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int32), _vp]),
+    "maba_selftest_wait_timeout": (ctypes.c_int, [_i64, _vp]),
     "maba_dgda_prefill": (ctypes.c_int, [T_P] * 10 + [_i32, _vp, _sz, _vp]),
     "maba_dgda_prefill_workspace_size": (_sz, [_i32, _i64, _i64, _i64, _i64, _i64]),
     "maba_dgda_step": (ctypes.c_int, [T_P] * 10 + [_vp]),

@@ -67,6 +67,11 @@ extern "C" int maba_abi_version(void) { return MABA_ABI_VERSION; }
 
 extern "C" const char* maba_last_error(void) { return maba::g_last_error; }
 
+extern "C" int maba_selftest_wait_timeout(int64_t limit_cycles, void* stream) {
+    if (limit_cycles <= 0) return maba::set_error(MABA_ERR_INVALID, "selftest_wait_timeout: limit must be positive");
+    return maba::wait_timeout_selftest((long long)limit_cycles, static_cast<cudaStream_t>(stream));
+}
+
 extern "C" int maba_device_error(int32_t* out, void* stream) {
     if (out == nullptr) return maba::set_error(MABA_ERR_INVALID, "device_error: out is null");
     int v = 0;

@@ -25,6 +25,7 @@ int sa_attention_mma(SaArgs& a, int64_t B, int dtype, cudaStream_t s);
 int sa_attention_tc(SaArgs& a, int64_t B, int dtype, cudaStream_t s);
 bool sa_attention_tc_supported(const SaArgs& a, int dtype);
 int device_error_take(cudaStream_t s, int* out);
+int wait_timeout_selftest(long long limit, cudaStream_t s);
 bool sa_attention_mma_supported(const SaArgs& a, int dtype);
 size_t sa_attention_mma_workspace(int dtype, int64_t B, int64_t Lq, int64_t Lkv, int64_t H, int64_t DC, int64_t K,
                                   int32_t block);

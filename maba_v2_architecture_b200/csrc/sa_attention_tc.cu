@@ -663,6 +663,27 @@ int sa_attention_tc(SaArgs& a, int64_t B, int dtype, cudaStream_t s) {
     return check_launch("sa_attention(tcgen05)");
 }
 
+// One warp waits on an mbarrier that nothing ever arrives on, with the same
+// bounded wait as the pipelines above; the wait runs out after ~limit cycles,
+// the kernel raises the device error word (2) and returns normally.
+__global__ void wait_timeout_selftest_kernel(long long limit) {
+    __shared__ uint64_t bar;
+    __shared__ int abort_flag;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        abort_flag = 0;
+        fence_barrier_init();
+    }
+    __syncthreads();
+    const bool ok = mbar_wait_warp(&bar, 0, &abort_flag, limit);
+    if (threadIdx.x == 0 && !ok) atomicExch(&g_device_error, 2);
+}
+
+int wait_timeout_selftest(long long limit, cudaStream_t s) {
+    wait_timeout_selftest_kernel<<<1, 32, 0, s>>>(limit);
+    return check_launch("selftest_wait_timeout");
+}
+
 int device_error_take(cudaStream_t s, int* out) {
     int v = 0;
     cudaError_t e = cudaMemcpyFromSymbolAsync(&v, g_device_error, sizeof(int), 0, cudaMemcpyDeviceToHost, s);

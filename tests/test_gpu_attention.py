@@ -161,3 +161,17 @@ def test_dgda_layer_vs_reference():
     assert_rel(S, g["S_steps"], RTOL_FP32, "state after steps")
     assert_rel(yf, g["y_full"], RTOL_FP32, "full")
     assert_rel(Sf, g["S_full"], RTOL_FP32, "full state")
+
+
+def test_bounded_wait_runs_out_and_reports():
+    """A pipeline wait that can never complete gives up after its limit: the kernel
+    returns, the device error word reads 2 (then clears), and the context stays usable."""
+    from maba_v2_architecture_b200 import _native as N
+    assert N.device_error() == 0
+    stream = torch.cuda.current_stream().cuda_stream
+    N.check(N.lib().maba_selftest_wait_timeout(2_000_000, stream), "selftest")  # ~1 ms at 1.9 GHz
+    torch.cuda.synchronize()
+    assert N.device_error() == 2
+    assert N.device_error() == 0
+    x = torch.ones(4, device=DEV)
+    assert float((x * 2).sum()) == 8.0  # the context still works
