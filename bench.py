@@ -181,6 +181,11 @@ class OpTimers:
 
 MY_LAUNCHES_PER_STEP = None  # filled from the op list below
 
+# DRAM bytes per launch of the two candidate dominant kernels, from the ncu captures
+# summarised under profiles/ (read + write of one launch on this workload)
+TRAFFIC = {"sa_attention": 202.1e6 + 126.4e6, "dgda_prefill": 503.4e6 + 378.2e6}
+TRAFFIC_FILE = {"sa_attention": "sa_attention_tc_config2.md", "dgda_prefill": "dgda_prep_config2.md"}
+
 
 def count_launches(mb, L, BH):
     """Kernels of libmaba_b200 launched per step (cuBLAS GEMMs not counted)."""
@@ -421,7 +426,10 @@ def run_ours(args):
             "e2e": {"value": world * T_TOK / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
             "roofline": {"kernel": dom, "bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
-                         "frac": achieved / peak, "traffic": None, "peak_source": pk["source"]},
+                         "frac": achieved / peak, "traffic": TRAFFIC.get(dom), "traffic_unit": "bytes per launch",
+                         "traffic_source": "dram__bytes_read.sum + dram__bytes_write.sum of one ncu launch "
+                                           "(profiles/" + TRAFFIC_FILE.get(dom, "") + ")",
+                         "peak_source": pk["source"]},
             "per_op_ms": {k: round(v, 4) for k, v in per_op.items()},
             "gpu_launches": count_launches(mb, T_TOK, H) * args.steps,
             "clocks": clk,
