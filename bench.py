@@ -188,11 +188,14 @@ TRAFFIC_FILE = {"sa_attention": "sa_attention_tc_config2.md", "dgda_prefill": "d
 
 
 def count_launches(mb, L, BH):
-    """Kernels of libmaba_b200 launched per step (cuBLAS GEMMs not counted)."""
+    """Kernels of libmaba_b200 launched per step (cuBLAS GEMMs not counted): DGDA prep, segment
+    transitions, combine, segment states, output (chunk-parallel path; one scan launch when the
+    sequence is a single segment); centroids; top-k penalty table, centroid-norm tiles, prefix max,
+    tile scan; HCA pooling; attention."""
     lib = mb._native.lib()
-    seg = lib.maba_dgda_prefill_workspace_size(2, 1, H, L, DH, DH) > 0
-    dgda = 3 if seg else 1
-    return dgda + 1 + 2 + 1 + 1  # dgda, centroids, penalty table + top-k, hca pool, attention
+    chunked = lib.maba_dgda_prefill_workspace_size(2, 1, H, L, DH, DH) > 0
+    dgda = 5 if chunked else 1
+    return dgda + 1 + 4 + 1 + 1
 
 
 def attention_units(idx, L):

@@ -151,6 +151,9 @@ struct TopkArgs {
     int64_t L, nb;
     int64_t q_pos0;  // absolute position of query row 0 (prefill)
     const int64_t* pos_dev;  // decode at a device-held position: nb = *pos_dev / block + 1 (<= nb)
+    const float* cpref;      // [B][ntiles] prefix max of centroid norms over 64-block tiles (pruning), or null
+    int64_t ntiles;
+    int vecload;             // q and centroids: unit stride on d, 16-byte aligned rows (16-bit types)
     int D, block, keff, decode;
     float scale_f;
     double scale_d;
@@ -162,6 +165,52 @@ __global__ void penalty_table_kernel(float* pen, int64_t n, float lam) {
         // fl32(lambda) * fl32(log1p(delta)), the fp32 arithmetic of cpu_indexer.py:101
         float l = (float)log1p((double)i);
         pen[i] = __fmul_rn(lam, l);
+    }
+}
+
+// Max centroid norm of each 64-block tile (grid = (ntiles, B), 64 threads).
+template <typename T>
+__global__ void centroid_tile_norm_kernel(const T* c, int64_t sc0, int64_t sc1, int64_t sc2, int64_t nb, int D,
+                                          float* tmax, int64_t ntiles) {
+    __shared__ float wmax[2];
+    const int64_t b = blockIdx.y, n = (int64_t)blockIdx.x * 64 + threadIdx.x;
+    float ss = 0.f;
+    if (n < nb)
+        for (int d = 0; d < D; ++d) {
+            const float x = Cvt<T>::to_f(c[b * sc0 + n * sc1 + d * sc2]);
+            ss = fmaf(x, x, ss);
+        }
+    float m = sqrtf(ss);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((threadIdx.x & 31) == 0) wmax[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) tmax[b * ntiles + blockIdx.x] = fmaxf(wmax[0], wmax[1]);
+}
+
+// pref[j] = max(tmax[0..j]) per batch row (grid = B, 256 threads, chunked scan).
+__global__ void tile_prefix_max_kernel(const float* tmax, float* pref, int64_t ntiles) {
+    __shared__ float part[256];
+    const int64_t b = blockIdx.x;
+    const int tid = threadIdx.x;
+    const int64_t per = (ntiles + 255) / 256, j0 = tid * per;
+    float m = 0.f;
+    for (int64_t j = j0; j < j0 + per && j < ntiles; ++j) m = fmaxf(m, tmax[b * ntiles + j]);
+    part[tid] = m;
+    __syncthreads();
+    if (tid == 0) {
+        float run = 0.f;
+        for (int i = 0; i < 256; ++i) {
+            const float x = part[i];
+            part[i] = run;  // exclusive prefix max
+            run = fmaxf(run, x);
+        }
+    }
+    __syncthreads();
+    float run = part[tid];
+    for (int64_t j = j0; j < j0 + per && j < ntiles; ++j) {
+        run = fmaxf(run, tmax[b * ntiles + j]);
+        pref[b * ntiles + j] = run;
     }
 }
 
@@ -199,13 +248,46 @@ constexpr int kTT = 64;   // tokens per CTA
 constexpr int kTN = 64;   // candidates per tile
 constexpr int kTopkThreads = 256;
 
+constexpr int kLQ = kTT + 4;  // padded smem rows: 16-byte aligned, conflict-free transposed stores
+constexpr int kLC = kTN + 4;
+
+// Loads a [rows x D] tile (rows r0 .. r0+63 of a [.., rows, D] tensor, row stride sr,
+// scaled by `scale`) transposed into dst[d * ld + r]; rows at or past `nrows` read 0.
+template <typename T, typename SC>
+__device__ __forceinline__ void load_tile_t(SC* dst, int ld, const T* base, int64_t sr, int64_t sd, int64_t r0,
+                                            int64_t nrows, int D, SC scale, bool vec, int tid) {
+    if constexpr (sizeof(T) == 2) {
+        if (vec) {
+            // one 16-byte row piece per thread; a warp covers 32 consecutive rows of one piece,
+            // so the transposed stores hit 32 distinct banks
+            for (int e = tid; e < 64 * (D / 8); e += kTopkThreads) {
+                const int r = e & 63, ch = e >> 6;
+                const int64_t row = r0 + r;
+                uint4 v = make_uint4(0, 0, 0, 0);
+                if (row < nrows) v = *reinterpret_cast<const uint4*>(base + row * sr + ch * 8);
+                const T* x = reinterpret_cast<const T*>(&v);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) dst[(ch * 8 + j) * ld + r] = load_as<SC>(x + j) * scale;
+            }
+            return;
+        }
+    }
+    for (int e = tid; e < 64 * D; e += kTopkThreads) {
+        const int r = e / D, d = e - (e / D) * D;
+        const int64_t row = r0 + r;
+        SC x = SC(0);
+        if (row < nrows) x = load_as<SC>(base + row * sr + d * sd) * scale;
+        dst[d * ld + r] = x;
+    }
+}
+
 template <typename T, typename SC>
 __global__ void __launch_bounds__(kTopkThreads) topk_tile_kernel(TopkArgs a) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const int D = a.D;
-    SC* Qs = reinterpret_cast<SC*>(smem_raw);   // [D][kTT]
-    SC* Cs = Qs + (size_t)D * kTT;              // [D][kTN]
-    SC* Ss = Cs + (size_t)D * kTN;              // [kTT][kTN+1]
+    SC* Qs = reinterpret_cast<SC*>(smem_raw);   // [D][kLQ]
+    SC* Cs = Qs + (size_t)D * kLQ;              // [D][kLC]
+    SC* Ss = Cs + (size_t)D * kLC;              // [kTT][kTN+1]
     const int64_t b = blockIdx.y;
     const int64_t t0 = (int64_t)blockIdx.x * kTT;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -213,12 +295,21 @@ __global__ void __launch_bounds__(kTopkThreads) topk_tile_kernel(TopkArgs a) {
     const T* c = static_cast<const T*>(a.c);
     const SC scale = scale_of<SC>(a);
 
-    for (int e = tid; e < kTT * D; e += kTopkThreads) {
-        const int tt = e / D, d = e - (e / D) * D;
-        const int64_t t = t0 + tt;
-        SC x = SC(0);
-        if (t < a.L) x = load_as<SC>(q + b * a.sq[0] + t * a.sq[1] + d * a.sq[2]) * scale;
-        Qs[d * kTT + tt] = x;
+    load_tile_t<T, SC>(Qs, kLQ, q + b * a.sq[0], a.sq[1], a.sq[2], t0, a.L, D, scale, a.vecload != 0, tid);
+    const bool prune = a.cpref != nullptr && a.scores == nullptr;
+    // norms of this warp's 8 scaled query rows (for the candidate bound)
+    SC qn[8];
+    if (prune) {
+        __syncthreads();
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int tt = warp * 8 + j;
+            SC ss = SC(0);
+            for (int d = lane; d < D; d += 32) ss += Qs[d * kLQ + tt] * Qs[d * kLQ + tt];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(kFull, ss, o);
+            qn[j] = sqrt(ss);
+        }
     }
 
     const int64_t tlast = (t0 + kTT - 1 < a.L ? t0 + kTT - 1 : a.L - 1);
@@ -235,14 +326,29 @@ __global__ void __launch_bounds__(kTopkThreads) topk_tile_kernel(TopkArgs a) {
 
     const int ty = tid >> 4, tx = tid & 15;
     for (int64_t n0 = (n_hi / kTN) * kTN; n0 >= 0; n0 -= kTN) {
-        __syncthreads();
-        for (int e = tid; e < kTN * D; e += kTopkThreads) {
-            const int nn = e / D, d = e - (e / D) * D;
-            const int64_t n = n0 + nn;
-            SC x = SC(0);
-            if (n < a.nb) x = load_as<SC>(c + b * a.sc[0] + n * a.sc[1] + d * a.sc[2]);
-            Cs[d * kTN + nn] = x;
+        if (prune && n0 < (n_hi / kTN) * kTN) {
+            // Every candidate left has index < n0 + kTN, so its score is at most
+            // |q| max|c| (prefix max over the tiles left) minus the smallest penalty left.
+            // The scan stops when that bound is strictly below every token's current
+            // k-th best (ties go to the lower index, so equality must keep scanning).
+            const float cm = a.cpref[b * a.ntiles + n0 / kTN];
+            bool done = true;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int64_t t = t0 + warp * 8 + j;
+                const SC th = __shfl_sync(kFull, ls[j], a.keff - 1);
+                if (t < a.L) {
+                    const int64_t qb = query_block(a, t);
+                    const int64_t nhi = n0 + kTN - 1 < qb ? n0 + kTN - 1 : qb;
+                    SC bound = qn[j] * (SC)cm * (SC)1.00001 - (SC)a.pen[qb - nhi];
+                    bound += (bound < SC(0) ? -bound : bound) * (SC)1e-6 + (SC)1e-30;
+                    if (!(bound < th)) done = false;
+                }
+            }
+            if (__syncthreads_and(done)) break;
         }
+        __syncthreads();
+        load_tile_t<T, SC>(Cs, kLC, c + b * a.sc[0], a.sc[1], a.sc[2], n0, a.nb, D, SC(1), a.vecload != 0, tid);
         __syncthreads();
 
         SC acc[4][4];
@@ -253,9 +359,9 @@ __global__ void __launch_bounds__(kTopkThreads) topk_tile_kernel(TopkArgs a) {
         for (int d = 0; d < D; ++d) {
             SC qa[4], cb[4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) qa[i] = Qs[d * kTT + 4 * ty + i];
+            for (int i = 0; i < 4; ++i) qa[i] = Qs[d * kLQ + 4 * ty + i];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) cb[j] = Cs[d * kTN + 4 * tx + j];
+            for (int j = 0; j < 4; ++j) cb[j] = Cs[d * kLC + 4 * tx + j];
 #pragma unroll
             for (int i = 0; i < 4; ++i)
 #pragma unroll
@@ -572,7 +678,7 @@ int launch_topk(TopkArgs& a, int64_t B, cudaStream_t s) {
         kern<<<grid, kTopkThreads, smem, s>>>(a);
         return check_launch("index_topk(token)");
     }
-    const size_t smem = sizeof(SC) * ((size_t)D * kTT + (size_t)D * kTN + (size_t)kTT * (kTN + 1));
+    const size_t smem = sizeof(SC) * ((size_t)D * kLQ + (size_t)D * kLC + (size_t)kTT * (kTN + 1));
     if (smem > 200 * 1024) return set_error(MABA_ERR_UNSUPPORTED, "index_topk: d_idx=%d too large", D);
     auto kern = topk_tile_kernel<T, SC>;
     if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -633,17 +739,24 @@ extern "C" int maba_hca_pool(const maba_tensor* c_kv, const maba_tensor* out, in
     });
 }
 
+// Bytes after the penalty table: the decode split's partial lists, or the
+// centroid-norm tables of the pruned tile scan (never both in one call).
+static size_t topk_extra_bytes(int64_t B, int64_t L, int64_t nb, int32_t top_k) {
+    size_t extra = 0;
+    if (B * L <= 256 && nb >= 4 * kSplitCand && top_k <= 32)
+        extra = (size_t)B * L * decode_split_count(nb) * 32 * 8;
+    const size_t norms = 2 * (size_t)B * ceil_div(nb, (int64_t)kTN) * sizeof(float);
+    return extra > norms ? extra : norms;
+}
+
 extern "C" size_t maba_index_topk_workspace_size(int64_t B, int64_t L, int64_t nb, int32_t top_k) {
-    (void)B; (void)top_k;
     // penalty table; the block size is not known here, so size for the
     // largest query block any block_size >= 1 could produce is not bounded:
     // callers pass L and nb and the table holds max(nb, L) entries.
     int64_t n = nb > L ? nb : L;
     if (n < 1) n = 1;
     size_t bytes = (size_t)((n * sizeof(float) + 255) / 256 * 256);
-    if (B * L <= 256 && nb >= 4 * kSplitCand && top_k <= 32)  // room for the decode split partial lists
-        bytes += (size_t)B * L * decode_split_count(nb) * 32 * 8;
-    return bytes;
+    return bytes + topk_extra_bytes(B, L, nb, top_k);
 }
 
 static int index_topk_impl(const maba_tensor* q_idx, const maba_tensor* centroids, float lambda_dist,
@@ -721,6 +834,30 @@ static int index_topk_impl(const maba_tensor* q_idx, const maba_tensor* centroid
             }
         }
     }
+    // pruned tile scan: centroid-norm tables after the penalty table
+    const int64_t ntiles = ceil_div(nb, (int64_t)kTN);
+    const size_t off = (need + 255) / 256 * 256;
+    const bool vec_ok = (q_idx->dtype == MABA_BF16 || q_idx->dtype == MABA_F16) && D % 8 == 0 &&
+                        q_idx->stride[2] == 1 && centroids->stride[2] == 1 && q_idx->stride[1] % 8 == 0 &&
+                        centroids->stride[1] % 8 == 0 && q_idx->stride[0] % 8 == 0 && centroids->stride[0] % 8 == 0 &&
+                        (reinterpret_cast<uintptr_t>(q_idx->data) & 15u) == 0 &&
+                        (reinterpret_cast<uintptr_t>(centroids->data) & 15u) == 0;
+    a.vecload = vec_ok ? 1 : 0;
+    if (!decode && !present(scores_out) && L >= kTT && workspace_bytes >= off + 2 * (size_t)B * ntiles * sizeof(float) &&
+        q_idx->dtype != MABA_F64) {
+        float* tmax = reinterpret_cast<float*>(static_cast<char*>(workspace) + off);
+        float* pref = tmax + (size_t)B * ntiles;
+        MABA_TRY(MABA_DISPATCH_FLOAT(q_idx->dtype, "index_topk(norms)", [&] {
+            centroid_tile_norm_kernel<T><<<dim3((unsigned)ntiles, (unsigned)B), 64, 0, s>>>(
+                static_cast<const T*>(centroids->data), centroids->stride[0], centroids->stride[1],
+                centroids->stride[2], nb, (int)D, tmax, ntiles);
+            return check_launch("index_topk(norms)");
+        }));
+        tile_prefix_max_kernel<<<(unsigned)B, 256, 0, s>>>(tmax, pref, ntiles);
+        MABA_TRY(check_launch("index_topk(prefix max)"));
+        a.cpref = pref;
+        a.ntiles = ntiles;
+    }
     return MABA_DISPATCH_FLOAT(q_idx->dtype, "index_topk", [&] { return launch_topk<T>(a, B, s); });
 }
 
@@ -742,9 +879,10 @@ extern "C" int maba_index_topk_at(const maba_tensor* q_idx, const maba_tensor* c
 
 extern "C" size_t maba_index_topk_at_workspace_size(int64_t B, int64_t L, int64_t nb, int32_t top_k, int32_t block_size,
                                                     int64_t q_pos0) {
-    (void)B; (void)top_k;
     const int64_t n = penalty_len(L, nb, block_size > 0 ? block_size : 1, 0, q_pos0 > 0 ? q_pos0 : 0);
-    return (size_t)((n * sizeof(float) + 255) / 256 * 256);
+    const size_t norms = 2 * (size_t)B * ceil_div(nb, (int64_t)kTN) * sizeof(float);
+    (void)top_k;
+    return (size_t)((n * sizeof(float) + 255) / 256 * 256) + norms;
 }
 
 // ---------------------------------------------------------------------------

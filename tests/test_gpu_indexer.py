@@ -162,3 +162,37 @@ def test_superposition():
     olT = t["ol"].transpose(2, 3).contiguous().transpose(2, 3)
     np.testing.assert_allclose(mb.b200_stream_superposition(olT, t["os"], t["oh"], gate_logits=t["g3"]).cpu().numpy(),
                                g["o3"], rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("case", ["cfg2_bf16", "far_large_norms", "ties_lambda0", "fp32_scores_off"])
+def test_topk_pruned_scan_exact(case):
+    """The tile scan stops once |q| max|c| minus the smallest penalty left is strictly
+    below every token's k-th best: indices stay bit-identical to the full oracle scan,
+    including far blocks with large norms and exact ties (the lower index wins)."""
+    g = torch.Generator().manual_seed(77)
+    L, D = 8192, 64
+    nb = L // 64
+    lam, dt = 0.1, torch.float32
+    q = torch.randn(1, L, D, generator=g) / np.sqrt(128)
+    if case == "cfg2_bf16":
+        c = mb.b200_compute_centroids((torch.randn(1, L, D, generator=g) / np.sqrt(128)).to(DEV)).cpu()
+        dt = torch.bfloat16
+    elif case == "far_large_norms":
+        scale = 1.0 + 6.0 * (nb - torch.arange(nb, dtype=torch.float32)) / nb  # far blocks up to 7x larger
+        c = torch.randn(1, nb, D, generator=g) * scale[None, :, None]
+        lam = 0.01
+    elif case == "ties_lambda0":
+        c = torch.randn(1, nb, D, generator=g)
+        c[:, :64] = c[:, 64:128]  # block n and n + 64 identical: equal scores, lower index first
+        lam = 0.0
+    else:
+        c = torch.randn(1, nb, D, generator=g)
+    qd, cd = q.to(dt), c.to(dt)
+    idx = mb.b200_index_topk(qd.to(DEV), cd.to(DEV), lambda_dist=lam, top_k=32, block_size=64)
+    rows = np.arange(0, L, 7)
+    oidx = OI.index_topk(qd.float().numpy(), cd.float().numpy(), lambda_dist=lam, top_k=32, rows=rows)
+    np.testing.assert_array_equal(idx[0, torch.as_tensor(rows, device=DEV)].cpu().numpy(), oidx[0])
+    if case == "fp32_scores_off":
+        idx2, _ = mb.b200_index_topk(qd.to(DEV), cd.to(DEV), lambda_dist=lam, top_k=32, block_size=64,
+                                     return_scores=True)  # scores requested: the unpruned scan
+        assert torch.equal(idx, idx2)
