@@ -53,10 +53,10 @@ constexpr int KT = 64;            // keys per tile (= block size)
 constexpr int DCX = 128;          // latent dim
 constexpr int HPG = 2;            // heads per MMA tile
 constexpr int ROWS = QT * HPG;    // MMA rows
-constexpr int NS = 4;             // key-tile stages
+constexpr int NS = 6;             // key-tile stages
 constexpr int KMAX = 32;          // selected blocks per token
 constexpr int UMAX = QT * KMAX;   // union capacity
-constexpr int NTHR = 192;         // 6 warps
+constexpr int NTHR = 320;         // 10 warps: producer, MMA, 2 x 4 softmax
 constexpr int TMEM_COLS = 512;
 constexpr int COL_S = 0;
 constexpr int COL_O = 128;
@@ -67,23 +67,28 @@ constexpr uint32_t Q_HALF = ROWS * 128;     // 16 KB: 128 rows x 64 elements
 constexpr uint32_t Q_BYTES = 2 * Q_HALF;
 constexpr uint32_t KV_HALF = KT * 128;      // 8 KB: 64 rows x 64 elements
 constexpr uint32_t KV_BYTES = 2 * KV_HALF;
+constexpr uint32_t P_BYTES = ROWS * 128;    // 16 KB: P of one tile, 128 rows x 64 keys (16-bit)
 
 enum { B_QFULL = 0, B_QEMPTY = 2, B_KVFULL = 4, B_KVEMPTY = B_KVFULL + NS, B_SFULL = B_KVEMPTY + NS,
-       B_PFULL = B_SFULL + 2, B_ODONE = B_PFULL + 2, B_DRAIN = B_ODONE + 2, N_BARS = B_DRAIN + 1 };
+       B_PFULL = B_SFULL + 2, B_ODONE = B_PFULL + 2, B_SFREE = B_ODONE + 2, B_DRAIN = B_SFREE + 2,
+       N_BARS = B_DRAIN + 1 };
+static_assert(N_BARS <= 32, "barrier area holds 32 mbarriers");
 
 struct TcLayout {
-    uint32_t q, kv, bars, misc, umask, ulist, bitmap, wpref, scan, total;
+    uint32_t q, kv, p, bars, misc, umask, ulist, bitmap, wpref, scan, xch, total;
     __host__ __device__ explicit TcLayout(int nwords) {
         q = 0;
         kv = q + 2 * Q_BYTES;
-        bars = kv + NS * KV_BYTES;
+        p = kv + NS * KV_BYTES;
+        bars = p + 2 * P_BYTES;
         misc = bars + 32 * 8;
         umask = misc + 16;
         ulist = umask + UMAX * 8;
         bitmap = ulist + UMAX * 4;
         wpref = bitmap + nwords * 4;
         scan = wpref + nwords * 4;
-        total = scan + (NTHR + 16) * 4;
+        xch = scan + (NTHR + 16) * 4;  // tile maxima [2 groups][2 slots][128], row sums [2 groups][3][128]
+        total = xch + (2 * 2 + 2 * 3) * 128 * 4;
     }
 };
 
@@ -91,6 +96,31 @@ __device__ __forceinline__ float ex2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
+}
+
+// max of three (one instruction on sm_100)
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
+// {d0, d1} = {a0, a1} * b + c, one packed fp32 FMA
+__device__ __forceinline__ void fma2(float& d0, float& d1, float a0, float a1, float b, float c) {
+    asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %4};\n\tmov.b64 rc, {%5, %5};\n\t"
+        "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d0), "=f"(d1)
+        : "f"(a0), "f"(a1), "f"(b), "f"(c));
+}
+
+// {a0, a1} += {b0, b1}, one packed fp32 add
+__device__ __forceinline__ void add2(float& a0, float& a1, float b0, float b1) {
+    asm("{\n\t.reg .b64 ra, rb;\n\t"
+        "mov.b64 ra, {%0, %1};\n\tmov.b64 rb, {%2, %3};\n\t"
+        "add.rn.f32x2 ra, ra, rb;\n\tmov.b64 {%0, %1}, ra;\n\t}"
+        : "+f"(a0), "+f"(a1)
+        : "f"(b0), "f"(b1));
 }
 
 template <typename T> __device__ __forceinline__ uint32_t pack2(float lo, float hi);
@@ -114,6 +144,7 @@ __global__ void __launch_bounds__(NTHR, 1)
     const TcLayout LY(nwords);
     unsigned char* Qs = base + LY.q;
     unsigned char* KVs = base + LY.kv;
+    unsigned char* Ps = base + LY.p;
     uint64_t* bars = reinterpret_cast<uint64_t*>(base + LY.bars);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + LY.misc);
     volatile int* abort_f = reinterpret_cast<volatile int*>(base + LY.misc + 4);
@@ -137,7 +168,7 @@ __global__ void __launch_bounds__(NTHR, 1)
     if (tid == 0) {
         for (int i = 0; i < N_BARS; ++i) {
             uint32_t cnt = 1;
-            if (i == B_PFULL || i == B_PFULL + 1) cnt = 128;
+            if (i == B_PFULL || i == B_PFULL + 1 || i == B_SFREE || i == B_SFREE + 1) cnt = 128;
             mbar_init(&bars[i], cnt);
         }
         *abort_f = 0;
@@ -302,57 +333,83 @@ __global__ void __launch_bounds__(NTHR, 1)
         const uint64_t qd0 = sdesc_sw128(smem_addr(Qs), 16, 1024);
         const uint64_t kd0 = sdesc_sw128(smem_addr(KVs), 16, 1024);
         const uint64_t vd0 = sdesc_sw128(smem_addr(KVs), KV_HALF, 1024);
-        int hp = 0, j = 0, ij = 0;
+        const uint64_t pd0 = sdesc_sw128(smem_addr(Ps), 16, 1024);
+        // QK runs two tiles ahead of PV: QK(g) needs only that the group owning S
+        // buffer g&1 has loaded tile g-2 out of it (P goes to shared memory).
+        int gq = 0, jq = 0, hq = 0;  // next QK: global tile, tile of its head pair, head pair
         bool okm = true;
-        for (int g = 0; g <= G; ++g) {
-            if (g < G) {
-                const int st = g % NS, sb = g & 1, qb = hp & 1;
-                if (j == 0) okm = mbar_wait_warp(&bars[B_QFULL + qb], (hp >> 1) & 1, abort_f);
-                if (okm) okm = mbar_wait_warp(&bars[B_KVFULL + st], (g / NS) & 1, abort_f);
-                if (!okm) break;
-                tc_fence_after();
-                const uint64_t qd = qd0 + (uint64_t)(qb * (Q_BYTES >> 4));
-                const uint64_t kd = kd0 + (uint64_t)(st * (KV_BYTES >> 4));
+        auto issue_qk = [&]() {
+            const int st = gq % NS, sb = gq & 1, qb = hq & 1;
+            if (jq == 0) okm = mbar_wait_warp(&bars[B_QFULL + qb], (hq >> 1) & 1, abort_f);
+            if (okm) okm = mbar_wait_warp(&bars[B_KVFULL + st], (gq / NS) & 1, abort_f);
+            if (okm && gq >= 2) okm = mbar_wait_warp(&bars[B_SFREE + sb], ((gq - 2) >> 1) & 1, abort_f);
+            if (!okm) return;
+            tc_fence_after();
+            const uint64_t qd = qd0 + (uint64_t)(qb * (Q_BYTES >> 4));
+            const uint64_t kd = kd0 + (uint64_t)(st * (KV_BYTES >> 4));
 #pragma unroll
-                for (int k = 0; k < DCX / 16; ++k) {
-                    const uint32_t off_q = (k >> 2) * (Q_HALF >> 4) + (k & 3) * 2;
-                    const uint32_t off_k = (k >> 2) * (KV_HALF >> 4) + (k & 3) * 2;
-                    umma_f16_ss_elect(tmem + COL_S + sb * KT, qd + off_q, kd + off_k, ID_QK, k > 0 ? 1u : 0u);
-                }
-                umma_commit_elect(&bars[B_SFULL + sb]);
-                if (j == n_tiles - 1) umma_commit_elect(&bars[B_QEMPTY + qb]);
+            for (int k = 0; k < DCX / 16; ++k) {
+                const uint32_t off_q = (k >> 2) * (Q_HALF >> 4) + (k & 3) * 2;
+                const uint32_t off_k = (k >> 2) * (KV_HALF >> 4) + (k & 3) * 2;
+                umma_f16_ss_elect(tmem + COL_S + sb * KT, qd + off_q, kd + off_k, ID_QK, k > 0 ? 1u : 0u);
             }
-            if (g >= 1) {
-                const int i = g - 1, st = i % NS, sb = i & 1;
-                okm = mbar_wait_warp(&bars[B_PFULL + sb], (i >> 1) & 1, abort_f);
+            umma_commit_elect(&bars[B_SFULL + sb]);
+            if (jq == n_tiles - 1) umma_commit_elect(&bars[B_QEMPTY + qb]);
+            ++gq;
+            if (++jq == n_tiles) {
+                jq = 0;
+                ++hq;
+            }
+        };
+        issue_qk();
+        if (okm && gq < G) issue_qk();
+        int ij = 0;
+        for (int i = 0; i < G && okm; ++i) {
+            if (gq < G) {
+                issue_qk();  // QK(i + 2)
                 if (!okm) break;
-                tc_fence_after();
-                const int stream = ij < n_local ? 0 : (ij < n_local + U ? 1 : 2);
-                const bool first = ij == 0 || ij == n_local || ij == n_local + U;
-                const uint32_t dst = tmem + COL_O + stream * DCX;
-                const uint64_t vd = vd0 + (uint64_t)(st * (KV_BYTES >> 4));
+            }
+            const int st = i % NS, sb = i & 1;
+            okm = mbar_wait_warp(&bars[B_PFULL + sb], (i >> 1) & 1, abort_f);
+            if (!okm) break;
+            tc_fence_after();
+            const int stream = ij < n_local ? 0 : (ij < n_local + U ? 1 : 2);
+            const bool first = ij == 0 || ij == n_local || ij == n_local + U;
+            const uint32_t dst = tmem + COL_O + stream * DCX;
+            const uint64_t vd = vd0 + (uint64_t)(st * (KV_BYTES >> 4));
+            const uint64_t pd = pd0 + (uint64_t)(sb * (P_BYTES >> 4));
 #pragma unroll
-                for (int k = 0; k < KT / 16; ++k)
-                    umma_f16_ts_elect(dst, tmem + COL_S + sb * KT + k * 8, vd + (uint64_t)(k * (2048 >> 4)), ID_PV,
-                                      (k > 0 || !first) ? 1u : 0u);
-                umma_commit_elect(&bars[B_KVEMPTY + st]);
-                umma_commit_elect(&bars[B_ODONE + sb]);
-                if (++ij == n_tiles) ij = 0;
-            }
-            if (g < G && ++j == n_tiles) {
-                j = 0;
-                ++hp;
-            }
+            for (int k = 0; k < KT / 16; ++k)
+                umma_f16_ss_elect(dst, pd + (uint64_t)(k * 2), vd + (uint64_t)(k * (2048 >> 4)), ID_PV,
+                                  (k > 0 || !first) ? 1u : 0u);
+            umma_commit_elect(&bars[B_KVEMPTY + st]);
+            umma_commit_elect(&bars[B_ODONE + sb]);
+            if (++ij == n_tiles) ij = 0;
         }
         // every MMA issued has completed before TMEM is freed
         umma_commit_elect(&bars[B_DRAIN]);
         mbar_wait_warp(&bars[B_DRAIN], 0, nullptr);
     } else {
-        // ===================== softmax + epilogue (128 threads) ===============
+        // ===================== softmax + epilogue (256 threads) ===============
+        // Two groups of four warps, one warp per TMEM lane quarter in each.  Group wg
+        // owns the key tiles whose global index has parity wg (its S buffer is wg), so
+        // the two warps of a lane quarter, which share an SM sub-partition, work on
+        // consecutive tiles in different phases: one runs exponentials while the other
+        // loads and reduces.  The reference maximum of a row is a function of the tile
+        // maxima in tile order: each warp publishes its tiles' maxima to its partner
+        // (named barriers used as producer -> consumer pairs) and replays the
+        // partner's, so both hold the same reference at every tile.  Each warp keeps
+        // the row sums of its own tiles; the pair adds them at the end of a head pair.
+        // Every named-barrier call is unconditional (a wait that ran out only skips
+        // TMEM work), so the two warps always make the same calls.
+        const int wg = (warp - 2) >> 2;
         const int q4 = warp & 3;
         const int rid = q4 * 32 + lane;
         const int t = rid >> 1, hh = rid & 1;
         const bool rvalid = t < nt;
+        const int bar_mine = 1 + wg * 4 + q4, bar_other = 1 + (wg ^ 1) * 4 + q4, bar_pair = 9 + q4;
+        float* xmax = reinterpret_cast<float*>(base + LY.xch);  // [2 groups][2 slots][128]
+        float* xls = xmax + 2 * 2 * 128;                          // [2 groups][3 streams][128]
         // positions fit in 32 bits (Lkv < 2^31 on this path)
         const int pos = (int)(P0 + t);
         const int lkv = (int)a.Lkv;
@@ -368,197 +425,238 @@ __global__ void __launch_bounds__(NTHR, 1)
         const unsigned long long tbit = 1ull << t;
         const T* ckv = static_cast<const T*>(a.ckv) + b * a.sc[0];
         auto clampk = [](int x) { return x < 0 ? 0 : (x > KT ? KT : x); };
-        // stream of tile j and the valid columns of this row: [a1, b1) and the sinks [0, b2)
-        auto bounds = [&](int j, int& stream, int& a1, int& b1, int& b2) {
+        auto stream_of = [&](int j) { return j < n_local ? 0 : (j < n_local + U ? 1 : 2); };
+        // valid columns of this row in tile j: [a1, b1) and the sinks [0, b2)
+        auto bounds = [&](int j, int& a1, int& b1, int& b2) {
             a1 = 0;
             b1 = 0;
             b2 = 0;
+            if (!rvalid) return;
             if (j < n_local) {
-                stream = 0;
                 const int row0 = sink_tile ? (j == 0 ? 0 : (int)ws + (j - 1) * KT) : (int)ws + j * KT;
-                if (rvalid) {
-                    a1 = clampk(lo_p - row0);
-                    b1 = clampk(pos - row0 + 1);
-                    b2 = clampk(sink_end - row0);
-                }
+                a1 = clampk(lo_p - row0);
+                b1 = clampk(pos - row0 + 1);
+                b2 = clampk(sink_end - row0);
             } else if (j < n_local + U) {
-                stream = 1;
                 const int u = j - n_local;
-                const int row0 = ulist[u] * KT;
-                if (rvalid && (umask[u] & tbit)) b1 = clampk(sp_end - row0);
+                if (umask[u] & tbit) b1 = clampk(sp_end - ulist[u] * KT);
             } else {
-                stream = 2;
-                if (rvalid) b1 = clampk(nv_hca - (j - n_local - U) * KT);
+                b1 = clampk(nv_hca - (j - n_local - U) * KT);
             }
         };
-        int nstream = 0, na1 = 0, nb1 = 0, nb2 = 0;
-        bounds(0, nstream, na1, nb1, nb2);
-        bool ok = true;
-        int g = 0;
-        for (int hp = 0; hp < NH && ok; ++hp) {
-            float lsum0 = 0.f, lsum1 = 0.f, lsum2 = 0.f;
+        auto pair_sync = [&](int id) { asm volatile("bar.sync %0, 64;" ::"r"(id) : "memory"); };
+        bool okw = true;  // every wait of this warp completed
+        for (int hp = 0; hp < NH; ++hp) {
+            const int g0 = hp * n_tiles;
+            float l0 = 0.f, l1 = 0.f, l2 = 0.f;  // this warp's share of the row sums per stream
             float m_cur = -INFINITY, l_cur = 0.f;
             int cur = -1;
-            for (int j = 0; j < n_tiles; ++j, ++g) {
-                const int sb = g & 1;
-                const int stream = nstream, a1 = na1, b1 = nb1, b2 = nb2;
-                if (stream != cur) {
-                    if (cur == 0) lsum0 = l_cur;
-                    else if (cur == 1) lsum1 = l_cur;
+            // folds the maximum mx (log2 units) of the next tile, of stream st, into the
+            // running state; returns the factor of the rescale it causes (1: none)
+            auto apply = [&](int st, float mx) -> float {
+                if (st != cur) {
+                    if (cur == 0) l0 = l_cur;
+                    else if (cur == 1) l1 = l_cur;
                     m_cur = -INFINITY;
                     l_cur = 0.f;
-                    cur = stream;
+                    cur = st;
                 }
-                ok = mbar_wait_warp(&bars[B_SFULL + sb], (g >> 1) & 1, abort_f);
-                if (!ok) break;
-                tc_fence_after();
-                const uint32_t ts = tmem + lane_base + COL_S + sb * KT;
-                uint32_t s[64];
-                tmem_ld32(ts, s);
-                tmem_ld32(ts + 32, s + 32);
-                // next tile's bounds while the load is in flight
-                bounds(j + 1 < n_tiles ? j + 1 : 0, nstream, na1, nb1, nb2);
-                tmem_wait_ld_pin64(s);
-                // row class: none (no valid column), full (all 64), or partial
-                const bool none = b1 <= a1 && b2 == 0;
-                const bool full = a1 == 0 && b1 == KT;
-                float m8[8];
-#pragma unroll
-                for (int i = 0; i < 8; ++i) m8[i] = -INFINITY;
-                if (__any_sync(0xffffffffu, !none && !full)) {
-                    unsigned long long vm = 0ull;
-                    if (b1 > a1) vm = (b1 >= 64 ? ~0ull : ((1ull << b1) - 1ull)) & ~((1ull << a1) - 1ull);
-                    if (b2 > 0) vm |= b2 >= 64 ? ~0ull : ((1ull << b2) - 1ull);
-                    const uint32_t vlo = (uint32_t)vm, vhi = (uint32_t)(vm >> 32);
-#pragma unroll
-                    for (int c = 0; c < KT; ++c) {
-                        const bool v = ((c < 32 ? vlo : vhi) >> (c & 31)) & 1u;
-                        const float x = v ? __uint_as_float(s[c]) : -INFINITY;
-                        s[c] = __float_as_uint(x);
-                        m8[c & 7] = fmaxf(m8[c & 7], x);
-                    }
-                } else {
-#pragma unroll
-                    for (int c = 0; c < KT; ++c) m8[c & 7] = fmaxf(m8[c & 7], __uint_as_float(s[c]));
-                }
-                float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                                 fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7]))) * LOG2E;
-                if (none) mx = -INFINITY;
                 float fac = 1.f;
-                bool resc = false;
                 if (mx != -INFINITY) {
                     if (m_cur == -INFINITY) {
                         m_cur = mx;
                     } else if (mx > m_cur + RESCALE_T) {
                         fac = ex2(m_cur - mx);
                         m_cur = mx;
-                        resc = true;
+                        l_cur *= fac;
                     }
                 }
-                // rows without a valid column give p = 0 (ex2(-inf)); scores are finite
-                const float nmu = none ? -INFINITY : (m_cur == -INFINITY ? 0.f : -m_cur);
-                float ps[4] = {0.f, 0.f, 0.f, 0.f};
-                uint32_t pk[32];
-#pragma unroll
-                for (int c = 0; c < KT; c += 2) {
-                    const float p0 = ex2(fmaf(__uint_as_float(s[c]), LOG2E, nmu));
-                    const float p1 = ex2(fmaf(__uint_as_float(s[c + 1]), LOG2E, nmu));
-                    ps[(c >> 1) & 3] += p0 + p1;
-                    pk[c >> 1] = pack2<T>(p0, p1);
-                }
-                l_cur = l_cur * fac + ((ps[0] + ps[1]) + (ps[2] + ps[3]));
-                tmem_st32(ts, pk);  // P over the first 32 columns of the S buffer
-                if (__any_sync(0xffffffffu, resc)) {
-                    // every PV so far (the latest: tile g-1) has completed before O is rescaled
-                    if (g >= 1) {
-                        ok = mbar_wait_warp(&bars[B_ODONE + ((g - 1) & 1)], ((g - 1) >> 1) & 1, abort_f);
-                        if (!ok) break;
-                    }
+                return fac;
+            };
+            for (int j = (g0 & 1) == wg ? 0 : 1; j < n_tiles; j += 2) {
+                const int gg = g0 + j;
+                const int st = stream_of(j);
+                int a1, b1, b2;
+                bounds(j, a1, b1, b2);
+                const bool none = b1 <= a1 && b2 == 0;
+                const bool full = a1 == 0 && b1 >= KT;
+                const bool oks = mbar_wait_warp(&bars[B_SFULL + wg], (gg >> 1) & 1, abort_f);
+                okw = okw && oks;
+                const uint32_t ts = tmem + lane_base + COL_S + wg * KT;
+                uint32_t s[KT];
+                float mt = -INFINITY;
+                if (oks) {
                     tc_fence_after();
-                    const uint32_t to = tmem + lane_base + COL_O + stream * DCX;
+                    tmem_ld32(ts, s);
+                    tmem_ld32(ts + 32, s + 32);
+                    tmem_wait_ld_pin64(s);
+                }
+                // S is in registers: the MMA warp may compute tile gg+2 into this buffer
+                tc_fence_before();
+                mbar_arrive(&bars[B_SFREE + wg]);
+                if (oks) {
+                    if (__any_sync(0xffffffffu, !none && !full)) {
+                        unsigned long long vm = 0ull;
+                        if (b1 > a1) vm = (b1 >= 64 ? ~0ull : ((1ull << b1) - 1ull)) & ~((1ull << a1) - 1ull);
+                        if (b2 > 0) vm |= b2 >= 64 ? ~0ull : ((1ull << b2) - 1ull);
 #pragma unroll
-                    for (int cc = 0; cc < DCX / 32; ++cc) {
-                        uint32_t o[32];
-                        tmem_ld32(to + cc * 32, o);
-                        tmem_wait_ld();
+                        for (int c = 0; c < KT; ++c)
+                            if (!((vm >> c) & 1ull)) s[c] = __float_as_uint(-INFINITY);
+                    }
+                    float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-                        for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * fac);
-                        tmem_st32(to + cc * 32, o);
+                    for (int c = 0; c < KT; c += 2)
+                        m4[(c >> 1) & 3] = fmax3(m4[(c >> 1) & 3], __uint_as_float(s[c]), __uint_as_float(s[c + 1]));
+                    mt = none ? -INFINITY : fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * LOG2E;
+                }
+                // the partner's previous tile of this head pair, then this one
+                if (j >= 1) {
+                    pair_sync(bar_other);
+                    apply(stream_of(j - 1), xmax[((wg ^ 1) * 2 + (((gg - 1) >> 1) & 1)) * 128 + rid]);
+                }
+                xmax[(wg * 2 + ((gg >> 1) & 1)) * 128 + rid] = mt;
+                asm volatile("bar.arrive %0, 64;" ::"r"(bar_mine) : "memory");
+                const float fac = apply(st, mt);
+                if (oks) {
+                    // rows without a valid column give p = 0 (ex2(-inf)); scores are finite
+                    const float nmu = none ? -INFINITY : (m_cur == -INFINITY ? 0.f : -m_cur);
+                    float sa0 = 0.f, sa1 = 0.f, sb0 = 0.f, sb1 = 0.f;
+                    uint32_t pk[KT / 2];
+#pragma unroll
+                    for (int c = 0; c < KT; c += 4) {
+                        float x0, x1, x2, x3;
+                        fma2(x0, x1, __uint_as_float(s[c]), __uint_as_float(s[c + 1]), LOG2E, nmu);
+                        fma2(x2, x3, __uint_as_float(s[c + 2]), __uint_as_float(s[c + 3]), LOG2E, nmu);
+                        const float p0 = ex2(x0), p1 = ex2(x1), p2 = ex2(x2), p3 = ex2(x3);
+                        add2(sa0, sa1, p0, p1);
+                        add2(sb0, sb1, p2, p3);
+                        pk[c >> 1] = pack2<T>(p0, p1);
+                        pk[(c >> 1) + 1] = pack2<T>(p2, p3);
+                    }
+                    l_cur += (sa0 + sa1) + (sb0 + sb1);
+                    // P into shared-memory buffer wg (the A operand of PV, 128-byte swizzled
+                    // rows) once PV(gg-2) has read the buffer
+                    const bool okp =
+                        gg < 2 || mbar_wait_warp(&bars[B_ODONE + wg], ((gg - 2) >> 1) & 1, abort_f);
+                    okw = okw && okp;
+                    if (okp) {
+                        unsigned char* prow = Ps + wg * P_BYTES + (rid >> 3) * 1024 + (rid & 7) * 128;
+#pragma unroll
+                        for (int c = 0; c < 8; ++c)
+                            *reinterpret_cast<uint4*>(prow + ((c ^ (rid & 7)) << 4)) =
+                                make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+                        fence_proxy_async_smem();
+                    }
+                }
+                if (__any_sync(0xffffffffu, fac != 1.f)) {
+                    // every PV so far (the latest: tile gg-1, the partner's) has completed
+                    const bool okr = mbar_wait_warp(&bars[B_ODONE + ((gg - 1) & 1)], ((gg - 1) >> 1) & 1, abort_f);
+                    okw = okw && okr;
+                    if (okr) {
+                        tc_fence_after();
+                        const uint32_t to = tmem + lane_base + COL_O + st * DCX;
+#pragma unroll 1
+                        for (int cc = 0; cc < DCX / 32; ++cc) {
+                            uint32_t o[32];
+                            tmem_ld32(to + cc * 32, o);
+                            tmem_wait_ld();
+#pragma unroll
+                            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * fac);
+                            tmem_st32(to + cc * 32, o);
+                        }
                     }
                 }
                 tmem_wait_st();
                 tc_fence_before();
-                mbar_arrive(&bars[B_PFULL + sb]);
+                mbar_arrive(&bars[B_PFULL + wg]);
             }
-            if (!ok) break;
-            if (cur == 0) lsum0 = l_cur;
-            else if (cur == 1) lsum1 = l_cur;
-            else if (cur == 2) lsum2 = l_cur;
+            // the partner's last tile, if it owns it
+            const int gend = g0 + n_tiles;
+            if (((gend - 1) & 1) != wg) {
+                pair_sync(bar_other);
+                apply(stream_of(n_tiles - 1), xmax[((wg ^ 1) * 2 + (((gend - 1) >> 1) & 1)) * 128 + rid]);
+            }
+            if (cur == 0) l0 = l_cur;
+            else if (cur == 1) l1 = l_cur;
+            else if (cur == 2) l2 = l_cur;
             // ------------------------- epilogue of head pair hp ------------------
-            // the last two PVs of the head pair (tiles g-2, g-1) have completed
-            if (g >= 2)
-                ok = mbar_wait_warp(&bars[B_ODONE + (g & 1)], ((g - 2) >> 1) & 1, abort_f);
-            if (ok) ok = mbar_wait_warp(&bars[B_ODONE + ((g - 1) & 1)], ((g - 1) >> 1) & 1, abort_f);
-            if (!ok) break;
-            tc_fence_after();
-            const int h = hp * HPG + hh;
-            float g0 = 0.f, g1 = 0.f, g2 = 0.f;
-            if (rvalid) {
-                const T* gp = static_cast<const T*>(a.gate);
-                const T* gr = a.gate4d ? gp + b * a.sg[0] + h * a.sg[1] + (q0 + t) * a.sg[2]
-                                       : gp + b * a.sg[0] + (q0 + t) * a.sg[1];
-                const int64_t gs = a.gate4d ? a.sg[3] : a.sg[2];
-                g0 = Cvt<T>::to_f(gr[0]);
-                g1 = Cvt<T>::to_f(gr[gs]);
-                g2 = Cvt<T>::to_f(gr[2 * gs]);
-                const float m = fmaxf(g0, fmaxf(g1, g2));
-                const float e0 = expf(g0 - m), e1 = expf(g1 - m), e2 = expf(g2 - m);
-                const float inv = 1.f / (e0 + e1 + e2);
-                g0 = e0 * inv;
-                g1 = e1 * inv;
-                g2 = e2 * inv;
-            }
-            const bool u0 = lsum0 > 0.f, u1 = lsum1 > 0.f, u2 = lsum2 > 0.f;
-            const float f0 = u0 ? g0 / lsum0 : 0.f, f1 = u1 ? g1 / lsum1 : 0.f, f2 = u2 ? g2 / lsum2 : 0.f;
-            const bool early = rvalid && pos < a.hca_r - 1;  // HCA: mean of the latent prefix
-            T* orow = static_cast<T*>(a.out) + b * a.so[0] + (q0 + (rvalid ? t : 0)) * a.so[1] + (int64_t)h * a.so[2];
-            const uint32_t to = tmem + lane_base + COL_O;
-#pragma unroll 1
-            for (int cc = 0; cc < DCX / 32; ++cc) {
-                uint32_t o0[32], o1[32], o2[32];
-                tmem_ld32(to + cc * 32, o0);
-                tmem_ld32(to + DCX + cc * 32, o1);
-                tmem_ld32(to + 2 * DCX + cc * 32, o2);
-                tmem_wait_ld();
-                float v[32];
-#pragma unroll
-                for (int e = 0; e < 32; ++e) {
-                    float x = u0 ? f0 * __uint_as_float(o0[e]) : 0.f;
-                    x += u1 ? f1 * __uint_as_float(o1[e]) : 0.f;
-                    x += u2 ? f2 * __uint_as_float(o2[e]) : 0.f;
-                    v[e] = x;
-                }
-                if (early) {
-                    const float w = g2 / float(pos + 1);
-                    for (int64_t jj = 0; jj <= pos; ++jj) {
-                        const T* cr = ckv + jj * a.sc[1] + cc * 32;
-#pragma unroll
-                        for (int e = 0; e < 32; ++e) v[e] += w * Cvt<T>::to_f(cr[e]);
-                    }
-                }
+            // the last two PVs of the head pair (tiles gend-2, gend-1) have completed
+            bool oke = gend < 2 || mbar_wait_warp(&bars[B_ODONE + (gend & 1)], ((gend - 2) >> 1) & 1, abort_f);
+            if (oke) oke = mbar_wait_warp(&bars[B_ODONE + ((gend - 1) & 1)], ((gend - 1) >> 1) & 1, abort_f);
+            okw = okw && oke;
+            xls[(wg * 3 + 0) * 128 + rid] = l0;
+            xls[(wg * 3 + 1) * 128 + rid] = l1;
+            xls[(wg * 3 + 2) * 128 + rid] = l2;
+            pair_sync(bar_pair);
+            // row sums over both warps' tiles
+            const float L0 = l0 + xls[((wg ^ 1) * 3 + 0) * 128 + rid];
+            const float L1 = l1 + xls[((wg ^ 1) * 3 + 1) * 128 + rid];
+            const float L2 = l2 + xls[((wg ^ 1) * 3 + 2) * 128 + rid];
+            if (okw) {
+                tc_fence_after();
+                const int h = hp * HPG + hh;
+                float g0v = 0.f, g1v = 0.f, g2v = 0.f;
                 if (rvalid) {
+                    const T* gp = static_cast<const T*>(a.gate);
+                    const T* gr = a.gate4d ? gp + b * a.sg[0] + h * a.sg[1] + (q0 + t) * a.sg[2]
+                                           : gp + b * a.sg[0] + (q0 + t) * a.sg[1];
+                    const int64_t gs = a.gate4d ? a.sg[3] : a.sg[2];
+                    g0v = Cvt<T>::to_f(gr[0]);
+                    g1v = Cvt<T>::to_f(gr[gs]);
+                    g2v = Cvt<T>::to_f(gr[2 * gs]);
+                    const float m = fmaxf(g0v, fmaxf(g1v, g2v));
+                    const float e0 = expf(g0v - m), e1 = expf(g1v - m), e2 = expf(g2v - m);
+                    const float inv = 1.f / (e0 + e1 + e2);
+                    g0v = e0 * inv;
+                    g1v = e1 * inv;
+                    g2v = e2 * inv;
+                }
+                const bool u0 = L0 > 0.f, u1 = L1 > 0.f, u2 = L2 > 0.f;
+                const float f0 = u0 ? g0v / L0 : 0.f, f1 = u1 ? g1v / L1 : 0.f, f2 = u2 ? g2v / L2 : 0.f;
+                const bool early = rvalid && pos < a.hca_r - 1;  // HCA: mean of the latent prefix
+                T* orow =
+                    static_cast<T*>(a.out) + b * a.so[0] + (q0 + (rvalid ? t : 0)) * a.so[1] + (int64_t)h * a.so[2];
+                const uint32_t to = tmem + lane_base + COL_O + wg * 64;
+#pragma unroll 1
+                for (int cc = 0; cc < 2; ++cc) {
+                    const int col0 = wg * 64 + cc * 32;
+                    uint32_t r0[32], r1[32], r2[32];
+                    tmem_ld32(to + cc * 32, r0);
+                    tmem_ld32(to + DCX + cc * 32, r1);
+                    tmem_ld32(to + 2 * DCX + cc * 32, r2);
+                    tmem_wait_ld();
+                    float v[32];
 #pragma unroll
-                    for (int e8 = 0; e8 < 4; ++e8) {
-                        uint4 w4 = make_uint4(pack2<T>(v[8 * e8 + 0], v[8 * e8 + 1]),
-                                              pack2<T>(v[8 * e8 + 2], v[8 * e8 + 3]),
-                                              pack2<T>(v[8 * e8 + 4], v[8 * e8 + 5]),
-                                              pack2<T>(v[8 * e8 + 6], v[8 * e8 + 7]));
-                        *reinterpret_cast<uint4*>(orow + cc * 32 + 8 * e8) = w4;
+                    for (int e = 0; e < 32; ++e) {
+                        float x = u0 ? f0 * __uint_as_float(r0[e]) : 0.f;
+                        x += u1 ? f1 * __uint_as_float(r1[e]) : 0.f;
+                        x += u2 ? f2 * __uint_as_float(r2[e]) : 0.f;
+                        v[e] = x;
+                    }
+                    if (early) {
+                        const float w = g2v / float(pos + 1);
+                        for (int jj = 0; jj <= pos; ++jj) {
+                            const T* cr = ckv + (int64_t)jj * a.sc[1] + col0;
+#pragma unroll
+                            for (int e = 0; e < 32; ++e) v[e] += w * Cvt<T>::to_f(cr[e]);
+                        }
+                    }
+                    if (rvalid) {
+#pragma unroll
+                        for (int e8 = 0; e8 < 4; ++e8) {
+                            uint4 w4 = make_uint4(pack2<T>(v[8 * e8 + 0], v[8 * e8 + 1]),
+                                                  pack2<T>(v[8 * e8 + 2], v[8 * e8 + 3]),
+                                                  pack2<T>(v[8 * e8 + 4], v[8 * e8 + 5]),
+                                                  pack2<T>(v[8 * e8 + 6], v[8 * e8 + 7]));
+                            *reinterpret_cast<uint4*>(orow + col0 + 8 * e8) = w4;
+                        }
                     }
                 }
             }
-            // the next head pair's PVs overwrite O: every TMEM read above is complete
+            // both warps have read O before either arrives for the next head pair's
+            // first tile (whose PV overwrites O)
             tc_fence_before();
+            pair_sync(bar_pair);
         }
     }
     tc_fence_before();

@@ -37,6 +37,20 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
                  : "memory");
 }
+// Blocking test with a suspend-time hint: the warp sleeps (issuing nothing)
+// until the phase completes or about `hint_ns` nanoseconds passed.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
@@ -85,10 +99,13 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
 __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort,
                                                long long limit = 2000000000ll) {
     if (__all_sync(0xffffffffu, mbar_test(bar, parity))) return true;
-    if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
+    // Sleeping waits: a polling loop would take issue slots from the other
+    // warps of its SM sub-partition (the softmax warps beside the MMA issuer).
+    // The hint bounds each sleep, so the time limit and *abort are still read
+    // every ~20 us.
     const long long t0 = clock64();
     while (true) {
-        if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
+        if (__all_sync(0xffffffffu, mbar_try_wait_sleep(bar, parity, 20000u))) return true;
         const bool stop = (abort != nullptr && *abort) || (clock64() - t0 > limit);
         if (__any_sync(0xffffffffu, stop)) {
             if (abort != nullptr && clock64() - t0 > limit) *abort = 1;
@@ -160,7 +177,27 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
         "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
         : "memory");
 }
+// 32 lanes x 16 consecutive 32-bit columns (store).
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+        "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// Waits for the loads and ties the 32 destination registers to the wait.
+__device__ __forceinline__ void tmem_wait_ld_pin32(uint32_t* r) {
+    asm volatile(
+        "tcgen05.wait::ld.sync.aligned;"
+        : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+          "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]),
+          "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]),
+          "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+        :
+        : "memory");
+}
 // Waits for the loads and ties the 64 destination registers to the wait, so no
 // use of them is scheduled before the data has arrived.
 __device__ __forceinline__ void tmem_wait_ld_pin64(uint32_t* r) {
