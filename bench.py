@@ -191,11 +191,12 @@ def count_launches(mb, L, BH):
     """Kernels of libmaba_b200 launched per step (cuBLAS GEMMs not counted): DGDA prep, segment
     transitions, combine, segment states, output (chunk-parallel path; one scan launch when the
     sequence is a single segment); centroids; top-k penalty table, centroid-norm tiles, prefix max,
-    tile scan; HCA pooling; attention."""
+    tile scan; HCA pooling; attention: key-tile norms, bound-referenced pass, running-maximum
+    pass over the tiles the first one listed (an empty grid when none)."""
     lib = mb._native.lib()
     chunked = lib.maba_dgda_prefill_workspace_size(2, 1, H, L, DH, DH) > 0
     dgda = 5 if chunked else 1
-    return dgda + 1 + 4 + 1 + 1
+    return dgda + 1 + 4 + 1 + 3
 
 
 def attention_units(idx, L):

@@ -24,6 +24,7 @@ int sa_attention_simt(SaArgs& a, int64_t B, int dtype, cudaStream_t s);
 int sa_attention_mma(SaArgs& a, int64_t B, int dtype, cudaStream_t s);
 int sa_attention_tc(SaArgs& a, int64_t B, int dtype, cudaStream_t s);
 bool sa_attention_tc_supported(const SaArgs& a, int dtype);
+size_t sa_attention_tc_workspace(int64_t B, int64_t Lq, int64_t Lkv, int64_t NC);
 int device_error_take(cudaStream_t s, int* out);
 int wait_timeout_selftest(long long limit, cudaStream_t s);
 bool sa_attention_mma_supported(const SaArgs& a, int dtype);
@@ -42,7 +43,10 @@ inline size_t sa_attention_workspace_bytes(int dtype, int64_t B, int64_t Lq, int
                                            int32_t hca_r) {
     size_t a = sa_attention_mma_workspace(dtype, B, Lq, Lkv, H, DC, K, block);
     size_t b = sa_attention_decode_workspace(B, Lq, Lkv, H, DC, K, block, window, n_sinks, hca_r);
-    return a > b ? a : b;
+    // key-tile norms of the tcgen05 kernel (pooled entries: at most ceil(Lkv / r))
+    size_t c = sa_attention_tc_workspace(B, Lq, Lkv, hca_r > 0 ? (Lkv + hca_r - 1) / hca_r : 0);
+    if (b > a) a = b;
+    return a > c ? a : c;
 }
 
 // Single-token queries take the split-K decode kernels when the caller gave

@@ -56,7 +56,13 @@ constexpr int ROWS = QT * HPG;    // MMA rows
 constexpr int NS = 6;             // key-tile stages
 constexpr int KMAX = 32;          // selected blocks per token
 constexpr int UMAX = QT * KMAX;   // union capacity
-constexpr int NTHR = 320;         // 10 warps: producer, MMA, 2 x 4 softmax
+// 12 warps in three warpgroups: 0-7 softmax (two groups of four), 8 TMA producer,
+// 9 QK issuer, 10 PV issuer, 11 idle.  The last warpgroup gives registers to the
+// softmax warpgroups (setmaxnreg): 256 x REG_SOFTMAX + 128 x REG_OTHER equals
+// 384 x REG_LAUNCH, the registers the block is launched with.
+constexpr int NTHR = 384;
+constexpr int REG_LAUNCH = 168, REG_SOFTMAX = 224, REG_OTHER = 56;
+static_assert(256 * REG_SOFTMAX + 128 * REG_OTHER <= NTHR * REG_LAUNCH, "register split exceeds the launch");
 constexpr int TMEM_COLS = 512;
 constexpr int COL_S = 0;
 constexpr int COL_O = 128;
@@ -71,7 +77,7 @@ constexpr uint32_t P_BYTES = ROWS * 128;    // 16 KB: P of one tile, 128 rows x 
 
 enum { B_QFULL = 0, B_QEMPTY = 2, B_KVFULL = 4, B_KVEMPTY = B_KVFULL + NS, B_SFULL = B_KVEMPTY + NS,
        B_PFULL = B_SFULL + 2, B_ODONE = B_PFULL + 2, B_SFREE = B_ODONE + 2, B_DRAIN = B_SFREE + 2,
-       N_BARS = B_DRAIN + 1 };
+       N_BARS = B_DRAIN + 2 };
 static_assert(N_BARS <= 32, "barrier area holds 32 mbarriers");
 
 struct TcLayout {
@@ -87,8 +93,10 @@ struct TcLayout {
         bitmap = ulist + UMAX * 4;
         wpref = bitmap + nwords * 4;
         scan = wpref + nwords * 4;
-        xch = scan + (NTHR + 16) * 4;  // tile maxima [2 groups][2 slots][128], row sums [2 groups][3][128]
-        total = xch + (2 * 2 + 2 * 3) * 128 * 4;
+        // tile maxima [2 groups][2 slots][128], row sums [2 groups][3][128],
+        // reference inputs [2 groups][2][128], stream key-norm maxima [4]
+        xch = scan + (NTHR + 16) * 4;
+        total = xch + (2 * 2 + 2 * 3 + 2 * 2) * 128 * 4 + 16;
     }
 };
 
@@ -123,6 +131,15 @@ __device__ __forceinline__ void add2(float& a0, float& a1, float b0, float b1) {
         : "f"(b0), "f"(b1));
 }
 
+template <typename T> __device__ __forceinline__ float2 unpack2(uint32_t v);
+template <> __device__ __forceinline__ float2 unpack2<__nv_bfloat16>(uint32_t v) {
+    return make_float2(__uint_as_float(v << 16), __uint_as_float(v & 0xffff0000u));
+}
+template <> __device__ __forceinline__ float2 unpack2<__half>(uint32_t v) {
+    __half2 h = *reinterpret_cast<__half2*>(&v);
+    return __half22float2(h);
+}
+
 template <typename T> __device__ __forceinline__ uint32_t pack2(float lo, float hi);
 template <> __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float lo, float hi) {
     __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
@@ -133,11 +150,16 @@ template <> __device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi
     return *reinterpret_cast<uint32_t*>(&v);
 }
 
-template <typename T>
+// EXACT = false: bound-referenced softmax (16-bit bf16 only); a CTA any of whose
+// head pairs misses the range condition appends its unit to redo_list.
+// EXACT = true: running-maximum softmax; with redo_list the grid covers the
+// listed units only (blocks past *redo_count return at once).
+template <typename T, bool EXACT>
 __global__ void __launch_bounds__(NTHR, 1)
     sa_attention_tc_kernel(const SaArgs a, const __grid_constant__ CUtensorMap tm_q,
                            const __grid_constant__ CUtensorMap tm_c, const __grid_constant__ CUtensorMap tm_h,
-                           int nwords) {
+                           int nwords, const float* __restrict__ tnc, const float* __restrict__ tnh, int ntc,
+                           int nth, int* __restrict__ redo_count, int* __restrict__ redo_list) {
     extern __shared__ unsigned char smem_dyn[];
     unsigned char* base =
         reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
@@ -155,8 +177,13 @@ __global__ void __launch_bounds__(NTHR, 1)
     int* scan = reinterpret_cast<int*>(base + LY.scan);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int64_t q0 = (int64_t)blockIdx.x * QT;
-    const int64_t b = blockIdx.y;
+    int unit = blockIdx.y * gridDim.x + blockIdx.x;
+    if (EXACT && redo_list != nullptr) {
+        if (unit >= *redo_count) return;
+        unit = redo_list[unit];
+    }
+    const int64_t q0 = (int64_t)(unit % gridDim.x) * QT;
+    const int64_t b = unit / gridDim.x;
     const int NH = a.H / HPG;
     const int nt = (int)((a.Lq - q0) < QT ? (a.Lq - q0) : QT);
     const int64_t P0 = a.Lkv - a.Lq + q0;  // absolute position of query row 0 of the tile
@@ -169,6 +196,7 @@ __global__ void __launch_bounds__(NTHR, 1)
         for (int i = 0; i < N_BARS; ++i) {
             uint32_t cnt = 1;
             if (i == B_PFULL || i == B_PFULL + 1 || i == B_SFREE || i == B_SFREE + 1) cnt = 128;
+            if (i == B_QEMPTY || i == B_QEMPTY + 1) cnt = 1 + 8;  // the last QK's commit + 8 softmax warps
             mbar_init(&bars[i], cnt);
         }
         *abort_f = 0;
@@ -179,16 +207,28 @@ __global__ void __launch_bounds__(NTHR, 1)
         prefetch_tmap(&tm_c);
         prefetch_tmap(&tm_h);
     }
-    if (warp == 1) tmem_alloc<TMEM_COLS>(tmem_slot);
+    if (warp == 9) tmem_alloc<TMEM_COLS>(tmem_slot);
 
     // ---------------- union of the selected blocks -------------------------
     for (int i = tid; i < nwords; i += NTHR) bitmap[i] = 0u;
     __syncthreads();
-    for (int e = tid; e < nt * K; e += NTHR) {
-        const int t = e / K, sl = e - t * K;
-        const int64_t n = tix[(q0 + t) * a.st[1] + sl * a.st[2]];
-        if (n >= 0 && n < nb_kv && n * KT <= P0 + t) atomicOr(&bitmap[n >> 5], 1u << (n & 31));
+    // this thread's selected blocks (all loads in flight together; -1: none or not causal)
+    constexpr int SEL_PER = (QT * KMAX + NTHR - 1) / NTHR;
+    int sel[SEL_PER];
+#pragma unroll
+    for (int k = 0; k < SEL_PER; ++k) {
+        const int e = tid + k * NTHR;
+        int64_t n = -1;
+        if (e < nt * K) {
+            const int t = e / K, sl = e - t * K;
+            n = tix[(q0 + t) * a.st[1] + sl * a.st[2]];
+            if (!(n >= 0 && n < nb_kv && n * KT <= P0 + t)) n = -1;
+        }
+        sel[k] = (int)n;
     }
+#pragma unroll
+    for (int k = 0; k < SEL_PER; ++k)
+        if (sel[k] >= 0) atomicOr(&bitmap[sel[k] >> 5], 1u << (sel[k] & 31));
     __syncthreads();
     {
         const int per = (nwords + NTHR - 1) / NTHR;
@@ -242,11 +282,12 @@ __global__ void __launch_bounds__(NTHR, 1)
     }
     __syncthreads();
     const int U = scan[NTHR];
-    for (int e = tid; e < nt * K; e += NTHR) {
-        const int t = e / K, sl = e - t * K;
-        const int64_t n = tix[(q0 + t) * a.st[1] + sl * a.st[2]];
-        if (n >= 0 && n < nb_kv && n * KT <= P0 + t) {
-            const int wi = (int)(n >> 5);
+#pragma unroll
+    for (int k = 0; k < SEL_PER; ++k) {
+        const int n = sel[k];
+        if (n >= 0) {
+            const int t = (tid + k * NTHR) / K;
+            const int wi = n >> 5;
             const int r = wpref[wi] + __popc(bitmap[wi] & ((1u << (n & 31)) - 1u));
             atomicOr(&umask[r], 1ull << t);
         }
@@ -272,7 +313,9 @@ __global__ void __launch_bounds__(NTHR, 1)
     const int G = NH * n_tiles;
     constexpr bool BF = std::is_same<T, __nv_bfloat16>::value;
 
-    if (warp == 0) {
+    if (warp >= 8) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REG_OTHER));
+    if (warp == 8) {
         // ============================ TMA producer ============================
         // The whole warp runs the loop (warp-uniform coordinates and waits); one
         // elected lane issues the copies.
@@ -323,86 +366,98 @@ __global__ void __launch_bounds__(NTHR, 1)
             const int last = ((g - 1 - s) / NS) * NS + s;
             mbar_wait_warp(&bars[B_KVFULL + s], (last / NS) & 1, nullptr);
         }
-    } else if (warp == 1) {
-        // ============================ MMA issuer ==============================
-        // The whole warp runs the loop; the descriptors are warp-uniform and one
-        // elected lane issues each MMA / commit.  Descriptor bases are built once:
+    } else if (warp == 9 || warp == 10) {
+        // ========================= MMA issuers ================================
+        // Warp 9 issues the QK products, warp 10 the PV products, so that each
+        // sleeps only on its own conditions (an MMA issue blocks its warp while the
+        // tensor pipe is full).  QK(g) needs its key tile and that the group owning
+        // S buffer g&1 has loaded tile g-2 out of it; PV(g) needs P(g) in shared
+        // memory.  QK(g) has completed before PV(g) is issued (the softmax loaded
+        // S(g)), so the PV warp's commit also frees the key tile.  The whole warp
+        // runs each loop; one elected lane issues.  Descriptor bases are built once:
         // a start address moves by adding (bytes >> 4) to the descriptor.
         constexpr uint32_t ID_QK = idesc_f16(ROWS, KT, BF, false, false);
         constexpr uint32_t ID_PV = idesc_f16(ROWS, DCX, BF, false, true);
-        const uint64_t qd0 = sdesc_sw128(smem_addr(Qs), 16, 1024);
-        const uint64_t kd0 = sdesc_sw128(smem_addr(KVs), 16, 1024);
-        const uint64_t vd0 = sdesc_sw128(smem_addr(KVs), KV_HALF, 1024);
-        const uint64_t pd0 = sdesc_sw128(smem_addr(Ps), 16, 1024);
-        // QK runs two tiles ahead of PV: QK(g) needs only that the group owning S
-        // buffer g&1 has loaded tile g-2 out of it (P goes to shared memory).
-        int gq = 0, jq = 0, hq = 0;  // next QK: global tile, tile of its head pair, head pair
-        bool okm = true;
-        auto issue_qk = [&]() {
-            const int st = gq % NS, sb = gq & 1, qb = hq & 1;
-            if (jq == 0) okm = mbar_wait_warp(&bars[B_QFULL + qb], (hq >> 1) & 1, abort_f);
-            if (okm) okm = mbar_wait_warp(&bars[B_KVFULL + st], (gq / NS) & 1, abort_f);
-            if (okm && gq >= 2) okm = mbar_wait_warp(&bars[B_SFREE + sb], ((gq - 2) >> 1) & 1, abort_f);
-            if (!okm) return;
-            tc_fence_after();
-            const uint64_t qd = qd0 + (uint64_t)(qb * (Q_BYTES >> 4));
-            const uint64_t kd = kd0 + (uint64_t)(st * (KV_BYTES >> 4));
-#pragma unroll
-            for (int k = 0; k < DCX / 16; ++k) {
-                const uint32_t off_q = (k >> 2) * (Q_HALF >> 4) + (k & 3) * 2;
-                const uint32_t off_k = (k >> 2) * (KV_HALF >> 4) + (k & 3) * 2;
-                umma_f16_ss_elect(tmem + COL_S + sb * KT, qd + off_q, kd + off_k, ID_QK, k > 0 ? 1u : 0u);
-            }
-            umma_commit_elect(&bars[B_SFULL + sb]);
-            if (jq == n_tiles - 1) umma_commit_elect(&bars[B_QEMPTY + qb]);
-            ++gq;
-            if (++jq == n_tiles) {
-                jq = 0;
-                ++hq;
-            }
-        };
-        issue_qk();
-        if (okm && gq < G) issue_qk();
-        int ij = 0;
-        for (int i = 0; i < G && okm; ++i) {
-            if (gq < G) {
-                issue_qk();  // QK(i + 2)
+        if (warp == 9) {
+            const uint64_t qd0 = sdesc_sw128(smem_addr(Qs), 16, 1024);
+            const uint64_t kd0 = sdesc_sw128(smem_addr(KVs), 16, 1024);
+            int jq = 0, hq = 0;
+            for (int gq = 0; gq < G; ++gq) {
+                const int st = gq % NS, sb = gq & 1, qb = hq & 1;
+                bool okm = true;
+                if (jq == 0) okm = mbar_wait_warp(&bars[B_QFULL + qb], (hq >> 1) & 1, abort_f);
+                if (okm) okm = mbar_wait_warp(&bars[B_KVFULL + st], (gq / NS) & 1, abort_f);
+                if (okm && gq >= 2) okm = mbar_wait_warp(&bars[B_SFREE + sb], ((gq - 2) >> 1) & 1, abort_f);
                 if (!okm) break;
-            }
-            const int st = i % NS, sb = i & 1;
-            okm = mbar_wait_warp(&bars[B_PFULL + sb], (i >> 1) & 1, abort_f);
-            if (!okm) break;
-            tc_fence_after();
-            const int stream = ij < n_local ? 0 : (ij < n_local + U ? 1 : 2);
-            const bool first = ij == 0 || ij == n_local || ij == n_local + U;
-            const uint32_t dst = tmem + COL_O + stream * DCX;
-            const uint64_t vd = vd0 + (uint64_t)(st * (KV_BYTES >> 4));
-            const uint64_t pd = pd0 + (uint64_t)(sb * (P_BYTES >> 4));
+                tc_fence_after();
+                const uint64_t qd = qd0 + (uint64_t)(qb * (Q_BYTES >> 4));
+                const uint64_t kd = kd0 + (uint64_t)(st * (KV_BYTES >> 4));
 #pragma unroll
-            for (int k = 0; k < KT / 16; ++k)
-                umma_f16_ss_elect(dst, pd + (uint64_t)(k * 2), vd + (uint64_t)(k * (2048 >> 4)), ID_PV,
-                                  (k > 0 || !first) ? 1u : 0u);
-            umma_commit_elect(&bars[B_KVEMPTY + st]);
-            umma_commit_elect(&bars[B_ODONE + sb]);
-            if (++ij == n_tiles) ij = 0;
+                for (int k = 0; k < DCX / 16; ++k) {
+                    const uint32_t off_q = (k >> 2) * (Q_HALF >> 4) + (k & 3) * 2;
+                    const uint32_t off_k = (k >> 2) * (KV_HALF >> 4) + (k & 3) * 2;
+                    umma_f16_ss_elect(tmem + COL_S + sb * KT, qd + off_q, kd + off_k, ID_QK, k > 0 ? 1u : 0u);
+                }
+                umma_commit_elect(&bars[B_SFULL + sb]);
+                if (jq == n_tiles - 1) umma_commit_elect(&bars[B_QEMPTY + qb]);
+                if (++jq == n_tiles) {
+                    jq = 0;
+                    ++hq;
+                }
+            }
+        } else {
+            const uint64_t vd0 = sdesc_sw128(smem_addr(KVs), KV_HALF, 1024);
+            const uint64_t pd0 = sdesc_sw128(smem_addr(Ps), 16, 1024);
+            int ij = 0;
+            for (int i = 0; i < G; ++i) {
+                const int st = i % NS, sb = i & 1;
+                if (!mbar_wait_warp(&bars[B_PFULL + sb], (i >> 1) & 1, abort_f)) break;
+                tc_fence_after();
+                const int stream = ij < n_local ? 0 : (ij < n_local + U ? 1 : 2);
+                const bool first = ij == 0 || ij == n_local || ij == n_local + U;
+                const uint32_t dst = tmem + COL_O + stream * DCX;
+                const uint64_t vd = vd0 + (uint64_t)(st * (KV_BYTES >> 4));
+                const uint64_t pd = pd0 + (uint64_t)(sb * (P_BYTES >> 4));
+#pragma unroll
+                for (int k = 0; k < KT / 16; ++k)
+                    umma_f16_ss_elect(dst, pd + (uint64_t)(k * 2), vd + (uint64_t)(k * (2048 >> 4)), ID_PV,
+                                      (k > 0 || !first) ? 1u : 0u);
+                umma_commit_elect(&bars[B_KVEMPTY + st]);
+                umma_commit_elect(&bars[B_ODONE + sb]);
+                if (++ij == n_tiles) ij = 0;
+            }
         }
-        // every MMA issued has completed before TMEM is freed
-        umma_commit_elect(&bars[B_DRAIN]);
-        mbar_wait_warp(&bars[B_DRAIN], 0, nullptr);
+        // every MMA this warp issued has completed before TMEM is freed
+        const int db = B_DRAIN + (warp == 9 ? 0 : 1);
+        umma_commit_elect(&bars[db]);
+        mbar_wait_warp(&bars[db], 0, nullptr);
+    }
     } else {
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REG_SOFTMAX));
         // ===================== softmax + epilogue (256 threads) ===============
         // Two groups of four warps, one warp per TMEM lane quarter in each.  Group wg
         // owns the key tiles whose global index has parity wg (its S buffer is wg), so
         // the two warps of a lane quarter, which share an SM sub-partition, work on
         // consecutive tiles in different phases: one runs exponentials while the other
-        // loads and reduces.  The reference maximum of a row is a function of the tile
-        // maxima in tile order: each warp publishes its tiles' maxima to its partner
-        // (named barriers used as producer -> consumer pairs) and replays the
-        // partner's, so both hold the same reference at every tile.  Each warp keeps
-        // the row sums of its own tiles; the pair adds them at the end of a head pair.
-        // Every named-barrier call is unconditional (a wait that ran out only skips
-        // TMEM work), so the two warps always make the same calls.
-        const int wg = (warp - 2) >> 2;
+        // loads and stores.  Each warp keeps the row sums of its own tiles; the pair
+        // adds them at the end of a head pair.
+        //
+        // Reference maxima.  Softmax is invariant to the reference m subtracted from
+        // the scores; it only has to keep every exponent in range.  Before a head
+        // pair's tiles, each row gets per stream an upper bound of its scores,
+        // |q| * (max key norm of the stream's tiles), and one exact score of a key it
+        // attends to (a probe).  With m = min(bound, probe + 60) every score s of the
+        // stream has s - m <= 60 and the stream maximum has max - m >= -60 (natural
+        // log units), whenever bound - probe <= 120: then P = exp(s - m) needs no
+        // running maximum, no rescale of O and no exchange between the two warps.
+        // When some row of the CTA misses that condition (or no key norms were
+        // given), the head pair runs the exact running-maximum form instead: the
+        // pair publishes its tiles' maxima to each other (named barriers used as
+        // producer -> consumer pairs) and replays the partner's, so both hold the
+        // same lazily rescaled reference at every tile.  Every named-barrier call is
+        // unconditional (a wait that ran out only skips TMEM work), so the two warps
+        // always make the same calls.
+        const int wg = warp >> 2;
         const int q4 = warp & 3;
         const int rid = q4 * 32 + lane;
         const int t = rid >> 1, hh = rid & 1;
@@ -410,6 +465,8 @@ __global__ void __launch_bounds__(NTHR, 1)
         const int bar_mine = 1 + wg * 4 + q4, bar_other = 1 + (wg ^ 1) * 4 + q4, bar_pair = 9 + q4;
         float* xmax = reinterpret_cast<float*>(base + LY.xch);  // [2 groups][2 slots][128]
         float* xls = xmax + 2 * 2 * 128;                          // [2 groups][3 streams][128]
+        float* xref = xls + 2 * 3 * 128;                          // [2 groups][2][128]
+        float* mstr = xref + 2 * 2 * 128;                         // key-norm maxima per stream
         // positions fit in 32 bits (Lkv < 2^31 on this path)
         const int pos = (int)(P0 + t);
         const int lkv = (int)a.Lkv;
@@ -445,10 +502,189 @@ __global__ void __launch_bounds__(NTHR, 1)
             }
         };
         auto pair_sync = [&](int id) { asm volatile("bar.sync %0, 64;" ::"r"(id) : "memory"); };
-        bool okw = true;  // every wait of this warp completed
+        auto all_sync = [&]() { asm volatile("bar.sync 13, 256;" ::: "memory"); };
+        // ---- largest key norm of each stream's tiles (one warp; all read after a barrier)
+        if (warp == 0) {
+            float ml = 0.f, mu = 0.f, mh = 0.f;
+            if (tnc != nullptr) {
+                const float* nc = tnc + b * ntc;
+                for (int j = lane; j < n_tiles; j += 32) {
+                    if (j < n_local) {
+                        const int row0 = sink_tile ? (j == 0 ? 0 : (int)ws + (j - 1) * KT) : (int)ws + j * KT;
+                        ml = fmaxf(ml, nc[row0 / KT]);
+                    } else if (j < n_local + U) {
+                        mu = fmaxf(mu, nc[ulist[j - n_local]]);
+                    } else {
+                        mh = fmaxf(mh, tnh[b * nth + (j - n_local - U)]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                ml = fmaxf(ml, __shfl_xor_sync(0xffffffffu, ml, o));
+                mu = fmaxf(mu, __shfl_xor_sync(0xffffffffu, mu, o));
+                mh = fmaxf(mh, __shfl_xor_sync(0xffffffffu, mh, o));
+            }
+            if (lane == 0) {
+                mstr[0] = ml;
+                mstr[1] = mu;
+                mstr[2] = mh;
+            }
+        }
+        all_sync();
+        const float Mloc = mstr[0], Muni = mstr[1], Mhca = mstr[2];
+        // probe keys of this row: itself (local), its first attended union key, pooled entry 0
+        int probe_u = -1;
+        if (rvalid) {
+            for (int u = 0; u < U; ++u) {
+                if ((umask[u] & tbit) && ulist[u] * KT < sp_end) {
+                    probe_u = ulist[u] * KT;
+                    break;
+                }
+            }
+        }
+        // q . k over d_c = 128 for the query row rid of Q buffer qb (128-byte swizzled
+        // rows in two 64-column halves) and a key row in global memory (k == null: |q|^2)
+        auto qdot = [&](int qb, const T* k) -> float {
+            const unsigned char* qrow = Qs + qb * Q_BYTES + (rid >> 3) * 1024 + (rid & 7) * 128;
+            float acc0 = 0.f, acc1 = 0.f;
+#pragma unroll
+            for (int c = 0; c < 16; ++c) {
+                const uint4 qv =
+                    *reinterpret_cast<const uint4*>(qrow + (c >> 3) * Q_HALF + (((c & 7) ^ (rid & 7)) << 4));
+                const uint4 kv = k != nullptr ? *reinterpret_cast<const uint4*>(k + c * 8) : qv;
+                const uint32_t qa[4] = {qv.x, qv.y, qv.z, qv.w}, ka[4] = {kv.x, kv.y, kv.z, kv.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 qf = unpack2<T>(qa[e]), kf = unpack2<T>(ka[e]);
+                    acc0 = fmaf(qf.x, kf.x, acc0);
+                    acc1 = fmaf(qf.y, kf.y, acc1);
+                }
+            }
+            return acc0 + acc1;
+        };
+        const T* hcab = a.NC > 0 ? static_cast<const T*>(a.hca) + b * a.sh[0] : nullptr;
+        bool okw = true;    // every wait of this warp completed
+        bool redo = false;  // some head pair missed the range condition of the bound references
         for (int hp = 0; hp < NH; ++hp) {
-            const int g0 = hp * n_tiles;
+            const int g0 = hp * n_tiles, gend = g0 + n_tiles;
             float l0 = 0.f, l1 = 0.f, l2 = 0.f;  // this warp's share of the row sums per stream
+            // ---- reference maxima of this head pair (group 0: |q|^2 and the local
+            // probe, group 1: the union and HCA probes)
+            // gate logits of this row's head, read now and used by the epilogue
+            float graw0 = 0.f, graw1 = 0.f, graw2 = 0.f;
+            if (rvalid) {
+                const int h = hp * HPG + hh;
+                const T* gp = static_cast<const T*>(a.gate);
+                const T* gr = a.gate4d ? gp + b * a.sg[0] + h * a.sg[1] + (q0 + t) * a.sg[2]
+                                       : gp + b * a.sg[0] + (q0 + t) * a.sg[1];
+                const int64_t gs = a.gate4d ? a.sg[3] : a.sg[2];
+                graw0 = Cvt<T>::to_f(gr[0]);
+                graw1 = Cvt<T>::to_f(gr[gs]);
+                graw2 = Cvt<T>::to_f(gr[2 * gs]);
+            }
+            const int qb = hp & 1;
+            const bool okq = mbar_wait_warp(&bars[B_QFULL + qb], (hp >> 1) & 1, abort_f);
+            okw = okw && okq;
+            float v0 = 0.f, v1 = 0.f;
+            if (!EXACT && okq && rvalid && tnc != nullptr) {
+                if (wg == 0) {
+                    v0 = qdot(qb, nullptr);
+                    v1 = qdot(qb, ckv + (int64_t)pos * a.sc[1]);
+                } else {
+                    if (probe_u >= 0) v0 = qdot(qb, ckv + (int64_t)probe_u * a.sc[1]);
+                    if (nv_hca > 0) v1 = qdot(qb, hcab);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars[B_QEMPTY + qb]);  // Q read; the MMA warp commits its last QK
+            if constexpr (!EXACT) {
+                xref[(wg * 2 + 0) * 128 + rid] = v0;
+                xref[(wg * 2 + 1) * 128 + rid] = v1;
+                pair_sync(bar_pair);
+                const float qn = sqrtf(wg == 0 ? v0 : xref[0 * 128 + rid]) * 1.0001f;
+                const float pl = wg == 0 ? v1 : xref[1 * 128 + rid];
+                const float pu = wg == 1 ? v0 : xref[2 * 128 + rid];
+                const float ph = wg == 1 ? v1 : xref[3 * 128 + rid];
+                constexpr float RANGE = 60.f;
+                const float ul = qn * Mloc, uu = qn * Muni, uh = qn * Mhca;
+                const float rl0 = fminf(ul, pl + RANGE) * LOG2E;
+                const float rl1 = fminf(uu, pu + RANGE) * LOG2E;
+                const float rl2 = fminf(uh, ph + RANGE) * LOG2E;
+                // streams without a key for this row take no reference
+                const bool rowok = !rvalid || ((ul - pl <= 2.f * RANGE) && (probe_u < 0 || uu - pu <= 2.f * RANGE) &&
+                                               (nv_hca == 0 || uh - ph <= 2.f * RANGE));
+                int fast;
+                asm volatile("{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
+                             "bar.red.and.pred q, 13, 256, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+                             : "=r"(fast)
+                             : "r"((uint32_t)(rowok && tnc != nullptr))
+                             : "memory");
+                if (!fast) redo = true;
+                // ------------- bound-referenced tiles: no maximum, no rescale -------------
+                for (int j = (g0 & 1) == wg ? 0 : 1; j < n_tiles; j += 2) {
+                    const int gg = g0 + j;
+                    const int st = stream_of(j);
+                    int a1, b1, b2;
+                    bounds(j, a1, b1, b2);
+                    const bool none = b1 <= a1 && b2 == 0;
+                    const bool full = a1 == 0 && b1 >= KT;
+                    const bool oks = mbar_wait_warp(&bars[B_SFULL + wg], (gg >> 1) & 1, abort_f);
+                    okw = okw && oks;
+                    const uint32_t ts = tmem + lane_base + COL_S + wg * KT;
+                    uint32_t s[KT];
+                    if (oks) {
+                        tc_fence_after();
+                        tmem_ld32(ts, s);
+                        tmem_ld32(ts + 32, s + 32);
+                        tmem_wait_ld_pin64(s);
+                    }
+                    // S is in registers: the MMA warp may compute tile gg+2 into this buffer
+                    tc_fence_before();
+                    mbar_arrive(&bars[B_SFREE + wg]);
+                    if (oks) {
+                        if (__any_sync(0xffffffffu, !none && !full)) {
+                            unsigned long long vm = 0ull;
+                            if (b1 > a1) vm = (b1 >= 64 ? ~0ull : ((1ull << b1) - 1ull)) & ~((1ull << a1) - 1ull);
+                            if (b2 > 0) vm |= b2 >= 64 ? ~0ull : ((1ull << b2) - 1ull);
+#pragma unroll
+                            for (int c = 0; c < KT; ++c)
+                                if (!((vm >> c) & 1ull)) s[c] = __float_as_uint(-INFINITY);
+                        }
+                        // rows without a valid column give p = 0 (ex2(-inf)); scores are finite
+                        const float nmu = none ? -INFINITY : -(st == 0 ? rl0 : (st == 1 ? rl1 : rl2));
+                        float sa0 = 0.f, sa1 = 0.f, sb0 = 0.f, sb1 = 0.f;
+                        uint32_t pk[KT / 2];
+#pragma unroll
+                        for (int c = 0; c < KT; c += 4) {
+                            float x0, x1, x2, x3;
+                            fma2(x0, x1, __uint_as_float(s[c]), __uint_as_float(s[c + 1]), LOG2E, nmu);
+                            fma2(x2, x3, __uint_as_float(s[c + 2]), __uint_as_float(s[c + 3]), LOG2E, nmu);
+                            const float p0 = ex2(x0), p1 = ex2(x1), p2 = ex2(x2), p3 = ex2(x3);
+                            add2(sa0, sa1, p0, p1);
+                            add2(sb0, sb1, p2, p3);
+                            pk[c >> 1] = pack2<T>(p0, p1);
+                            pk[(c >> 1) + 1] = pack2<T>(p2, p3);
+                        }
+                        const float ls = (sa0 + sa1) + (sb0 + sb1);
+                        if (st == 0) l0 += ls;
+                        else if (st == 1) l1 += ls;
+                        else l2 += ls;
+                        const bool okp =
+                            gg < 2 || mbar_wait_warp(&bars[B_ODONE + wg], ((gg - 2) >> 1) & 1, abort_f);
+                        okw = okw && okp;
+                        if (okp) {
+                            unsigned char* prow = Ps + wg * P_BYTES + (rid >> 3) * 1024 + (rid & 7) * 128;
+#pragma unroll
+                            for (int c = 0; c < 8; ++c)
+                                *reinterpret_cast<uint4*>(prow + ((c ^ (rid & 7)) << 4)) =
+                                    make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+                            fence_proxy_async_smem();
+                        }
+                    }
+                    mbar_arrive(&bars[B_PFULL + wg]);
+                }
+            } else {
             float m_cur = -INFINITY, l_cur = 0.f;
             int cur = -1;
             // folds the maximum mx (log2 units) of the next tile, of stream st, into the
@@ -473,112 +709,112 @@ __global__ void __launch_bounds__(NTHR, 1)
                 }
                 return fac;
             };
-            for (int j = (g0 & 1) == wg ? 0 : 1; j < n_tiles; j += 2) {
-                const int gg = g0 + j;
-                const int st = stream_of(j);
-                int a1, b1, b2;
-                bounds(j, a1, b1, b2);
-                const bool none = b1 <= a1 && b2 == 0;
-                const bool full = a1 == 0 && b1 >= KT;
-                const bool oks = mbar_wait_warp(&bars[B_SFULL + wg], (gg >> 1) & 1, abort_f);
-                okw = okw && oks;
-                const uint32_t ts = tmem + lane_base + COL_S + wg * KT;
-                uint32_t s[KT];
-                float mt = -INFINITY;
-                if (oks) {
-                    tc_fence_after();
-                    tmem_ld32(ts, s);
-                    tmem_ld32(ts + 32, s + 32);
-                    tmem_wait_ld_pin64(s);
-                }
-                // S is in registers: the MMA warp may compute tile gg+2 into this buffer
-                tc_fence_before();
-                mbar_arrive(&bars[B_SFREE + wg]);
-                if (oks) {
-                    if (__any_sync(0xffffffffu, !none && !full)) {
-                        unsigned long long vm = 0ull;
-                        if (b1 > a1) vm = (b1 >= 64 ? ~0ull : ((1ull << b1) - 1ull)) & ~((1ull << a1) - 1ull);
-                        if (b2 > 0) vm |= b2 >= 64 ? ~0ull : ((1ull << b2) - 1ull);
-#pragma unroll
-                        for (int c = 0; c < KT; ++c)
-                            if (!((vm >> c) & 1ull)) s[c] = __float_as_uint(-INFINITY);
-                    }
-                    float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-                    for (int c = 0; c < KT; c += 2)
-                        m4[(c >> 1) & 3] = fmax3(m4[(c >> 1) & 3], __uint_as_float(s[c]), __uint_as_float(s[c + 1]));
-                    mt = none ? -INFINITY : fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * LOG2E;
-                }
-                // the partner's previous tile of this head pair, then this one
-                if (j >= 1) {
-                    pair_sync(bar_other);
-                    apply(stream_of(j - 1), xmax[((wg ^ 1) * 2 + (((gg - 1) >> 1) & 1)) * 128 + rid]);
-                }
-                xmax[(wg * 2 + ((gg >> 1) & 1)) * 128 + rid] = mt;
-                asm volatile("bar.arrive %0, 64;" ::"r"(bar_mine) : "memory");
-                const float fac = apply(st, mt);
-                if (oks) {
-                    // rows without a valid column give p = 0 (ex2(-inf)); scores are finite
-                    const float nmu = none ? -INFINITY : (m_cur == -INFINITY ? 0.f : -m_cur);
-                    float sa0 = 0.f, sa1 = 0.f, sb0 = 0.f, sb1 = 0.f;
-                    uint32_t pk[KT / 2];
-#pragma unroll
-                    for (int c = 0; c < KT; c += 4) {
-                        float x0, x1, x2, x3;
-                        fma2(x0, x1, __uint_as_float(s[c]), __uint_as_float(s[c + 1]), LOG2E, nmu);
-                        fma2(x2, x3, __uint_as_float(s[c + 2]), __uint_as_float(s[c + 3]), LOG2E, nmu);
-                        const float p0 = ex2(x0), p1 = ex2(x1), p2 = ex2(x2), p3 = ex2(x3);
-                        add2(sa0, sa1, p0, p1);
-                        add2(sb0, sb1, p2, p3);
-                        pk[c >> 1] = pack2<T>(p0, p1);
-                        pk[(c >> 1) + 1] = pack2<T>(p2, p3);
-                    }
-                    l_cur += (sa0 + sa1) + (sb0 + sb1);
-                    // P into shared-memory buffer wg (the A operand of PV, 128-byte swizzled
-                    // rows) once PV(gg-2) has read the buffer
-                    const bool okp =
-                        gg < 2 || mbar_wait_warp(&bars[B_ODONE + wg], ((gg - 2) >> 1) & 1, abort_f);
-                    okw = okw && okp;
-                    if (okp) {
-                        unsigned char* prow = Ps + wg * P_BYTES + (rid >> 3) * 1024 + (rid & 7) * 128;
-#pragma unroll
-                        for (int c = 0; c < 8; ++c)
-                            *reinterpret_cast<uint4*>(prow + ((c ^ (rid & 7)) << 4)) =
-                                make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-                        fence_proxy_async_smem();
-                    }
-                }
-                if (__any_sync(0xffffffffu, fac != 1.f)) {
-                    // every PV so far (the latest: tile gg-1, the partner's) has completed
-                    const bool okr = mbar_wait_warp(&bars[B_ODONE + ((gg - 1) & 1)], ((gg - 1) >> 1) & 1, abort_f);
-                    okw = okw && okr;
-                    if (okr) {
+                for (int j = (g0 & 1) == wg ? 0 : 1; j < n_tiles; j += 2) {
+                    const int gg = g0 + j;
+                    const int st = stream_of(j);
+                    int a1, b1, b2;
+                    bounds(j, a1, b1, b2);
+                    const bool none = b1 <= a1 && b2 == 0;
+                    const bool full = a1 == 0 && b1 >= KT;
+                    const bool oks = mbar_wait_warp(&bars[B_SFULL + wg], (gg >> 1) & 1, abort_f);
+                    okw = okw && oks;
+                    const uint32_t ts = tmem + lane_base + COL_S + wg * KT;
+                    uint32_t s[KT];
+                    float mt = -INFINITY;
+                    if (oks) {
                         tc_fence_after();
-                        const uint32_t to = tmem + lane_base + COL_O + st * DCX;
-#pragma unroll 1
-                        for (int cc = 0; cc < DCX / 32; ++cc) {
-                            uint32_t o[32];
-                            tmem_ld32(to + cc * 32, o);
-                            tmem_wait_ld();
-#pragma unroll
-                            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * fac);
-                            tmem_st32(to + cc * 32, o);
+                        tmem_ld32(ts, s);
+                        tmem_ld32(ts + 32, s + 32);
+                        tmem_wait_ld_pin64(s);
+                    }
+                    // S is in registers: the MMA warp may compute tile gg+2 into this buffer
+                    tc_fence_before();
+                    mbar_arrive(&bars[B_SFREE + wg]);
+                    if (oks) {
+                        if (__any_sync(0xffffffffu, !none && !full)) {
+                            unsigned long long vm = 0ull;
+                            if (b1 > a1) vm = (b1 >= 64 ? ~0ull : ((1ull << b1) - 1ull)) & ~((1ull << a1) - 1ull);
+                            if (b2 > 0) vm |= b2 >= 64 ? ~0ull : ((1ull << b2) - 1ull);
+    #pragma unroll
+                            for (int c = 0; c < KT; ++c)
+                                if (!((vm >> c) & 1ull)) s[c] = __float_as_uint(-INFINITY);
+                        }
+                        float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+    #pragma unroll
+                        for (int c = 0; c < KT; c += 2)
+                            m4[(c >> 1) & 3] = fmax3(m4[(c >> 1) & 3], __uint_as_float(s[c]), __uint_as_float(s[c + 1]));
+                        mt = none ? -INFINITY : fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * LOG2E;
+                    }
+                    // the partner's previous tile of this head pair, then this one
+                    if (j >= 1) {
+                        pair_sync(bar_other);
+                        apply(stream_of(j - 1), xmax[((wg ^ 1) * 2 + (((gg - 1) >> 1) & 1)) * 128 + rid]);
+                    }
+                    xmax[(wg * 2 + ((gg >> 1) & 1)) * 128 + rid] = mt;
+                    asm volatile("bar.arrive %0, 64;" ::"r"(bar_mine) : "memory");
+                    const float fac = apply(st, mt);
+                    if (oks) {
+                        // rows without a valid column give p = 0 (ex2(-inf)); scores are finite
+                        const float nmu = none ? -INFINITY : (m_cur == -INFINITY ? 0.f : -m_cur);
+                        float sa0 = 0.f, sa1 = 0.f, sb0 = 0.f, sb1 = 0.f;
+                        uint32_t pk[KT / 2];
+    #pragma unroll
+                        for (int c = 0; c < KT; c += 4) {
+                            float x0, x1, x2, x3;
+                            fma2(x0, x1, __uint_as_float(s[c]), __uint_as_float(s[c + 1]), LOG2E, nmu);
+                            fma2(x2, x3, __uint_as_float(s[c + 2]), __uint_as_float(s[c + 3]), LOG2E, nmu);
+                            const float p0 = ex2(x0), p1 = ex2(x1), p2 = ex2(x2), p3 = ex2(x3);
+                            add2(sa0, sa1, p0, p1);
+                            add2(sb0, sb1, p2, p3);
+                            pk[c >> 1] = pack2<T>(p0, p1);
+                            pk[(c >> 1) + 1] = pack2<T>(p2, p3);
+                        }
+                        l_cur += (sa0 + sa1) + (sb0 + sb1);
+                        // P into shared-memory buffer wg (the A operand of PV, 128-byte swizzled
+                        // rows) once PV(gg-2) has read the buffer
+                        const bool okp =
+                            gg < 2 || mbar_wait_warp(&bars[B_ODONE + wg], ((gg - 2) >> 1) & 1, abort_f);
+                        okw = okw && okp;
+                        if (okp) {
+                            unsigned char* prow = Ps + wg * P_BYTES + (rid >> 3) * 1024 + (rid & 7) * 128;
+    #pragma unroll
+                            for (int c = 0; c < 8; ++c)
+                                *reinterpret_cast<uint4*>(prow + ((c ^ (rid & 7)) << 4)) =
+                                    make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+                            fence_proxy_async_smem();
                         }
                     }
+                    if (__any_sync(0xffffffffu, fac != 1.f)) {
+                        // every PV so far (the latest: tile gg-1, the partner's) has completed
+                        const bool okr = mbar_wait_warp(&bars[B_ODONE + ((gg - 1) & 1)], ((gg - 1) >> 1) & 1, abort_f);
+                        okw = okw && okr;
+                        if (okr) {
+                            tc_fence_after();
+                            const uint32_t to = tmem + lane_base + COL_O + st * DCX;
+    #pragma unroll 1
+                            for (int cc = 0; cc < DCX / 32; ++cc) {
+                                uint32_t o[32];
+                                tmem_ld32(to + cc * 32, o);
+                                tmem_wait_ld();
+    #pragma unroll
+                                for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * fac);
+                                tmem_st32(to + cc * 32, o);
+                            }
+                        }
+                    }
+                    tmem_wait_st();
+                    tc_fence_before();
+                    mbar_arrive(&bars[B_PFULL + wg]);
                 }
-                tmem_wait_st();
-                tc_fence_before();
-                mbar_arrive(&bars[B_PFULL + wg]);
+                // the partner's last tile, if it owns it
+                if (((gend - 1) & 1) != wg) {
+                    pair_sync(bar_other);
+                    apply(stream_of(n_tiles - 1), xmax[((wg ^ 1) * 2 + (((gend - 1) >> 1) & 1)) * 128 + rid]);
+                }
+                if (cur == 0) l0 = l_cur;
+                else if (cur == 1) l1 = l_cur;
+                else if (cur == 2) l2 = l_cur;
             }
-            // the partner's last tile, if it owns it
-            const int gend = g0 + n_tiles;
-            if (((gend - 1) & 1) != wg) {
-                pair_sync(bar_other);
-                apply(stream_of(n_tiles - 1), xmax[((wg ^ 1) * 2 + (((gend - 1) >> 1) & 1)) * 128 + rid]);
-            }
-            if (cur == 0) l0 = l_cur;
-            else if (cur == 1) l1 = l_cur;
-            else if (cur == 2) l2 = l_cur;
             // ------------------------- epilogue of head pair hp ------------------
             // the last two PVs of the head pair (tiles gend-2, gend-1) have completed
             bool oke = gend < 2 || mbar_wait_warp(&bars[B_ODONE + (gend & 1)], ((gend - 2) >> 1) & 1, abort_f);
@@ -595,15 +831,8 @@ __global__ void __launch_bounds__(NTHR, 1)
             if (okw) {
                 tc_fence_after();
                 const int h = hp * HPG + hh;
-                float g0v = 0.f, g1v = 0.f, g2v = 0.f;
+                float g0v = graw0, g1v = graw1, g2v = graw2;
                 if (rvalid) {
-                    const T* gp = static_cast<const T*>(a.gate);
-                    const T* gr = a.gate4d ? gp + b * a.sg[0] + h * a.sg[1] + (q0 + t) * a.sg[2]
-                                           : gp + b * a.sg[0] + (q0 + t) * a.sg[1];
-                    const int64_t gs = a.gate4d ? a.sg[3] : a.sg[2];
-                    g0v = Cvt<T>::to_f(gr[0]);
-                    g1v = Cvt<T>::to_f(gr[gs]);
-                    g2v = Cvt<T>::to_f(gr[2 * gs]);
                     const float m = fmaxf(g0v, fmaxf(g1v, g2v));
                     const float e0 = expf(g0v - m), e1 = expf(g1v - m), e2 = expf(g2v - m);
                     const float inv = 1.f / (e0 + e1 + e2);
@@ -658,10 +887,11 @@ __global__ void __launch_bounds__(NTHR, 1)
             tc_fence_before();
             pair_sync(bar_pair);
         }
+        if (!EXACT && redo && warp == 0 && lane == 0 && redo_list != nullptr) redo_list[atomicAdd(redo_count, 1)] = unit;
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 1) {
+    if (warp == 9) {
         tc_fence_after();
         tmem_dealloc<TMEM_COLS>(tmem);
     }
@@ -709,9 +939,54 @@ bool make_map(CUtensorMap* m, int dtype, const void* ptr, int rank, const int64_
 inline bool a16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 inline bool s16(int64_t stride_elems) { return ((stride_elems * 2) % 16) == 0 && stride_elems > 0; }
 
+// Largest L2 norm of the rows of each 64-row tile of c_kv [B, L, 128] (tiles
+// 0..ntc-1) and of the pooled HCA entries [B, NC, 128] (tiles ntc..ntc+nth-1),
+// scaled by 1 + 1e-3 so that |q| * norm bounds every score of the tile.
+template <typename T>
+__global__ void __launch_bounds__(256)
+    kv_tile_norm_kernel(const T* __restrict__ c, int64_t cb, int64_t cr, int64_t L, int ntc, const T* __restrict__ h,
+                        int64_t hb, int64_t hr, int64_t NC, int nth, float* __restrict__ out_c,
+                        float* __restrict__ out_h, int* __restrict__ zero) {
+    if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) *zero = 0;
+    __shared__ float wmax[8];
+    const int64_t b = blockIdx.y;
+    const int tile = blockIdx.x;
+    const bool isc = tile < ntc;
+    const T* base = isc ? c + b * cb : h + b * hb;
+    const int64_t rs = isc ? cr : hr, n = isc ? L : NC;
+    const int64_t r0 = (int64_t)(isc ? tile : tile - ntc) * KT;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float m = 0.f;
+    for (int r = warp; r < KT; r += 8) {
+        const int64_t row = r0 + r;
+        if (row >= n) break;
+        const uint2 v = *reinterpret_cast<const uint2*>(base + row * rs + lane * 4);
+        const float2 x = unpack2<T>(v.x), y = unpack2<T>(v.y);
+        float ss = x.x * x.x + x.y * x.y + y.x * y.x + y.y * y.y;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        m = fmaxf(m, sqrtf(ss));
+    }
+    if (lane == 0) wmax[warp] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float mm = 0.f;
+        for (int i = 0; i < 8; ++i) mm = fmaxf(mm, wmax[i]);
+        mm *= 1.001f;
+        if (isc) out_c[b * ntc + tile] = mm;
+        else out_h[b * nth + (tile - ntc)] = mm;
+    }
+}
+
 int tc_nwords(const SaArgs& a) { return (int)(((a.Lkv + KT - 1) / KT + 31) / 32) + 1; }
 
 }  // namespace
+
+size_t sa_attention_tc_workspace(int64_t B, int64_t Lq, int64_t Lkv, int64_t NC) {
+    // key-tile norms, the redo count (16 bytes) and the redo list (one int per unit)
+    return (size_t)B * (size_t)(ceil_div(Lkv, KT) + ceil_div(NC, KT)) * sizeof(float) + 16 +
+           (size_t)B * (size_t)ceil_div(Lq, QT) * sizeof(int);
+}
 
 bool sa_attention_tc_supported(const SaArgs& a, int dtype) {
     if (dtype != MABA_BF16 && dtype != MABA_F16) return false;
@@ -727,7 +1002,22 @@ bool sa_attention_tc_supported(const SaArgs& a, int dtype) {
     return encode_fn() != nullptr;
 }
 
+// The register split of the kernels (setmaxnreg) assumes REG_LAUNCH registers
+// per thread at launch; a build with another count must not launch them (an
+// increase beyond the block's registers would never complete).
+template <typename T, bool EXACT> bool tc_regs_ok() {
+    static const bool ok = [] {
+        cudaFuncAttributes fa{};
+        return cudaFuncGetAttributes(&fa, sa_attention_tc_kernel<T, EXACT>) == cudaSuccess &&
+               fa.numRegs == REG_LAUNCH;
+    }();
+    return ok;
+}
+
 int sa_attention_tc(SaArgs& a, int64_t B, int dtype, cudaStream_t s) {
+    if (dtype == MABA_BF16 ? !(tc_regs_ok<__nv_bfloat16, true>() && tc_regs_ok<__nv_bfloat16, false>())
+                           : !tc_regs_ok<__half, true>())
+        return sa_attention_mma(a, B, dtype, s);
     const int nwords = tc_nwords(a);
     const size_t smem = TcLayout(nwords).total + 1024;
     CUtensorMap mq, mc, mh;
@@ -748,15 +1038,40 @@ int sa_attention_tc(SaArgs& a, int64_t B, int dtype, cudaStream_t s) {
             mh = mc;  // no HCA tiles are scheduled
         }
     }
-    dim3 grid((unsigned)ceil_div(a.Lq, QT), (unsigned)B);
+    // Bound-referenced pass (bf16, when the caller gave the workspace for the key
+    // norms and the redo list), then the running-maximum pass over the units it
+    // listed; otherwise the running-maximum pass over every unit.
+    const int ntc = (int)ceil_div(a.Lkv, KT), nth = (int)ceil_div(a.NC, KT);
+    const int nqt = (int)ceil_div(a.Lq, QT);
+    dim3 grid((unsigned)nqt, (unsigned)B);
+    float* tnc = nullptr;
+    float* tnh = nullptr;
+    int* redo_count = nullptr;
+    int* redo_list = nullptr;
+    if (dtype == MABA_BF16 && a.workspace != nullptr &&
+        a.workspace_bytes >= sa_attention_tc_workspace(B, a.Lq, a.Lkv, a.NC)) {
+        tnc = static_cast<float*>(a.workspace);
+        tnh = tnc + B * ntc;
+        redo_count = reinterpret_cast<int*>(tnh + B * nth);
+        redo_list = redo_count + 4;
+        using BT = __nv_bfloat16;
+        kv_tile_norm_kernel<BT><<<dim3((unsigned)(ntc + nth), (unsigned)B), 256, 0, s>>>(
+            static_cast<const BT*>(a.ckv), a.sc[0], a.sc[1], a.Lkv, ntc, static_cast<const BT*>(a.hca), a.sh[0],
+            a.sh[1], a.NC, nth, tnc, tnh, redo_count);
+        MABA_TRY(check_launch("sa_attention(key tile norms)"));
+        auto fast = sa_attention_tc_kernel<BT, false>;
+        cudaFuncSetAttribute(fast, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        fast<<<grid, NTHR, smem, s>>>(a, mq, mc, mh, nwords, tnc, tnh, ntc, nth, redo_count, redo_list);
+        MABA_TRY(check_launch("sa_attention(tcgen05, bound references)"));
+    }
     if (dtype == MABA_BF16) {
-        auto kern = sa_attention_tc_kernel<__nv_bfloat16>;
+        auto kern = sa_attention_tc_kernel<__nv_bfloat16, true>;
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        kern<<<grid, NTHR, smem, s>>>(a, mq, mc, mh, nwords);
+        kern<<<grid, NTHR, smem, s>>>(a, mq, mc, mh, nwords, nullptr, nullptr, ntc, nth, redo_count, redo_list);
     } else {
-        auto kern = sa_attention_tc_kernel<__half>;
+        auto kern = sa_attention_tc_kernel<__half, true>;
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        kern<<<grid, NTHR, smem, s>>>(a, mq, mc, mh, nwords);
+        kern<<<grid, NTHR, smem, s>>>(a, mq, mc, mh, nwords, nullptr, nullptr, ntc, nth, nullptr, nullptr);
     }
     return check_launch("sa_attention(tcgen05)");
 }

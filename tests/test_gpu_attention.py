@@ -73,6 +73,30 @@ def test_tc_kernel_vs_oracle(B, Lq, Lkv, H, K, window, sinks, gate4d, dt):
     assert_rel(out, ref, RTOL_BF16, str(dt))
 
 
+@pytest.mark.parametrize("scale_rows", [None, "all", "some"])
+def test_tc_bound_references_and_exact_redo(scale_rows):
+    """bf16 prefill takes bound-referenced exponentials; query rows whose score range
+    is too wide for them (large |q| * |k|) send their tile to the running-maximum
+    pass.  Both must match the oracle."""
+    B, Lq, Lkv, H, K, window = 1, 512, 512, 4, 8, 128
+    qhat, c, top, gate = rand_case(B, Lq, Lkv, H, 128, K, 64, seed=99)
+    if scale_rows == "all":
+        qhat = qhat * 60.0
+    elif scale_rows == "some":
+        qhat[:, 200:230] *= 80.0  # one 64-query tile misses the range condition
+    dt = torch.bfloat16
+    cd = c.to(DEV, dt)
+    hca = mb.b200_hca_pool(cd, 64)
+    out = mb.b200_sa_attention(qhat.to(DEV, dt), cd, hca, top.to(DEV), gate.to(DEV, dt), window_size=window,
+                               n_sinks=4, block_size=64, hca_r=64)
+    torch.cuda.synchronize()
+    assert mb._native.device_error() == 0
+    ref = OA.sa_attention_latent(qhat.to(dt).float().numpy(), c.to(dt).float().numpy(), top.numpy(),
+                                 gate.to(dt).float().numpy(), window, 4, 64, 64)
+    assert bool(torch.isfinite(out.float()).all())
+    assert_rel(out, ref, RTOL_BF16, str(scale_rows))
+
+
 def load_sa(name):
     g = sub(golden("sa_layer"), f"{name}.")
     window, block, top_k, r = (int(v) for v in g["kw"])
