@@ -53,7 +53,7 @@ constexpr int KT = 64;            // keys per tile (= block size)
 constexpr int DCX = 128;          // latent dim
 constexpr int HPG = 2;            // heads per MMA tile
 constexpr int ROWS = QT * HPG;    // MMA rows
-constexpr int NS = 6;             // key-tile stages
+constexpr int NS = 4;             // key-tile stages
 constexpr int KMAX = 32;          // selected blocks per token
 constexpr int UMAX = QT * KMAX;   // union capacity
 // 12 warps in three warpgroups: 0-7 softmax (two groups of four), 8 TMA producer,
@@ -76,7 +76,7 @@ constexpr uint32_t KV_BYTES = 2 * KV_HALF;
 constexpr uint32_t P_BYTES = ROWS * 128;    // 16 KB: P of one tile, 128 rows x 64 keys (16-bit)
 
 enum { B_QFULL = 0, B_QEMPTY = 2, B_KVFULL = 4, B_KVEMPTY = B_KVFULL + NS, B_SFULL = B_KVEMPTY + NS,
-       B_PFULL = B_SFULL + 2, B_ODONE = B_PFULL + 2, B_SFREE = B_ODONE + 2, B_DRAIN = B_SFREE + 2,
+       B_PFULL = B_SFULL + 2, B_ODONE = B_PFULL + 2, B_SFREE = B_ODONE + 4, B_DRAIN = B_SFREE + 2,
        N_BARS = B_DRAIN + 2 };
 static_assert(N_BARS <= 32, "barrier area holds 32 mbarriers");
 
@@ -86,7 +86,7 @@ struct TcLayout {
         q = 0;
         kv = q + 2 * Q_BYTES;
         p = kv + NS * KV_BYTES;
-        bars = p + 2 * P_BYTES;
+        bars = p + 4 * P_BYTES;  // P of tile g in buffer g & 3
         misc = bars + 32 * 8;
         umask = misc + 16;
         ulist = umask + UMAX * 8;
@@ -417,13 +417,13 @@ __global__ void __launch_bounds__(NTHR, 1)
                 const bool first = ij == 0 || ij == n_local || ij == n_local + U;
                 const uint32_t dst = tmem + COL_O + stream * DCX;
                 const uint64_t vd = vd0 + (uint64_t)(st * (KV_BYTES >> 4));
-                const uint64_t pd = pd0 + (uint64_t)(sb * (P_BYTES >> 4));
+                const uint64_t pd = pd0 + (uint64_t)((i & 3) * (P_BYTES >> 4));
 #pragma unroll
                 for (int k = 0; k < KT / 16; ++k)
                     umma_f16_ss_elect(dst, pd + (uint64_t)(k * 2), vd + (uint64_t)(k * (2048 >> 4)), ID_PV,
                                       (k > 0 || !first) ? 1u : 0u);
                 umma_commit_elect(&bars[B_KVEMPTY + st]);
-                umma_commit_elect(&bars[B_ODONE + sb]);
+                umma_commit_elect(&bars[B_ODONE + (i & 3)]);  // PV(i) completes phase i >> 2 of barrier i & 3
                 if (++ij == n_tiles) ij = 0;
             }
         }
@@ -566,6 +566,57 @@ __global__ void __launch_bounds__(NTHR, 1)
         const T* hcab = a.NC > 0 ? static_cast<const T*>(a.hca) + b * a.sh[0] : nullptr;
         bool okw = true;    // every wait of this warp completed
         bool redo = false;  // some head pair missed the range condition of the bound references
+        // Reads Q of head pair hq (then releases it to the producer) and, in the
+        // bound-referenced kernel, sets the row's reference maxima (log2 units) and
+        // returns whether every row of the CTA meets the range condition.
+        auto head_refs = [&](int hq, float& r0, float& r1, float& r2) -> bool {
+            const int qb = hq & 1;
+            const bool okq = mbar_wait_warp(&bars[B_QFULL + qb], (hq >> 1) & 1, abort_f);
+            okw = okw && okq;
+            float v0 = 0.f, v1 = 0.f;
+            if (!EXACT && okq && rvalid && tnc != nullptr) {
+                if (wg == 0) {
+                    v0 = qdot(qb, nullptr);
+                    v1 = qdot(qb, ckv + (int64_t)pos * a.sc[1]);
+                } else {
+                    if (probe_u >= 0) v0 = qdot(qb, ckv + (int64_t)probe_u * a.sc[1]);
+                    if (nv_hca > 0) v1 = qdot(qb, hcab);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars[B_QEMPTY + qb]);  // Q read; the QK warp commits its last QK
+            if constexpr (EXACT) {
+                r0 = r1 = r2 = 0.f;
+                return false;
+            } else {
+                xref[(wg * 2 + 0) * 128 + rid] = v0;
+                xref[(wg * 2 + 1) * 128 + rid] = v1;
+                pair_sync(bar_pair);
+                const float qn = sqrtf(wg == 0 ? v0 : xref[0 * 128 + rid]) * 1.0001f;
+                const float pl = wg == 0 ? v1 : xref[1 * 128 + rid];
+                const float pu = wg == 1 ? v0 : xref[2 * 128 + rid];
+                const float ph = wg == 1 ? v1 : xref[3 * 128 + rid];
+                // the partner has read this warp's slots before either writes them again
+                pair_sync(bar_pair);
+                constexpr float RANGE = 60.f;
+                const float ul = qn * Mloc, uu = qn * Muni, uh = qn * Mhca;
+                r0 = fminf(ul, pl + RANGE) * LOG2E;
+                r1 = fminf(uu, pu + RANGE) * LOG2E;
+                r2 = fminf(uh, ph + RANGE) * LOG2E;
+                // streams without a key for this row take no reference
+                const bool rowok = !rvalid || ((ul - pl <= 2.f * RANGE) && (probe_u < 0 || uu - pu <= 2.f * RANGE) &&
+                                               (nv_hca == 0 || uh - ph <= 2.f * RANGE));
+                int all_ok;
+                asm volatile("{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
+                             "bar.red.and.pred q, 13, 256, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+                             : "=r"(all_ok)
+                             : "r"((uint32_t)(rowok && tnc != nullptr))
+                             : "memory");
+                return all_ok != 0;
+            }
+        };
+        float rl0, rl1, rl2;
+        bool fast = head_refs(0, rl0, rl1, rl2);
         for (int hp = 0; hp < NH; ++hp) {
             const int g0 = hp * n_tiles, gend = g0 + n_tiles;
             float l0 = 0.f, l1 = 0.f, l2 = 0.f;  // this warp's share of the row sums per stream
@@ -583,50 +634,16 @@ __global__ void __launch_bounds__(NTHR, 1)
                 graw1 = Cvt<T>::to_f(gr[gs]);
                 graw2 = Cvt<T>::to_f(gr[2 * gs]);
             }
-            const int qb = hp & 1;
-            const bool okq = mbar_wait_warp(&bars[B_QFULL + qb], (hp >> 1) & 1, abort_f);
-            okw = okw && okq;
-            float v0 = 0.f, v1 = 0.f;
-            if (!EXACT && okq && rvalid && tnc != nullptr) {
-                if (wg == 0) {
-                    v0 = qdot(qb, nullptr);
-                    v1 = qdot(qb, ckv + (int64_t)pos * a.sc[1]);
-                } else {
-                    if (probe_u >= 0) v0 = qdot(qb, ckv + (int64_t)probe_u * a.sc[1]);
-                    if (nv_hca > 0) v1 = qdot(qb, hcab);
-                }
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bars[B_QEMPTY + qb]);  // Q read; the MMA warp commits its last QK
             if constexpr (!EXACT) {
-                xref[(wg * 2 + 0) * 128 + rid] = v0;
-                xref[(wg * 2 + 1) * 128 + rid] = v1;
-                pair_sync(bar_pair);
-                const float qn = sqrtf(wg == 0 ? v0 : xref[0 * 128 + rid]) * 1.0001f;
-                const float pl = wg == 0 ? v1 : xref[1 * 128 + rid];
-                const float pu = wg == 1 ? v0 : xref[2 * 128 + rid];
-                const float ph = wg == 1 ? v1 : xref[3 * 128 + rid];
-                constexpr float RANGE = 60.f;
-                const float ul = qn * Mloc, uu = qn * Muni, uh = qn * Mhca;
-                const float rl0 = fminf(ul, pl + RANGE) * LOG2E;
-                const float rl1 = fminf(uu, pu + RANGE) * LOG2E;
-                const float rl2 = fminf(uh, ph + RANGE) * LOG2E;
-                // streams without a key for this row take no reference
-                const bool rowok = !rvalid || ((ul - pl <= 2.f * RANGE) && (probe_u < 0 || uu - pu <= 2.f * RANGE) &&
-                                               (nv_hca == 0 || uh - ph <= 2.f * RANGE));
-                int fast;
-                asm volatile("{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
-                             "bar.red.and.pred q, 13, 256, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
-                             : "=r"(fast)
-                             : "r"((uint32_t)(rowok && tnc != nullptr))
-                             : "memory");
                 if (!fast) redo = true;
                 // ------------- bound-referenced tiles: no maximum, no rescale -------------
-                for (int j = (g0 & 1) == wg ? 0 : 1; j < n_tiles; j += 2) {
+                const int j0 = (g0 & 1) == wg ? 0 : 1;
+                int na1 = 0, nb1 = 0, nb2 = 0;
+                if (j0 < n_tiles) bounds(j0, na1, nb1, nb2);
+                for (int j = j0; j < n_tiles; j += 2) {
                     const int gg = g0 + j;
                     const int st = stream_of(j);
-                    int a1, b1, b2;
-                    bounds(j, a1, b1, b2);
+                    const int a1 = na1, b1 = nb1, b2 = nb2;
                     const bool none = b1 <= a1 && b2 == 0;
                     const bool full = a1 == 0 && b1 >= KT;
                     const bool oks = mbar_wait_warp(&bars[B_SFULL + wg], (gg >> 1) & 1, abort_f);
@@ -637,8 +654,10 @@ __global__ void __launch_bounds__(NTHR, 1)
                         tc_fence_after();
                         tmem_ld32(ts, s);
                         tmem_ld32(ts + 32, s + 32);
-                        tmem_wait_ld_pin64(s);
                     }
+                    // the next own tile's bounds while the loads are in flight
+                    if (j + 2 < n_tiles) bounds(j + 2, na1, nb1, nb2);
+                    if (oks) tmem_wait_ld_pin64(s);
                     // S is in registers: the MMA warp may compute tile gg+2 into this buffer
                     tc_fence_before();
                     mbar_arrive(&bars[B_SFREE + wg]);
@@ -670,11 +689,12 @@ __global__ void __launch_bounds__(NTHR, 1)
                         if (st == 0) l0 += ls;
                         else if (st == 1) l1 += ls;
                         else l2 += ls;
+                        // P buffer gg & 3 once PV(gg-4) has read it
                         const bool okp =
-                            gg < 2 || mbar_wait_warp(&bars[B_ODONE + wg], ((gg - 2) >> 1) & 1, abort_f);
+                            gg < 4 || mbar_wait_warp(&bars[B_ODONE + (gg & 3)], ((gg - 4) >> 2) & 1, abort_f);
                         okw = okw && okp;
                         if (okp) {
-                            unsigned char* prow = Ps + wg * P_BYTES + (rid >> 3) * 1024 + (rid & 7) * 128;
+                            unsigned char* prow = Ps + (gg & 3) * P_BYTES + (rid >> 3) * 1024 + (rid & 7) * 128;
 #pragma unroll
                             for (int c = 0; c < 8; ++c)
                                 *reinterpret_cast<uint4*>(prow + ((c ^ (rid & 7)) << 4)) =
@@ -772,11 +792,12 @@ __global__ void __launch_bounds__(NTHR, 1)
                         l_cur += (sa0 + sa1) + (sb0 + sb1);
                         // P into shared-memory buffer wg (the A operand of PV, 128-byte swizzled
                         // rows) once PV(gg-2) has read the buffer
+                        // P buffer gg & 3 once PV(gg-4) has read it
                         const bool okp =
-                            gg < 2 || mbar_wait_warp(&bars[B_ODONE + wg], ((gg - 2) >> 1) & 1, abort_f);
+                            gg < 4 || mbar_wait_warp(&bars[B_ODONE + (gg & 3)], ((gg - 4) >> 2) & 1, abort_f);
                         okw = okw && okp;
                         if (okp) {
-                            unsigned char* prow = Ps + wg * P_BYTES + (rid >> 3) * 1024 + (rid & 7) * 128;
+                            unsigned char* prow = Ps + (gg & 3) * P_BYTES + (rid >> 3) * 1024 + (rid & 7) * 128;
     #pragma unroll
                             for (int c = 0; c < 8; ++c)
                                 *reinterpret_cast<uint4*>(prow + ((c ^ (rid & 7)) << 4)) =
@@ -786,7 +807,7 @@ __global__ void __launch_bounds__(NTHR, 1)
                     }
                     if (__any_sync(0xffffffffu, fac != 1.f)) {
                         // every PV so far (the latest: tile gg-1, the partner's) has completed
-                        const bool okr = mbar_wait_warp(&bars[B_ODONE + ((gg - 1) & 1)], ((gg - 1) >> 1) & 1, abort_f);
+                        const bool okr = mbar_wait_warp(&bars[B_ODONE + ((gg - 1) & 3)], ((gg - 1) >> 2) & 1, abort_f);
                         okw = okw && okr;
                         if (okr) {
                             tc_fence_after();
@@ -815,10 +836,13 @@ __global__ void __launch_bounds__(NTHR, 1)
                 else if (cur == 1) l1 = l_cur;
                 else if (cur == 2) l2 = l_cur;
             }
+            // the next head pair's references (overlaps the last PVs of this one)
+            float nl0 = 0.f, nl1 = 0.f, nl2 = 0.f;
+            const bool nfast = hp + 1 < NH ? head_refs(hp + 1, nl0, nl1, nl2) : false;
             // ------------------------- epilogue of head pair hp ------------------
             // the last two PVs of the head pair (tiles gend-2, gend-1) have completed
-            bool oke = gend < 2 || mbar_wait_warp(&bars[B_ODONE + (gend & 1)], ((gend - 2) >> 1) & 1, abort_f);
-            if (oke) oke = mbar_wait_warp(&bars[B_ODONE + ((gend - 1) & 1)], ((gend - 1) >> 1) & 1, abort_f);
+            bool oke = gend < 2 || mbar_wait_warp(&bars[B_ODONE + ((gend - 2) & 3)], ((gend - 2) >> 2) & 1, abort_f);
+            if (oke) oke = mbar_wait_warp(&bars[B_ODONE + ((gend - 1) & 3)], ((gend - 1) >> 2) & 1, abort_f);
             okw = okw && oke;
             xls[(wg * 3 + 0) * 128 + rid] = l0;
             xls[(wg * 3 + 1) * 128 + rid] = l1;
@@ -886,6 +910,10 @@ __global__ void __launch_bounds__(NTHR, 1)
             // first tile (whose PV overwrites O)
             tc_fence_before();
             pair_sync(bar_pair);
+            rl0 = nl0;
+            rl1 = nl1;
+            rl2 = nl2;
+            fast = nfast;
         }
         if (!EXACT && redo && warp == 0 && lane == 0 && redo_list != nullptr) redo_list[atomicAdd(redo_count, 1)] = unit;
     }
