@@ -73,6 +73,13 @@ class ClockSampler:
         for line in self.proc.stdout:
             self.lines.append((time.time(), line.strip()))
 
+    def wait_ready(self, n=3, timeout=10.0):
+        """Block until nvidia-smi has delivered n samples: its start-up (NVML initialisation)
+        stalled the GPU for tens of ms when it overlapped timed steps."""
+        t_end = time.time() + timeout
+        while self.proc is not None and len(self.lines) < n and time.time() < t_end:
+            time.sleep(0.05)
+
     def window(self, t0, t1):
         self.t0, self.t1 = t0, t1
 
@@ -358,16 +365,18 @@ def run_ours(args):
         if world > 1:
             dist.barrier(device_ids=[local])
 
+    # the clock sampler starts before the warm-up and is sampling before timing begins
+    clocks = ClockSampler(local)
+    clocks.start()
+
     # warm-up
     for _ in range(args.warmup):
         hot_path_step(mb, d, weights)
     torch.cuda.synchronize()
+    clocks.wait_ready()
 
     # device-timed region: inputs resident in HBM
     timers = OpTimers(torch)
-    clocks = ClockSampler(local)
-    clocks.start()
-    time.sleep(1.0)  # let nvidia-smi start sampling
     barrier()
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
