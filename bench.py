@@ -190,7 +190,8 @@ MY_LAUNCHES_PER_STEP = None  # filled from the op list below
 
 # DRAM bytes per launch of the two candidate dominant kernels, from the ncu captures
 # summarised under profiles/ (read + write of one launch on this workload)
-TRAFFIC = {"sa_attention": 202.1e6 + 126.4e6, "dgda_prefill": 503.4e6 + 378.2e6}
+# (attention: the T=32,768 capture scaled by 2, the units of a T=65,536 launch)
+TRAFFIC = {"sa_attention": 2 * (101.38e6 + 41.53e6), "dgda_prefill": 503.4e6 + 378.2e6}
 TRAFFIC_FILE = {"sa_attention": "sa_attention_tc_config2.md", "dgda_prefill": "dgda_prep_config2.md"}
 
 
@@ -318,6 +319,9 @@ def run_only(args):
     import maba_v2_architecture_b200 as mb
     from maba_v2_architecture_b200.ops import absorb_queries
 
+    global T_TOK
+    if args.tokens:
+        T_TOK = args.tokens
     dev = torch.device("cuda", 0)
     host, weights = build_inputs(dev)
     d = {k: v.to(dev) for k, v in host.items()}
@@ -600,6 +604,8 @@ def main():
     ap.add_argument("--decode-steps", type=int, default=256)
     ap.add_argument("--only", default=None, choices=["sa_attention", "dgda_prefill", "index_topk"],
                     help="profile helper: run one op of the step, print no JSON")
+    ap.add_argument("--tokens", type=int, default=None,
+                    help="profile helper: sequence length of the --only workload (default: the bench's)")
     args = ap.parse_args()
     args.warmup_only = args.warmup
     if args.warmup < 3:
