@@ -9,30 +9,34 @@
 // One CTA per 64 query tokens; it runs the heads two at a time (128 MMA rows,
 // row m = 2 t + h) over one tile schedule built once per CTA.  The tiles of
 // all head pairs form one sequence g = hp * n_tiles + j, so every pipeline
-// barrier's phases simply count g.
-//  * warp 0: TMA producer -- the Q tile of each head pair into one
-//    of two buffers (box 64 x 2 heads x 64 tokens, two 64-wide halves of d_c),
-//    and every latent key tile into a 4-stage ring (box 64 rows x 64 columns,
-//    twice); all with 128-byte swizzle;
-//  * warp 1: allocates the 512 TMEM columns and issues the MMAs (whole warp
-//    runs the loop, one elected lane issues):
-//    S = Q K^T (M=128, N=64, K=128; K-major A and B) into one of two TMEM S
-//    buffers, and O_s += P V (M=128, N=128, K=64; A = P read from TMEM,
-//    B = the same key tile read MN-major) into the TMEM accumulator of the
-//    tile's stream;
-//  * warps 2..5 (128 threads, thread = TMEM lane = MMA row): masked online
-//    softmax of the S tile (ex2), P (16-bit) written back over the first 32
-//    columns of its S buffer, lazy rescaling of O in TMEM (only when a row's
-//    running maximum grows by more than 2^8), and the epilogue of each head
-//    pair: O_local / l, O_sparse / l, O_hca / l weighted by the gate.
-// TMEM: S/P buffers in columns [0,128), O of stream s in [128+128s, 256+128s).
-// The MMAs of one thread run in issue order, so QK of tile g+2 (which
-// overwrites S/P buffer g&1) is issued only after PV of tile g read P.
+// barrier's phases simply count g.  12 warps in three warpgroups:
+//  * warps 0..7: softmax and epilogue, two groups of four (warp w handles TMEM
+//    lane quarter w & 3, one thread per MMA row); group w >> 2 owns the tiles
+//    g with g & 1 == group and S buffer `group`.  Per tile: load S from TMEM,
+//    release the S buffer, exponentials against the row's reference maximum,
+//    P (16-bit) into shared-memory buffer g & 3 (128-byte swizzled rows, the A
+//    operand of PV), arrive.  Per head pair: the gate-weighted sum of the
+//    three streams' O / l;
+//  * warp 8: TMA producer -- the Q tile of each head pair into one of two
+//    buffers (box 64 x 2 heads x 64 tokens, two 64-wide halves of d_c), every
+//    latent key tile into a 4-stage ring (box 64 rows x 64 columns, twice);
+//    all with 128-byte swizzle;
+//  * warp 9: allocates the 512 TMEM columns and issues S = Q K^T (M=128,
+//    N=64, K=128; K-major A and B) into the owning group's S buffer, two
+//    tiles ahead of the softmax;
+//  * warp 10: issues O_s += P V (M=128, N=128, K=64; A = P from shared
+//    memory, B = the same key tile read MN-major) into the TMEM accumulator of
+//    the tile's stream; its commits free the key stage and the P buffer;
+//  * warp 11: idle (completes the warpgroup that lends registers).
+// TMEM: S buffers in columns [0,128), O of stream s in [128+128s, 256+128s).
+// The bound-referenced instantiation (EXACT = false) needs no running
+// maximum: see the comment above the softmax code; the running-maximum one
+// (EXACT = true) serves fp16 and the CTAs the first pass listed.
 // The sparse stream runs over the union of the blocks the 64 tokens selected
 // (bitmap + popcount ranks + 64-bit token masks), as in the mma kernel.
 //
 // Every mbarrier wait is bounded: a wait that runs out raises a shared abort
-// flag, all roles leave their loops, the MMA issuer drains its MMAs and the
+// flag, all roles leave their loops, the MMA issuers drain their MMAs and the
 // producer its copies (bounded again), TMEM is freed and the device error word
 // read by maba_device_error() is set.
 #include "sa_attention.cuh"
