@@ -124,8 +124,119 @@ __global__ void __launch_bounds__(kStepThreads) dgda_step_kernel(StepArgs a) {
     }
 }
 
+// fp32 state, dk = dv = 64, unit-stride state rows: one warp per (b, h), the
+// state slice held in registers (lane l owns columns 2l, 2l+1 of all 64 rows,
+// read and written as float2 rows of 256 contiguous bytes per warp), so the
+// only memory traffic is the state in and out once; the per-row vectors
+// (decay, b*k, k, q) are broadcast from shared memory four at a time.
+constexpr int kFastWarps = 4;
+
+template <typename T>
+__global__ void __launch_bounds__(kFastWarps * 32) dgda_step_fast_kernel(StepArgs a, int64_t nbh) {
+    __shared__ __align__(16) float vec[kFastWarps][4][64];  // decay, b*k, k, q
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t bh = (int64_t)blockIdx.x * kFastWarps + warp;
+    if (bh >= nbh) return;  // the whole warp; no block-wide barrier follows
+    const int64_t bi = bh / a.H, hi = bh % a.H;
+    const T* q = static_cast<const T*>(a.q);
+    const T* k = static_cast<const T*>(a.k);
+    const T* v = static_cast<const T*>(a.v);
+    const T* bb = static_cast<const T*>(a.b);
+    const T* w = static_cast<const T*>(a.w);
+    const int j0 = 2 * lane;
+    // the state slice first: 64 independent 8-byte loads in flight per lane
+    float2 s[64];
+    if (a.state != nullptr) {
+        const float* st = static_cast<const float*>(a.state) + bi * a.ss[0] + hi * a.ss[1] + j0;
+#pragma unroll
+        for (int i = 0; i < 64; ++i) s[i] = *reinterpret_cast<const float2*>(st + (int64_t)i * a.ss[2]);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 64; ++i) s[i] = make_float2(0.f, 0.f);
+    }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        const int i = lane + 32 * r;
+        const float ki = load_as<float>(k + bi * a.sk[0] + hi * a.sk[1] + i * a.sk[2]);
+        const float bi_ = load_as<float>(bb + bi * a.sb[0] + hi * a.sb[1] + i * a.sb[2]);
+        float al;
+        if (a.alpha != nullptr)
+            al = load_as<float>(static_cast<const T*>(a.alpha) + bi * a.sa[0] + hi * a.sa[1] + i * a.sa[2]);
+        else
+            al = expf(load_as<float>(static_cast<const T*>(a.log_alpha) + bi * a.sla[0] + hi * a.sla[1] +
+                                     i * a.sla[2]));
+        vec[warp][0][i] = al;
+        vec[warp][1][i] = bi_ * ki;
+        vec[warp][2][i] = ki;
+        vec[warp][3][i] = load_as<float>(q + bi * a.sq[0] + hi * a.sq[1] + i * a.sq[2]);
+    }
+    const float wv0 = load_as<float>(w + bi * a.sw[0] + hi * a.sw[1] + j0 * a.sw[2]) *
+                      load_as<float>(v + bi * a.sv[0] + hi * a.sv[1] + j0 * a.sv[2]);
+    const float wv1 = load_as<float>(w + bi * a.sw[0] + hi * a.sw[1] + (j0 + 1) * a.sw[2]) *
+                      load_as<float>(v + bi * a.sv[0] + hi * a.sv[1] + (j0 + 1) * a.sv[2]);
+    __syncwarp();
+    // decayed state and pred_j = sum_i (b k)_i Sd_ij for this lane's two columns
+    float p0 = 0.f, p1 = 0.f;
+#pragma unroll
+    for (int i4 = 0; i4 < 16; ++i4) {
+        const float4 al = *reinterpret_cast<const float4*>(&vec[warp][0][4 * i4]);
+        const float4 bk = *reinterpret_cast<const float4*>(&vec[warp][1][4 * i4]);
+        const float alv[4] = {al.x, al.y, al.z, al.w}, bkv[4] = {bk.x, bk.y, bk.z, bk.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            float2& x = s[4 * i4 + e];
+            x.x *= alv[e];
+            x.y *= alv[e];
+            p0 = fmaf(bkv[e], x.x, p0);
+            p1 = fmaf(bkv[e], x.y, p1);
+        }
+    }
+    const float d0 = wv0 - p0, d1 = wv1 - p1;
+    // S' = Sd + k delta^T (written once), o_j = sum_i q_i S'_ij
+    float* ns = static_cast<float*>(a.new_state) + bi * a.sns[0] + hi * a.sns[1] + j0;
+    float o0 = 0.f, o1 = 0.f;
+#pragma unroll
+    for (int i4 = 0; i4 < 16; ++i4) {
+        const float4 kk = *reinterpret_cast<const float4*>(&vec[warp][2][4 * i4]);
+        const float4 qq = *reinterpret_cast<const float4*>(&vec[warp][3][4 * i4]);
+        const float kv[4] = {kk.x, kk.y, kk.z, kk.w}, qv[4] = {qq.x, qq.y, qq.z, qq.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int i = 4 * i4 + e;
+            float2 x = s[i];
+            x.x = fmaf(kv[e], d0, x.x);
+            x.y = fmaf(kv[e], d1, x.y);
+            *reinterpret_cast<float2*>(ns + (int64_t)i * a.sns[2]) = x;
+            o0 = fmaf(qv[e], x.x, o0);
+            o1 = fmaf(qv[e], x.y, o1);
+        }
+    }
+    T* o = static_cast<T*>(a.out) + bi * a.so[0] + hi * a.so[1];
+    store_from<T, float>(o + j0 * a.so[2], o0);
+    store_from<T, float>(o + (j0 + 1) * a.so[2], o1);
+}
+
+bool step_fast_ok(const StepArgs& a) {
+    auto al8 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 7) == 0; };
+    if (a.dk != 64 || a.dv != 64) return false;
+    if (a.sns[3] != 1 || (a.sns[2] & 1) || (a.sns[1] & 1) || (a.sns[0] & 1) || !al8(a.new_state)) return false;
+    if (a.state != nullptr && (a.ss[3] != 1 || (a.ss[2] & 1) || (a.ss[1] & 1) || (a.ss[0] & 1) || !al8(a.state)))
+        return false;
+    return true;
+}
+
 template <typename T, typename TS>
 int launch_step(StepArgs& a, int64_t B, cudaStream_t stream) {
+    if constexpr (std::is_same<TS, float>::value && !std::is_same<T, double>::value) {
+        if (step_fast_ok(a)) {
+            const int64_t nbh = B * a.H;
+            if (nbh > 0) {
+                dgda_step_fast_kernel<T><<<(unsigned)ceil_div(nbh, kFastWarps), kFastWarps * 32, 0, stream>>>(a, nbh);
+                return check_launch("dgda_step");
+            }
+            return MABA_OK;
+        }
+    }
     using ACC = typename std::conditional<sizeof(T) == 8, double, float>::type;
     const int nrg = (kStepThreads / a.dv) > 0 ? (kStepThreads / a.dv) : 1;
     const size_t smem = sizeof(ACC) * ((size_t)a.dk * a.dv + 4 * a.dk + 2 * a.dv + (size_t)nrg * a.dv);

@@ -218,6 +218,30 @@ def test_step_bf16_with_fp32_state():
     assert_rel(S, rS, 1e-5, "S")
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("B,H,with_state", [(3, 5, True), (1, 1, False), (64, 10, True)])
+def test_step_register_path_matches_generic_and_oracle(dtype, B, H, with_state):
+    """fp32 state, d = 64, unit-stride rows take the register-resident kernel (one warp per
+    head, B*H not a multiple of its 4 warps per CTA); a column-major state view takes the
+    generic kernel.  Both against each other and the fp64 oracle."""
+    x = dgda_inputs(B=B, T=1, H=H, seed=30 + B, per_channel=True)
+    args = [x[k][:, :, 0].to(DEV, dtype) for k in ("q", "k", "v", "alpha", "b", "w")]
+    s0 = (torch.randn(B, H, 64, 64) * 0.1) if with_state else None
+    st = s0.to(DEV) if with_state else None
+    o, S = mb.b200_dgda_step(*args, state=st, state_dtype=torch.float32)
+    assert S.dtype == torch.float32
+    if with_state:
+        st_cm = st.transpose(2, 3).contiguous().transpose(2, 3)  # same values, column-major rows
+        o_g, S_g = mb.b200_dgda_step(*args, state=st_cm)
+        torch.testing.assert_close(S, S_g.contiguous(), rtol=1e-5, atol=1e-6)
+        torch.testing.assert_close(o.float(), o_g.float(), rtol=2e-2 if dtype != torch.float32 else 1e-5,
+                                   atol=1e-5)
+    ref = [a.double().cpu().numpy() for a in args]
+    ro, rS = OD.dgda_step(*ref, state=s0.double().numpy() if with_state else None)
+    assert_rel(S, rS, 1e-5, "S")
+    assert_rel(o, ro, RTOL_FP32 if dtype == torch.float32 else RTOL_BF16, "o")
+
+
 # ---------------------------------------------------------------- tensor-core (16-bit) chunk kernel
 @pytest.mark.parametrize("dtype,rtol", [(torch.bfloat16, RTOL_BF16), (torch.float16, RTOL_FP16 * 2)])
 @pytest.mark.parametrize("B,H,L", [(1, 2, 4096), (2, 10, 700), (1, 1, 129)])
