@@ -191,7 +191,7 @@ MY_LAUNCHES_PER_STEP = None  # filled from the op list below
 # DRAM bytes per launch of the two candidate dominant kernels, from the ncu captures
 # summarised under profiles/ (read + write of one launch on this workload)
 # (attention: the T=32,768 capture scaled by 2, the units of a T=65,536 launch)
-TRAFFIC = {"sa_attention": 2 * (101.38e6 + 41.53e6), "dgda_prefill": 503.4e6 + 378.2e6}
+TRAFFIC = {"sa_attention": 2 * (101.37e6 + 41.29e6), "dgda_prefill": 503.4e6 + 378.2e6}
 TRAFFIC_FILE = {"sa_attention": "sa_attention_tc_config2.md", "dgda_prefill": "dgda_prep_config2.md"}
 
 
@@ -323,6 +323,18 @@ def run_only(args):
     if args.tokens:
         T_TOK = args.tokens
     dev = torch.device("cuda", 0)
+    if args.only == "dgda_step":
+        # one decode step of every head of a batch: fp32 state [B, H, 64, 64], bf16 vectors
+        g = torch.Generator(device=dev).manual_seed(5)
+        st = torch.randn(args.batch, H, DH, DH, device=dev, generator=g) * 0.1
+        vec = [torch.randn(args.batch, H, DH, device=dev, generator=g).to(torch.bfloat16) for _ in range(6)]
+        la = (-vec[5].float().abs()).to(torch.bfloat16)
+        torch.cuda.synchronize()
+        for _ in range(args.warmup_only + args.steps):
+            mb.b200_dgda_step(vec[0], vec[1], vec[2], None, vec[3], vec[4], state=st, log_alpha=la)
+        torch.cuda.synchronize()
+        print(f"ran dgda_step B={args.batch} x{args.warmup_only + args.steps}")
+        return
     host, weights = build_inputs(dev)
     d = {k: v.to(dev) for k, v in host.items()}
     tv = lambda t: t.transpose(1, 2)
@@ -602,10 +614,11 @@ def main():
     ap.add_argument("--no-extras", action="store_true", help="skip the config-3 prefill and config-4 decode fields")
     ap.add_argument("--decode-ctx", type=int, default=1048576)
     ap.add_argument("--decode-steps", type=int, default=256)
-    ap.add_argument("--only", default=None, choices=["sa_attention", "dgda_prefill", "index_topk"],
+    ap.add_argument("--only", default=None, choices=["sa_attention", "dgda_prefill", "index_topk", "dgda_step"],
                     help="profile helper: run one op of the step, print no JSON")
     ap.add_argument("--tokens", type=int, default=None,
                     help="profile helper: sequence length of the --only workload (default: the bench's)")
+    ap.add_argument("--batch", type=int, default=512, help="profile helper: batch of --only dgda_step")
     args = ap.parse_args()
     args.warmup_only = args.warmup
     if args.warmup < 3:
