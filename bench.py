@@ -20,6 +20,7 @@ sequence (weak scaling, no collective on the data path); time = max over ranks.
 from __future__ import annotations
 
 import argparse
+import gc
 import json
 import os
 import statistics
@@ -369,7 +370,11 @@ def run_ours(args):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if world > 1:
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+        import datetime
+
+        # a short timeout: a rank that stops answering ends the others' collectives with an error
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local),
+                                timeout=datetime.timedelta(seconds=120))
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
 
@@ -391,8 +396,11 @@ def run_ours(args):
     torch.cuda.synchronize()
     clocks.wait_ready()
 
-    # device-timed region: inputs resident in HBM
+    # device-timed region: inputs resident in HBM.  The Python garbage collector is off while
+    # steps are enqueued: a collection pass (10-20 ms) in the middle of a step left the GPU idle.
     timers = OpTimers(torch)
+    gc.collect()
+    gc.disable()
     barrier()
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -406,6 +414,7 @@ def run_ours(args):
     barrier()
     clocks.window(wall0, wall1)
     clk = clocks.stop()
+    gc.enable()
     ms = start.elapsed_time(end) / args.steps
     if world > 1:
         t = torch.tensor([ms], device=dev)
@@ -422,6 +431,13 @@ def run_ours(args):
         t = torch.tensor([e2e_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
+
+    # one 1,048,576-token sequence split across the ranks (config 5a's layout)
+    split = None
+    if not args.no_seq_split:
+        del d
+        torch.cuda.empty_cache()
+        split = seq_split_prefill(torch, mb, dev, world, rank, barrier, SPLIT_TOKENS)
 
     if rank == 0:
         pk = peaks()
@@ -460,13 +476,14 @@ def run_ours(args):
                                            "(profiles/" + TRAFFIC_FILE.get(dom, "") + ")",
                          "peak_source": pk["source"]},
             "per_op_ms": {k: round(v, 4) for k, v in per_op.items()},
+            "seq_split_1m": split,
             "gpu_launches": count_launches(mb, T_TOK, H) * args.steps,
             "clocks": clk,
         }
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(budget_s=args.cpu_budget)
         if world == 1 and not args.no_extras:
-            del d, out
+            del out
             torch.cuda.empty_cache()
             line["extras"] = {"config3_prefill": config3_prefill(dev),
                               "config4_decode": config4_decode(dev, ctx=args.decode_ctx, steps=args.decode_steps)}
@@ -474,6 +491,78 @@ def run_ours(args):
     if world > 1:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
+
+
+SPLIT_TOKENS = 1 << 20
+
+
+def seq_split_prefill(torch, mb, dev, world, rank, barrier, total, reps=2):
+    """The hot path (DGDA op + DG-Indexer + MABA-SA) over ONE sequence of `total` tokens cut
+    into `world` contiguous segments, one per rank, sized for equal work
+    (parallel.balanced_segments: later segments attend longer prefixes, so they are shorter)
+    (maba_v2_architecture_b200.parallel):
+    DGDA exchanges the segment transitions, MABA-SA the latent rows, centroids and pooled
+    rows (NCCL all-gather); everything else is local.  Inputs are drawn on the device
+    (config-2 distributions, seeded per rank).  Device time of `reps` passes after one
+    warm-up pass, max over ranks; tokens/s counts the whole sequence."""
+    import torch.distributed as dist
+
+    from maba_v2_architecture_b200 import parallel as par
+    from maba_v2_architecture_b200.ops import absorb_queries
+
+    bounds = par.balanced_segments(total, world)
+    Ls = bounds[rank + 1] - bounds[rank]
+    g = torch.Generator(device=dev).manual_seed(4000 + rank)
+    bf = torch.bfloat16
+    rn = lambda *shape: torch.randn(*shape, device=dev, generator=g)
+    q = torch.nn.functional.normalize(rn(1, H, Ls, DH), dim=-1).to(bf)
+    k = torch.nn.functional.normalize(rn(1, H, Ls, DH), dim=-1).to(bf)
+    v = rn(1, H, Ls, DH).to(bf)
+    b = torch.sigmoid(rn(1, H, Ls, DH)).to(bf)
+    w = torch.sigmoid(rn(1, H, Ls, DH)).to(bf)
+    la = (-torch.nn.functional.softplus(rn(1, H, Ls, DH) + 2.0)).to(bf)
+    sc = 1.0 / (DC ** 0.5)
+    c_kv = (rn(1, Ls, DC) * sc).to(bf)
+    q_att = (rn(1, Ls, H, DH) * sc).to(bf)
+    q_idx = (rn(1, Ls, DIDX) * sc).to(bf)
+    k_idx = (rn(1, Ls, DIDX) * sc).to(bf)
+    gate = rn(1, Ls, 3).to(bf)
+    w_uk = (rn(H * DH, DC) * 0.02).to(bf)
+    p = par.SAParams(window=WINDOW, sinks=SINKS, block=BLOCK, hca_r=HCA_R, top_k=TOPK, lam=LAM)
+
+    def one():
+        if world > 1:
+            o_d, _ = par.sp_dgda_prefill(q, k, v, b, w, la)
+            qhat = absorb_queries(q_att, w_uk, H, 1.0 / (DH ** 0.5))
+            o_a, _ = par.sp_sa_prefill(qhat, c_kv, q_idx, k_idx, gate, p)
+        else:
+            o_d, _ = mb.b200_dgda_prefill(q, k, v, None, b, w, log_alpha=la, state_dtype=torch.float32)
+            qhat = absorb_queries(q_att, w_uk, H, 1.0 / (DH ** 0.5))
+            c, cent, hca = par.sa_segment_phase_a(c_kv, k_idx, p)
+            o_a, _ = par.sa_segment_phase_b(qhat, q_idx, gate, [c], [cent], [hca], 0, p)
+        return o_d, o_a
+
+    one()
+    torch.cuda.synchronize()
+    barrier()
+    gc.collect()
+    gc.disable()  # no collection pass while the passes are enqueued
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        one()
+    e1.record()
+    torch.cuda.synchronize()
+    gc.enable()
+    ms = e0.elapsed_time(e1) / reps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return {"tokens": total, "segments": [b - a for a, b in zip(bounds, bounds[1:])], "ranks": world,
+            "ms": round(ms, 3),
+            "tok_s": total / (ms * 1e-3), "time": "device, max over ranks, exchanges included",
+            "scaling": "strong"}
 
 
 def e2e_pipelined(torch, mb, host, weights, dev, steps, barrier):
@@ -493,6 +582,8 @@ def e2e_pipelined(torch, mb, host, weights, dev, steps, barrier):
     keep = []
     barrier()
     torch.cuda.synchronize()
+    gc.collect()
+    gc.disable()  # no collection pass while steps are enqueued
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(comp)
     s_in.wait_stream(comp)
@@ -517,6 +608,7 @@ def e2e_pipelined(torch, mb, host, weights, dev, steps, barrier):
     comp.wait_stream(s_in)
     e1.record(comp)
     torch.cuda.synchronize()
+    gc.enable()
     barrier()
     del keep
     return e0.elapsed_time(e1) / steps, h2d, d2h
@@ -612,6 +704,7 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=20.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="skip the config-3 prefill and config-4 decode fields")
+    ap.add_argument("--no-seq-split", action="store_true", help="skip the 1M-token sequence-split field")
     ap.add_argument("--decode-ctx", type=int, default=1048576)
     ap.add_argument("--decode-steps", type=int, default=256)
     ap.add_argument("--only", default=None, choices=["sa_attention", "dgda_prefill", "index_topk", "dgda_step"],

@@ -97,10 +97,12 @@ struct TcLayout {
         bitmap = ulist + UMAX * 4;
         wpref = bitmap + nwords * 4;
         scan = wpref + nwords * 4;
-        // tile maxima [2 groups][2 slots][128], row sums [2 groups][3][128],
-        // reference inputs [2 groups][2][128], stream key-norm maxima [4]
-        xch = scan + (NTHR + 16) * 4;
-        total = xch + (2 * 2 + 2 * 3 + 2 * 2) * 128 * 4 + 16;
+        // After the prologue the scan area holds: tile maxima (the running-maximum
+        // kernel) or reference inputs (the bound-referenced one), both
+        // [2 groups][2][128]; row sums [2 groups][3][128]; stream key-norm maxima [4]
+        xch = scan;
+        const uint32_t xbytes = (2 * 2 + 2 * 3) * 128 * 4 + 16, sbytes = (NTHR + 16) * 4;
+        total = xch + (xbytes > sbytes ? xbytes : sbytes);
     }
 };
 
@@ -469,8 +471,8 @@ __global__ void __launch_bounds__(NTHR, 1)
         const int bar_mine = 1 + wg * 4 + q4, bar_other = 1 + (wg ^ 1) * 4 + q4, bar_pair = 9 + q4;
         float* xmax = reinterpret_cast<float*>(base + LY.xch);  // [2 groups][2 slots][128]
         float* xls = xmax + 2 * 2 * 128;                          // [2 groups][3 streams][128]
-        float* xref = xls + 2 * 3 * 128;                          // [2 groups][2][128]
-        float* mstr = xref + 2 * 2 * 128;                         // key-norm maxima per stream
+        float* xref = xmax;                                       // [2 groups][2][128] (bound-referenced kernel)
+        float* mstr = xls + 2 * 3 * 128;                          // key-norm maxima per stream
         // positions fit in 32 bits (Lkv < 2^31 on this path)
         const int pos = (int)(P0 + t);
         const int lkv = (int)a.Lkv;

@@ -80,6 +80,39 @@ def _gather(t: torch.Tensor, group) -> List[torch.Tensor]:
     return out
 
 
+def _gather_rows(t: torch.Tensor, group) -> List[torch.Tensor]:
+    """All-gather of [B, n_r, d] tensors whose n_r differ between ranks (padded to the
+    largest, then cut back)."""
+    n = torch.tensor([t.shape[1]], dtype=torch.int64, device=t.device)
+    ns = [int(x.item()) for x in _gather(n, group)]
+    m = max(ns)
+    if t.shape[1] < m:
+        pad = torch.zeros(t.shape[0], m - t.shape[1], *t.shape[2:], dtype=t.dtype, device=t.device)
+        t = torch.cat([t, pad], dim=1)
+    return [x[:, :k] for x, k in zip(_gather(t, group), ns)]
+
+
+def balanced_segments(total: int, world: int, unit: int = 64, flat: float = 67.0, slope: float = 1.0 / 4096) -> List[int]:
+    """Segment boundaries [0, b_1, ..., total] (multiples of `unit`) that give every rank the
+    same work under a per-token cost flat + slope * position: the three-stream attention
+    grows with the position through the pooled-HCA stream (pos / (64 * 64) key tiles of 64
+    per query tile and head pair) while DGDA and the other streams cost the same per token
+    (`flat`, in the same tile units, from the measured single-GPU split of the step)."""
+    def cost(x):
+        return flat * x + 0.5 * slope * x * x
+    tot = cost(total)
+    bounds = [0]
+    for r in range(1, world):
+        target = tot * r / world
+        # solve cost(x) = target for x >= 0
+        a, b_, c = 0.5 * slope, flat, -target
+        x = (-b_ + (b_ * b_ - 4 * a * c) ** 0.5) / (2 * a) if a > 0 else target / flat
+        x = int(round(x / unit)) * unit
+        bounds.append(min(max(x, bounds[-1] + unit), total - (world - r) * unit))
+    bounds.append(total)
+    return bounds
+
+
 # ------------------------------------------------------------------ DGDA
 def dgda_segment_phase_a(q, k, v, b, w, la, backend=None):
     """Local: the segment's transition."""
@@ -129,13 +162,14 @@ def sa_segment_phase_b(qhat_local, q_idx_local, gate_local, c_all: Sequence[torc
     removes as well (maba_sparse/layers/sparse_attention.py:117-164)."""
     backend = backend or B200Backend()
     Ls = qhat_local.shape[1]
-    end = (rank + 1) * Ls
+    start = sum(int(c.shape[1]) for c in c_all[:rank])  # segments may differ in length
+    end = start + Ls
     c_prefix = torch.cat(list(c_all[: rank + 1]), dim=1)
     # The whole centroid table: future blocks score -inf, but the table's length sets
     # min(top_k, nb) and the filler indices, which then match the single-GPU indexer.
     cent = torch.cat(list(cent_all), dim=1)
     hca = torch.cat(list(hca_all[: rank + 1]), dim=1)
-    idx = backend.index_topk_at(q_idx_local, cent, p.lam, p.top_k, p.block, rank * Ls)
+    idx = backend.index_topk_at(q_idx_local, cent, p.lam, p.top_k, p.block, start)
     o = backend.sa_attention(qhat_local, c_prefix, hca if hca.shape[1] else None, idx, gate_local, p.window,
                              p.sinks, p.block, p.hca_r)
     assert c_prefix.shape[1] == end
@@ -144,11 +178,12 @@ def sa_segment_phase_b(qhat_local, q_idx_local, gate_local, c_all: Sequence[torc
 
 def sp_sa_prefill(qhat_local, c_local, q_idx_local, k_idx_local, gate_local, p: SAParams, group=None,
                   backend=None):
-    """Sequence-split DG-Indexer + MABA-SA prefill of this rank's segment."""
+    """Sequence-split DG-Indexer + MABA-SA prefill of this rank's segment (contiguous
+    segments in rank order; their lengths may differ, e.g. ``balanced_segments``)."""
     Ls = c_local.shape[1]
     if Ls % p.block or Ls % p.hca_r:
         raise ValueError(f"segment length {Ls} must be a multiple of block {p.block} and r {p.hca_r}")
     rank = dist.get_rank(group)
     c, cent, hca = sa_segment_phase_a(c_local, k_idx_local, p, backend)
-    return sa_segment_phase_b(qhat_local, q_idx_local, gate_local, _gather(c, group), _gather(cent, group),
-                              _gather(hca, group), rank, p, backend)
+    return sa_segment_phase_b(qhat_local, q_idx_local, gate_local, _gather_rows(c, group),
+                              _gather_rows(cent, group), _gather_rows(hca, group), rank, p, backend)

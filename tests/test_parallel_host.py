@@ -82,6 +82,46 @@ def test_sa_sequence_split_emulated(P):
     assert_rel(torch.cat([o for o, _ in res], dim=1), o_ref, 1e-5, "latent output")
 
 
+def _cut(t, bounds, r, dim):
+    return t.narrow(dim, bounds[r], bounds[r + 1] - bounds[r])
+
+
+def test_unequal_segments_emulated():
+    """Contiguous segments of different lengths (as balanced_segments makes them)."""
+    bounds = [0, 192, 256, 384]
+    P = len(bounds) - 1
+    be = OracleBackend()
+    q, k, v, b, w, la = _dgda_inputs(7, L=bounds[-1])
+    segs = [[_cut(t, bounds, r, 2) for t in (q, k, v, b, w, la)] for r in range(P)]
+    trans = [par.dgda_segment_phase_a(*sg, backend=be) for sg in segs]
+    outs = [par.dgda_segment_phase_b(*segs[r], trans, r, backend=be) for r in range(P)]
+    o_ref, S_ref = od.dgda_sequential(q, k, v, b=b, w=w, log_alpha=la)
+    assert_rel(torch.cat([o for o, _ in outs], dim=2), o_ref, 1e-5, "dgda o")
+    assert_rel(outs[-1][1], S_ref, 1e-5, "dgda final state")
+    qhat, c, qi, ki, gate = _sa_inputs(8, T=bounds[-1])
+    p = par.SAParams(window=96, sinks=4, block=64, hca_r=64, top_k=3, lam=0.1)
+    parts = [par.sa_segment_phase_a(_cut(c, bounds, r, 1), _cut(ki, bounds, r, 1), p, backend=be) for r in range(P)]
+    c_all, cent_all, hca_all = (list(x) for x in zip(*parts))
+    res = [par.sa_segment_phase_b(_cut(qhat, bounds, r, 1), _cut(qi, bounds, r, 1), _cut(gate, bounds, r, 1),
+                                  c_all, cent_all, hca_all, r, p, backend=be) for r in range(P)]
+    cent = oi.compute_centroids(ki.numpy(), 64)
+    idx_ref = oi.index_topk(qi.numpy(), cent, 0.1, 3, 64)
+    assert np.array_equal(torch.cat([i for _, i in res], dim=1).numpy(), idx_ref)
+    o_ref = oa.sa_attention_latent(qhat.numpy(), c.numpy(), idx_ref, gate.numpy(), 96, 4, 64, 64)
+    assert_rel(torch.cat([o for o, _ in res], dim=1), o_ref, 1e-5, "latent output")
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_balanced_segments(world):
+    total, flat, slope = 1 << 20, 67.0, 1.0 / 4096
+    bnd = par.balanced_segments(total, world, flat=flat, slope=slope)
+    assert bnd[0] == 0 and bnd[-1] == total and len(bnd) == world + 1
+    assert all(b % 64 == 0 for b in bnd) and all(x < y for x, y in zip(bnd, bnd[1:]))
+    cost = [flat * (e - s) + 0.5 * slope * (e * e - s * s) for s, e in zip(bnd, bnd[1:])]
+    assert max(cost) / min(cost) < 1.01
+    assert bnd[1] - bnd[0] >= bnd[-1] - bnd[-2]  # later (longer-prefix) segments are shorter
+
+
 def test_sa_split_rejects_ragged_segments():
     qhat, c, qi, ki, gate = _sa_inputs(4, T=96)
     with pytest.raises(ValueError, match="multiple of block"):
@@ -94,31 +134,33 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, out_dir):
+def _worker(rank, world, port, out_dir, bounds):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         be = OracleBackend()
-        q, k, v, b, w, la = _dgda_inputs(5, L=128 * world)
-        o, S = par.sp_dgda_prefill(*[_seg(t, rank, world, 2) for t in (q, k, v, b, w, la)], backend=be)
-        qhat, c, qi, ki, gate = _sa_inputs(6, T=128 * world)
+        q, k, v, b, w, la = _dgda_inputs(5, L=bounds[-1])
+        o, S = par.sp_dgda_prefill(*[_cut(t, bounds, rank, 2) for t in (q, k, v, b, w, la)], backend=be)
+        qhat, c, qi, ki, gate = _sa_inputs(6, T=bounds[-1])
         p = par.SAParams(window=96, sinks=4, block=64, hca_r=64, top_k=3, lam=0.1)
-        so, sidx = par.sp_sa_prefill(*[_seg(t, rank, world, 1) for t in (qhat, c, qi, ki, gate)], p, backend=be)
+        so, sidx = par.sp_sa_prefill(*[_cut(t, bounds, rank, 1) for t in (qhat, c, qi, ki, gate)], p, backend=be)
         torch.save({"o": o, "S": S, "so": so, "sidx": sidx}, os.path.join(out_dir, f"r{rank}.pt"))
         dist.barrier()
     finally:
         dist.destroy_process_group()
 
 
-def test_sequence_split_gloo_world2(tmp_path):
+@pytest.mark.parametrize("bounds", [[0, 128, 256], [0, 192, 256]], ids=["equal", "unequal"])
+def test_sequence_split_gloo_world2(tmp_path, bounds):
     world = 2
-    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, start_method="spawn")
+    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path), bounds), nprocs=world,
+                       start_method="spawn")
     res = [torch.load(tmp_path / f"r{r}.pt") for r in range(world)]
-    q, k, v, b, w, la = _dgda_inputs(5, L=128 * world)
+    q, k, v, b, w, la = _dgda_inputs(5, L=bounds[-1])
     o_ref, S_ref = od.dgda_sequential(q, k, v, b=b, w=w, log_alpha=la)
     assert_rel(torch.cat([r["o"] for r in res], dim=2), o_ref, 1e-5, "dgda o")
     assert_rel(res[-1]["S"], S_ref, 1e-5, "dgda final state")
-    qhat, c, qi, ki, gate = _sa_inputs(6, T=128 * world)
+    qhat, c, qi, ki, gate = _sa_inputs(6, T=bounds[-1])
     idx_ref = oi.index_topk(qi.numpy(), oi.compute_centroids(ki.numpy(), 64), 0.1, 3, 64)
     assert np.array_equal(torch.cat([r["sidx"] for r in res], dim=1).numpy(), idx_ref)
     o_sa = oa.sa_attention_latent(qhat.numpy(), c.numpy(), idx_ref, gate.numpy(), 96, 4, 64, 64)
