@@ -529,12 +529,24 @@ def seq_split_prefill(torch, mb, dev, world, rank, barrier, total, reps=2):
     gate = rn(1, Ls, 3).to(bf)
     w_uk = (rn(H * DH, DC) * 0.02).to(bf)
     p = par.SAParams(window=WINDOW, sinks=SINKS, block=BLOCK, hca_r=HCA_R, top_k=TOPK, lam=LAM)
+    # the DGDA exchange on its own communicator, so that it and the MABA-SA exchange do not
+    # queue behind each other (each NCCL communicator runs its collectives in order)
+    pg_dgda = dist.new_group(backend="nccl") if world > 1 else None
 
     def one():
         if world > 1:
-            o_d, _ = par.sp_dgda_prefill(q, k, v, b, w, la)
+            # exchanges are issued in the same order on every rank: the MABA-SA tables first
+            # (cheap to produce), then the DGDA payloads (rank 0's needs its whole prefill);
+            # ranks > 0 run their attention while rank 0 runs that prefill
+            c, cent, hca = par.sa_segment_phase_a(c_kv, k_idx, p)
+            c_all, cent_all, hca_all = (par._gather_rows(t, None) for t in (c, cent, hca))
+            mine, done = par.dgda_split_payload(q, k, v, b, w, la, rank, world)
+            trans = [torch.empty_like(mine) for _ in range(world)]
+            work = dist.all_gather(trans, mine, group=pg_dgda, async_op=True)
             qhat = absorb_queries(q_att, w_uk, H, 1.0 / (DH ** 0.5))
-            o_a, _ = par.sp_sa_prefill(qhat, c_kv, q_idx, k_idx, gate, p)
+            o_a, _ = par.sa_segment_phase_b(qhat, q_idx, gate, c_all, cent_all, hca_all, rank, p)
+            work.wait()
+            o_d = done[0] if done is not None else par.dgda_segment_phase_b(q, k, v, b, w, la, trans, rank)[0]
         else:
             o_d, _ = mb.b200_dgda_prefill(q, k, v, None, b, w, log_alpha=la, state_dtype=torch.float32)
             qhat = absorb_queries(q_att, w_uk, H, 1.0 / (DH ** 0.5))
@@ -546,7 +558,8 @@ def seq_split_prefill(torch, mb, dev, world, rank, barrier, total, reps=2):
     torch.cuda.synchronize()
     barrier()
     gc.collect()
-    gc.disable()  # no collection pass while the passes are enqueued
+    gc.disable()  # no collection pass while the passes are enqueued (the size exchange of the
+    #               row gathers syncs the host once per pass)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(reps):
@@ -554,6 +567,8 @@ def seq_split_prefill(torch, mb, dev, world, rank, barrier, total, reps=2):
     e1.record()
     torch.cuda.synchronize()
     gc.enable()
+    if pg_dgda is not None:
+        dist.destroy_process_group(pg_dgda)
     ms = e0.elapsed_time(e1) / reps
     if world > 1:
         t = torch.tensor([ms], device=dev)

@@ -128,11 +128,35 @@ def dgda_segment_phase_b(q, k, v, b, w, la, trans: Sequence[torch.Tensor], rank:
     return backend.dgda_prefill(q, k, v, b, w, la, S)
 
 
+def dgda_split_payload(q, k, v, b, w, la, rank: int, world: int, backend=None):
+    """Local part before the exchange of the sequence-split DGDA prefill.  Rank 0 runs its
+    prefill at once and publishes its final state as the transition [S_end | 0] (P = 0,
+    so folding it yields S_end whatever came before); ranks 1..world-2 publish their
+    transitions; the last rank's would never be used, so it sends zeros.
+    Returns (payload [B,H,64,128] fp32, (o, S_end) for rank 0 else None)."""
+    backend = backend or B200Backend()
+    B, H = q.shape[:2]
+    dk, dv = q.shape[-1], v.shape[-1]
+    if rank == 0:
+        o, S_end = backend.dgda_prefill(q, k, v, b, w, la, None)
+        mine = torch.zeros(B, H, DP, 2 * DP, dtype=torch.float32, device=q.device)
+        mine[..., :dk, :dv] = S_end.float().to(q.device)
+        return mine, (o, S_end)
+    if rank < world - 1:
+        return dgda_segment_phase_a(q, k, v, b, w, la, backend), None
+    return torch.zeros(B, H, DP, 2 * DP, dtype=torch.float32, device=q.device), None
+
+
 def sp_dgda_prefill(q, k, v, b, w, la, group=None, backend=None):
     """Sequence-split DGDA prefill: this rank's segment of q..la ([B,H,Ls,d] views).
-    Returns (o of the segment, state at the end of the segment)."""
-    rank = dist.get_rank(group)
-    trans = _gather(dgda_segment_phase_a(q, k, v, b, w, la, backend), group)
+    Returns (o of the segment, state at the end of the segment).  One all-gather of
+    the payloads of ``dgda_split_payload``; every rank r > 0 then folds the first r
+    entries into its starting state and runs its output pass."""
+    rank, world = dist.get_rank(group), dist.get_world_size(group)
+    mine, done = dgda_split_payload(q, k, v, b, w, la, rank, world, backend)
+    trans = _gather(mine, group)
+    if done is not None:
+        return done
     return dgda_segment_phase_b(q, k, v, b, w, la, trans, rank, backend)
 
 

@@ -108,7 +108,8 @@ class OracleBackend:
 
     def dgda_prefill(self, q, k, v, b, w, la, initial_state):
         o, S = self.od.dgda_sequential(to_np(q), to_np(k), to_np(v), b=to_np(b), w=to_np(w),
-                                       initial_state=to_np(initial_state), log_alpha=to_np(la))
+                                       initial_state=None if initial_state is None else to_np(initial_state),
+                                       log_alpha=to_np(la))
         return self._t(o, q), torch.from_numpy(S).float()
 
     def compute_centroids(self, k_idx, block):

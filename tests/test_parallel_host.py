@@ -66,6 +66,22 @@ def test_dgda_sequence_split_emulated(P):
     assert_rel(outs[-1][1], S_ref, 1e-5, "final state")
 
 
+@pytest.mark.parametrize("P", [2, 3, 4])
+def test_dgda_split_payload_protocol_emulated(P):
+    """The exchanged payloads of sp_dgda_prefill: rank 0's final state as [S_end | 0],
+    transitions of the middle ranks, zeros from the last; every rank's output pass from
+    the folded state reproduces the single-sequence recurrence."""
+    q, k, v, b, w, la = _dgda_inputs(9, L=64 * P)
+    be = OracleBackend()
+    segs = [[_seg(t, r, P, 2) for t in (q, k, v, b, w, la)] for r in range(P)]
+    pays = [par.dgda_split_payload(*segs[r], r, P, backend=be) for r in range(P)]
+    trans = [m for m, _ in pays]
+    outs = [pays[0][1]] + [par.dgda_segment_phase_b(*segs[r], trans, r, backend=be) for r in range(1, P)]
+    o_ref, S_ref = od.dgda_sequential(q, k, v, b=b, w=w, log_alpha=la)
+    assert_rel(torch.cat([o for o, _ in outs], dim=2), o_ref, 1e-5, "o")
+    assert_rel(outs[-1][1], S_ref, 1e-5, "final state")
+
+
 @pytest.mark.parametrize("P", [2, 4])
 def test_sa_sequence_split_emulated(P):
     qhat, c, qi, ki, gate = _sa_inputs(3, T=128 * P)
