@@ -166,9 +166,12 @@ def _worker(rank, world, port, out_dir, bounds):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("bounds", [[0, 128, 256], [0, 192, 256]], ids=["equal", "unequal"])
-def test_sequence_split_gloo_world2(tmp_path, bounds):
-    world = 2
+@pytest.mark.parametrize("bounds", [[0, 128, 256], [0, 192, 256], [0, 128, 192, 256, 384]],
+                         ids=["equal", "unequal", "world4"])
+def test_sequence_split_gloo(tmp_path, bounds):
+    """world 2 (equal and unequal segments) and world 4 (rank 0's final state, two
+    middle-rank transitions, the last rank's zeros) through the real collectives."""
+    world = len(bounds) - 1
     mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path), bounds), nprocs=world,
                        start_method="spawn")
     res = [torch.load(tmp_path / f"r{r}.pt") for r in range(world)]
