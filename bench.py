@@ -197,14 +197,21 @@ TRAFFIC_FILE = {"sa_attention": "sa_attention_tc_config2.md", "dgda_prefill": "d
 
 
 def count_launches(mb, L, BH):
-    """Kernels of libmaba_b200 launched per step (cuBLAS GEMMs not counted): DGDA prep, segment
-    transitions, combine, segment states, output (chunk-parallel path; one scan launch when the
-    sequence is a single segment); centroids; top-k penalty table, centroid-norm tiles, prefix max,
+    """Kernels of libmaba_b200 launched per step (cuBLAS GEMMs not counted): the DGDA op (see
+    below); centroids; top-k penalty table, centroid-norm tiles, prefix max,
     tile scan; HCA pooling; attention: key-tile norms, bound-referenced pass, running-maximum
     pass over the tiles the first one listed (an empty grid when none)."""
+    import torch
+
     lib = mb._native.lib()
     chunked = lib.maba_dgda_prefill_workspace_size(2, 1, H, L, DH, DH) > 0
-    dgda = 5 if chunked else 1
+    # chunk-parallel DGDA: prep, segment transitions, ceil(log2 nseg) rounds of the
+    # transition scan, segment starts, segment states, output (one window here)
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    nch = (L + 63) // 64
+    nseg = max(1, min((2 * sms) // BH if BH < sms else 1, nch // 8, 32))
+    rounds = max(0, (nseg - 1).bit_length()) if nseg > 1 else 0
+    dgda = (4 + rounds + 1 if nseg > 1 else 3) if chunked else 1
     return dgda + 1 + 4 + 1 + 3
 
 
