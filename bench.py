@@ -245,8 +245,9 @@ def config3_prefill(dev, steps: int = 3, warmup: int = 1):
     model.set_state_dtype(torch.float32)
     ids = torch.randint(0, 32768, (8, 8192), generator=torch.Generator().manual_seed(2)).to(dev)
     with torch.no_grad():
+        out = None
         for _ in range(warmup):
-            model(ids)
+            out = model(ids)  # outputs kept alive as in the timed loop
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
@@ -397,9 +398,12 @@ def run_ours(args):
     clocks = ClockSampler(local)
     clocks.start()
 
-    # warm-up
+    # warm-up, shaped like the timed loop: each step's outputs stay alive while the next
+    # step allocates, so the caching allocator already holds two steps' worth when timing
+    # starts (otherwise the second timed step waited on fresh device allocations)
+    out = None
     for _ in range(args.warmup):
-        hot_path_step(mb, d, weights)
+        out = hot_path_step(mb, d, weights)
     torch.cuda.synchronize()
     clocks.wait_ready()
 
@@ -601,38 +605,44 @@ def e2e_pipelined(torch, mb, host, weights, dev, steps, barrier):
     d2h = sum(t.numel() * t.element_size() for t in outs[0])
     in_ready = [torch.cuda.Event() for _ in range(2)]
     in_free = [torch.cuda.Event() for _ in range(2)]
-    keep = []
+
+    def run(n):
+        s_in.wait_stream(comp)
+        s_out.wait_stream(comp)
+        for i in range(n):
+            slot = i % 2
+            with torch.cuda.stream(s_in):
+                if i >= 2:
+                    s_in.wait_event(in_free[slot])
+                for k, v in pinned.items():
+                    bufs[slot][k].copy_(v, non_blocking=True)
+                in_ready[slot].record(s_in)
+            comp.wait_event(in_ready[slot])
+            od, osa, _ = hot_path_step(mb, bufs[slot], weights)
+            in_free[slot].record(comp)
+            with torch.cuda.stream(s_out):
+                s_out.wait_stream(comp)
+                outs[slot][0].copy_(od, non_blocking=True)
+                outs[slot][1].copy_(osa, non_blocking=True)
+            # the allocator reuses the results' blocks only after their copies have run
+            od.record_stream(s_out)
+            osa.record_stream(s_out)
+        comp.wait_stream(s_out)
+        comp.wait_stream(s_in)
+
+    run(3)  # untimed pass: the allocator settles on the pipelined loop's footprint
+    torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
     gc.collect()
     gc.disable()  # no collection pass while steps are enqueued
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(comp)
-    s_in.wait_stream(comp)
-    s_out.wait_stream(comp)
-    for i in range(steps):
-        slot = i % 2
-        with torch.cuda.stream(s_in):
-            if i >= 2:
-                s_in.wait_event(in_free[slot])
-            for k, v in pinned.items():
-                bufs[slot][k].copy_(v, non_blocking=True)
-            in_ready[slot].record(s_in)
-        comp.wait_event(in_ready[slot])
-        od, osa, _ = hot_path_step(mb, bufs[slot], weights)
-        in_free[slot].record(comp)
-        with torch.cuda.stream(s_out):
-            s_out.wait_stream(comp)
-            outs[slot][0].copy_(od, non_blocking=True)
-            outs[slot][1].copy_(osa, non_blocking=True)
-        keep.append((od, osa))  # results stay alive until their copies are done
-    comp.wait_stream(s_out)
-    comp.wait_stream(s_in)
+    run(steps)
     e1.record(comp)
     torch.cuda.synchronize()
     gc.enable()
     barrier()
-    del keep
     return e0.elapsed_time(e1) / steps, h2d, d2h
 
 

@@ -153,10 +153,36 @@ def require_cuda(*tensors: Optional[torch.Tensor], op: str) -> None:
             )
 
 
+_ws_cache: dict = {}
+_ws_lock = threading.Lock()
+
+
 def workspace(nbytes: int, device: torch.device) -> Optional[torch.Tensor]:
+    """Scratch for one op call, reused across calls on the same device and stream.
+
+    Ops on one stream run in order, so consecutive calls can share the buffer; a
+    larger request replaces it.  Keeping it avoids a several-hundred-MB allocation
+    per call (the DGDA record buffer), which the caching allocator could turn into a
+    blocking cudaMalloc in the middle of a stream of launches."""
     if nbytes <= 0:
         return None
-    return torch.empty(int(nbytes), dtype=torch.uint8, device=device)
+    dev = torch.device(device)
+    if dev.index is None:
+        dev = torch.device(dev.type, torch.cuda.current_device())
+    key = (dev.index, torch.cuda.current_stream(dev).cuda_stream)
+    with _ws_lock:
+        bufs = _ws_cache.setdefault(key, [])
+        if not bufs or bufs[-1].numel() < nbytes:
+            # smaller buffers stay alive: a captured CUDA graph may still point at them
+            bufs.append(torch.empty(int(nbytes), dtype=torch.uint8, device=dev))
+        return bufs[-1]
+
+
+def release_workspaces() -> None:
+    """Drops the cached per-stream scratch buffers (they are re-created on demand); only
+    safe when no captured CUDA graph still uses them."""
+    with _ws_lock:
+        _ws_cache.clear()
 
 
 def device_error(device: Optional[torch.device] = None) -> int:
