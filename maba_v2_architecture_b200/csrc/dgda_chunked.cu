@@ -1,23 +1,23 @@
 // Chunk-parallel DGDA prefill for 16-bit inputs: the preparation pass (per-chunk
-// WY/UT records), the state scan and the output pass.
+// WY/UT records) and the state scan, which also writes the outputs.
 //
 // Same recurrence as dgda_prefill_mma.cu (reference maba_sparse/kernels/
 // common.py:256-265, chunked form cpu_dgda.py:101-146) with the per-chunk WY/UT
 // quantities precomputed in parallel over all chunks (record: dgda_prefill.cuh):
 //   S' = e^{G_end} S + (k e^{G_end-G})^T (U - W S) = e^{G_end} S + N - M S
 //   o  = (q e^G) S + A (U - W S)                   = QW S + AU
-// so the sequential part per chunk is one 64x64x64 product (scan) and the output
-// one product per chunk, independent across chunks (out pass).  The decay term
-// e^{G_end} S stays in fp32; only the correction M S and the increment N pass
-// through 16-bit operands, as in the single-pass kernel.
+// so the sequential part per chunk is one 64x64x64 product for the state and one
+// for the chunk's outputs.  The decay term e^{G_end} S stays in fp32; only the
+// correction M S, the increment N and the output product pass through 16-bit
+// operands, as in the single-pass kernel.
 //
-// Scan (grid = (B*H, segments), 8 warps): the next chunk's M, N are fetched by
-// cp.async while the current product runs; the state is held in fp32
+// Scan (grid = (B*H, segments), 8 warps): the next chunk's record tiles are
+// fetched by cp.async while the current products run; the state is held in fp32
 // accumulator registers, with a double-buffered 16-bit copy in shared memory
-// that feeds the MMA and is what the output pass reads as the chunk's start
-// state.  Modes: 0 -- one segment from the initial state; 1 -- the affine
-// transition [R | P] of each segment (the augmented state starts at [0 | I]:
-// X' = e^{G_end} X + [N | 0] - M X); 2 -- each segment from its start state.
+// that feeds both products.  Modes: 0 -- one segment from the initial state;
+// 1 -- the affine transition [R | P] of each segment (the augmented state starts
+// at [0 | I]: X' = e^{G_end} X + [N | 0] - M X; no outputs); 2 -- each segment
+// from its start state.
 #include "dgda_prefill.cuh"
 #include "mma_util.cuh"
 
@@ -46,11 +46,12 @@ __device__ __forceinline__ void fetch_tile(T* dst, const unsigned char* src, int
     }
 }
 
-template <int NCOL>
+template <int NCOL, bool OUT>
 struct ScanSmem {
     static constexpr int LN = NCOL + 8;
     static constexpr size_t TILE = (size_t)C * LB * 2;
-    static constexpr size_t REC = 2 * TILE + 64 * 4;               // M, N, dend
+    static constexpr size_t QW = 2 * TILE + 64 * 4, AU = QW + TILE;  // output operands (OUT)
+    static constexpr size_t REC = QW + (OUT ? 2 * TILE : 0);        // M, N, dend[, QW, AU]
     static constexpr size_t SB = 2 * REC;                          // 2 x [D][LN] 16-bit state
     static constexpr size_t SBSZ = (size_t)D * LN * 2;
     static constexpr size_t TOTAL = SB + 2 * SBSZ;
@@ -59,7 +60,8 @@ struct ScanSmem {
 template <typename T, typename TS, int MODE>
 __global__ void __launch_bounds__(NTH, 2) dgda_scan_kernel(PrefillArgs a) {
     constexpr int NCOL = MODE == 1 ? 2 * D : D;
-    using SM = ScanSmem<NCOL>;
+    constexpr bool OUT = MODE != 1;  // modes 0 and 2 produce the chunk outputs
+    using SM = ScanSmem<NCOL, OUT>;
     constexpr int LN = SM::LN;
     constexpr int NTW = NCOL / 16;
     extern __shared__ __align__(16) unsigned char sm[];
@@ -77,6 +79,11 @@ __global__ void __launch_bounds__(NTH, 2) dgda_scan_kernel(PrefillArgs a) {
     int64_t c_end = MODE == 0 ? a.nch : c_begin + a.seg_len / C;
     if (c_end > a.nch) c_end = a.nch;
     const unsigned char* recs = a.ws_chunk + (size_t)bh * a.nch * CHUNK_REC;
+    using T2 = typename std::conditional<std::is_same<T, __half>::value, __half2, __nv_bfloat162>::type;
+    T* out = OUT ? static_cast<T*>(a.out) + bi * a.so[0] + hi * a.so[1] : nullptr;
+    // paired (4-byte) output stores: unit column stride, even dv, 4-byte aligned rows
+    const bool pair_out = OUT && a.so[3] == 1 && (dv & 1) == 0 &&
+                          ((reinterpret_cast<uintptr_t>(out) | (uintptr_t)(a.so[2] * 2)) & 3) == 0;
 
     auto fetch = [&](int64_t c, int buf) {
         unsigned char* base = sm + buf * SM::REC;
@@ -84,6 +91,10 @@ __global__ void __launch_bounds__(NTH, 2) dgda_scan_kernel(PrefillArgs a) {
         fetch_tile<T>(reinterpret_cast<T*>(base), r + CH_M, tid);
         fetch_tile<T>(reinterpret_cast<T*>(base + SM::TILE), r + CH_N, tid);
         if (tid < 16) cp_async16(base + 2 * SM::TILE + tid * 16, r + CH_DEND + tid * 16);
+        if (OUT) {
+            fetch_tile<T>(reinterpret_cast<T*>(base + SM::QW), r + CH_QW, tid);
+            fetch_tile<T>(reinterpret_cast<T*>(base + SM::AU), r + CH_AU, tid);
+        }
         cp_async_commit();
     };
     if (c_begin < c_end) fetch(c_begin, 0);
@@ -120,15 +131,6 @@ __global__ void __launch_bounds__(NTH, 2) dgda_scan_kernel(PrefillArgs a) {
         const float* dend = reinterpret_cast<const float*>(sm + buf * SM::REC + 2 * SM::TILE);
         const T* Sc = SB + buf * (SM::SBSZ / 2);        // state at the chunk start (16-bit)
         T* Sn = SB + (buf ^ 1) * (SM::SBSZ / 2);        // state after the chunk
-        if (MODE != 1) {
-            // the chunk's start state, for the output pass
-            unsigned char* dst = const_cast<unsigned char*>(recs) + (size_t)c * CHUNK_REC + CH_S;
-            for (int e = tid; e < 64 * 8; e += NTH) {
-                const int r = e >> 3, c8 = (e & 7) * 8;
-                *reinterpret_cast<uint4*>(dst + (size_t)(r * 64 + c8) * 2) =
-                    *reinterpret_cast<const uint4*>(Sc + r * LN + c8);
-            }
-        }
         // S' = e^{G_end} S + [N | 0] - M S
         float macc[NTW][4] = {};
         warp_mma<T, false, true, NTW>(macc, Mt + wr * LB, LB, Sc + wc, LN, D, lane);
@@ -142,6 +144,37 @@ __global__ void __launch_bounds__(NTH, 2) dgda_scan_kernel(PrefillArgs a) {
                 sacc[n][e] = fmaf(sacc[n][e], dend[r], nv - macc[n][e]);
             }
         store_acc16<T, NTW>(Sn + wr * LN + wc, LN, sacc, lane);
+        if constexpr (OUT) {
+            // the chunk's outputs from its start state: o = QW S + AU
+            const T* QWt = reinterpret_cast<const T*>(sm + buf * SM::REC + SM::QW);
+            const T* AUt = reinterpret_cast<const T*>(sm + buf * SM::REC + SM::AU);
+            float qacc[NTW][4] = {};
+            warp_mma<T, false, true, NTW>(qacc, QWt + wr * LB, LB, Sc + wc, LN, D, lane);
+            const int64_t t0 = c * C;
+#pragma unroll
+            for (int n = 0; n < NTW; ++n)
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int r = wr + fr + h * 8;
+                    const int col = wc + n * 8 + fc;
+                    const int64_t t = t0 + r;
+                    if (t >= a.L) continue;
+                    const float o0 = qacc[n][2 * h] + Cvt<T>::to_f(AUt[r * LB + col]);
+                    const float o1 = qacc[n][2 * h + 1] + Cvt<T>::to_f(AUt[r * LB + col + 1]);
+                    T* dst = out + t * a.so[2] + (int64_t)col * a.so[3];
+                    if (pair_out) {
+                        if (col < dv) {
+                            T2 v2;
+                            v2.x = to16<T>(o0);
+                            v2.y = to16<T>(o1);
+                            *reinterpret_cast<T2*>(dst) = v2;
+                        }
+                    } else {
+                        if (col < dv) dst[0] = to16<T>(o0);
+                        if (col + 1 < dv) dst[a.so[3]] = to16<T>(o1);
+                    }
+                }
+        }
     }
     cp_async_wait_all();
     // ---- results -------------------------------------------------------------
@@ -561,50 +594,6 @@ __global__ void __launch_bounds__(NTH, 2) dgda_prep_kernel(PrefillArgs a) {
 }
 
 // Output pass: o = QW S + AU per chunk, independent across chunks.
-struct OutSmem {
-    static constexpr size_t TILE = (size_t)C * LB * 2;
-    static constexpr size_t QW = 0, S = TILE, AU = 2 * TILE;
-    static constexpr size_t TOTAL = 3 * TILE;
-};
-
-template <typename T>
-__global__ void __launch_bounds__(NTH) dgda_out_kernel(PrefillArgs a) {
-    extern __shared__ __align__(16) unsigned char sm[];
-    T* QWt = reinterpret_cast<T*>(sm + OutSmem::QW);
-    T* St = reinterpret_cast<T*>(sm + OutSmem::S);
-    T* AUt = reinterpret_cast<T*>(sm + OutSmem::AU);
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int64_t ci = blockIdx.x;  // chunk over (b*h, chunk)
-    const int bh = (int)(ci / a.nch);
-    const int64_t c = ci - (int64_t)bh * a.nch;
-    const int64_t bi = bh / a.H, hi = bh % a.H;
-    constexpr int NTW = D / 16;
-    const int wr = (warp & 3) * 16, wc = (warp >> 2) * (D / 2);
-    const int fr = lane >> 2, fc = (lane & 3) * 2;
-    const unsigned char* rec = a.ws_chunk + (size_t)ci * CHUNK_REC;
-    fetch_tile<T>(QWt, rec + CH_QW, tid);
-    fetch_tile<T>(St, rec + CH_S, tid);
-    fetch_tile<T>(AUt, rec + CH_AU, tid);
-    cp_async_commit();
-    cp_async_wait_all();
-    __syncthreads();
-    float qacc[NTW][4] = {};
-    warp_mma<T, false, true, NTW>(qacc, QWt + wr * LB, LB, St + wc, LB, D, lane);
-    T* o = static_cast<T*>(a.out);
-    const int64_t t0 = c * C;
-#pragma unroll
-    for (int n = 0; n < NTW; ++n)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const int r = wr + fr + (e >> 1) * 8;
-            const int col = wc + n * 8 + fc + (e & 1);
-            const int64_t t = t0 + r;
-            if (t < a.L && col < a.dv)
-                o[bi * a.so[0] + hi * a.so[1] + t * a.so[2] + (int64_t)col * a.so[3]] =
-                    to16<T>(qacc[n][e] + Cvt<T>::to_f(AUt[r * LB + col]));
-        }
-}
-
 template <typename K>
 int smem_attr(K kern, size_t bytes) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
@@ -614,7 +603,7 @@ int smem_attr(K kern, size_t bytes) {
 
 template <typename T, typename TS, int MODE>
 int scan_one(const PrefillArgs& a, dim3 grid, cudaStream_t s) {
-    constexpr size_t smem = ScanSmem<MODE == 1 ? 2 * D : D>::TOTAL;
+    constexpr size_t smem = ScanSmem<MODE == 1 ? 2 * D : D, MODE != 1>::TOTAL;
     auto kern = dgda_scan_kernel<T, TS, MODE>;
     MABA_TRY(smem_attr(kern, smem));
     kern<<<grid, NTH, smem, s>>>(a);
@@ -638,14 +627,6 @@ int prep_one(const PrefillArgs& a, int64_t BH, cudaStream_t s) {
     return check_launch("dgda_prefill(prep)");
 }
 
-template <typename T>
-int out_one(const PrefillArgs& a, int64_t BH, cudaStream_t s) {
-    auto kern = dgda_out_kernel<T>;
-    MABA_TRY(smem_attr(kern, OutSmem::TOTAL));
-    kern<<<(unsigned)(BH * a.nch), NTH, OutSmem::TOTAL, s>>>(a);
-    return check_launch("dgda_prefill(out)");
-}
-
 }  // namespace
 
 int dgda_scan_launch(const PrefillArgs& a, dim3 grid, int mode, int dtype, int state_dtype, cudaStream_t s) {
@@ -661,12 +642,6 @@ int dgda_scan_launch(const PrefillArgs& a, dim3 grid, int mode, int dtype, int s
 int dgda_prep_launch(const PrefillArgs& a, int64_t BH, int dtype, cudaStream_t s) {
     if (dtype == MABA_BF16) return prep_one<__nv_bfloat16>(a, BH, s);
     if (dtype == MABA_F16) return prep_one<__half>(a, BH, s);
-    return set_error(MABA_ERR_DTYPE, "dgda_prefill(chunked): 16-bit inputs only");
-}
-
-int dgda_out_launch(const PrefillArgs& a, int64_t BH, int dtype, cudaStream_t s) {
-    if (dtype == MABA_BF16) return out_one<__nv_bfloat16>(a, BH, s);
-    if (dtype == MABA_F16) return out_one<__half>(a, BH, s);
     return set_error(MABA_ERR_DTYPE, "dgda_prefill(chunked): 16-bit inputs only");
 }
 

@@ -636,7 +636,7 @@ int set_smem(K kern, size_t bytes) {
 }
 
 // Chunk-parallel prefill (16-bit): per window, the preparation pass over all
-// chunks, the segmented state scan, and the output pass.
+// chunks and the segmented state scan (which writes the outputs).
 template <typename T>
 int launch_chunked(const PrefillArgs& a0, int64_t BH, const ChunkPlan& p, int dtype, int sdtype, cudaStream_t s,
                    void* ws) {
@@ -697,7 +697,6 @@ int launch_chunked(const PrefillArgs& a0, int64_t BH, const ChunkPlan& p, int dt
             MABA_TRY(check_launch("dgda_prefill(segment starts)"));
             MABA_TRY(dgda_scan_launch(a, grid, 2, dtype, sdtype, s));
         }
-        MABA_TRY(dgda_out_launch(a, BH, dtype, s));
     }
     return MABA_OK;
 }

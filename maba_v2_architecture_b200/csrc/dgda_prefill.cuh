@@ -26,7 +26,7 @@ struct PrefillArgs {
 // KT = k e^{G_end - G}, QT = q e^G and A = tril(q . decay . k):
 //   M  = KT^T W    N  = KT^T U      (state update: S' = e^{G_end} S + N - M S)
 //   QW = QT - A W  AU = A U         (output: o = QW S + AU)
-//   S  = state at the chunk start (written by the scan)
+//   S  = (unused slot: QT while the preparation pass runs)
 //   dend = e^{G_end}  (fp32 [64])
 // While the preparation pass runs, the N and S slots hold KT and QT.
 constexpr size_t CH_TILE = 64 * 64 * 2;
@@ -40,11 +40,10 @@ constexpr size_t CHUNK_REC = 5 * CH_TILE + 64 * 4;
 size_t dgda_mma_smem_bytes(int mode);
 int dgda_mma_launch(const PrefillArgs& a, dim3 grid, int mode, int dtype, int state_dtype, cudaStream_t s);
 
-// Chunk-parallel path (16-bit): the state scan over chunk records
-// (mode 0: one segment from the initial state; 1: segment transitions;
-// 2: segments from their start states) and the output pass.
+// Chunk-parallel path (16-bit): the state scan over chunk records, which writes
+// the outputs in modes 0 and 2 (mode 0: one segment from the initial state;
+// 1: segment transitions; 2: segments from their start states).
 int dgda_scan_launch(const PrefillArgs& a, dim3 grid, int mode, int dtype, int state_dtype, cudaStream_t s);
-int dgda_out_launch(const PrefillArgs& a, int64_t BH, int dtype, cudaStream_t s);
 int dgda_prep_launch(const PrefillArgs& a, int64_t BH, int dtype, cudaStream_t s);
 
 }  // namespace maba
