@@ -374,7 +374,7 @@ __global__ void __launch_bounds__(NTH, 2) dgda_prep_kernel(PrefillArgs a) {
     const float pr1 = blk == 0 ? 0.f : (blk == 1 ? bend1[0] : (blk == 2 ? bend1[1] : bend1[2]));
 
     // ---------------- decayed operands ----------------------------------------------
-    // QT and KT wait in the record (slots of N and S) until the epilogue needs them
+    // QT and KT wait in the record (slots of N and AU) until the epilogue needs them
     T* QTg = reinterpret_cast<T*>(rec + CH_QT_TMP);
     T* KTg = reinterpret_cast<T*>(rec + CH_KT_TMP);
     auto st2 = [](T* p, float x, float y) {
@@ -593,7 +593,6 @@ __global__ void __launch_bounds__(NTH, 2) dgda_prep_kernel(PrefillArgs a) {
     if (tid < D) reinterpret_cast<float*>(rec + CH_DEND)[tid] = dend[tid];
 }
 
-// Output pass: o = QW S + AU per chunk, independent across chunks.
 template <typename K>
 int smem_attr(K kern, size_t bytes) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
