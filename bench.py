@@ -205,13 +205,12 @@ def count_launches(mb, L, BH):
 
     lib = mb._native.lib()
     chunked = lib.maba_dgda_prefill_workspace_size(2, 1, H, L, DH, DH) > 0
-    # chunk-parallel DGDA: prep, segment transitions, ceil(log2 nseg) rounds of the
-    # transition scan, segment starts, segment states and outputs (one window here)
+    # chunk-parallel DGDA: prep, segment transitions, segment starts (transition
+    # chain), segment states and outputs (one window here)
     sms = torch.cuda.get_device_properties(0).multi_processor_count
     nch = (L + 63) // 64
     nseg = max(1, min((2 * sms) // BH if BH < sms else 1, nch // 8, 32))
-    rounds = max(0, (nseg - 1).bit_length()) if nseg > 1 else 0
-    dgda = (4 + rounds if nseg > 1 else 2) if chunked else 1
+    dgda = (4 if nseg > 1 else 2) if chunked else 1
     return dgda + 1 + 4 + 1 + 3
 
 

@@ -421,109 +421,90 @@ __global__ void __launch_bounds__(NT) dgda_combine_kernel(PrefillArgs a) {
     }
 }
 
-// Log-depth form of the combine (chunk-parallel path).  The transition of
-// segment s is the affine map T_s: S -> P_s S + R_s, stored [R_s | P_s]
-// (64 x 128 fp32).  One round of the inclusive scan over a (b,h)'s segments:
-// out_s = T_s o in_{s-d} = [P_s R' + R_s | P_s P'] for s >= d, in_s otherwise;
-// after rounds d = 1, 2, 4, ... segment s holds the map of segments 0..s.
-// One CTA per (b,h, segment); P_s staged padded, [R' | P'] staged as is.
-__global__ void __launch_bounds__(NT) dgda_tree_round_kernel(const float* in, float* out, int nseg, int d) {
-    extern __shared__ __align__(16) float tr_sm[];
-    const int bh = blockIdx.x, sg = blockIdx.y, tid = threadIdx.x;
-    const float* Ts = in + ((size_t)bh * nseg + sg) * DP * 2 * DP;
-    float* Os = out + ((size_t)bh * nseg + sg) * DP * 2 * DP;
-    if (sg < d) {
-        for (int e = tid * 4; e < DP * 2 * DP; e += NT * 4)
-            *reinterpret_cast<float4*>(Os + e) = *reinterpret_cast<const float4*>(Ts + e);
-        return;
-    }
-    const float* Tr = in + ((size_t)bh * nseg + sg - d) * DP * 2 * DP;
-    float* Pm = tr_sm;                 // [64][65]
-    float* X = tr_sm + DP * (DP + 1);  // [64][128]
-    for (int e = tid; e < DP * DP; e += NT) Pm[(e >> 6) * (DP + 1) + (e & 63)] = Ts[(e >> 6) * 2 * DP + DP + (e & 63)];
-    for (int e = tid * 4; e < DP * 2 * DP; e += NT * 4)
-        *reinterpret_cast<float4*>(X + e) = *reinterpret_cast<const float4*>(Tr + e);
-    __syncthreads();
-    const int ti = tid >> 4, tj = tid & 15;  // rows 4 ti .. 4 ti + 3, columns 8 tj .. 8 tj + 7
-    float acc[4][8];
-#pragma unroll
-    for (int r = 0; r < 4; ++r)
-#pragma unroll
-        for (int c = 0; c < 8; ++c) acc[r][c] = 0.f;
-#pragma unroll 4
-    for (int k = 0; k < DP; ++k) {
-        const float4 x0 = *reinterpret_cast<const float4*>(X + k * 2 * DP + 8 * tj);
-        const float4 x1 = *reinterpret_cast<const float4*>(X + k * 2 * DP + 8 * tj + 4);
-        const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-#pragma unroll
-        for (int r = 0; r < 4; ++r) {
-            const float pv = Pm[(4 * ti + r) * (DP + 1) + k];
-#pragma unroll
-            for (int c = 0; c < 8; ++c) acc[r][c] = fmaf(pv, xv[c], acc[r][c]);
-        }
-    }
-#pragma unroll
-    for (int r = 0; r < 4; ++r) {
-        const int row = 4 * ti + r, col = 8 * tj;
-        float v[8];
-#pragma unroll
-        for (int c = 0; c < 8; ++c) v[c] = acc[r][c] + (col < DP ? Ts[row * 2 * DP + col + c] : 0.f);
-        *reinterpret_cast<float4*>(Os + row * 2 * DP + col) = make_float4(v[0], v[1], v[2], v[3]);
-        *reinterpret_cast<float4*>(Os + row * 2 * DP + col + 4) = make_float4(v[4], v[5], v[6], v[7]);
-    }
-}
+// Starting state of every segment (chunk-parallel path) by the chain
+// start[0] = S0 (or 0), start[s+1] = P_s start[s] + R_s over the segment
+// transitions [R_s | P_s].  The columns of the state evolve independently, so one
+// (b,h)'s chain is split over 64 / CH_COLS CTAs (grid = (B*H, 64 / CH_COLS)), each
+// carrying CH_COLS columns: a step is a 64 x 64 x CH_COLS product.  Thread layout:
+// row tid & 63, columns 4 (tid >> 6) .. + 3 of the CTA's slice.  P_s sits in a padded
+// tile (row stride 65: a warp's 32 rows at one column fall in distinct banks); the
+// next segment's P and R are loaded into registers while the current step runs.
+constexpr int CH_COLS = 8;
+constexpr int CH_NT = 64 * CH_COLS / 4;
 
-// Starting state of every segment from the scanned maps: S_start(0) = S0,
-// S_start(s) = P S0 + R of the map of segments 0..s-1 (R alone when S0 = 0).
 template <typename TS>
-__global__ void __launch_bounds__(NT) dgda_tree_starts_kernel(PrefillArgs a, const float* comp) {
-    __shared__ float S0[DP * DP];
-    __shared__ float Pm[DP * (DP + 1)];
-    const int bh = blockIdx.x, sg = blockIdx.y, tid = threadIdx.x;
+__global__ void __launch_bounds__(CH_NT) dgda_chain_starts_kernel(PrefillArgs a, const float* trans) {
+    __shared__ float Pm[2][DP * (DP + 1)];
+    __shared__ __align__(16) float Sx[DP * CH_COLS];
+    const int tid = threadIdx.x;
+    const int bh = blockIdx.x, cb = blockIdx.y * CH_COLS;
     const int64_t bi = bh / a.H, hi = bh % a.H;
-    float* dst = a.ws_start + ((size_t)bh * a.nseg + sg) * DP * DP;
-    const bool has0 = a.init != nullptr;
-    if (has0 || sg == 0) {
-        for (int e = tid; e < DP * DP; e += NT) {
-            const int dd = e >> 6, c = e & 63;
-            float v = 0.f;
-            if (has0 && dd < a.dk && c < a.dv)
-                v = load_as<float>(static_cast<const TS*>(a.init) + bi * a.si[0] + hi * a.si[1] + (int64_t)dd * a.si[2] +
-                                   (int64_t)c * a.si[3]);
-            S0[e] = v;
+    const int row = tid & 63, c4 = (tid >> 6) * 4;  // this thread's state entries: (row, cb + c4 .. + 3)
+    const float* tr = trans + (size_t)bh * a.nseg * DP * 2 * DP;
+    constexpr int PF = DP * DP / 4 / CH_NT;  // float4 of P per thread
+    float4 pre[PF];
+    float4 rpre;
+    auto load = [&](int sg) {
+        const float* T = tr + (size_t)sg * DP * 2 * DP;
+#pragma unroll
+        for (int i = 0; i < PF; ++i) {
+            const int f = tid + CH_NT * i, r = f >> 4, c = (f & 15) * 4;
+            pre[i] = *reinterpret_cast<const float4*>(T + r * 2 * DP + DP + c);
         }
-    }
-    if (sg == 0) {
-        __syncthreads();
-        for (int e = tid; e < DP * DP; e += NT) dst[e] = S0[e];
-        return;
-    }
-    const float* T = comp + ((size_t)bh * a.nseg + sg - 1) * DP * 2 * DP;
-    if (!has0) {
-        for (int e = tid * 4; e < DP * DP; e += NT * 4)
-            *reinterpret_cast<float4*>(dst + e) = *reinterpret_cast<const float4*>(T + (e >> 6) * 2 * DP + (e & 63));
-        return;
-    }
-    for (int e = tid; e < DP * DP; e += NT) Pm[(e >> 6) * (DP + 1) + (e & 63)] = T[(e >> 6) * 2 * DP + DP + (e & 63)];
-    __syncthreads();
-    const int tr = tid >> 4, tc = tid & 15;  // rows tr + 16 m, columns tc + 16 kk
-    float acc[4][4];
+        rpre = *reinterpret_cast<const float4*>(T + row * 2 * DP + cb + c4);
+    };
+    auto stage = [&](int buf) {
 #pragma unroll
-    for (int m = 0; m < 4; ++m)
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) acc[m][kk] = T[(tr + 16 * m) * 2 * DP + tc + 16 * kk];
-    for (int k = 0; k < DP; ++k) {
-#pragma unroll
-        for (int m = 0; m < 4; ++m) {
-            const float pv = Pm[(tr + 16 * m) * (DP + 1) + k];
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk) acc[m][kk] = fmaf(pv, S0[k * DP + tc + 16 * kk], acc[m][kk]);
+        for (int i = 0; i < PF; ++i) {
+            const int f = tid + CH_NT * i, r = f >> 4, c = (f & 15) * 4;
+            float* d = &Pm[buf][r * (DP + 1) + c];
+            d[0] = pre[i].x;
+            d[1] = pre[i].y;
+            d[2] = pre[i].z;
+            d[3] = pre[i].w;
         }
+    };
+    float st[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int c = cb + c4 + j;
+        float v = 0.f;
+        if (a.init != nullptr && row < a.dk && c < a.dv)
+            v = load_as<float>(static_cast<const TS*>(a.init) + bi * a.si[0] + hi * a.si[1] + (int64_t)row * a.si[2] +
+                               (int64_t)c * a.si[3]);
+        st[j] = v;
     }
+    if (a.nseg > 1) {
+        load(0);
+        stage(0);
+    }
+    float4 rcur = rpre;
+    for (int sg = 0; sg < a.nseg; ++sg) {
+        float* dst = a.ws_start + ((size_t)bh * a.nseg + sg) * DP * DP + (size_t)row * DP + cb + c4;
+        *reinterpret_cast<float4*>(dst) = make_float4(st[0], st[1], st[2], st[3]);
+        if (sg + 1 >= a.nseg) break;
+        *reinterpret_cast<float4*>(&Sx[row * CH_COLS + c4]) = make_float4(st[0], st[1], st[2], st[3]);
+        if (sg + 2 < a.nseg) load(sg + 1);
+        __syncthreads();  // P_sg staged, the state slice in Sx
+        const float* P = Pm[sg & 1] + row * (DP + 1);
+        float acc[4] = {rcur.x, rcur.y, rcur.z, rcur.w};
+#pragma unroll 16
+        for (int k = 0; k < DP; ++k) {
+            const float p = P[k];
+            const float4 x = *reinterpret_cast<const float4*>(&Sx[k * CH_COLS + c4]);
+            acc[0] = fmaf(p, x.x, acc[0]);
+            acc[1] = fmaf(p, x.y, acc[1]);
+            acc[2] = fmaf(p, x.z, acc[2]);
+            acc[3] = fmaf(p, x.w, acc[3]);
+        }
+        if (sg + 2 < a.nseg) {
+            stage((sg + 1) & 1);
+            rcur = rpre;
+        }
+        __syncthreads();  // every read of Sx and of Pm[sg & 1] is done
 #pragma unroll
-    for (int m = 0; m < 4; ++m)
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) dst[(tr + 16 * m) * DP + tc + 16 * kk] = acc[m][kk];
+        for (int j = 0; j < 4; ++j) st[j] = acc[j];
+    }
 }
 
 // Composes the per-segment transitions of one (b,h) into the transition of the
@@ -622,9 +603,9 @@ ChunkPlan chunk_plan(int64_t BH, int64_t L) {
     if (nseg > 32) nseg = 32;
     p.nseg = nseg < 2 ? 1 : (int)nseg;
     p.rec_bytes = (size_t)BH * p.win * CHUNK_REC;
-    // records, transitions, segment starts, the carried state, the scan's second buffer
+    // records, transitions, segment starts, the carried state
     p.bytes = p.rec_bytes + (size_t)BH * p.nseg * (DP * 2 * DP + DP * DP) * sizeof(float) +
-              (size_t)BH * DP * DP * sizeof(float) + (size_t)BH * p.nseg * DP * 2 * DP * sizeof(float);
+              (size_t)BH * DP * DP * sizeof(float);
     return p;
 }
 
@@ -644,7 +625,6 @@ int launch_chunked(const PrefillArgs& a0, int64_t BH, const ChunkPlan& p, int dt
     float* trans = reinterpret_cast<float*>(base + p.rec_bytes);
     float* start = trans + (size_t)BH * p.nseg * DP * 2 * DP;
     float* carry = start + (size_t)BH * p.nseg * DP * DP;  // fp32 [B][H][64][64] between windows
-    float* scratch = carry + (size_t)BH * DP * DP;          // second buffer of the transition scan
     for (int64_t w = 0; w < p.nwin; ++w) {
         PrefillArgs a = a0;
         const int64_t t0 = w * p.win * 64;
@@ -680,20 +660,11 @@ int launch_chunked(const PrefillArgs& a0, int64_t BH, const ChunkPlan& p, int dt
             a.ws_start = start;
             const dim3 grid((unsigned)BH, (unsigned)a.nseg);
             MABA_TRY(dgda_scan_launch(a, grid, 1, dtype, sdtype, s));
-            // starting state of every segment: log-depth scan of the transitions
-            // (ceil(log2 nseg) rounds, all segments of all heads in parallel)
-            const float* cur = trans;
-            float* nxt = scratch;
-            const size_t rsm = (size_t)(DP * (DP + 1) + DP * 2 * DP) * sizeof(float);
-            MABA_TRY(set_smem(dgda_tree_round_kernel, rsm));
-            for (int d = 1; d < a.nseg; d <<= 1) {
-                dgda_tree_round_kernel<<<grid, NT, rsm, s>>>(cur, nxt, a.nseg, d);
-                MABA_TRY(check_launch("dgda_prefill(transition scan)"));
-                cur = nxt;
-                nxt = (nxt == scratch) ? trans : scratch;
-            }
-            if (sdtype == MABA_F32) dgda_tree_starts_kernel<float><<<grid, NT, 0, s>>>(a, cur);
-            else dgda_tree_starts_kernel<T><<<grid, NT, 0, s>>>(a, cur);
+            // starting state of every segment: the transition chain, each (b,h)'s
+            // state columns split over 64 / CH_COLS CTAs
+            const dim3 cgrid((unsigned)BH, (unsigned)(DP / CH_COLS));
+            if (sdtype == MABA_F32) dgda_chain_starts_kernel<float><<<cgrid, CH_NT, 0, s>>>(a, trans);
+            else dgda_chain_starts_kernel<T><<<cgrid, CH_NT, 0, s>>>(a, trans);
             MABA_TRY(check_launch("dgda_prefill(segment starts)"));
             MABA_TRY(dgda_scan_launch(a, grid, 2, dtype, sdtype, s));
         }

@@ -62,10 +62,71 @@ __global__ void pool_kernel(PoolArgs a) {
     }
 }
 
+// Vectorised form for unit-stride, 16-byte aligned rows of 16- or 32-bit values:
+// one thread per (block, 16-byte column group), the block's rows loaded 16 at a
+// time (all in flight together) and added in row order, t = start, start + 1, ...
+// -- the same fp32 sequence per column as pool_kernel, so the results are identical.
+template <typename TI, typename TO>
+__global__ void __launch_bounds__(64) pool_vec_kernel(PoolArgs a) {
+    constexpr int VEC = 16 / sizeof(TI);
+    constexpr int ROWS = 16;
+    const int ng = a.D / VEC;
+    const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t bi = blockIdx.y;
+    if (g >= a.nblk * ng) return;
+    const int64_t n = g / ng;
+    const int c0 = (int)(g - n * ng) * VEC;
+    const int64_t start = n * a.block;
+    int64_t end = start + a.block;
+    const bool padded = end > a.L;
+    if (padded) end = a.L;
+    const TI* p = static_cast<const TI*>(a.in) + bi * a.si[0] + c0;
+    float sum[VEC], mx[VEC];
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) {
+        sum[v] = 0.f;
+        mx[v] = padded ? 0.f : -INFINITY;
+    }
+    for (int64_t t = start; t < end; t += ROWS) {
+        uint4 buf[ROWS];
+#pragma unroll
+        for (int i = 0; i < ROWS; ++i)
+            if (t + i < end) buf[i] = *reinterpret_cast<const uint4*>(p + (t + i) * a.si[1]);
+#pragma unroll
+        for (int i = 0; i < ROWS; ++i)
+            if (t + i < end) {
+                const TI* x = reinterpret_cast<const TI*>(&buf[i]);
+#pragma unroll
+                for (int v = 0; v < VEC; ++v) {
+                    const float xv = Cvt<TI>::to_f(x[v]);
+                    sum[v] += xv;
+                    mx[v] = xv > mx[v] ? xv : mx[v];
+                }
+            }
+    }
+    TO* out = static_cast<TO*>(a.out) + bi * a.so[0] + n * a.so[1];
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) {
+        const float mean = sum[v] / float(a.block);
+        const float r = a.mode == 0 ? 0.5f * (mean + mx[v]) : mean;
+        store_from<TO, float>(out + (int64_t)(c0 + v) * a.so[2], r);
+    }
+}
+
 template <typename TI, typename TO>
 int launch_pool(PoolArgs& a, int64_t B, cudaStream_t s, const char* what) {
     using ACC = typename std::conditional<sizeof(TI) == 8, double, float>::type;
     if (a.nblk == 0 || B == 0) return MABA_OK;
+    if constexpr (sizeof(TI) != 8) {
+        constexpr int VEC = 16 / sizeof(TI);
+        const bool vec = a.si[2] == 1 && a.D % VEC == 0 && a.si[1] % VEC == 0 && a.si[0] % VEC == 0 &&
+                         (reinterpret_cast<uintptr_t>(a.in) & 15) == 0;
+        if (vec) {
+            const int64_t n = a.nblk * (a.D / VEC);
+            pool_vec_kernel<TI, TO><<<dim3((unsigned)ceil_div(n, (int64_t)64), (unsigned)B), 64, 0, s>>>(a);
+            return check_launch(what);
+        }
+    }
     dim3 grid((unsigned)a.nblk, (unsigned)B);
     int threads = a.D >= 128 ? 128 : (a.D >= 64 ? 64 : 32);
     pool_kernel<TI, TO, ACC><<<grid, threads, 0, s>>>(a);
