@@ -278,6 +278,37 @@ __global__ void __launch_bounds__(NTH, 2) dgda_prep_kernel(PrefillArgs a) {
     const T* lal = a.log_alpha ? static_cast<const T*>(a.log_alpha) + bi * a.sla[0] + hi * a.sla[1] : nullptr;
     const T* al = a.alpha ? static_cast<const T*>(a.alpha) + bi * a.sa[0] + hi * a.sa[1] : nullptr;
 
+    // the next wave's inputs into L2: one line prefetch per 128-byte row segment of
+    // each of the six operands (rows are 16-byte aligned, a.vec8)
+    if (a.pf_ahead > 0) {
+        const int64_t nxt = (int64_t)blockIdx.y * gridDim.x + blockIdx.x + a.pf_ahead;
+        const int64_t pc = nxt / gridDim.x;
+        if (pc < a.nch) {
+            const int64_t pbh = nxt - pc * gridDim.x, pb = pbh / a.H, ph = pbh % a.H;
+            for (int e = tid; e < 6 * C; e += NTH) {
+                const int op = e / C;
+                const int64_t t = pc * C + (e - op * C);
+                if (t >= a.L) continue;
+                const T* src;
+                int n;
+                switch (op) {
+                    case 0: src = static_cast<const T*>(a.q) + pb * a.sq[0] + ph * a.sq[1] + t * a.sq[2]; n = dk; break;
+                    case 1: src = static_cast<const T*>(a.k) + pb * a.sk[0] + ph * a.sk[1] + t * a.sk[2]; n = dk; break;
+                    case 2: src = static_cast<const T*>(a.b) + pb * a.sb[0] + ph * a.sb[1] + t * a.sb[2]; n = dk; break;
+                    case 3: src = static_cast<const T*>(a.v) + pb * a.sv[0] + ph * a.sv[1] + t * a.sv[2]; n = dv; break;
+                    case 4: src = static_cast<const T*>(a.w) + pb * a.sw[0] + ph * a.sw[1] + t * a.sw[2]; n = dv; break;
+                    default:
+                        src = a.log_alpha
+                                  ? static_cast<const T*>(a.log_alpha) + pb * a.sla[0] + ph * a.sla[1] + t * a.sla[2]
+                                  : static_cast<const T*>(a.alpha) + pb * a.sa[0] + ph * a.sa[1] + t * a.sa[2];
+                        n = dk;
+                }
+                for (int o = 0; o < n; o += 64)  // 64 16-bit values = one 128-byte line
+                    asm volatile("prefetch.global.L2 [%0];" ::"l"(src + o));
+            }
+        }
+    }
+
     // ---------------- log-decays of this thread's 8 x 2 slice ------------------------
     // warp rg owns rows 8 rg .. 8 rg + 7 (half of block blk = rg / 2); lane owns columns
     // d0, d0 + 1: every load / store of a row is one coalesced 128-byte access per warp
@@ -622,7 +653,14 @@ template <typename T>
 int prep_one(const PrefillArgs& a, int64_t BH, cudaStream_t s) {
     auto kern = dgda_prep_kernel<T>;
     MABA_TRY(smem_attr(kern, prep::TOTAL));
-    kern<<<dim3((unsigned)BH, (unsigned)a.nch), NTH, prep::TOTAL, s>>>(a);
+    PrefillArgs b = a;
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, NTH, prep::TOTAL) != cudaSuccess) {
+        (void)cudaGetLastError();
+        per_sm = 0;
+    }
+    b.pf_ahead = (int64_t)per_sm * sm_count();
+    kern<<<dim3((unsigned)BH, (unsigned)a.nch), NTH, prep::TOTAL, s>>>(b);
     return check_launch("dgda_prefill(prep)");
 }
 

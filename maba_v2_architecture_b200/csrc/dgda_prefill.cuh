@@ -19,6 +19,9 @@ struct PrefillArgs {
     // chunk-parallel path (16-bit inputs): one record per (b*h, chunk)
     unsigned char* ws_chunk;  // [B*H][nch] records of CHUNK_REC bytes
     int64_t nch;              // chunks per (b, h)
+    // preparation pass: a CTA prefetches into L2 the inputs of the CTA this many
+    // places after it in launch order (one wave ahead; 0: no prefetch)
+    int64_t pf_ahead;
 };
 
 // Chunk record of the chunk-parallel path: 16-bit 64x64 tiles and the chunk's
