@@ -356,6 +356,9 @@ __global__ void __launch_bounds__(kTopkThreads) topk_tile_kernel(TopkArgs a) {
     const T* c = static_cast<const T*>(a.c);
     const SC scale = scale_of<SC>(a);
 
+    // query block of each of the CTA's tokens, computed once (a 64-bit division)
+    __shared__ int64_t qbs[kTT];
+    if (tid < kTT) qbs[tid] = query_block(a, t0 + tid);
     load_tile_t<T, SC>(Qs, kLQ, q + b * a.sq[0], a.sq[1], a.sq[2], t0, a.L, D, scale, a.vecload != 0, tid);
     const bool prune = a.cpref != nullptr && a.scores == nullptr;
     // norms of this warp's 8 scaled query rows (for the candidate bound)
@@ -374,7 +377,8 @@ __global__ void __launch_bounds__(kTopkThreads) topk_tile_kernel(TopkArgs a) {
     }
 
     const int64_t tlast = (t0 + kTT - 1 < a.L ? t0 + kTT - 1 : a.L - 1);
-    int64_t n_hi = query_block(a, tlast);
+    __syncthreads();  // qbs
+    int64_t n_hi = qbs[tlast - t0];
     if (n_hi > a.nb - 1) n_hi = a.nb - 1;
 
     SC ls[8];
@@ -399,7 +403,7 @@ __global__ void __launch_bounds__(kTopkThreads) topk_tile_kernel(TopkArgs a) {
                 const int64_t t = t0 + warp * 8 + j;
                 const SC th = __shfl_sync(kFull, ls[j], a.keff - 1);
                 if (t < a.L) {
-                    const int64_t qb = query_block(a, t);
+                    const int64_t qb = qbs[warp * 8 + j];
                     const int64_t nhi = n0 + kTN - 1 < qb ? n0 + kTN - 1 : qb;
                     SC bound = qn[j] * (SC)cm * (SC)1.00001 - (SC)a.pen[qb - nhi];
                     bound += (bound < SC(0) ? -bound : bound) * (SC)1e-6 + (SC)1e-30;
@@ -432,7 +436,7 @@ __global__ void __launch_bounds__(kTopkThreads) topk_tile_kernel(TopkArgs a) {
         for (int i = 0; i < 4; ++i) {
             const int tt = 4 * ty + i;
             const int64_t t = t0 + tt;
-            const int64_t qb = query_block(a, t);
+            const int64_t qb = qbs[tt];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 const int nn = 4 * tx + j;
@@ -457,7 +461,7 @@ __global__ void __launch_bounds__(kTopkThreads) topk_tile_kernel(TopkArgs a) {
             const int tt = warp * 8 + j;
             const int64_t t = t0 + tt;
             if (t < a.L) {
-                const int64_t qb = query_block(a, t);
+                const int64_t qb = qbs[tt];
                 const int64_t nmax = qb < a.nb - 1 ? qb : a.nb - 1;
 #pragma unroll
                 for (int half = 0; half < 2; ++half) {
