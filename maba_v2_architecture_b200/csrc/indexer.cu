@@ -356,9 +356,17 @@ __global__ void __launch_bounds__(kTopkThreads) topk_tile_kernel(TopkArgs a) {
     const T* c = static_cast<const T*>(a.c);
     const SC scale = scale_of<SC>(a);
 
-    // query block of each of the CTA's tokens, computed once (a 64-bit division)
+    // query block of each of the CTA's tokens, computed once (a 64-bit division), and
+    // the last candidate block it may select (-1 for rows past the end); block indices
+    // fit in 32 bits, so the per-candidate arithmetic below is 32-bit
     __shared__ int64_t qbs[kTT];
-    if (tid < kTT) qbs[tid] = query_block(a, t0 + tid);
+    __shared__ int qb32[kTT], lim32[kTT];
+    if (tid < kTT) {
+        const int64_t qb = query_block(a, t0 + tid);
+        qbs[tid] = qb;
+        qb32[tid] = (int)qb;
+        lim32[tid] = t0 + tid < a.L ? (int)(qb < a.nb - 1 ? qb : a.nb - 1) : -1;
+    }
     load_tile_t<T, SC>(Qs, kLQ, q + b * a.sq[0], a.sq[1], a.sq[2], t0, a.L, D, scale, a.vecload != 0, tid);
     const bool prune = a.cpref != nullptr && a.scores == nullptr;
     // norms of this warp's 8 scaled query rows (for the candidate bound)
@@ -435,14 +443,13 @@ __global__ void __launch_bounds__(kTopkThreads) topk_tile_kernel(TopkArgs a) {
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const int tt = 4 * ty + i;
-            const int64_t t = t0 + tt;
-            const int64_t qb = qbs[tt];
+            const int qb = qb32[tt], lim = lim32[tt];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 const int nn = 4 * tx + j;
-                const int64_t n = n0 + nn;
+                const int n = (int)n0 + nn;
                 SC v = -INFINITY;
-                if (t < a.L && n <= qb && n < a.nb) v = acc[i][j] - (SC)a.pen[qb - n];
+                if (n <= lim) v = acc[i][j] - (SC)a.pen[qb - n];
                 Ss[tt * (kTN + 1) + nn] = v;
             }
         }
@@ -459,19 +466,17 @@ __global__ void __launch_bounds__(kTopkThreads) topk_tile_kernel(TopkArgs a) {
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             const int tt = warp * 8 + j;
-            const int64_t t = t0 + tt;
-            if (t < a.L) {
-                const int64_t qb = qbs[tt];
-                const int64_t nmax = qb < a.nb - 1 ? qb : a.nb - 1;
+            const int lim = lim32[tt];
+            if (lim >= 0) {
 #pragma unroll
                 for (int half = 0; half < 2; ++half) {
                     const int nn = half * 32 + lane;
-                    const int64_t n = n0 + nn;
+                    const int n = (int)n0 + nn;
                     SC s = -INFINITY;
                     int ci = INT_MAX;
-                    if (n <= nmax) {
+                    if (n <= lim) {
                         s = Ss[tt * (kTN + 1) + nn];
-                        ci = (int)n;
+                        ci = n;
                     }
                     warp_offer(ls[j], li[j], s, ci, a.keff, lane);
                 }
