@@ -452,7 +452,9 @@ __global__ void __launch_bounds__(NTH, 2) dgda_prep_kernel(PrefillArgs a) {
         for (int I = 1; I < 4; ++I)
             if (I > blk) st2(KHs + (kh_off(I) + r) * LB + d0, k0 * (ck0[I - 1] * r0), k1 * (ck1[I - 1] * r1));
     }
-    __threadfence();  // QT, KT reach L2 before this CTA reads them back (cp.async.cg)
+    // (QT and KT are read back only by this CTA, after the barriers below: a CTA
+    // barrier orders its threads' global writes before their later reads, so no
+    // device-wide fence is needed)
     for (int e = tid; e < C * C; e += NTH) {  // strictly-upper off-diagonal blocks
         const int i = e >> 6, j = e & 63;
         if ((j >> 4) > (i >> 4)) {
@@ -575,7 +577,7 @@ __global__ void __launch_bounds__(NTH, 2) dgda_prep_kernel(PrefillArgs a) {
         T* QTs = reinterpret_cast<T*>(sm + EP_QT);
         T* W16 = reinterpret_cast<T*>(sm + EP_W);
         T* U16 = reinterpret_cast<T*>(sm + EP_U);
-        fetch_tile<T>(KTs, rec + CH_KT_TMP, tid);  // written by this CTA above (fenced)
+        fetch_tile<T>(KTs, rec + CH_KT_TMP, tid);  // written by this CTA before the barriers above
         fetch_tile<T>(QTs, rec + CH_QT_TMP, tid);
         cp_async_commit();
         {
