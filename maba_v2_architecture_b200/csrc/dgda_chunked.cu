@@ -455,12 +455,16 @@ __global__ void __launch_bounds__(NTH, 2) dgda_prep_kernel(PrefillArgs a) {
     // (QT and KT are read back only by this CTA, after the barriers below: a CTA
     // barrier orders its threads' global writes before their later reads, so no
     // device-wide fence is needed)
-    for (int e = tid; e < C * C; e += NTH) {  // strictly-upper off-diagonal blocks
-        const int i = e >> 6, j = e & 63;
-        if ((j >> 4) > (i >> 4)) {
-            AMs[i * LB + j] = to16<T>(0.f);
-            LMs[i * LB + j] = to16<T>(0.f);
-        }
+    // strictly-upper off-diagonal 16x16 blocks of A and L are zero: 6 blocks x 16 rows
+    // x two 16-byte pieces per matrix
+    for (int e = tid; e < 2 * 6 * 16 * 2; e += NTH) {
+        const int mat = e / 192, r = e - mat * 192;
+        const int blkid = r >> 5, row16 = (r >> 1) & 15, half = r & 1;
+        // block (I, J) with J > I, enumerated (0,1) (0,2) (0,3) (1,2) (1,3) (2,3)
+        const int I = blkid < 3 ? 0 : (blkid < 5 ? 1 : 2);
+        const int J = blkid < 3 ? blkid + 1 : (blkid < 5 ? blkid - 1 : 3);
+        T* base = (mat ? LMs : AMs) + (16 * I + row16) * LB + 16 * J + 8 * half;
+        *reinterpret_cast<uint4*>(base) = make_uint4(0u, 0u, 0u, 0u);
     }
     __syncthreads();
     // ---------------- A / L blocks -------------------------------------------------------
@@ -521,20 +525,22 @@ __global__ void __launch_bounds__(NTH, 2) dgda_prep_kernel(PrefillArgs a) {
         store_acc16<T, 2>((isL ? LMs : AMs) + (16 * I) * LB + 16 * n16, LB, acc, lane);
     }
     __syncthreads();
-    // ---------------- 16x16 diagonal inverses of (I + L) (fp32, 4 partial sums) --------
+    // ---------------- 16x16 diagonal inverses of (I + L) (fp32) --------------------------
+    // column c of block db by forward substitution in column (axpy) order: once
+    // tcol[m] is final, every later row takes -L[r][m] tcol[m] -- one FMA per step on
+    // the dependency chain, the loads of L independent of it
     if (tid < 64) {
         const int db = tid >> 4, c = tid & 15;
+        const float* Lb = LDs + db * 16 * 17;
         float tcol[16];
 #pragma unroll
         for (int r = 0; r < 16; ++r) tcol[r] = r == c ? 1.f : 0.f;
 #pragma unroll
-        for (int r = 1; r < 16; ++r) {
-            if (r > c) {
-                float s4[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int m = 0; m < 15; ++m) {
+            if (m >= c) {
+                const float tm = tcol[m];
 #pragma unroll
-                for (int m = 0; m < 15; ++m)
-                    if (m >= c && m < r) s4[m & 3] = fmaf(LDs[(db * 16 + r) * 17 + m], tcol[m], s4[m & 3]);
-                tcol[r] = -((s4[0] + s4[1]) + (s4[2] + s4[3]));
+                for (int r = m + 1; r < 16; ++r) tcol[r] = fmaf(-Lb[r * 17 + m], tm, tcol[r]);
             }
         }
 #pragma unroll
