@@ -512,24 +512,13 @@ __global__ void __launch_bounds__(NTH, 2) dgda_prep_kernel(PrefillArgs a) {
         LMs[i * LB + j] = to16<T>(lv);
         LDs[(db * 16 + ii) * 17 + jj] = lv;
     }
-    for (int tile = warp; tile < 12; tile += 8) {
-        // off-diagonal 16x16 tiles: I=1: tiles 0,1; I=2: 2..5; I=3: 6..11 (first I give A, next I give L)
-        const int I = tile < 2 ? 1 : (tile < 6 ? 2 : 3);
-        const int t_in = tile - (I == 1 ? 0 : (I == 2 ? 2 : 6));
-        const bool isL = t_in >= I;
-        const int n16 = isL ? t_in - I : t_in;
-        float acc[2][4] = {};
-        const T* Ap = (isL ? BHs : QHs) + (16 * (I - 1)) * LB;
-        const T* Bp = KHs + (kh_off(I) + 16 * n16) * LB;
-        warp_mma<T, false, false, 2>(acc, Ap, LB, Bp, LB, D, lane);
-        store_acc16<T, 2>((isL ? LMs : AMs) + (16 * I) * LB + 16 * n16, LB, acc, lane);
-    }
     __syncthreads();
     // ---------------- 16x16 diagonal inverses of (I + L) (fp32) --------------------------
-    // column c of block db by forward substitution in column (axpy) order: once
-    // tcol[m] is final, every later row takes -L[r][m] tcol[m] -- one FMA per step on
-    // the dependency chain, the loads of L independent of it
-    if (tid < 64) {
+    // Warps 0-1 (they need only the diagonal blocks of L): column c of block db by
+    // forward substitution in column (axpy) order -- once tcol[m] is final, every later
+    // row takes -L[r][m] tcol[m], one FMA per step on the dependency chain, the loads
+    // of L independent of it.
+    if (warp < 2) {  // tid < 64
         const int db = tid >> 4, c = tid & 15;
         const float* Lb = LDs + db * 16 * 17;
         float tcol[16];
@@ -545,6 +534,20 @@ __global__ void __launch_bounds__(NTH, 2) dgda_prep_kernel(PrefillArgs a) {
         }
 #pragma unroll
         for (int r = 0; r < 16; ++r) TDs[(db * 16 + r) * LT + c] = to16<T>(tcol[r]);
+    } else {
+        // meanwhile warps 2-7: the off-diagonal 16x16 tiles of A and L
+        for (int tile = warp - 2; tile < 12; tile += 6) {
+            // off-diagonal 16x16 tiles: I=1: tiles 0,1; I=2: 2..5; I=3: 6..11 (first I give A, next I give L)
+            const int I = tile < 2 ? 1 : (tile < 6 ? 2 : 3);
+            const int t_in = tile - (I == 1 ? 0 : (I == 2 ? 2 : 6));
+            const bool isL = t_in >= I;
+            const int n16 = isL ? t_in - I : t_in;
+            float acc[2][4] = {};
+            const T* Ap = (isL ? BHs : QHs) + (16 * (I - 1)) * LB;
+            const T* Bp = KHs + (kh_off(I) + 16 * n16) * LB;
+            warp_mma<T, false, false, 2>(acc, Ap, LB, Bp, LB, D, lane);
+            store_acc16<T, 2>((isL ? LMs : AMs) + (16 * I) * LB + 16 * n16, LB, acc, lane);
+        }
     }
     __syncthreads();
     // ---------------- T = (I + L)^{-1} by blocks --------------------------------------
