@@ -202,7 +202,7 @@ __global__ void __launch_bounds__(NTH, 2) dgda_scan_kernel(PrefillArgs a) {
 // at once), prefix-sums the log-decays in registers (group totals exchanged
 // through shared memory), and produces every decayed operand of its slice
 // directly -- nothing fp32 of size C x D is staged in shared memory.
-//   QT = q e^G, KT = k e^{G_end - G}            -> chunk record (global)
+//   QT = q e^G, KT = k e^{G_end - G}            -> registers (packed pairs) until the epilogue
 //   BT = (b k) e^G, WV = w v                    -> shared (operands of W, U)
 //   QD, BD, KD (diagonal factors around the block's first row), QH, BH, KH
 //   (off-diagonal factors around the end of the previous block)  -> shared
@@ -405,9 +405,14 @@ __global__ void __launch_bounds__(NTH, 2) dgda_prep_kernel(PrefillArgs a) {
     const float pr1 = blk == 0 ? 0.f : (blk == 1 ? bend1[0] : (blk == 2 ? bend1[1] : bend1[2]));
 
     // ---------------- decayed operands ----------------------------------------------
-    // QT and KT wait in the record (slots of N and AU) until the epilogue needs them
-    T* QTg = reinterpret_cast<T*>(rec + CH_QT_TMP);
-    T* KTg = reinterpret_cast<T*>(rec + CH_KT_TMP);
+    // QT and KT stay in registers (packed 16-bit pairs) until the epilogue stages them
+    uint32_t qtp[8], ktp[8];
+    auto pk2 = [](float x, float y) {
+        T2 v2;
+        v2.x = to16<T>(x);
+        v2.y = to16<T>(y);
+        return *reinterpret_cast<uint32_t*>(&v2);
+    };
     auto st2 = [](T* p, float x, float y) {
         T2 v2;
         v2.x = to16<T>(x);
@@ -436,8 +441,8 @@ __global__ void __launch_bounds__(NTH, 2) dgda_prep_kernel(PrefillArgs a) {
         const float f0 = __expf(G0[i] - g00), f1 = __expf(G1[i] - g01);  // <= 1
         const float r0 = __fdividef(1.f, f0), r1 = __fdividef(1.f, f1);
         const float e0 = cg0 * f0, e1 = cg1 * f1;
-        st2(QTg + r * 64 + d0, q0 * e0, q1 * e1);
-        st2(KTg + r * 64 + d0, k0 * (ce0 * r0), k1 * (ce1 * r1));
+        qtp[i] = pk2(q0 * e0, q1 * e1);
+        ktp[i] = pk2(k0 * (ce0 * r0), k1 * (ce1 * r1));
         st2(BTs + r * LB + d0, bk0 * e0, bk1 * e1);
         st2(WVs + r * LB + d0, fx(wv[i]) * fx(vv[i]), fy(wv[i]) * fy(vv[i]));
         st2(QDs + r * LB + d0, q0 * f0, q1 * f1);
@@ -452,9 +457,6 @@ __global__ void __launch_bounds__(NTH, 2) dgda_prep_kernel(PrefillArgs a) {
         for (int I = 1; I < 4; ++I)
             if (I > blk) st2(KHs + (kh_off(I) + r) * LB + d0, k0 * (ck0[I - 1] * r0), k1 * (ck1[I - 1] * r1));
     }
-    // (QT and KT are read back only by this CTA, after the barriers below: a CTA
-    // barrier orders its threads' global writes before their later reads, so no
-    // device-wide fence is needed)
     // strictly-upper off-diagonal 16x16 blocks of A and L are zero: 6 blocks x 16 rows
     // x two 16-byte pieces per matrix
     for (int e = tid; e < 2 * 6 * 16 * 2; e += NTH) {
@@ -586,9 +588,11 @@ __global__ void __launch_bounds__(NTH, 2) dgda_prep_kernel(PrefillArgs a) {
         T* QTs = reinterpret_cast<T*>(sm + EP_QT);
         T* W16 = reinterpret_cast<T*>(sm + EP_W);
         T* U16 = reinterpret_cast<T*>(sm + EP_U);
-        fetch_tile<T>(KTs, rec + CH_KT_TMP, tid);  // written by this CTA before the barriers above
-        fetch_tile<T>(QTs, rec + CH_QT_TMP, tid);
-        cp_async_commit();
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            *reinterpret_cast<uint32_t*>(KTs + (8 * rg + i) * LB + d0) = ktp[i];
+            *reinterpret_cast<uint32_t*>(QTs + (8 * rg + i) * LB + d0) = qtp[i];
+        }
         {
             float wacc[NTW][4] = {};
             float uacc[NTW][4] = {};
@@ -597,8 +601,7 @@ __global__ void __launch_bounds__(NTH, 2) dgda_prep_kernel(PrefillArgs a) {
             store_acc16<T, NTW>(W16 + wr * LB + wc, LB, wacc, lane);
             store_acc16<T, NTW>(U16 + wr * LB + wc, LB, uacc, lane);
         }
-        cp_async_wait_all();
-        __syncthreads();  // W, U, KT, QT in shared memory; the temporary slots are free
+        __syncthreads();  // W, U, KT, QT in shared memory
         auto put = [&](size_t off, const float (&acc)[NTW][4], const T* sub) {
             T* g = reinterpret_cast<T*>(rec + off);
 #pragma unroll

@@ -30,10 +30,8 @@ struct PrefillArgs {
 //   M  = KT^T W    N  = KT^T U      (state update: S' = e^{G_end} S + N - M S)
 //   QW = QT - A W  AU = A U         (output: o = QW S + AU)
 //   dend = e^{G_end}  (fp32 [64])
-// While the preparation pass runs, the N and AU slots hold KT and QT.
 constexpr size_t CH_TILE = 64 * 64 * 2;
 constexpr size_t CH_M = 0, CH_N = CH_TILE, CH_QW = 2 * CH_TILE, CH_AU = 3 * CH_TILE, CH_DEND = 4 * CH_TILE;
-constexpr size_t CH_KT_TMP = CH_N, CH_QT_TMP = CH_AU;
 constexpr size_t CHUNK_REC = 4 * CH_TILE + 64 * 4;
 
 // Tensor-core chunk kernels for 16-bit inputs (dk, dv <= 64).
