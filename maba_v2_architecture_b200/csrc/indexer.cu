@@ -342,8 +342,9 @@ __device__ __forceinline__ void load_tile_t(SC* dst, int ld, const T* base, int6
     }
 }
 
+// fp32 scores: three CTAs per SM (80 registers; the warp sort and merge are latency-bound)
 template <typename T, typename SC>
-__global__ void __launch_bounds__(kTopkThreads) topk_tile_kernel(TopkArgs a) {
+__global__ void __launch_bounds__(kTopkThreads, sizeof(SC) == 4 ? 3 : 2) topk_tile_kernel(TopkArgs a) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const int D = a.D;
     SC* Qs = reinterpret_cast<SC*>(smem_raw);   // [D][kLQ]
