@@ -37,6 +37,27 @@ def test_centroids_bf16_and_strided():
                                   OI.compute_centroids(k.cpu().numpy(), 64))
 
 
+@pytest.mark.parametrize("L", [64, 100, 1000, 4097])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_vectorised_pooling_matches_oracle(L, dtype):
+    """Unit-stride rows take the 16-byte row-load pooling: batch 2, ragged tail blocks,
+    D = 64 (centroids) and D = 128 (HCA rows).  Centroids equal the oracle's sequential
+    fp32 sums bit for bit (then rounded to the output dtype); the HCA means (complete
+    blocks only) match the fp64 oracle."""
+    g = torch.Generator().manual_seed(L)
+    k = (torch.randn(2, L, 64, generator=g) / 8).to(dtype)
+    c = mb.b200_compute_centroids(k.to(DEV), block_size=64)
+    ref = torch.from_numpy(OI.compute_centroids(k.float().numpy(), 64)).to(dtype)
+    assert c.dtype == dtype and torch.equal(c.cpu(), ref)
+    ckv = (torch.randn(2, L, 128, generator=g) / 8).to(dtype)
+    for out_dtype in (None, torch.float32):
+        h = mb.b200_hca_pool(ckv.to(DEV), 64, out_dtype=out_dtype)
+        href = OI.hca_pool(ckv.float().numpy(), 64)
+        assert tuple(h.shape) == href.shape == (2, L // 64, 128)
+        tol = 1e-5 if (out_dtype == torch.float32 or dtype == torch.float32) else 1e-2
+        np.testing.assert_allclose(h.float().cpu().numpy(), href, rtol=tol, atol=tol * 1e-2)
+
+
 def _tk_inputs(ci, B, L):
     torch.manual_seed(400 + ci)
     return torch.randn(B, L, 64), torch.randn(B, L, 64)
