@@ -197,6 +197,12 @@ __device__ __forceinline__ void warp_offer(SC& ls, int& li, SC cs, int ci, int k
         ci = INT_MAX;
     }
     warp_sort_desc(cs, ci, lane);
+    // into an empty list (all sentinels) the sorted batch is the merge result
+    if (__shfl_sync(kFull, li, 0) == INT_MAX && __shfl_sync(kFull, ls, 0) == -INFINITY) {
+        ls = cs;
+        li = ci;
+        return;
+    }
     warp_merge(ls, li, cs, ci, lane);
 }
 
