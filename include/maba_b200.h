@@ -168,16 +168,31 @@ MABA_API size_t maba_index_topk_at_workspace_size(int64_t B, int64_t L, int64_t 
  * not pay cudaMalloc's implicit device synchronisation, or a thin foreign-
  * language binding that only ever receives device pointers from elsewhere.
  * Same arguments, results and errors as maba_index_topk minus the workspace.
- * Its scratch (the penalty table) is one file-scope device array of
- * MABA_NOALLOC_PENALTY_MAX floats (256 KiB) that every GPU which loads this
- * library holds until the process exits; requests needing more entries
- * (max(nb, ceil(L / block_size)) in prefill, nb in decode) are rejected with
- * MABA_ERR_UNSUPPORTED.  The first call on a device looks the array up (once
- * per device, with that device current): make that first call before any
- * stream capture.  All calls share the array and the kernel rewrites every
- * entry it reads, so nothing needs clearing between calls; calls that overlap
- * on the GPU (different streams, or different host threads) race on it and
- * must be serialised by the caller.  Allocates nothing. */
+ * Its scratch is one file-scope device array of MABA_NOALLOC_PENALTY_MAX
+ * floats (256 KiB) that every GPU which loads this library holds until the
+ * process exits.  A call uses it for up to three things, in this order:
+ *   1. the distance-penalty table, max(nb, ceil(L / block_size)) floats in
+ *      prefill, nb in decode (always);
+ *   2. the per-tile centroid norms and their prefix maxima of the pruned tile
+ *      scan, 2 * B * ceil(nb / 64) floats after the table rounded up to 256
+ *      bytes (prefill with scores_out absent and L >= 64);
+ *   3. the partial candidate lists of the split decode scan,
+ *      B * L * ceil(nb / 512) * 32 (score, index) pairs after the table
+ *      (decode with scores_out absent, nb >= 2048 and B * L <= 256).
+ * Requests whose penalty table alone does not fit are rejected with
+ * MABA_ERR_UNSUPPORTED.  When the table fits but region 2 or 3 does not, the
+ * call runs the unpruned scan or the unsplit decode scan instead: the indices
+ * are the same, but such near-limit shapes can be much slower than
+ * maba_index_topk with a workspace.  Each call rewrites every region it reads
+ * before reading it, so nothing needs clearing between calls; calls that
+ * overlap on the GPU (different streams, or different host threads) race on
+ * all three regions and must be serialised by the caller.
+ * The first call on a device looks the array's device address up (once per
+ * device, with that device current) and keeps it for the life of the
+ * process: make that first call before any stream capture, and do not use
+ * this entry point across a device reset (cudaDeviceReset, or a primary-
+ * context reset by the host framework), after which the kept address is
+ * stale.  Allocates nothing. */
 #define MABA_NOALLOC_PENALTY_MAX 65536
 MABA_API int maba_index_topk_noalloc(const maba_tensor* q_idx, const maba_tensor* centroids,
                                      float lambda_dist, int32_t top_k, int32_t block_size, int32_t decode,

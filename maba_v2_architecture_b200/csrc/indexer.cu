@@ -963,8 +963,12 @@ extern "C" size_t maba_index_topk_at_workspace_size(int64_t B, int64_t L, int64_
 }
 
 // ---------------------------------------------------------------------------
-// Workspace-free variant (maba_index_topk_noalloc): the penalty table lives in
-// a fixed file-scope device array instead of caller memory.
+// Workspace-free variant (maba_index_topk_noalloc): the scratch of
+// index_topk_impl -- the penalty table, then either the pruned scan's centroid
+// norm tables or the split decode scan's partial lists, each only when it fits
+// behind the table -- lives in a fixed file-scope device array instead of
+// caller memory.  The array's device address is looked up once per device and
+// kept for the life of the process (not valid across a device reset).
 // ---------------------------------------------------------------------------
 #include <mutex>
 

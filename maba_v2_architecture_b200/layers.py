@@ -321,13 +321,24 @@ class MabaSparseAttention(nn.Module):
         q = self.q_proj(x).view(b, l, self.n_heads, self.d_head)
         qhat = absorb_queries(q, self.k_up_proj.weight, self.n_heads, self.scale)
         hca = b200_hca_pool(c_full, self.hca_pool_size) if c_full.shape[1] >= self.hca_pool_size else None
-        return b200_sa_attention(qhat, c_full, hca, top_idx, self.stream_gate(x), window_size=self.window_size,
-                                 n_sinks=self.n_sink_tokens, block_size=self.block_size, hca_r=self.hca_pool_size)
+        gate = self.stream_gate(x)
+        keep = None
+        if self.ablation_mode == "no_hca":
+            # The reference zeroes the HCA stream and keeps the 3-way gate
+            # (sparse_attention.py:268-271): g0*o_loc + g1*o_sp = (1 - g2) * (g0'*o_loc + g1'*o_sp),
+            # g' the softmax of the first two logits, so the fused kernel runs with the HCA
+            # logit at -inf and the result is scaled by 1 - g2.
+            keep = 1.0 - torch.softmax(gate.float(), dim=-1)[..., 2]
+            gate = gate.clone()
+            gate[..., 2] = float("-inf")
+        o = b200_sa_attention(qhat, c_full, hca, top_idx, gate, window_size=self.window_size,
+                              n_sinks=self.n_sink_tokens, block_size=self.block_size, hca_r=self.hca_pool_size)
+        if keep is not None:
+            o = (o.float() * keep.view(b, l, 1, 1)).to(o.dtype)
+        return o
 
     def forward(self, x: torch.Tensor, past_c_kv: Optional[torch.Tensor] = None,
                 past_centroids: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
-        if self.ablation_mode == "no_hca":
-            raise NotImplementedError("ablation_mode='no_hca' is not part of the fused MABA-SA kernel")
         b, l, _ = x.shape
         ck = self.indexer._cached_k_idx
         if past_c_kv is None or (ck is not None and ck.shape[1] != past_c_kv.shape[1]):

@@ -16,10 +16,12 @@ Two layouts:
     output pass from it;
   - MABA-SA: a query may attend any earlier token (sparse blocks anywhere in the
     prefix, HCA over all complete blocks, the window and sinks), so the ranks
-    all-gather the latent rows, the block centroids and the pooled HCA rows
-    (d_c=128 / d_idx=64 per token or block); each rank then scores and attends
-    its own queries at their absolute positions (``q_pos0``; the attention's
-    queries sit at the end of the gathered prefix).
+    exchange the latent rows, the block centroids and the pooled HCA rows
+    (d_c=128 / d_idx=64 per token or block) as a prefix exchange -- rank j sends
+    its rows to the later ranks only, into their preallocated whole-sequence
+    tables; each rank then scores and attends its own queries at their
+    absolute positions (``q_pos0``; the attention's queries sit at the end of
+    the received prefix).
 
 Each layout is written as local phases around one exchange so the same code
 runs with NCCL (one process per GPU), with gloo on CPU (tests inject a CPU
@@ -78,18 +80,6 @@ def _gather(t: torch.Tensor, group) -> List[torch.Tensor]:
     out = [torch.empty_like(t) for _ in range(world)]
     dist.all_gather(out, t.contiguous(), group=group)
     return out
-
-
-def _gather_rows(t: torch.Tensor, group) -> List[torch.Tensor]:
-    """All-gather of [B, n_r, d] tensors whose n_r differ between ranks (padded to the
-    largest, then cut back)."""
-    n = torch.tensor([t.shape[1]], dtype=torch.int64, device=t.device)
-    ns = [int(x.item()) for x in _gather(n, group)]
-    m = max(ns)
-    if t.shape[1] < m:
-        pad = torch.zeros(t.shape[0], m - t.shape[1], *t.shape[2:], dtype=t.dtype, device=t.device)
-        t = torch.cat([t, pad], dim=1)
-    return [x[:, :k] for x, k in zip(_gather(t, group), ns)]
 
 
 def balanced_segments(total: int, world: int, unit: int = 64, flat: float = 67.0, slope: float = 1.0 / 4096) -> List[int]:
@@ -200,14 +190,93 @@ def sa_segment_phase_b(qhat_local, q_idx_local, gate_local, c_all: Sequence[torc
     return o, idx
 
 
+def exchange_prefix(bufs: Sequence[torch.Tensor], bounds: Sequence[int], units: Sequence[int], rank: int,
+                    group=None) -> None:
+    """Prefix exchange of per-token tables between the ranks of a sequence split.
+
+    ``bufs[i]`` is a [B, bounds[-1] // units[i], d] table (one row per ``units[i]``
+    tokens) in which this rank's own rows, ``bounds[rank] // u .. bounds[rank+1] // u``,
+    are already in place.  Afterwards rows ``0 .. bounds[rank+1] // u`` hold every earlier
+    rank's rows too: rank j sends its rows to every later rank only (point-to-point, one
+    batch), since no query attends a later segment.  Rows of later ranks are left as they
+    were.  Every rank issues its sends and receives in the same order, so the batch pairs
+    up; the exchange is asynchronous to the host (NCCL runs it on its own stream and the
+    current stream waits for it)."""
+    world = len(bounds) - 1
+    ops = []
+    for buf, u in zip(bufs, units):
+        for bi in range(buf.shape[0]):
+            for j in range(world):
+                if j == rank:
+                    continue
+                seg = j if j < rank else rank      # rows received from j, or this rank's rows sent to j
+                lo, hi = bounds[seg] // u, bounds[seg + 1] // u
+                if hi > lo:
+                    ops.append(dist.P2POp(dist.irecv if j < rank else dist.isend, buf[bi, lo:hi], j, group))
+    if ops:
+        for req in dist.batch_isend_irecv(ops):
+            req.wait()
+
+
+def sa_segment_tables(c_buf: torch.Tensor, cent_buf: torch.Tensor, hca_buf: torch.Tensor, k_idx_local: torch.Tensor,
+                      start: int, p: SAParams, backend=None) -> None:
+    """Local: this rank's block centroids and pooled HCA rows, written into their rows of the
+    whole-sequence tables (its latent rows are already in ``c_buf[:, start:start+Ls]``)."""
+    backend = backend or B200Backend()
+    Ls = k_idx_local.shape[1]
+    nb0, nb = start // p.block, Ls // p.block
+    nh0, nh = start // p.hca_r, Ls // p.hca_r
+    cent_buf[:, nb0:nb0 + nb] = backend.compute_centroids(k_idx_local, p.block)
+    if nh:
+        hca_buf[:, nh0:nh0 + nh] = backend.hca_pool(c_buf[:, start:start + Ls], p.hca_r)
+
+
+def sa_segment_attention(qhat_local, q_idx_local, gate_local, c_buf, cent_buf, hca_buf, start: int, p: SAParams,
+                         backend=None):
+    """Local: indexer + three-stream attention of this segment's queries (absolute positions
+    start .. start+Ls-1) over the prefix rows of the whole-sequence tables.  The centroid table
+    keeps its full length: future blocks score -inf whatever their rows hold, and the table's
+    length sets min(top_k, nb) and the filler indices, which then match the single-GPU indexer.
+    Filler blocks past the prefix are dropped by the attention; every token they name lies after
+    the query, which the reference's causal mask removes as well
+    (maba_sparse/layers/sparse_attention.py:117-164)."""
+    backend = backend or B200Backend()
+    end = start + qhat_local.shape[1]
+    idx = backend.index_topk_at(q_idx_local, cent_buf, p.lam, p.top_k, p.block, start)
+    nh = end // p.hca_r
+    o = backend.sa_attention(qhat_local, c_buf[:, :end], hca_buf[:, :nh] if nh else None, idx, gate_local,
+                             p.window, p.sinks, p.block, p.hca_r)
+    return o, idx
+
+
+def segment_bounds(Ls: int, group=None) -> List[int]:
+    """Segment boundaries from every rank's segment length (one small all-gather)."""
+    n = torch.tensor([Ls], dtype=torch.int64, device="cuda" if dist.get_backend(group) == "nccl" else "cpu")
+    sizes = [int(x.item()) for x in _gather(n, group)]
+    bounds = [0]
+    for k in sizes:
+        bounds.append(bounds[-1] + k)
+    return bounds
+
+
 def sp_sa_prefill(qhat_local, c_local, q_idx_local, k_idx_local, gate_local, p: SAParams, group=None,
-                  backend=None):
+                  backend=None, bounds: Optional[Sequence[int]] = None):
     """Sequence-split DG-Indexer + MABA-SA prefill of this rank's segment (contiguous
-    segments in rank order; their lengths may differ, e.g. ``balanced_segments``)."""
-    Ls = c_local.shape[1]
+    segments in rank order; their lengths may differ, e.g. ``balanced_segments``; pass
+    ``bounds`` when they are known to skip the size exchange).  Rank r receives only the
+    latent rows, centroids and pooled rows of ranks < r."""
+    B, Ls, dc = c_local.shape
     if Ls % p.block or Ls % p.hca_r:
         raise ValueError(f"segment length {Ls} must be a multiple of block {p.block} and r {p.hca_r}")
     rank = dist.get_rank(group)
-    c, cent, hca = sa_segment_phase_a(c_local, k_idx_local, p, backend)
-    return sa_segment_phase_b(qhat_local, q_idx_local, gate_local, _gather_rows(c, group),
-                              _gather_rows(cent, group), _gather_rows(hca, group), rank, p, backend)
+    if bounds is None:
+        bounds = segment_bounds(Ls, group)
+    total, start = bounds[-1], bounds[rank]
+    c_buf = torch.empty(B, total, dc, dtype=c_local.dtype, device=c_local.device)
+    cent_buf = torch.zeros(B, total // p.block, k_idx_local.shape[2], dtype=k_idx_local.dtype,
+                           device=k_idx_local.device)
+    hca_buf = torch.empty(B, total // p.hca_r, dc, dtype=c_local.dtype, device=c_local.device)
+    c_buf[:, start:start + Ls] = c_local
+    sa_segment_tables(c_buf, cent_buf, hca_buf, k_idx_local, start, p, backend)
+    exchange_prefix([c_buf, cent_buf, hca_buf], bounds, [1, p.block, p.hca_r], rank, group)
+    return sa_segment_attention(qhat_local, q_idx_local, gate_local, c_buf, cent_buf, hca_buf, start, p, backend)
