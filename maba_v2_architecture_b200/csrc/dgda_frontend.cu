@@ -1,0 +1,348 @@
+// DGDA front end: everything the DGDA layer computes between its projections and
+// the recurrence, in one pass over the projected features.
+//
+// Reference (maba_sparse/layers/dgda.py): the causal depthwise conv (kernel
+// K = 4) with history and SiLU on q, k and v (_apply_conv :103-122, called at
+// :186-190 and :254-258), the gates b = sigmoid(gate_erase x), w = sigmoid(
+// gate_write x), log alpha = max(-softplus(gate_alpha x), -14) (:192-197,
+// :260-264), and the per-head L2 normalisation k / (||k|| + eps) (:207, :270).
+//
+// Layout: every operand is a [B, L, C] view (any strides; C = H * d), the six
+// projected inputs typically being column ranges of one fused projection
+// output.  One thread owns 8 consecutive channels of one section and a run of
+// RUN consecutive tokens: it keeps the last K-1 conv inputs in registers, so
+// each input row is read once; threads of one token run cover all six sections
+// in channel order, so a warp's loads of a row are contiguous.  The head norm
+// of k is a shuffle reduction over the d/8 lanes of a head (d/8 a power of two
+// <= 32, so a head never straddles a warp).
+#include "common.cuh"
+
+namespace maba {
+namespace {
+
+constexpr int kVec = 8;       // channels per thread
+constexpr int kRun = 8;       // tokens per thread
+constexpr int kMaxTaps = 8;   // conv kernel size limit
+constexpr int kFeThreads = 256;
+
+struct FeSection {
+    const void* x;            // projected input [B, L, C]
+    void* out;                // feature output [B, L, C]
+    int64_t sx[3], so[3];
+};
+
+struct FeArgs {
+    FeSection sec[6];         // q, k, v, alpha, erase (b), write (w)
+    const void* conv[3];      // [C, K] taps of q, k, v
+    int64_t sconv[3][2];
+    const void* hist[3];      // [B, C, K-1] conv inputs before token 0 (nullptr: zeros)
+    int64_t sh[3][3];
+    int64_t B, L;
+    int C[6];                 // channels per section (q, k, alpha, erase: H*dk; v, write: H*dv)
+    int groups[6];            // C / 8
+    int gbase[7];             // prefix sums of groups: thread index of each section inside a token run
+    int per_run;              // threads per token run: gbase[6] rounded up to a warp
+    int K;                    // conv taps
+    int hw;                   // lanes per head of the k section (dk / 8)
+    float eps;
+    int hist_f32;             // history stored as float32 (else the feature dtype)
+};
+
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, int64_t stride, float* v) {
+#pragma unroll
+    for (int i = 0; i < kVec; ++i) v[i] = Cvt<T>::to_f(p[i * stride]);
+}
+
+template <>
+__device__ __forceinline__ void load8<__nv_bfloat16>(const __nv_bfloat16* p, int64_t stride, float* v) {
+    if (stride == 1 && (reinterpret_cast<uintptr_t>(p) & 15u) == 0) {
+        const uint4 u = *reinterpret_cast<const uint4*>(p);
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 f = __bfloat1622float2(h[i]);
+            v[2 * i] = f.x;
+            v[2 * i + 1] = f.y;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < kVec; ++i) v[i] = __bfloat162float(p[i * stride]);
+    }
+}
+
+template <typename T>
+__device__ __forceinline__ void store8(T* p, int64_t stride, const float* v) {
+#pragma unroll
+    for (int i = 0; i < kVec; ++i) p[i * stride] = Cvt<T>::from_f(v[i]);
+}
+
+template <>
+__device__ __forceinline__ void store8<__nv_bfloat16>(__nv_bfloat16* p, int64_t stride, const float* v) {
+    if (stride == 1 && (reinterpret_cast<uintptr_t>(p) & 15u) == 0) {
+        uint4 u;
+        __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+        *reinterpret_cast<uint4*>(p) = u;
+    } else {
+#pragma unroll
+        for (int i = 0; i < kVec; ++i) p[i * stride] = __float2bfloat16_rn(v[i]);
+    }
+}
+
+__device__ __forceinline__ float silu_f(float x) { return x / (1.f + expf(-x)); }
+__device__ __forceinline__ float sigmoid_f(float x) { return 1.f / (1.f + expf(-x)); }
+// -softplus(x) clamped at -14; softplus(x) = x above 20 (torch's threshold), log1p(e^x) below
+__device__ __forceinline__ float neg_softplus_clamped(float x) {
+    const float sp = x > 20.f ? x : log1pf(expf(x));
+    return fmaxf(-sp, -14.f);
+}
+
+template <typename T, int K>
+__global__ void __launch_bounds__(kFeThreads) dgda_frontend_kernel(FeArgs a, int64_t nruns) {
+    const int per_run = a.per_run;
+    const int64_t gid = (int64_t)blockIdx.x * kFeThreads + threadIdx.x;
+    const int64_t total = a.B * nruns * per_run;
+    const int64_t gg = gid < total ? gid : 0;
+    const int slot = (int)(gg % per_run);
+    const bool live = gid < total && slot < a.gbase[6];
+    const int64_t run = (gg / per_run) % nruns;
+    const int64_t b = gg / ((int64_t)per_run * nruns);
+    int s = 0;
+#pragma unroll
+    for (int i = 1; i < 6; ++i) s += slot >= a.gbase[i] ? 1 : 0;
+    const int g = slot - a.gbase[s];
+    const int c0 = g * kVec;
+    const FeSection& sec = a.sec[s];
+    const T* x = static_cast<const T*>(sec.x) + b * sec.sx[0] + (int64_t)c0 * sec.sx[2];
+    T* out = static_cast<T*>(sec.out) + b * sec.so[0] + (int64_t)c0 * sec.so[2];
+    const int64_t t0 = run * kRun;
+    const bool conv = s < 3;
+
+    // conv taps of these 8 channels and the K-1 inputs before t0
+    float w[K][kVec];
+    float win[K][kVec];  // win[j] = input at t0 - (K-1) + j, j < K-1
+    if (conv && live) {
+        const T* cw = static_cast<const T*>(a.conv[s]);
+#pragma unroll
+        for (int j = 0; j < K; ++j)
+#pragma unroll
+            for (int i = 0; i < kVec; ++i)
+                w[j][i] = Cvt<T>::to_f(cw[(int64_t)(c0 + i) * a.sconv[s][0] + j * a.sconv[s][1]]);
+#pragma unroll
+        for (int j = 0; j < K - 1; ++j) {
+            const int64_t t = t0 - (K - 1) + j;
+            if (t >= 0) {
+                load8<T>(x + t * sec.sx[1], sec.sx[2], win[j]);
+            } else if (a.hist[s] != nullptr) {
+                const int64_t hj = (K - 1) + t;  // column of the history (oldest first)
+                const int64_t base = b * a.sh[s][0] + hj * a.sh[s][2];
+#pragma unroll
+                for (int i = 0; i < kVec; ++i) {
+                    const int64_t off = base + (int64_t)(c0 + i) * a.sh[s][1];
+                    win[j][i] = a.hist_f32 ? static_cast<const float*>(a.hist[s])[off]
+                                           : Cvt<T>::to_f(static_cast<const T*>(a.hist[s])[off]);
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < kVec; ++i) win[j][i] = 0.f;
+            }
+        }
+    }
+#pragma unroll 1
+    for (int r = 0; r < kRun; ++r) {
+        const int64_t t = t0 + r;
+        const bool ok = live && t < a.L;
+        float v[kVec];
+        if (ok) load8<T>(x + t * sec.sx[1], sec.sx[2], v);
+        float y[kVec];
+        if (conv) {
+#pragma unroll
+            for (int i = 0; i < kVec; ++i) {
+                float acc = 0.f;
+#pragma unroll
+                for (int j = 0; j < K - 1; ++j) acc = fmaf(w[j][i], win[j][i], acc);
+                acc = fmaf(w[K - 1][i], ok ? v[i] : 0.f, acc);
+                y[i] = silu_f(acc);
+            }
+#pragma unroll
+            for (int j = 0; j + 1 < K - 1; ++j)
+#pragma unroll
+                for (int i = 0; i < kVec; ++i) win[j][i] = win[j + 1][i];
+            if constexpr (K > 1)
+#pragma unroll
+                for (int i = 0; i < kVec; ++i) win[K - 2][i] = ok ? v[i] : 0.f;
+        } else if (s == 3) {
+#pragma unroll
+            for (int i = 0; i < kVec; ++i) y[i] = ok ? neg_softplus_clamped(v[i]) : 0.f;
+        } else {
+#pragma unroll
+            for (int i = 0; i < kVec; ++i) y[i] = ok ? sigmoid_f(v[i]) : 0.f;
+        }
+        // per-head L2 norm of k: every lane takes part in the shuffles
+        float ss = 0.f;
+#pragma unroll
+        for (int i = 0; i < kVec; ++i) ss = fmaf(y[i], y[i], ss);
+        for (int o = a.hw >> 1; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (s == 1) {
+            const float inv = 1.f / (sqrtf(ss) + a.eps);
+#pragma unroll
+            for (int i = 0; i < kVec; ++i) y[i] *= inv;
+        }
+        if (ok) store8<T>(out + t * sec.so[1], sec.so[2], y);
+    }
+}
+
+// new conv history [B, C, K-1]: the last K-1 inputs of [history | x]
+template <typename T, typename TH>
+__global__ void dgda_frontend_hist_kernel(FeArgs a, void* nq, void* nk, void* nv, int64_t snh0, int64_t snh1,
+                                          int64_t snh2, int64_t snh3, int64_t snh4, int64_t snh5, int64_t snh6,
+                                          int64_t snh7, int64_t snh8) {
+    const int64_t sn[3][3] = {{snh0, snh1, snh2}, {snh3, snh4, snh5}, {snh6, snh7, snh8}};
+    void* dst[3] = {nq, nk, nv};
+    const int K1 = a.K - 1;
+    const int64_t per_b = (int64_t)(a.C[0] + a.C[1] + a.C[2]) * K1;
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= a.B * per_b) return;
+    const int64_t b = i / per_b;
+    int64_t rem = i % per_b;
+    int s = 0;
+    while (s < 2 && rem >= (int64_t)a.C[s] * K1) { rem -= (int64_t)a.C[s] * K1; ++s; }
+    if (dst[s] == nullptr) return;
+    const int64_t c = rem / K1;
+    const int j = (int)(rem % K1);
+    const int64_t t = a.L - K1 + j;  // time index of history column j
+    float v = 0.f;
+    if (t >= 0) {
+        const FeSection& sec = a.sec[s];
+        v = Cvt<T>::to_f(static_cast<const T*>(sec.x)[b * sec.sx[0] + t * sec.sx[1] + c * sec.sx[2]]);
+    } else if (a.hist[s] != nullptr) {
+        const int64_t off = b * a.sh[s][0] + c * a.sh[s][1] + (K1 + t) * a.sh[s][2];
+        v = a.hist_f32 ? static_cast<const float*>(a.hist[s])[off] : Cvt<T>::to_f(static_cast<const T*>(a.hist[s])[off]);
+    }
+    static_cast<TH*>(dst[s])[b * sn[s][0] + c * sn[s][1] + j * sn[s][2]] = Cvt<TH>::from_f(v);
+}
+
+}  // namespace
+}  // namespace maba
+
+using namespace maba;
+
+extern "C" int maba_dgda_frontend(const maba_tensor* proj, const maba_tensor* conv_w, const maba_tensor* hist,
+                                  const maba_tensor* out, const maba_tensor* new_hist, int32_t n_heads, float eps,
+                                  void* stream) {
+    if (proj == nullptr || conv_w == nullptr || out == nullptr)
+        return set_error(MABA_ERR_INVALID, "dgda_frontend: proj[6], conv_w[3] and out[6] are required");
+    if (n_heads <= 0) return set_error(MABA_ERR_INVALID, "dgda_frontend: n_heads must be positive");
+    for (int s = 0; s < 6; ++s)
+        if (!present(&proj[s]) || proj[s].ndim != 3)
+            return set_error(MABA_ERR_INVALID, "dgda_frontend: proj[%d] must be [B, L, C]", s);
+    const int dt = proj[0].dtype;
+    if (dt != MABA_F32 && dt != MABA_BF16 && dt != MABA_F16)
+        return set_error(MABA_ERR_DTYPE, "dgda_frontend: float32 / float16 / bfloat16 features only");
+    const int64_t B = proj[0].shape[0], L = proj[0].shape[1];
+    FeArgs a{};
+    a.B = B; a.L = L; a.eps = eps;
+    for (int s = 0; s < 6; ++s) {
+        const int64_t C = proj[s].shape[2];
+        const int64_t sp[3] = {B, L, C};
+        MABA_TRY(expect_shape(&proj[s], "dgda_frontend: proj", 3, sp));
+        MABA_TRY(expect_dtype(&proj[s], "dgda_frontend: proj", dt));
+        MABA_TRY(expect_shape(&out[s], "dgda_frontend: out", 3, sp));
+        MABA_TRY(expect_dtype(&out[s], "dgda_frontend: out", dt));
+        if (C <= 0 || C % kVec != 0 || C % n_heads != 0)
+            return set_error(MABA_ERR_UNSUPPORTED, "dgda_frontend: channels (%lld) must be a multiple of 8 and of the "
+                             "head count", (long long)C);
+        a.C[s] = (int)C;
+        a.groups[s] = (int)(C / kVec);
+        a.sec[s].x = proj[s].data; a.sec[s].out = out[s].data;
+        for (int i = 0; i < 3; ++i) { a.sec[s].sx[i] = proj[s].stride[i]; a.sec[s].so[i] = out[s].stride[i]; }
+    }
+    // q, k, alpha, erase share H*dk channels; v and write share H*dv
+    if (a.C[1] != a.C[0] || a.C[3] != a.C[0] || a.C[4] != a.C[0] || a.C[5] != a.C[2])
+        return set_error(MABA_ERR_INVALID, "dgda_frontend: q/k/alpha/erase and v/write channel counts must agree");
+    const int dk = a.C[1] / n_heads;
+    a.hw = dk / kVec;
+    if (dk % kVec != 0 || a.hw > 32 || (a.hw & (a.hw - 1)) != 0)
+        return set_error(MABA_ERR_UNSUPPORTED, "dgda_frontend: dk = %d must be 8 x a power of two <= 256", dk);
+    a.gbase[0] = 0;
+    for (int s = 0; s < 6; ++s) a.gbase[s + 1] = a.gbase[s] + a.groups[s];
+    // whole warps per token run: a head's lanes of the k section then never straddle a warp
+    a.per_run = (a.gbase[6] + 31) / 32 * 32;
+    int K = -1;
+    for (int s = 0; s < 3; ++s) {
+        if (!present(&conv_w[s]) || conv_w[s].ndim != 2 || conv_w[s].shape[0] != a.C[s])
+            return set_error(MABA_ERR_INVALID, "dgda_frontend: conv_w[%d] must be [C, K]", s);
+        MABA_TRY(expect_dtype(&conv_w[s], "dgda_frontend: conv_w", dt));
+        if (K < 0) K = (int)conv_w[s].shape[1];
+        if (conv_w[s].shape[1] != K) return set_error(MABA_ERR_INVALID, "dgda_frontend: conv kernel sizes differ");
+        a.conv[s] = conv_w[s].data;
+        a.sconv[s][0] = conv_w[s].stride[0]; a.sconv[s][1] = conv_w[s].stride[1];
+    }
+    if (K < 1 || K > kMaxTaps) return set_error(MABA_ERR_UNSUPPORTED, "dgda_frontend: conv kernel size 1..%d", kMaxTaps);
+    a.K = K;
+    int hdt = -1;
+    for (int s = 0; s < 3; ++s) {
+        const maba_tensor* hs[2] = {hist != nullptr ? &hist[s] : nullptr, new_hist != nullptr ? &new_hist[s] : nullptr};
+        for (const maba_tensor* h : hs) {
+            if (!present(h)) continue;
+            const int64_t sh[3] = {B, a.C[s], K - 1};
+            MABA_TRY(expect_shape(h, "dgda_frontend: conv history", 3, sh));
+            if (h->dtype != dt && h->dtype != MABA_F32)
+                return set_error(MABA_ERR_DTYPE, "dgda_frontend: conv history must be float32 or the feature dtype");
+            if (hdt < 0) hdt = h->dtype;
+            if (h->dtype != hdt) return set_error(MABA_ERR_DTYPE, "dgda_frontend: conv histories differ in dtype");
+        }
+        a.hist[s] = (hist != nullptr && present(&hist[s])) ? hist[s].data : nullptr;
+        for (int i = 0; i < 3; ++i) a.sh[s][i] = a.hist[s] ? hist[s].stride[i] : 0;
+    }
+    a.hist_f32 = (hdt == MABA_F32 && dt != MABA_F32) ? 1 : 0;
+    if (B == 0 || L == 0) return MABA_OK;
+    cudaStream_t st = as_stream(stream);
+    const int64_t nruns = ceil_div(L, kRun);
+    const int64_t threads = B * nruns * a.per_run;
+    const unsigned grid = (unsigned)ceil_div(threads, kFeThreads);
+    MABA_TRY(MABA_DISPATCH_FLOAT(dt, "dgda_frontend", [&] {
+        if constexpr (sizeof(T) == 8) {
+            return set_error(MABA_ERR_DTYPE, "dgda_frontend: float64");
+        } else {
+            switch (K) {
+                case 1: dgda_frontend_kernel<T, 1><<<grid, kFeThreads, 0, st>>>(a, nruns); break;
+                case 2: dgda_frontend_kernel<T, 2><<<grid, kFeThreads, 0, st>>>(a, nruns); break;
+                case 3: dgda_frontend_kernel<T, 3><<<grid, kFeThreads, 0, st>>>(a, nruns); break;
+                case 4: dgda_frontend_kernel<T, 4><<<grid, kFeThreads, 0, st>>>(a, nruns); break;
+                case 5: dgda_frontend_kernel<T, 5><<<grid, kFeThreads, 0, st>>>(a, nruns); break;
+                case 6: dgda_frontend_kernel<T, 6><<<grid, kFeThreads, 0, st>>>(a, nruns); break;
+                case 7: dgda_frontend_kernel<T, 7><<<grid, kFeThreads, 0, st>>>(a, nruns); break;
+                default: dgda_frontend_kernel<T, 8><<<grid, kFeThreads, 0, st>>>(a, nruns); break;
+            }
+            return check_launch("dgda_frontend");
+        }
+    }));
+    if (new_hist == nullptr || K == 1) return MABA_OK;
+    void* nh[3];
+    int64_t sn[9] = {0};
+    bool any = false;
+    for (int s = 0; s < 3; ++s) {
+        nh[s] = present(&new_hist[s]) ? new_hist[s].data : nullptr;
+        any = any || nh[s] != nullptr;
+        for (int i = 0; i < 3; ++i) sn[3 * s + i] = nh[s] ? new_hist[s].stride[i] : 0;
+    }
+    if (!any) return MABA_OK;
+    const int64_t n = B * (int64_t)(a.C[0] + a.C[1] + a.C[2]) * (K - 1);
+    const bool f32h = hdt == MABA_F32;
+    return MABA_DISPATCH_FLOAT(dt, "dgda_frontend(history)", [&] {
+        if constexpr (sizeof(T) == 8) {
+            return set_error(MABA_ERR_DTYPE, "dgda_frontend: float64");
+        } else {
+            if (f32h)
+                dgda_frontend_hist_kernel<T, float><<<(unsigned)ceil_div(n, 256), 256, 0, st>>>(
+                    a, nh[0], nh[1], nh[2], sn[0], sn[1], sn[2], sn[3], sn[4], sn[5], sn[6], sn[7], sn[8]);
+            else
+                dgda_frontend_hist_kernel<T, T><<<(unsigned)ceil_div(n, 256), 256, 0, st>>>(
+                    a, nh[0], nh[1], nh[2], sn[0], sn[1], sn[2], sn[3], sn[4], sn[5], sn[6], sn[7], sn[8]);
+            return check_launch("dgda_frontend(history)");
+        }
+    });
+}

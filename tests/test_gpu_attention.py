@@ -199,3 +199,24 @@ def test_bounded_wait_runs_out_and_reports():
     assert N.device_error() == 0
     x = torch.ones(4, device=DEV)
     assert float((x * 2).sum()) == 8.0  # the context still works
+
+
+@pytest.mark.parametrize("dt,rtol", [(torch.float32, RTOL_FP32), (torch.bfloat16, RTOL_BF16)])
+def test_no_hca_ablation_vs_oracle(dt, rtol):
+    """ablation_mode='no_hca' zeroes the HCA stream and keeps the three-way gate
+    (maba_sparse/layers/sparse_attention.py:268-271): g0*o_local + g1*o_sparse."""
+    cfg = MabaSparseConfig(dim=64, n_heads=2, d_head=32, window_size=48, block_size=16, top_k=4, hca_pool_size=16,
+                           dist_lambda=0.3)
+    layer = init_module_(MabaSparseAttention(cfg, ablation_mode="no_hca"), seed=41).eval().to(DEV, dt)
+    x = torch.randn(1, 150, 64, generator=torch.Generator().manual_seed(42)).to(DEV, dt)
+    with torch.no_grad():
+        c = layer.kv_down_proj(x)
+        idx, _ = layer.indexer(x)
+        q = layer.q_proj(x).view(1, 150, 2, 32)
+        qhat = mb.ops.absorb_queries(q, layer.k_up_proj.weight, 2, layer.scale)
+        out = layer.latent_attention(x, c, idx)
+        gate = layer.stream_gate(x)
+    st = OA.sa_streams(qhat.float().cpu().numpy(), c.float().cpu().numpy(), idx.cpu().numpy(), 48, 4, 16, 16)
+    g = OA.gate_softmax(gate.float().cpu().numpy())[:, :, None, :]
+    ref = g[..., 0:1] * st[0] + g[..., 1:2] * st[1]
+    assert_rel(out, ref, rtol, "no_hca latent output")
