@@ -232,92 +232,126 @@ def attention_units(idx, L):
     return int(n_loc.sum()), int(n_sp.sum()), int(n_hca.sum())
 
 
-def config3_prefill(dev, steps: int = 3, warmup: int = 1):
-    """Config 3: the 101M model (random N(0,0.02) weights, seed 2), bf16, forward over
-    B=8 x T=8,192 uniform ids; prefill tokens/s."""
+def _reference_model_101m(sd16, n_layers=None):
+    """The unmodified reference model (baseline/_ref) on its CPU path, float32, with the given
+    (bf16-rounded) weights; None where no reference install exists."""
+    try:
+        import_reference()
+        from maba_sparse.model import MabaSparseForCausalLM, get_101m_config as ref_cfg
+    except Exception:  # noqa: BLE001
+        return None
+    cfg = ref_cfg()
+    if n_layers is not None:
+        cfg.n_layers = cfg.num_layers = n_layers
+    m = MabaSparseForCausalLM(cfg).eval()
+    m.load_state_dict(sd16)
+    return m
+
+
+def config3_prefill(dev, steps: int = 3, warmup: int = 1, check_tokens: int = 256):
+    """Config 3: the 101M model (random N(0,0.02) weights, seed 2) on the engine, bf16, forward
+    over B=8 x T=8,192 uniform ids; prefill tokens/s.  Parity: the logits of the first
+    `check_tokens` positions of sequence 0 against the unmodified reference model on the CPU
+    (float32 with the same bf16-rounded weights; a causal model, so the prefix is exact)."""
     import torch
 
     from maba_v2_architecture_b200.config import get_101m_config
-    from maba_v2_architecture_b200.model import MabaSparseForCausalLM
-    from maba_v2_architecture_b200.workloads import init_module_
+    from maba_v2_architecture_b200.engine import MabaEngine, ModelShape, init_state_dict
 
-    model = init_module_(MabaSparseForCausalLM(get_101m_config()), seed=2).to(dev, torch.bfloat16).eval()
-    model.set_state_dtype(torch.float32)
+    cfg = get_101m_config()
+    sd = {k: v.to(torch.bfloat16) for k, v in init_state_dict(ModelShape.from_config(cfg), seed=2).items()}
+    eng = MabaEngine(cfg, sd, device=dev, dtype=torch.bfloat16)
     ids = torch.randint(0, 32768, (8, 8192), generator=torch.Generator().manual_seed(2)).to(dev)
-    with torch.no_grad():
-        out = None
-        for _ in range(warmup):
-            out = model(ids)  # outputs kept alive as in the timed loop
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(steps):
-            out = model(ids)
-        e1.record()
-        torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / steps
-    finite = bool(torch.isfinite(out.logits[:, -1].float()).all())
-    del model, out
-    torch.cuda.empty_cache()
-    return {"workload": "config3: 101M model (101,282,319 params) bf16, B=8 T=8192, random-init weights",
-            "value": 8 * 8192 / (ms * 1e-3), "unit": "tok/s", "ms_per_step": ms, "steps": steps,
-            "logits_finite": finite}
-
-
-def config4_decode(dev, ctx: int = 1048576, steps: int = 256, warmup: int = 3):
-    """Config 4: the 101M model (seed 3), bf16 weights and latent cache, fp32 DGDA state;
-    prefill `ctx` uniform ids at B=1 into the decode caches, then `steps` greedy tokens.
-    ms/token over the timed steps and the HBM bytes a step must touch."""
-    import torch
-
-    from maba_v2_architecture_b200.config import get_101m_config
-    from maba_v2_architecture_b200.decode import DecodeSession
-    from maba_v2_architecture_b200.model import MabaSparseForCausalLM
-    from maba_v2_architecture_b200.workloads import init_module_
-
-    model = init_module_(MabaSparseForCausalLM(get_101m_config()), seed=3).to(dev, torch.bfloat16).eval()
-    sess = DecodeSession(model, batch=1, max_len=ctx + steps + 2 * warmup + 16, dtype=torch.bfloat16)
-    ids = torch.randint(0, 32768, (1, ctx), generator=torch.Generator().manual_seed(3)).to(dev)
-    torch.cuda.synchronize()
-    t0 = time.time()
-    logits = sess.prefill(ids)
-    torch.cuda.synchronize()
-    prefill_s = time.time() - t0
-    del ids
-    tok = logits[:, -1].argmax(-1, keepdim=True)
-    # eager steps (one host call per op) for reference, then the captured CUDA-graph step
+    out = None
     for _ in range(warmup):
-        tok = sess.step(tok)[:, -1].argmax(-1, keepdim=True)
+        out = eng.forward(ids)  # outputs kept alive as in the timed loop
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for _ in range(8):
-        tok = sess.step(tok)[:, -1].argmax(-1, keepdim=True)
+    for _ in range(steps):
+        out = eng.forward(ids)
     e1.record()
     torch.cuda.synchronize()
-    eager_ms = e0.elapsed_time(e1) / 8
-    sess.capture(tok)
+    ms = e0.elapsed_time(e1) / steps
+    res = {"workload": "config3: 101M model (101,282,319 params) bf16, B=8 T=8192, random-init weights, "
+                       "MabaEngine prefill (all logits)",
+           "value": 8 * 8192 / (ms * 1e-3), "unit": "tok/s", "ms_per_step": ms, "steps": steps,
+           "logits_finite": bool(torch.isfinite(out[:, -1].float()).all())}
+    ref = _reference_model_101m({k: v.float() for k, v in sd.items()})
+    if ref is not None:
+        with torch.no_grad():
+            want = ref(ids[:1, :check_tokens].cpu()).logits.double()
+        got = out[:1, :check_tokens].double().cpu()
+        res["parity"] = {"vs": "unmodified reference model, CPU float32, same bf16-rounded weights",
+                         "positions": check_tokens, "max_rel": float((got - want).abs().max() / want.abs().max()),
+                         "argmax_agree": float((got.argmax(-1) == want.argmax(-1)).double().mean()),
+                         "tolerance": 2e-2}
+        res["parity"]["ok"] = res["parity"]["max_rel"] <= 2e-2
+    else:
+        res["parity"] = {"unavailable": "no reference install under baseline/_ref"}
+    del eng, out
+    torch.cuda.empty_cache()
+    return res
+
+
+def config4_decode(dev, ctx: int = 1048576, steps: int = 256, warmup: int = 3, forced: int = 4):
+    """Config 4: the 101M model (seed 3) on the engine, bf16 weights and latent cache, fp32
+    recurrent state; prefill `ctx` uniform ids at B=1 into the decode caches, then decode.
+    Parity: the first `forced` steps are teacher-forced with the next ids of the sequence and
+    their logits compared with one prefill over ctx + forced tokens (its last `forced`
+    positions).  Then `steps` greedy steps of the captured CUDA-graph step are timed:
+    ms/token and the HBM bytes a step must move (session.bytes_per_step) per ms."""
+    import torch
+
+    from maba_v2_architecture_b200.config import get_101m_config
+    from maba_v2_architecture_b200.engine import MabaEngine, ModelShape, init_state_dict
+
+    cfg = get_101m_config()
+    eng = MabaEngine(cfg, init_state_dict(ModelShape.from_config(cfg), seed=3), device=dev, dtype=torch.bfloat16)
+    ids = torch.randint(0, 32768, (1, ctx + forced), generator=torch.Generator().manual_seed(3)).to(dev)
+    sess = eng.new_session(batch=1, max_len=ctx + forced + steps + warmup + 16)
+    torch.cuda.synchronize()
+    t0 = time.time()
+    sess.prefill(ids[:, :ctx])
+    torch.cuda.synchronize()
+    prefill_s = time.time() - t0
+    sess.ids_buf.copy_(ids[:, ctx])
+    sess.capture()
+    got = []
+    for j in range(forced):
+        sess.ids_buf.copy_(ids[:, ctx + j])
+        got.append(sess.replay().clone())
+    want = eng.forward(ids, last_n=forced).float()[0]
+    got = torch.cat(got, 0)
+    rel = float((got - want).abs().max() / want.abs().max())
+    parity = {"vs": f"prefill of {ctx}+{forced} tokens (last {forced} positions)", "steps": forced, "max_rel": rel,
+              "argmax_agree": float((got.argmax(-1) == want.argmax(-1)).double().mean()), "tolerance": 2e-2,
+              "ok": rel <= 2e-2}
+    del want
+    torch.cuda.empty_cache()
+    # greedy decoding from the last forced token's argmax (already in ids_buf)
     for _ in range(warmup):
         sess.replay()
     torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(steps):
         sess.replay()
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / steps
-    L = sess.L
-    nb = L // 64
-    weights = 2 * sum(p.numel() for p in model.parameters())
-    state = 15 * 10 * 64 * 64 * 4 * 2
-    per_sa = (2048 + 132) * 128 * 2 + nb * 128 * 2 + nb * 64 * 2
-    step_bytes = weights + state + 5 * per_sa
-    del sess, model
+    step_bytes = sess.bytes_per_step()
+    res = {"workload": f"config4: 101M model bf16, B=1, prefill {ctx} ids then {steps} greedy steps "
+                       "(MabaEngine, captured CUDA-graph decode step)",
+           "ms_per_token": ms, "context": sess.length, "prefill_s": prefill_s, "hbm_bytes_per_step": step_bytes,
+           "hbm_gbs": step_bytes / (ms * 1e-3) / 1e9, "launches_per_step": sess.launches_per_step(),
+           "teacher_forced_parity": parity}
+    pk = peaks()
+    res["roofline"] = {"bound": "hbm", "achieved": res["hbm_gbs"], "peak": pk["hbm_gbs"], "unit": "GB/s",
+                       "frac": res["hbm_gbs"] / pk["hbm_gbs"], "peak_source": pk["source"]}
+    del sess, eng
     torch.cuda.empty_cache()
-    return {"workload": f"config4: 101M model bf16, B=1, prefill {ctx} ids then {steps} greedy steps "
-                        "(captured CUDA-graph decode step)",
-            "ms_per_token": ms, "eager_ms_per_token": eager_ms, "context": L, "prefill_s": prefill_s,
-            "hbm_bytes_per_step": step_bytes, "hbm_gbs": step_bytes / (ms * 1e-3) / 1e9}
+    return res
 
 
 def run_only(args):

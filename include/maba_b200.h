@@ -125,6 +125,29 @@ MABA_API int maba_dgda_step(const maba_tensor* q, const maba_tensor* k, const ma
                    const maba_tensor* out, const maba_tensor* new_state,
                    void* stream);
 
+/* ---- DGDA front end ------------------------------------------------------
+ * Replaces the feature path of DGDALayer between its projections and the
+ * recurrence (maba_sparse/layers/dgda.py):
+ *   _apply_conv :103-122 (causal depthwise conv with history + SiLU on q, k, v,
+ *   called at :186-190 and :254-258), the gates :192-197 / :260-264
+ *   (b = sigmoid, w = sigmoid, log alpha = max(-softplus, -14)) and the per-head
+ *   k normalisation k / (||k|| + eps) at :207 / :270.
+ * proj[6]: the projected inputs q, k, v, alpha, erase, write, each [B,L,C]
+ *   (C = H*dk for q, k, alpha, erase; H*dv for v, write; any strides);
+ * conv_w[3]: [C, K] taps of q, k, v (Conv1d weight [C,1,K] viewed 2-D);
+ * hist[3] (entries with NULL data = zero history; the pointer itself may be
+ *   NULL): [B, C, K-1] conv inputs before token 0, oldest first (the layer's
+ *   conv_state), float32 or the feature dtype;
+ * out[6]: q, k, v, log_alpha, b, w (the transforms of proj[0..5]), each
+ *   [B,L,C] in the feature dtype;
+ * new_hist[3] (optional, as hist; must not alias hist): the last K-1 inputs of
+ *   [hist | x], the conv_state the layer returns.
+ * Features float32 / float16 / bfloat16; C a multiple of 8; dk / 8 a power of
+ * two <= 32; K <= 8. */
+MABA_API int maba_dgda_frontend(const maba_tensor* proj, const maba_tensor* conv_w, const maba_tensor* hist,
+                                const maba_tensor* out, const maba_tensor* new_hist, int32_t n_heads, float eps,
+                                void* stream);
+
 /* ---- DG-Indexer block pooling ------------------------------------------
  * Replaces `compute_centroids`: dispatcher.py:399, common.py:329-350,
  * cpu_indexer.py:16-50.  k_idx: [B,L,d] -> out: [B,ceil(L/block),d],
@@ -269,6 +292,58 @@ MABA_API int maba_sa_attention_decode_at(const maba_tensor* qhat, const maba_ten
 MABA_API size_t maba_sa_attention_decode_at_workspace_size(int64_t B, int64_t Lcap, int64_t NCcap,
                                                            int64_t H, int64_t d_c, int64_t K, int32_t window,
                                                            int32_t n_sinks, int32_t block_size, int32_t hca_r);
+
+/* ---- Model engine: the block pieces around the hot-path ops --------------
+ * Used by the inference engine that runs whole models (prefill and decode)
+ * from a reference state dict; each replaces torch module code of
+ * maba_sparse/model.py.
+ *
+ * maba_rmsnorm_residual: x [N,D] float32 (updated in place when y is given):
+ *   x += gate * y (gate [D] float32 = sigmoid(res_gate), y [N,D] float32 or
+ *   h's dtype), then h_out = x * rsqrt(mean(x^2) + eps) * weight ([N,D], optional).
+ *   model.py:18-26 (RMSNorm), :107-108 / :126-127 (the gated residual adds). */
+MABA_API int maba_rmsnorm_residual(const maba_tensor* x, const maba_tensor* y, const maba_tensor* gate,
+                                   const maba_tensor* weight, float eps, const maba_tensor* h_out, void* stream);
+
+/* maba_swiglu: u [N, 2I] (gate | up projections) -> out [N, I] = silu(gate) * up;
+ *   model.py:28-37 (SwiGLUFFN). */
+MABA_API int maba_swiglu(const maba_tensor* u, const maba_tensor* out, void* stream);
+
+/* maba_decode_gemv: one decode-step GEMV, out = W h, for B <= 8 rows.
+ *   w: [rows, K] float32 / float16 / bfloat16, contiguous 16-byte-aligned rows, K % 8 == 0.
+ *   prologue 0 (norm):   h = RMSNorm(x) * aux, x [B,K] float32, aux [K] (w's dtype);
+ *            1 (gather): h = aux[ids[b]], aux [V,K] embedding table, ids int64 [B];
+ *            2 (vector): h = x, x [B,K] float32 or w's dtype.
+ *   epilogue 0 (store):    out [B,rows] (float32 or w's dtype) = W h + bias (bias float32 [rows], optional);
+ *            1 (residual): out [B,rows] float32 residual stream += gate * (W h), gate float32 [rows];
+ *            2 (dgda):     out [B,rows] float32 DGDA features from the rows q|k|v|alpha|erase|write:
+ *                          rows [0, n_conv) through the causal conv with taps [n_conv, Kc] and the
+ *                          float32 history hist [B, n_conv, Kc-1] (updated in place) and SiLU,
+ *                          rows [n_conv, alpha_end) -> max(-softplus, -14), the rest -> sigmoid
+ *                          (layers/dgda.py:238-270, the step's feature path);
+ *            3 (swiglu):   rows = 2I (gate rows then up rows), out [B,I] = silu(gate) * up;
+ *            4 (logits):   out float32 [B,rows] logits, ids_out int64 [B] their argmax (ties to
+ *                          the lower index), *pos_dev += 1 when pos_dev is not NULL; needs a
+ *                          workspace of maba_decode_gemv_workspace_size(B) bytes, zeroed before
+ *                          the first call (every call leaves it zeroed).
+ *   The pieces of MabaBlock.step / MabaSparseForCausalLM.step (model.py:111-129, 256-276):
+ *   embedding (FactorizedEmbeddings, :39-50), the norm-fused projections, the gated residual
+ *   adds, SwiGLU, the tied head with greedy selection (:304-305). */
+MABA_API int maba_decode_gemv(const maba_tensor* w, int32_t prologue, const maba_tensor* x,
+                              const maba_tensor* aux, float eps, const maba_tensor* ids, int32_t epilogue,
+                              const maba_tensor* out, const maba_tensor* bias, const maba_tensor* gate,
+                              const maba_tensor* taps, const maba_tensor* hist, int32_t n_conv, int32_t alpha_end,
+                              const maba_tensor* ids_out, int64_t* pos_dev, void* workspace,
+                              size_t workspace_bytes, void* stream);
+MABA_API size_t maba_decode_gemv_workspace_size(int64_t B);
+
+/* maba_decode_dgda_state: the recurrence of one decode step from the features of
+ *   maba_decode_gemv's dgda epilogue: feats float32 [B, 4*H*dk + 2*H*dv] (q|k|v|log
+ *   alpha|b|w, k not yet normalised), state float32 [B,H,dk,dv] contiguous (updated in
+ *   place), o_out float32 [B, H*dv]; k is divided by (||k_h|| + eps) first
+ *   (layers/dgda.py:270), then the step of common.py:271-309.  dk <= 64, dv <= 128. */
+MABA_API int maba_decode_dgda_state(const maba_tensor* feats, const maba_tensor* state, const maba_tensor* o_out,
+                                    int32_t n_heads, float eps, void* stream);
 
 #ifdef __cplusplus
 }

@@ -54,6 +54,13 @@ SIGNATURES = {
     "maba_dgda_prefill_workspace_size": (_sz, [_i32, _i64, _i64, _i64, _i64, _i64]),
     "maba_dgda_step": (ctypes.c_int, [T_P] * 10 + [_vp]),
     "maba_dgda_transition": (ctypes.c_int, [T_P] * 8 + [_vp, _sz, _vp]),
+    "maba_dgda_frontend": (ctypes.c_int, [T_P] * 5 + [_i32, _f32, _vp]),
+    "maba_rmsnorm_residual": (ctypes.c_int, [T_P, T_P, T_P, T_P, _f32, T_P, _vp]),
+    "maba_swiglu": (ctypes.c_int, [T_P, T_P, _vp]),
+    "maba_decode_gemv": (ctypes.c_int, [T_P, _i32, T_P, T_P, _f32, T_P, _i32, T_P, T_P, T_P, T_P, T_P, _i32, _i32,
+                                        T_P, _vp, _vp, _sz, _vp]),
+    "maba_decode_gemv_workspace_size": (_sz, [_i64]),
+    "maba_decode_dgda_state": (ctypes.c_int, [T_P, T_P, T_P, _i32, _f32, _vp]),
     "maba_dgda_transition_workspace_size": (_sz, [_i32, _i64, _i64, _i64]),
     "maba_compute_centroids": (ctypes.c_int, [T_P, T_P, _i32, _vp]),
     "maba_index_topk": (ctypes.c_int, [T_P, T_P, _f32, _i32, _i32, _i32, T_P, T_P, _vp, _sz, _vp]),
@@ -127,6 +134,16 @@ def desc(t: Optional[torch.Tensor]) -> Optional[MabaTensor]:
 
 def ref(d: Optional[MabaTensor]):
     return ctypes.byref(d) if d is not None else None
+
+
+def desc_array(tensors) -> ctypes.Array:
+    """Contiguous array of descriptors (an absent operand has NULL data), for the entry
+    points that take a fixed-length list of tensors."""
+    arr = (MabaTensor * len(tensors))()
+    for i, t in enumerate(tensors):
+        if t is not None:
+            arr[i] = desc(t)
+    return arr
 
 
 def stream_of(t: torch.Tensor) -> int:

@@ -1,0 +1,657 @@
+// Model-level kernels of the inference engine: the parts of a Maba block and of
+// the model head that surround the hot-path ops.
+//
+// Prefill (token-batched, many rows):
+//   maba_rmsnorm_residual -- x += sigmoid(res_gate) * y, then h = RMSNorm(x) * w
+//                            (maba_sparse/model.py:18-26 RMSNorm, :107-108 and
+//                            :126-127 the gated residuals), one warp per row;
+//   maba_swiglu           -- silu(gate) * up of the fused gate|up projection
+//                            (model.py:28-37 SwiGLUFFN).
+// Decode (a handful of rows, weight-streaming GEMVs with fused prologues and
+// epilogues, one launch per step of the block):
+//   maba_decode_gemv      -- out = W h (+ bias), with h = RMSNorm(x) * w, a gathered
+//                            embedding row or a plain vector, and the result
+//                            stored, added to the residual stream with its gate,
+//                            turned into the DGDA features (conv with history +
+//                            SiLU, gates), into SwiGLU products, or into logits
+//                            with their argmax.
+//   maba_decode_dgda_state -- k L2-norm + one recurrence step per (batch, head).
+//
+// A GEMV warp owns R = 2 output rows and streams their weights with 16-byte
+// loads (8 bf16), multiplying each chunk with all NB (<= 8) input vectors held
+// in shared memory; every CTA recomputes the input normalisation (a few KB).
+#include "common.cuh"
+
+namespace maba {
+namespace {
+
+constexpr int kGemvThreads = 256;
+constexpr int kGemvWarps = kGemvThreads / 32;
+constexpr int kRowsPerWarp = 2;
+constexpr int kRowsPerCta = kGemvWarps * kRowsPerWarp;
+
+enum Prologue { PRO_NORM = 0, PRO_GATHER = 1, PRO_VEC = 2 };
+enum Epilogue { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_DGDA = 2, EPI_SWIGLU = 3, EPI_LOGITS = 4 };
+
+struct GemvArgs {
+    const void* w;            // [rows, K] weight (dtype TW), row stride ldw
+    int64_t ldw;
+    int N;                    // outputs (SwiGLU: I, reading gate rows [0,I) and up rows [I,2I))
+    int K;
+    int B;
+    int pro, epi;
+    // prologue
+    const float* x; int64_t ldx;            // PRO_NORM: residual stream [B, K] fp32
+    const void* norm_w; float eps;           // PRO_NORM: RMSNorm weight [K] (TW)
+    const int64_t* ids; const void* emb; int64_t lde;  // PRO_GATHER: emb[ids[b]] rows (TW)
+    const void* vec; int64_t ldv; int vec_f32;          // PRO_VEC: [B, K] (fp32 or TW)
+    // epilogue
+    void* out; int64_t ldo; int out_f32;     // EPI_STORE / EPI_DGDA / EPI_SWIGLU / EPI_LOGITS output
+    const float* bias;                       // EPI_STORE: optional [N] fp32
+    float* xres; int64_t ldr; const float* gate;  // EPI_RESIDUAL: x[b][n] += gate[n] * y
+    const void* taps; int ktaps;             // EPI_DGDA: [nconv, ktaps] conv taps (TW)
+    float* hist; int64_t ldh;                // EPI_DGDA: [B, nconv, ktaps-1] fp32 conv history (updated)
+    int nconv, a_end;                        // EPI_DGDA: rows [0,nconv) conv, [nconv,a_end) alpha, the rest gates
+    unsigned long long* keys;                // EPI_LOGITS: per-b argmax keys (zero before the first call)
+    unsigned int* ticket;                    // EPI_LOGITS: CTA counter (zero before the first call)
+    int64_t* ids_out; int64_t* pos_dev;      // EPI_LOGITS: argmax ids [B]; position advanced by 1 (optional)
+};
+
+template <typename T>
+__device__ __forceinline__ void load_chunk8(const T* p, float* v) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = Cvt<T>::to_f(p[i]);
+}
+template <>
+__device__ __forceinline__ void load_chunk8<__nv_bfloat16>(const __nv_bfloat16* p, float* v) {
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(h[i]);
+        v[2 * i] = f.x;
+        v[2 * i + 1] = f.y;
+    }
+}
+template <>
+__device__ __forceinline__ void load_chunk8<float>(const float* p, float* v) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+    const float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+__device__ __forceinline__ float silu_f(float x) { return x / (1.f + expf(-x)); }
+__device__ __forceinline__ float sigmoid_f(float x) { return 1.f / (1.f + expf(-x)); }
+__device__ __forceinline__ float neg_softplus_clamped(float x) {
+    const float sp = x > 20.f ? x : log1pf(expf(x));
+    return fmaxf(-sp, -14.f);
+}
+// (value desc, index asc) as one unsigned key: larger key = better
+__device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
+    unsigned int u = __float_as_uint(v);
+    u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return ((unsigned long long)u << 32) | (unsigned long long)(0xFFFFFFFFu - (unsigned int)idx);
+}
+
+template <typename TW, int NB>
+__global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvArgs a) {
+    extern __shared__ float hs[];  // [NB][K] input vectors
+    __shared__ float red[kGemvWarps][NB];
+    __shared__ unsigned long long best[kGemvWarps][NB];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int K = a.K;
+    // ---- prologue: the NB input vectors in shared memory (fp32)
+    if (a.pro == PRO_NORM) {
+        for (int b = 0; b < NB; ++b) {
+            float ss = 0.f;
+            if (b < a.B)
+                for (int k = tid; k < K; k += kGemvThreads) {
+                    const float v = a.x[b * a.ldx + k];
+                    hs[b * K + k] = v;
+                    ss = fmaf(v, v, ss);
+                }
+            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+            if (lane == 0) red[warp][b] = ss;
+        }
+        __syncthreads();
+        for (int b = 0; b < NB; ++b) {
+            float ss = 0.f;
+#pragma unroll
+            for (int w = 0; w < kGemvWarps; ++w) ss += red[w][b];
+            const float r = rsqrtf(ss / (float)K + a.eps);
+            const TW* nw = static_cast<const TW*>(a.norm_w);
+            if (b < a.B)
+                for (int k = tid; k < K; k += kGemvThreads) hs[b * K + k] = hs[b * K + k] * r * Cvt<TW>::to_f(nw[k]);
+            else
+                for (int k = tid; k < K; k += kGemvThreads) hs[b * K + k] = 0.f;
+        }
+    } else if (a.pro == PRO_GATHER) {
+        const TW* e = static_cast<const TW*>(a.emb);
+        for (int b = 0; b < NB; ++b) {
+            const int64_t row = b < a.B ? a.ids[b] : 0;
+            for (int k = tid; k < K; k += kGemvThreads) hs[b * K + k] = b < a.B ? Cvt<TW>::to_f(e[row * a.lde + k]) : 0.f;
+        }
+    } else {
+        for (int b = 0; b < NB; ++b)
+            for (int k = tid; k < K; k += kGemvThreads) {
+                float v = 0.f;
+                if (b < a.B)
+                    v = a.vec_f32 ? static_cast<const float*>(a.vec)[b * a.ldv + k]
+                                  : Cvt<TW>::to_f(static_cast<const TW*>(a.vec)[b * a.ldv + k]);
+                hs[b * K + k] = v;
+            }
+    }
+    __syncthreads();
+
+    // ---- the warp's two rows (SwiGLU: the gate row n and the up row N + n)
+    const int n0 = blockIdx.x * kRowsPerCta + warp * kRowsPerWarp;
+    int rows[2];
+    const bool swiglu = a.epi == EPI_SWIGLU;
+    const int on = swiglu ? (int)blockIdx.x * (kRowsPerCta / 2) + warp : -1;  // SwiGLU output of this warp
+    if (swiglu) {
+        rows[0] = on;
+        rows[1] = a.N + on;
+    } else {
+        rows[0] = n0;
+        rows[1] = n0 + 1;
+    }
+    const int nrows_total = swiglu ? 2 * a.N : a.N;
+    const bool live0 = swiglu ? on < a.N : rows[0] < nrows_total;
+    const bool live1 = swiglu ? on < a.N : rows[1] < nrows_total;
+    float acc[2][NB];
+#pragma unroll
+    for (int r = 0; r < 2; ++r)
+#pragma unroll
+        for (int b = 0; b < NB; ++b) acc[r][b] = 0.f;
+    const TW* w0 = static_cast<const TW*>(a.w) + (int64_t)(live0 ? rows[0] : 0) * a.ldw;
+    const TW* w1 = static_cast<const TW*>(a.w) + (int64_t)(live1 ? rows[1] : 0) * a.ldw;
+    const int nch = K / 8;
+    for (int c = lane; c < nch; c += 32) {
+        float v0[8], v1[8];
+        if (live0) load_chunk8<TW>(w0 + c * 8, v0);
+        if (live1) load_chunk8<TW>(w1 + c * 8, v1);
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+            const float4 h0 = *reinterpret_cast<const float4*>(hs + b * K + c * 8);
+            const float4 h1 = *reinterpret_cast<const float4*>(hs + b * K + c * 8 + 4);
+            const float hv[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+            if (live0)
+#pragma unroll
+                for (int i = 0; i < 8; ++i) acc[0][b] = fmaf(v0[i], hv[i], acc[0][b]);
+            if (live1)
+#pragma unroll
+                for (int i = 0; i < 8; ++i) acc[1][b] = fmaf(v1[i], hv[i], acc[1][b]);
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < 2; ++r)
+#pragma unroll
+        for (int b = 0; b < NB; ++b)
+            for (int o = 16; o > 0; o >>= 1) acc[r][b] += __shfl_xor_sync(0xffffffffu, acc[r][b], o);
+
+    // ---- epilogue: lane b (< B) handles batch row b
+    unsigned long long mykey[NB];
+#pragma unroll
+    for (int b = 0; b < NB; ++b) mykey[b] = 0ull;
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+        if (lane != b || b >= a.B) continue;
+        if (swiglu) {
+            if (live0) {
+                const float y = silu_f(acc[0][b]) * acc[1][b];
+                if (a.out_f32) static_cast<float*>(a.out)[b * a.ldo + on] = y;
+                else static_cast<TW*>(a.out)[b * a.ldo + on] = Cvt<TW>::from_f(y);
+            }
+            continue;
+        }
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const bool lv = r == 0 ? live0 : live1;
+            if (!lv) continue;
+            const int n = rows[r];
+            float y = acc[r][b];
+            if (a.epi == EPI_STORE) {
+                if (a.bias) y += a.bias[n];
+                if (a.out_f32) static_cast<float*>(a.out)[b * a.ldo + n] = y;
+                else static_cast<TW*>(a.out)[b * a.ldo + n] = Cvt<TW>::from_f(y);
+            } else if (a.epi == EPI_RESIDUAL) {
+                a.xres[b * a.ldr + n] += a.gate[n] * y;
+            } else if (a.epi == EPI_DGDA) {
+                float f;
+                if (n < a.nconv) {
+                    const TW* tp = static_cast<const TW*>(a.taps) + (int64_t)n * a.ktaps;
+                    float* h = a.hist + b * a.ldh + (int64_t)n * (a.ktaps - 1);
+                    float cv = Cvt<TW>::to_f(tp[a.ktaps - 1]) * y;
+                    for (int j = 0; j < a.ktaps - 1; ++j) cv = fmaf(Cvt<TW>::to_f(tp[j]), h[j], cv);
+                    for (int j = 0; j + 1 < a.ktaps - 1; ++j) h[j] = h[j + 1];
+                    if (a.ktaps > 1) h[a.ktaps - 2] = y;
+                    f = silu_f(cv);
+                } else if (n < a.a_end) {
+                    f = neg_softplus_clamped(y);
+                } else {
+                    f = sigmoid_f(y);
+                }
+                static_cast<float*>(a.out)[b * a.ldo + n] = f;
+            } else {  // EPI_LOGITS
+                static_cast<float*>(a.out)[b * a.ldo + n] = y;
+                const unsigned long long k = argmax_key(y, n);
+                mykey[b] = k > mykey[b] ? k : mykey[b];
+            }
+        }
+    }
+    if (a.epi != EPI_LOGITS) return;
+    // ---- argmax: warp -> CTA -> global key, the last CTA publishes the ids
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+        const unsigned long long k = __shfl_sync(0xffffffffu, mykey[b], b);
+        if (lane == 0) best[warp][b] = k;
+    }
+    __syncthreads();
+    if (tid < NB && tid < a.B) {
+        unsigned long long k = 0ull;
+#pragma unroll
+        for (int w = 0; w < kGemvWarps; ++w) k = best[w][tid] > k ? best[w][tid] : k;
+        atomicMax(a.keys + tid, k);
+    }
+    __threadfence();
+    __syncthreads();
+    __shared__ unsigned int last;
+    if (tid == 0) last = atomicAdd(a.ticket, 1u) == gridDim.x - 1 ? 1u : 0u;
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    if (tid < a.B) {
+        const unsigned long long k = atomicExch(a.keys + tid, 0ull);
+        a.ids_out[tid] = (int64_t)(0xFFFFFFFFu - (unsigned int)(k & 0xFFFFFFFFull));
+    }
+    if (tid == 0) {
+        *a.ticket = 0u;
+        if (a.pos_dev) *a.pos_dev += 1;
+    }
+}
+
+// one recurrence step per (batch, head): k L2-norm, S' = a*S + k (w*v - (b*k)^T (a*S)), o = q^T S'
+constexpr int kStateThreads = 128;
+
+template <int VPL>  // dv / 32 columns per lane
+__global__ void __launch_bounds__(kStateThreads) dgda_state_kernel(const float* feats, int64_t ldf, float* state,
+                                                                   float* o, int64_t ldo, int H, int dk, int dv,
+                                                                   int off_q, int off_k, int off_v, int off_a,
+                                                                   int off_b, int off_w, float eps) {
+    const int b = blockIdx.y, h = blockIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    __shared__ float sq[256], sk[256], sa[256], sbk[256];
+    __shared__ float part[4][VPL * 32];
+    __shared__ float delta[VPL * 32];
+    __shared__ float knorm;
+    const float* f = feats + b * ldf;
+    for (int i = tid; i < dk; i += kStateThreads) {
+        sq[i] = f[off_q + h * dk + i];
+        sk[i] = f[off_k + h * dk + i];
+        sa[i] = expf(f[off_a + h * dk + i]);
+    }
+    __syncthreads();
+    if (warp == 0) {
+        float ss = 0.f;
+        for (int i = lane; i < dk; i += 32) ss = fmaf(sk[i], sk[i], ss);
+        for (int o2 = 16; o2 > 0; o2 >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o2);
+        if (lane == 0) knorm = 1.f / (sqrtf(ss) + eps);
+    }
+    __syncthreads();
+    for (int i = tid; i < dk; i += kStateThreads) {
+        sk[i] *= knorm;
+        sbk[i] = f[off_b + h * dk + i] * sk[i];
+    }
+    __syncthreads();
+    float* S = state + ((int64_t)b * H + h) * dk * dv;
+    // this warp's rows: i = warp, warp + 4, ...
+    float sd[16][VPL];
+    const int nrow = (dk - warp + 3) / 4;
+    float dp[VPL];
+#pragma unroll
+    for (int c = 0; c < VPL; ++c) dp[c] = 0.f;
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+        if (r >= nrow) continue;
+        const int i = warp + 4 * r;
+#pragma unroll
+        for (int c = 0; c < VPL; ++c) {
+            const int j = lane + 32 * c;
+            const float v = j < dv ? S[(int64_t)i * dv + j] * sa[i] : 0.f;
+            sd[r][c] = v;
+            dp[c] = fmaf(sbk[i], v, dp[c]);
+        }
+    }
+#pragma unroll
+    for (int c = 0; c < VPL; ++c) part[warp][lane + 32 * c] = dp[c];
+    __syncthreads();
+    for (int j = tid; j < dv; j += kStateThreads) {
+        const float wv = f[off_w + h * dv + j] * f[off_v + h * dv + j];
+        delta[j] = wv - (part[0][j] + part[1][j] + part[2][j] + part[3][j]);
+    }
+    __syncthreads();
+    float op[VPL];
+#pragma unroll
+    for (int c = 0; c < VPL; ++c) op[c] = 0.f;
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+        if (r >= nrow) continue;
+        const int i = warp + 4 * r;
+#pragma unroll
+        for (int c = 0; c < VPL; ++c) {
+            const int j = lane + 32 * c;
+            if (j >= dv) continue;
+            const float s2 = fmaf(sk[i], delta[j], sd[r][c]);
+            S[(int64_t)i * dv + j] = s2;
+            op[c] = fmaf(sq[i], s2, op[c]);
+        }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int c = 0; c < VPL; ++c) part[warp][lane + 32 * c] = op[c];
+    __syncthreads();
+    for (int j = tid; j < dv; j += kStateThreads)
+        o[b * ldo + h * dv + j] = part[0][j] + part[1][j] + part[2][j] + part[3][j];
+}
+
+// prefill: x += gate * y (optional), h = x * rsqrt(mean(x^2) + eps) * w; one warp per row
+template <typename TO, typename TY>
+__global__ void rmsnorm_residual_kernel(float* x, int64_t ldx, const TY* y, int64_t ldy, const float* gate,
+                                        const TO* w, float eps, TO* h, int64_t ldh, int64_t N, int D) {
+    const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= N) return;
+    float* xr = x + row * ldx;
+    float ss = 0.f;
+    for (int k = lane; k < D; k += 32) {
+        float v = xr[k];
+        if (y != nullptr) {
+            v += gate[k] * Cvt<TY>::to_f(y[row * ldy + k]);
+            xr[k] = v;
+        }
+        ss = fmaf(v, v, ss);
+    }
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float r = rsqrtf(ss / (float)D + eps);
+    if (h == nullptr) return;
+    for (int k = lane; k < D; k += 32) h[row * ldh + k] = Cvt<TO>::from_f(xr[k] * r * Cvt<TO>::to_f(w[k]));
+}
+
+template <typename T>
+__global__ void swiglu_kernel(const T* u, int64_t ldu, T* out, int64_t ldo, int64_t N, int I) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= N * I) return;
+    const int64_t row = i / I;
+    const int c = (int)(i % I);
+    const float g = Cvt<T>::to_f(u[row * ldu + c]);
+    const float v = Cvt<T>::to_f(u[row * ldu + I + c]);
+    out[row * ldo + c] = Cvt<T>::from_f(silu_f(g) * v);
+}
+
+int wdtype_ok(int dt) { return dt == MABA_F32 || dt == MABA_BF16 || dt == MABA_F16; }
+
+template <typename TW>
+int launch_gemv(GemvArgs& a, cudaStream_t s) {
+    const int outs = a.epi == EPI_SWIGLU ? a.N : a.N;
+    const int per_cta = a.epi == EPI_SWIGLU ? kRowsPerCta / 2 : kRowsPerCta;
+    const unsigned grid = (unsigned)ceil_div(outs, per_cta);
+    int nb = a.B <= 1 ? 1 : a.B <= 2 ? 2 : a.B <= 4 ? 4 : 8;
+    const size_t smem = sizeof(float) * (size_t)nb * a.K;
+    if (smem > 200 * 1024) return set_error(MABA_ERR_UNSUPPORTED, "decode_gemv: B x K too large for shared memory");
+    auto go = [&](auto kern) {
+        if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        kern<<<grid, kGemvThreads, smem, s>>>(a);
+        return check_launch("decode_gemv");
+    };
+    switch (nb) {
+        case 1: return go(gemv_kernel<TW, 1>);
+        case 2: return go(gemv_kernel<TW, 2>);
+        case 4: return go(gemv_kernel<TW, 4>);
+        default: return go(gemv_kernel<TW, 8>);
+    }
+}
+
+bool row_vec_ok(const maba_tensor* t) {
+    const int es = t->dtype == MABA_F32 ? 4 : 2;
+    return t->stride[1] == 1 && (t->stride[0] * es) % 16 == 0 && (reinterpret_cast<uintptr_t>(t->data) & 15u) == 0;
+}
+
+}  // namespace
+}  // namespace maba
+
+using namespace maba;
+
+// ---------------------------------------------------------------------------
+// prefill helpers
+// ---------------------------------------------------------------------------
+extern "C" int maba_rmsnorm_residual(const maba_tensor* x, const maba_tensor* y, const maba_tensor* gate,
+                                     const maba_tensor* weight, float eps, const maba_tensor* h_out, void* stream) {
+    if (!present(x) || x->ndim != 2 || x->dtype != MABA_F32 || x->stride[1] != 1)
+        return set_error(MABA_ERR_INVALID, "rmsnorm_residual: x must be a float32 [N, D] tensor with unit column stride");
+    const int64_t N = x->shape[0], D = x->shape[1];
+    const bool has_y = present(y);
+    if (has_y) {
+        const int64_t sy[2] = {N, D};
+        MABA_TRY(expect_shape(y, "rmsnorm_residual: y", 2, sy));
+        const int64_t sg[1] = {D};
+        MABA_TRY(expect_shape(gate, "rmsnorm_residual: gate", 1, sg));
+        MABA_TRY(expect_dtype(gate, "rmsnorm_residual: gate", MABA_F32));
+        if (y->stride[1] != 1 || gate->stride[0] != 1)
+            return set_error(MABA_ERR_INVALID, "rmsnorm_residual: unit column strides required");
+    }
+    const bool has_h = present(h_out);
+    int odt = MABA_F32;
+    if (has_h) {
+        const int64_t sh[2] = {N, D};
+        MABA_TRY(expect_shape(h_out, "rmsnorm_residual: h_out", 2, sh));
+        const int64_t sw[1] = {D};
+        MABA_TRY(expect_shape(weight, "rmsnorm_residual: weight", 1, sw));
+        MABA_TRY(expect_dtype(weight, "rmsnorm_residual: weight", h_out->dtype));
+        if (h_out->stride[1] != 1 || weight->stride[0] != 1)
+            return set_error(MABA_ERR_INVALID, "rmsnorm_residual: unit column strides required");
+        odt = h_out->dtype;
+    }
+    if (has_y && y->dtype != odt && y->dtype != MABA_F32)
+        return set_error(MABA_ERR_DTYPE, "rmsnorm_residual: y must be float32 or the output dtype");
+    if (N == 0) return MABA_OK;
+    cudaStream_t s = as_stream(stream);
+    const unsigned grid = (unsigned)ceil_div(N, 8);
+    float* xp = static_cast<float*>(x->data);
+    const float* gp = has_y ? static_cast<const float*>(gate->data) : nullptr;
+    const int64_t ldy = has_y ? y->stride[0] : 0, ldh = has_h ? h_out->stride[0] : 0;
+    return MABA_DISPATCH_FLOAT(odt, "rmsnorm_residual", [&] {
+        if constexpr (sizeof(T) == 8) {
+            return set_error(MABA_ERR_DTYPE, "rmsnorm_residual: float64");
+        } else {
+            const T* wp = has_h ? static_cast<const T*>(weight->data) : nullptr;
+            T* hp = has_h ? static_cast<T*>(h_out->data) : nullptr;
+            if (has_y && y->dtype == MABA_F32 && odt != MABA_F32)
+                rmsnorm_residual_kernel<T, float><<<grid, 256, 0, s>>>(
+                    xp, x->stride[0], static_cast<const float*>(y->data), ldy, gp, wp, eps, hp, ldh, N, (int)D);
+            else
+                rmsnorm_residual_kernel<T, T><<<grid, 256, 0, s>>>(
+                    xp, x->stride[0], has_y ? static_cast<const T*>(y->data) : nullptr, ldy, gp, wp, eps, hp, ldh, N,
+                    (int)D);
+            return check_launch("rmsnorm_residual");
+        }
+    });
+}
+
+extern "C" int maba_swiglu(const maba_tensor* u, const maba_tensor* out, void* stream) {
+    if (!present(u) || u->ndim != 2 || u->shape[1] % 2 != 0 || u->stride[1] != 1)
+        return set_error(MABA_ERR_INVALID, "swiglu: u must be [N, 2I] with unit column stride");
+    const int64_t N = u->shape[0], I = u->shape[1] / 2;
+    const int64_t so[2] = {N, I};
+    MABA_TRY(expect_shape(out, "swiglu: out", 2, so));
+    MABA_TRY(expect_dtype(out, "swiglu: out", u->dtype));
+    if (out->stride[1] != 1) return set_error(MABA_ERR_INVALID, "swiglu: unit column stride required");
+    if (N == 0 || I == 0) return MABA_OK;
+    cudaStream_t s = as_stream(stream);
+    return MABA_DISPATCH_FLOAT(u->dtype, "swiglu", [&] {
+        if constexpr (sizeof(T) == 8) {
+            return set_error(MABA_ERR_DTYPE, "swiglu: float64");
+        } else {
+            swiglu_kernel<T><<<(unsigned)ceil_div(N * I, 256), 256, 0, s>>>(
+                static_cast<const T*>(u->data), u->stride[0], static_cast<T*>(out->data), out->stride[0], N, (int)I);
+            return check_launch("swiglu");
+        }
+    });
+}
+
+// ---------------------------------------------------------------------------
+// decode GEMV with fused prologue / epilogue
+// ---------------------------------------------------------------------------
+extern "C" size_t maba_decode_gemv_workspace_size(int64_t B) { return (size_t)(B > 0 ? B : 1) * 8 + 16; }
+
+extern "C" int maba_decode_gemv(const maba_tensor* w, int32_t prologue, const maba_tensor* x,
+                                const maba_tensor* aux, float eps, const maba_tensor* ids, int32_t epilogue,
+                                const maba_tensor* out, const maba_tensor* bias, const maba_tensor* gate,
+                                const maba_tensor* taps, const maba_tensor* hist, int32_t n_conv, int32_t alpha_end,
+                                const maba_tensor* ids_out, int64_t* pos_dev, void* workspace,
+                                size_t workspace_bytes, void* stream) {
+    const maba_tensor* norm_w = aux;
+    if (!present(w) || w->ndim != 2 || !wdtype_ok(w->dtype))
+        return set_error(MABA_ERR_INVALID, "decode_gemv: w must be a [rows, K] float32 / float16 / bfloat16 weight");
+    if (!row_vec_ok(w) || w->shape[1] % 8 != 0)
+        return set_error(MABA_ERR_UNSUPPORTED, "decode_gemv: w rows must be contiguous, 16-byte aligned, K %% 8 == 0");
+    const int dt = w->dtype;
+    const int64_t rows = w->shape[0], K = w->shape[1];
+    GemvArgs a{};
+    a.w = w->data; a.ldw = w->stride[0]; a.K = (int)K; a.pro = prologue; a.epi = epilogue;
+    a.N = (int)(epilogue == EPI_SWIGLU ? rows / 2 : rows);
+    if (epilogue == EPI_SWIGLU && rows % 2 != 0) return set_error(MABA_ERR_INVALID, "decode_gemv: SwiGLU needs 2I rows");
+    int64_t B = -1;
+    if (prologue == PRO_NORM || prologue == PRO_VEC) {
+        if (!present(x) || x->ndim != 2 || x->shape[1] != K || x->stride[1] != 1)
+            return set_error(MABA_ERR_INVALID, "decode_gemv: x must be [B, K] with unit column stride");
+        B = x->shape[0];
+        if (prologue == PRO_NORM) {
+            MABA_TRY(expect_dtype(x, "decode_gemv: x", MABA_F32));
+            const int64_t sn[1] = {K};
+            MABA_TRY(expect_shape(norm_w, "decode_gemv: norm_w", 1, sn));
+            MABA_TRY(expect_dtype(norm_w, "decode_gemv: norm_w", dt));
+            a.x = static_cast<const float*>(x->data); a.ldx = x->stride[0]; a.norm_w = norm_w->data; a.eps = eps;
+        } else {
+            if (x->dtype != MABA_F32 && x->dtype != dt)
+                return set_error(MABA_ERR_DTYPE, "decode_gemv: vector must be float32 or the weight dtype");
+            a.vec = x->data; a.ldv = x->stride[0]; a.vec_f32 = x->dtype == MABA_F32;
+        }
+    } else if (prologue == PRO_GATHER) {
+        if (!present(ids) || ids->ndim != 1 || ids->dtype != MABA_I64 || ids->stride[0] != 1)
+            return set_error(MABA_ERR_INVALID, "decode_gemv: ids must be a contiguous int64 [B] tensor");
+        if (!present(norm_w) || norm_w->ndim != 2 || norm_w->shape[1] != K || norm_w->stride[1] != 1)
+            return set_error(MABA_ERR_INVALID, "decode_gemv: the embedding table (aux) must be [V, K]");
+        MABA_TRY(expect_dtype(norm_w, "decode_gemv: embedding", dt));
+        B = ids->shape[0];
+        a.ids = static_cast<const int64_t*>(ids->data); a.emb = norm_w->data; a.lde = norm_w->stride[0];
+    } else {
+        return set_error(MABA_ERR_INVALID, "decode_gemv: unknown prologue %d", prologue);
+    }
+    if (B <= 0 || B > 8) return set_error(MABA_ERR_UNSUPPORTED, "decode_gemv: batch 1..8");
+    a.B = (int)B;
+    if (!present(out) || out->ndim != 2 || out->shape[0] != B || out->stride[1] != 1)
+        return set_error(MABA_ERR_INVALID, "decode_gemv: out must be [B, N] with unit column stride");
+    a.out = out->data; a.ldo = out->stride[0]; a.out_f32 = out->dtype == MABA_F32;
+    if (out->dtype != MABA_F32 && out->dtype != dt)
+        return set_error(MABA_ERR_DTYPE, "decode_gemv: out must be float32 or the weight dtype");
+    switch (epilogue) {
+        case EPI_STORE:
+            if (out->shape[1] != a.N) return set_error(MABA_ERR_INVALID, "decode_gemv: out must have one column per row");
+            if (present(bias)) {
+                if (bias->ndim != 1 || bias->shape[0] != a.N || bias->dtype != MABA_F32 || bias->stride[0] != 1)
+                    return set_error(MABA_ERR_INVALID, "decode_gemv: bias must be a contiguous float32 [N]");
+                a.bias = static_cast<const float*>(bias->data);
+            }
+            break;
+        case EPI_RESIDUAL:
+            if (out->shape[1] != a.N || out->dtype != MABA_F32)
+                return set_error(MABA_ERR_INVALID, "decode_gemv: the residual stream (out) must be float32 [B, N]");
+            if (!present(gate) || gate->ndim != 1 || gate->shape[0] != a.N || gate->dtype != MABA_F32 || gate->stride[0] != 1)
+                return set_error(MABA_ERR_INVALID, "decode_gemv: gate must be a contiguous float32 [N]");
+            a.xres = static_cast<float*>(out->data); a.ldr = out->stride[0]; a.gate = static_cast<const float*>(gate->data);
+            break;
+        case EPI_DGDA: {
+            if (out->shape[1] != a.N || out->dtype != MABA_F32)
+                return set_error(MABA_ERR_INVALID, "decode_gemv: the DGDA features (out) must be float32 [B, N]");
+            if (n_conv < 0 || n_conv > alpha_end || alpha_end > a.N)
+                return set_error(MABA_ERR_INVALID, "decode_gemv: bad DGDA section bounds");
+            if (!present(taps) || taps->ndim != 2 || taps->shape[0] != n_conv || taps->stride[1] != 1 ||
+                taps->stride[0] != taps->shape[1] || taps->dtype != dt)
+                return set_error(MABA_ERR_INVALID, "decode_gemv: taps must be a contiguous [n_conv, K] weight");
+            const int kt = (int)taps->shape[1];
+            if (kt < 1 || kt > 8) return set_error(MABA_ERR_UNSUPPORTED, "decode_gemv: conv kernel size 1..8");
+            const int64_t shh[3] = {B, n_conv, kt - 1};
+            MABA_TRY(expect_shape(hist, "decode_gemv: hist", 3, shh));
+            MABA_TRY(expect_dtype(hist, "decode_gemv: hist", MABA_F32));
+            if (hist->stride[2] != 1 || hist->stride[1] != kt - 1)
+                return set_error(MABA_ERR_INVALID, "decode_gemv: hist rows must be contiguous");
+            a.taps = taps->data; a.ktaps = kt; a.hist = static_cast<float*>(hist->data); a.ldh = hist->stride[0];
+            a.nconv = n_conv; a.a_end = alpha_end;
+            break;
+        }
+        case EPI_SWIGLU:
+            if (out->shape[1] != a.N) return set_error(MABA_ERR_INVALID, "decode_gemv: SwiGLU out must be [B, I]");
+            break;
+        case EPI_LOGITS: {
+            if (out->shape[1] != a.N || out->dtype != MABA_F32)
+                return set_error(MABA_ERR_INVALID, "decode_gemv: logits (out) must be float32 [B, V]");
+            if (!present(ids_out) || ids_out->ndim != 1 || ids_out->shape[0] != B || ids_out->dtype != MABA_I64 ||
+                ids_out->stride[0] != 1)
+                return set_error(MABA_ERR_INVALID, "decode_gemv: ids_out must be a contiguous int64 [B]");
+            const size_t need = maba_decode_gemv_workspace_size(B);
+            if (workspace == nullptr || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 7u))
+                return set_error(MABA_ERR_WORKSPACE, "decode_gemv: zeroed, 8-byte aligned workspace of %zu bytes required",
+                                 need);
+            a.keys = static_cast<unsigned long long*>(workspace);
+            a.ticket = reinterpret_cast<unsigned int*>(static_cast<char*>(workspace) + (size_t)B * 8);
+            a.ids_out = static_cast<int64_t*>(ids_out->data);
+            a.pos_dev = pos_dev;
+            break;
+        }
+        default:
+            return set_error(MABA_ERR_INVALID, "decode_gemv: unknown epilogue %d", epilogue);
+    }
+    cudaStream_t s = as_stream(stream);
+    switch (dt) {
+        case MABA_F32: return launch_gemv<float>(a, s);
+        case MABA_F16: return launch_gemv<__half>(a, s);
+        default: return launch_gemv<__nv_bfloat16>(a, s);
+    }
+}
+
+extern "C" int maba_decode_dgda_state(const maba_tensor* feats, const maba_tensor* state, const maba_tensor* o_out,
+                                      int32_t n_heads, float eps, void* stream) {
+    if (!present(feats) || feats->ndim != 2 || feats->dtype != MABA_F32 || feats->stride[1] != 1)
+        return set_error(MABA_ERR_INVALID, "decode_dgda_state: feats must be float32 [B, 4*H*dk + 2*H*dv]");
+    if (!present(state) || state->ndim != 4 || state->dtype != MABA_F32)
+        return set_error(MABA_ERR_INVALID, "decode_dgda_state: state must be float32 [B, H, dk, dv]");
+    const int64_t B = state->shape[0], H = state->shape[1], dk = state->shape[2], dv = state->shape[3];
+    if (H != n_heads || feats->shape[0] != B || feats->shape[1] != 4 * H * dk + 2 * H * dv)
+        return set_error(MABA_ERR_INVALID, "decode_dgda_state: feats / state shapes disagree");
+    if (state->stride[3] != 1 || state->stride[2] != dv || state->stride[1] != dk * dv || state->stride[0] != H * dk * dv)
+        return set_error(MABA_ERR_INVALID, "decode_dgda_state: state must be contiguous");
+    if (dk > 64 || dv > 128 || dk <= 0 || dv <= 0)
+        return set_error(MABA_ERR_UNSUPPORTED, "decode_dgda_state: dk <= 64, dv <= 128");
+    const int64_t so[2] = {B, H * dv};
+    MABA_TRY(expect_shape(o_out, "decode_dgda_state: o_out", 2, so));
+    MABA_TRY(expect_dtype(o_out, "decode_dgda_state: o_out", MABA_F32));
+    if (o_out->stride[1] != 1) return set_error(MABA_ERR_INVALID, "decode_dgda_state: o_out unit column stride");
+    const int cqk = (int)(H * dk), cv = (int)(H * dv);
+    const int off_q = 0, off_k = cqk, off_v = 2 * cqk, off_a = 2 * cqk + cv, off_b = 3 * cqk + cv, off_w = 4 * cqk + cv;
+    cudaStream_t s = as_stream(stream);
+    dim3 grid((unsigned)H, (unsigned)B);
+    const float* fp = static_cast<const float*>(feats->data);
+    float* sp = static_cast<float*>(state->data);
+    float* op = static_cast<float*>(o_out->data);
+    if (dv <= 32)
+        dgda_state_kernel<1><<<grid, kStateThreads, 0, s>>>(fp, feats->stride[0], sp, op, o_out->stride[0], (int)H,
+                                                            (int)dk, (int)dv, off_q, off_k, off_v, off_a, off_b, off_w, eps);
+    else if (dv <= 64)
+        dgda_state_kernel<2><<<grid, kStateThreads, 0, s>>>(fp, feats->stride[0], sp, op, o_out->stride[0], (int)H,
+                                                            (int)dk, (int)dv, off_q, off_k, off_v, off_a, off_b, off_w, eps);
+    else
+        dgda_state_kernel<4><<<grid, kStateThreads, 0, s>>>(fp, feats->stride[0], sp, op, o_out->stride[0], (int)H,
+                                                            (int)dk, (int)dv, off_q, off_k, off_v, off_a, off_b, off_w, eps);
+    return check_launch("decode_dgda_state");
+}

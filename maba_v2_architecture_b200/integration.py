@@ -9,9 +9,11 @@ its layers) run the hot path on the sm_100a kernels:
   ``register_kernel`` (dispatcher.py:71-77), and its backend cache is cleared;
 * the layer-level paths that have no registry op are replaced by method patch:
   ``MabaSparseAttention.forward`` (sparse_attention.py:221-277, whose three
-  streams are inline torch code) by the fused latent-attention forward, and
+  streams are inline torch code) by the fused latent-attention forward,
   ``DGIndexer.forward`` (indexer.py:43-126, whose decode top-k is inline) by the
-  fused-kernel version;
+  fused-kernel version, and ``DGDALayer.forward`` / ``step`` (dgda.py:166-287,
+  whose conv, gates and k norm are separate torch ops) by the version with one
+  input GEMM and the fused front-end kernel;
 * ``MABA_STRICT_BACKEND=1`` is set so the reference dispatcher raises instead of
   silently falling back to its CPU reference.
 
@@ -60,15 +62,16 @@ def install(maba_sparse: Optional[Any] = None, patch_layers: bool = True, strict
     if patch_layers:
         sa_mod = importlib.import_module("maba_sparse.layers.sparse_attention")
         ix_mod = importlib.import_module("maba_sparse.layers.indexer")
-        ref_sa, ref_ix = sa_mod.MabaSparseAttention, ix_mod.DGIndexer
-        handle["methods"] = {
-            (ref_sa, "forward"): ref_sa.__dict__.get("forward"),
-            (ref_sa, "latent_attention"): ref_sa.__dict__.get("latent_attention"),
-            (ref_ix, "forward"): ref_ix.__dict__.get("forward"),
-        }
-        ref_sa.forward = _layers.MabaSparseAttention.forward
-        ref_sa.latent_attention = _layers.MabaSparseAttention.latent_attention
-        ref_ix.forward = _layers.DGIndexer.forward
+        dg_mod = importlib.import_module("maba_sparse.layers.dgda")
+        ref_sa, ref_ix, ref_dg = sa_mod.MabaSparseAttention, ix_mod.DGIndexer, dg_mod.DGDALayer
+        patches = [(ref_sa, "forward", _layers.MabaSparseAttention),
+                   (ref_sa, "latent_attention", _layers.MabaSparseAttention),
+                   (ref_ix, "forward", _layers.DGIndexer), (ref_dg, "forward", _layers.DGDALayer),
+                   (ref_dg, "step", _layers.DGDALayer), (ref_dg, "_features", _layers.DGDALayer),
+                   (ref_dg, "_in_proj_weight", _layers.DGDALayer)]
+        handle["methods"] = {(cls, name): cls.__dict__.get(name) for cls, name, _ in patches}
+        for cls, name, ours in patches:
+            setattr(cls, name, ours.__dict__[name])
     handle["dispatcher"] = disp
     return handle
 

@@ -5,9 +5,11 @@ forward/step signatures, return contracts and decode caches follow
 maba_sparse/layers/{dgda,indexer,sparse_attention}.py.  What changes is the
 compute behind them:
 
-* DGDA feeds the chunked prefill / decode kernels token-major strided views
-  (no ``.contiguous()`` copies) and receives the output token-major, so the
-  transpose back before ``o_proj`` is free;
+* DGDA runs its six input projections as one GEMM, then one front-end kernel
+  (causal conv + SiLU with history, gates, k L2-norm), and feeds the chunked
+  prefill / decode kernels token-major strided views of its output (no
+  ``.contiguous()`` copies); the recurrence writes its output token-major, so
+  the transpose back before ``o_proj`` is free;
 * the indexer's prefill and decode top-k run in one fused kernel each;
 * MABA-SA never up-projects keys or values: queries are absorbed into the
   d_c=128 latent space (qhat_h = scale * W_uk,h^T q_h), the three streams and
@@ -24,7 +26,8 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .dispatcher import dispatch_compute_centroids, dispatch_dgda_prefill, dispatch_dgda_step, dispatch_index_topk
-from .ops import absorb_queries, b200_hca_pool, b200_index_topk, b200_sa_attention, expand_values
+from .ops import (absorb_queries, b200_dgda_frontend, b200_hca_pool, b200_index_topk, b200_sa_attention,
+                  expand_values)
 
 
 class ConvState(tuple):
@@ -39,6 +42,50 @@ class ConvState(tuple):
 
     def as_tensor(self) -> torch.Tensor:
         return torch.stack(self, dim=1)
+
+
+def _fit_history(t: torch.Tensor, k1: int) -> torch.Tensor:
+    """[B, C, n] history -> [B, C, k1]: the last k1 columns, zero-padded on the left."""
+    n = t.shape[-1]
+    if n == k1:
+        return t
+    if n > k1:
+        return t[..., n - k1:]
+    return F.pad(t, (k1 - n, 0))
+
+
+def conv_history(conv_state, batch: int, widths, k1: int, device, dtype):
+    """The three conv histories ([B, C_i, k1], oldest first) from any conv-state form the
+    reference layer accepts (maba_sparse/layers/dgda.py:124-164): a (q, k, v) tuple or list,
+    such a tuple wrapped in a 1-tuple, a stacked [B, 3, C, n] tensor (also 5-D with the
+    history flattened), or a [B, C_total, n] tensor holding q|k|v channels (one shared
+    history when C_total is a single width).  None stays None (zero history)."""
+    if conv_state is None or k1 == 0:
+        return None
+    parts = None
+    if isinstance(conv_state, (tuple, list)):
+        if len(conv_state) == 1 and isinstance(conv_state[0], (tuple, list)):
+            conv_state = conv_state[0]
+        if len(conv_state) == 3:
+            parts = list(conv_state)
+    if parts is None:
+        if not isinstance(conv_state, torch.Tensor):
+            raise ValueError(f"Unsupported conv_state shape or type: {type(conv_state)}")
+        t = conv_state
+        if t.dim() in (4, 5) and t.shape[1] == 3:
+            t = t.reshape(batch, 3, t.shape[2], -1)
+            parts = [t[:, i] for i in range(3)]
+        else:
+            t = t.reshape(batch, -1, k1)
+            cqk, cv = widths[0], widths[2]
+            tot = t.shape[1]
+            if tot == 2 * cqk + cv:
+                parts = [t[:, :cqk], t[:, cqk:2 * cqk], t[:, 2 * cqk:]]
+            elif tot == cqk and cqk != cv:
+                parts = [t, t, torch.zeros(batch, cv, k1, dtype=t.dtype, device=t.device)]
+            else:
+                parts = [t, t, t]
+    return [_fit_history(p_.to(device=device, dtype=dtype), k1) for p_ in parts]
 
 
 class DGDALayer(nn.Module):
@@ -90,82 +137,48 @@ class DGDALayer(nn.Module):
         for conv in (self.conv_q, self.conv_k, self.conv_v):
             nn.init.normal_(conv.weight, mean=0.0, std=0.02)
 
-    def _apply_conv(self, x: torch.Tensor, conv: nn.Conv1d,
-                    conv_state: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
-        """Causal depthwise conv + SiLU with history; maba_sparse/layers/dgda.py:103-122."""
-        k = self.kernel_size
-        xt = x.transpose(1, 2)
-        if conv_state is not None:
-            if k > 1 and conv_state.shape[-1] != k - 1:
-                if conv_state.shape[-1] < k - 1:
-                    conv_state = F.pad(conv_state, (k - 1 - conv_state.shape[-1], 0))
-                else:
-                    conv_state = conv_state[:, :, -(k - 1):]
-            p = torch.cat([conv_state, xt], dim=2)
-        else:
-            p = F.pad(xt, (k - 1, 0)) if k > 1 else xt
-        ns = p[:, :, -(k - 1):].contiguous() if k > 1 else p[:, :, :0].contiguous()
-        y = F.silu(conv(p)).transpose(1, 2)
-        return y, ns
-
-    def _unpack_conv_state(self, conv_state, b_size: int, device: torch.device, dtype: torch.dtype):
-        """Accepts the conv-state forms of maba_sparse/layers/dgda.py:124-164."""
-        if conv_state is None:
-            return None, None, None
-
-        def cast(t):
-            return None if t is None else t.to(device=device, dtype=dtype)
-
-        k_hist = max(self.kernel_size - 1, 0)
-        if isinstance(conv_state, (tuple, list)):
-            if len(conv_state) == 3:
-                return cast(conv_state[0]), cast(conv_state[1]), cast(conv_state[2])
-            if len(conv_state) == 1 and isinstance(conv_state[0], (tuple, list)):
-                return cast(conv_state[0][0]), cast(conv_state[0][1]), cast(conv_state[0][2])
-        if isinstance(conv_state, torch.Tensor):
-            if conv_state.dim() == 4 and conv_state.shape[1] == 3:
-                return cast(conv_state[:, 0]), cast(conv_state[:, 1]), cast(conv_state[:, 2])
-            if conv_state.dim() == 5 and conv_state.shape[1] == 3:
-                cs = conv_state.reshape(b_size, 3, conv_state.shape[2], k_hist)
-                return cast(cs[:, 0]), cast(cs[:, 1]), cast(cs[:, 2])
-            cs = conv_state.reshape(b_size, -1, k_hist)
-            tot = cs.shape[1]
-            qk, vd = self.n_heads * self.d_k, self.n_heads * self.d_v
-            if tot == 2 * qk + vd:
-                return cast(cs[:, :qk]), cast(cs[:, qk:2 * qk]), cast(cs[:, 2 * qk:])
-            if tot == qk and qk == vd:
-                return cast(cs), cast(cs), cast(cs)
-            if tot == qk:
-                return cast(cs), cast(cs), torch.zeros(b_size, vd, k_hist, device=device, dtype=dtype)
-            return cast(cs), cast(cs), cast(cs)
-        raise ValueError(f"Unsupported conv_state shape or type: {type(conv_state)}")
+    def _in_proj_weight(self) -> torch.Tensor:
+        """The six input projections (q, k, v, alpha, erase, write) stacked into one
+        [4*H*dk + 2*H*dv, dim] weight, so the layer runs one GEMM; rebuilt only when a
+        weight changes (new tensor or in-place update)."""
+        ws = (self.q_proj.weight, self.k_proj.weight, self.v_proj.weight, self.gate_alpha.weight,
+              self.gate_erase.weight, self.gate_write.weight)
+        key = tuple((w.data_ptr(), w._version, w.dtype, w.device) for w in ws)
+        cached = self.__dict__.get("_in_proj_cache")
+        if cached is None or cached[0] != key:
+            cached = (key, torch.cat([w.detach() for w in ws], dim=0))
+            self.__dict__["_in_proj_cache"] = cached
+        return cached[1]
 
     def _features(self, x, conv_state):
+        """Projections (one GEMM) + the fused front end (conv + SiLU, gates, k norm).
+        Returns q, k, v, b, w, log_alpha as [B,H,L,d] views of one token-major buffer and
+        the new conv state."""
         b, l, _ = x.shape
         h, dk, dv = self.n_heads, self.d_k, self.d_v
-        cq, ck, cv = self._unpack_conv_state(conv_state, b, x.device, x.dtype)
-        q, nq = self._apply_conv(self.q_proj(x), self.conv_q, cq)
-        k, nk = self._apply_conv(self.k_proj(x), self.conv_k, ck)
-        v, nv = self._apply_conv(self.v_proj(x), self.conv_v, cv)
-        eb = torch.sigmoid(self.gate_erase(x))
-        ew = torch.sigmoid(self.gate_write(x))
-        la = torch.clamp(-F.softplus(self.gate_alpha(x)), min=-14.0)
-        # token-major [B, L, H, d] viewed as [B, H, L, d]: the kernels read strides, no copies
-        q = q.view(b, l, h, dk).transpose(1, 2)
-        k = k.view(b, l, h, dk)
-        k = (k / (torch.linalg.vector_norm(k, dim=-1, keepdim=True) + self.eps)).transpose(1, 2)
-        v = v.view(b, l, h, dv).transpose(1, 2)
-        eb = eb.view(b, l, h, dk).transpose(1, 2)
-        ew = ew.view(b, l, h, dv).transpose(1, 2)
-        la = la.view(b, l, h, dk).transpose(1, 2)
-        dt = q.dtype
-        return q, k.to(dt), v.to(dt), eb.to(dt), ew.to(dt), la.to(dt), ConvState((nq, nk, nv))
+        cqk, cv = h * dk, h * dv
+        kh = max(self.kernel_size - 1, 0)
+        proj = F.linear(x, self._in_proj_weight())
+        widths = (cqk, cqk, cv, cqk, cqk, cv)
+        cols, c0 = [], 0
+        for wd in widths:
+            cols.append(proj[:, :, c0:c0 + wd])
+            c0 += wd
+        hist = conv_history(conv_state, b, (cqk, cqk, cv), kh, x.device, x.dtype)
+        taps = [c.weight.detach().view(c.weight.shape[0], -1) for c in (self.conv_q, self.conv_k, self.conv_v)]
+        (q, k, v, la, eb, ew), nh = b200_dgda_frontend(cols, taps, hist, n_heads=h, eps=self.eps)
+
+        def heads(t, d):  # token-major [B, L, H*d] viewed as [B, H, L, d]: the kernels read strides
+            return t.view(b, l, h, d).transpose(1, 2)
+
+        return (heads(q, dk), heads(k, dk), heads(v, dv), heads(eb, dk), heads(ew, dv), heads(la, dk),
+                ConvState(tuple(nh)))
 
     def forward(self, x: torch.Tensor, state: Optional[torch.Tensor] = None, conv_state=None,
                 chunk_size: Optional[int] = None, inversion_method: Optional[str] = None):
         b, l, d = x.shape
         h, dk, dv = self.n_heads, self.d_k, self.d_v
-        sdt = self.state_dtype or x.dtype
+        sdt = getattr(self, "state_dtype", None) or x.dtype
         if l == 0:
             es = state.clone() if state is not None else torch.zeros(b, h, dk, dv, dtype=sdt, device=x.device)
             kh = max(self.kernel_size - 1, 0)
@@ -187,7 +200,7 @@ class DGDALayer(nn.Module):
         b, l = x.shape[0], x.shape[1]
         assert l == 1
         h, dv = self.n_heads, self.d_v
-        sdt = self.state_dtype or x.dtype
+        sdt = getattr(self, "state_dtype", None) or x.dtype
         q, k, v, eb, ew, la, ncs = self._features(x, conv_state)
         if state is not None:
             state = state.to(sdt)

@@ -192,6 +192,43 @@ def b200_dgda_transition(q, k, v, alpha=None, b=None, w=None, log_alpha=None) ->
     return out
 
 
+def b200_dgda_frontend(proj, conv_w, hist=None, n_heads: int = 10, eps: float = 1e-6, new_hist: bool = True,
+                       hist_dtype: Optional[torch.dtype] = None, out: Optional[torch.Tensor] = None):
+    """The DGDA layer's feature path after its projections, in one kernel.
+
+    Reference: maba_sparse/layers/dgda.py:103-122 (_apply_conv: causal depthwise
+    conv with history, SiLU), :192-197 (gates) and :207 (k / (||k|| + eps)).
+    ``proj``: six [B,L,C] tensors (q, k, v, alpha, erase, write projections; any
+    strides, e.g. column slices of one fused projection); ``conv_w``: three [C,K]
+    taps; ``hist``: None or three [B,C,K-1] conv histories (oldest first).
+    Returns ``(feats, new_hist)``: feats = (q, k, v, log_alpha, b, w), [B,L,C] column
+    views of one token-major buffer ``out`` ([B,L,sum C], allocated when None);
+    new_hist = three [B,C,K-1] tensors in ``hist_dtype`` (default: the feature dtype),
+    or None when ``new_hist`` is False."""
+    x0 = proj[0]
+    N.require_cuda(*proj, *conv_w, op="dgda_frontend")
+    B, L, _ = x0.shape
+    widths = [int(t.shape[2]) for t in proj]
+    total = sum(widths)
+    if out is None:
+        out = torch.empty(B, L, total, dtype=x0.dtype, device=x0.device)
+    feats, c0 = [], 0
+    for wd in widths:
+        feats.append(out[:, :, c0:c0 + wd])
+        c0 += wd
+    K = int(conv_w[0].shape[1])
+    nh = None
+    if new_hist:
+        hd = hist_dtype or (hist[0].dtype if hist is not None else x0.dtype)
+        nh = [torch.empty(B, widths[i], K - 1, dtype=hd, device=x0.device) for i in range(3)]
+    rc = N.lib().maba_dgda_frontend(N.desc_array(proj), N.desc_array(conv_w),
+                                    N.desc_array(hist) if hist is not None else None, N.desc_array(feats),
+                                    N.desc_array(nh) if nh is not None else None, int(n_heads), float(eps),
+                                    N.stream_of(x0))
+    N.check(rc, "maba_dgda_frontend")
+    return tuple(feats), nh
+
+
 def _squeeze_step(t: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
     if t is not None and t.dim() == 4 and t.shape[2] == 1:
         return t.squeeze(2)
@@ -510,6 +547,7 @@ __all__ = [
     "b200_hca_pool",
     "b200_sa_attention",
     "b200_dgda_transition",
+    "b200_dgda_frontend",
     "b200_decode_cache_append",
     "b200_index_topk_decode_at",
     "b200_sa_attention_decode_at",
