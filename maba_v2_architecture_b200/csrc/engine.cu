@@ -15,7 +15,12 @@
 //                            turned into the DGDA features (conv with history +
 //                            SiLU, gates), into SwiGLU products, or into logits
 //                            with their argmax.
-//   maba_decode_dgda_state -- k L2-norm + one recurrence step per (batch, head).
+//   maba_decode_dgda_state -- k L2-norm + one recurrence step per (batch, head,
+//                            group of 16 state columns).
+// The decode kernels are launched with programmatic dependent launch: each one
+// loads what does not depend on its predecessor (its weights, its state slice)
+// before waiting for it, so in a captured decode step the weight streams of
+// consecutive kernels overlap.
 //
 // A GEMV warp owns R = 2 output rows and streams their weights with 16-byte
 // loads (8 bf16), multiplying each chunk with all NB (<= 8) input vectors held
@@ -81,6 +86,27 @@ __device__ __forceinline__ void load_chunk8<float>(const float* p, float* v) {
     v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
 }
 
+// 8 weights in their storage type (one 16-byte load for 16-bit types, two for float32)
+template <typename T> struct Chunk8 { uint4 u[sizeof(T) == 4 ? 2 : 1]; };
+template <typename T>
+__device__ __forceinline__ void load_raw8(const T* p, Chunk8<T>& c) {
+#pragma unroll
+    for (int i = 0; i < (sizeof(T) == 4 ? 2 : 1); ++i) c.u[i] = __ldg(reinterpret_cast<const uint4*>(p) + i);
+}
+template <typename T>
+__device__ __forceinline__ void unpack8(const Chunk8<T>& c, float* v) {
+    const T* e = reinterpret_cast<const T*>(c.u);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = Cvt<T>::to_f(e[i]);
+}
+
+// Programmatic dependent launch: the next kernel of the stream may start once every
+// CTA of this one has started, and runs its independent prologue (weight loads) while
+// this one finishes; griddep_wait() blocks until the previous kernel has completed and
+// its writes are visible.  Both are no-ops for a kernel launched without the attribute.
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ float silu_f(float x) { return x / (1.f + expf(-x)); }
 __device__ __forceinline__ float sigmoid_f(float x) { return 1.f / (1.f + expf(-x)); }
 __device__ __forceinline__ float neg_softplus_clamped(float x) {
@@ -94,13 +120,45 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
     return ((unsigned long long)u << 32) | (unsigned long long)(0xFFFFFFFFu - (unsigned int)idx);
 }
 
+constexpr int kPrefetch = 6;  // weight chunks per lane and row loaded before the dependency wait
+
 template <typename TW, int NB>
 __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvArgs a) {
     extern __shared__ float hs[];  // [NB][K] input vectors
     __shared__ float red[kGemvWarps][NB];
     __shared__ unsigned long long best[kGemvWarps][NB];
+    griddep_launch_dependents();
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int K = a.K;
+    // ---- the warp's two rows (SwiGLU: the gate row n and the up row N + n) and their
+    // first weight chunks: the weights do not depend on the previous kernel
+    const int n0 = blockIdx.x * kRowsPerCta + warp * kRowsPerWarp;
+    int rows[2];
+    const bool swiglu = a.epi == EPI_SWIGLU;
+    const int on = swiglu ? (int)blockIdx.x * (kRowsPerCta / 2) + warp : -1;  // SwiGLU output of this warp
+    if (swiglu) {
+        rows[0] = on;
+        rows[1] = a.N + on;
+    } else {
+        rows[0] = n0;
+        rows[1] = n0 + 1;
+    }
+    const int nrows_total = swiglu ? 2 * a.N : a.N;
+    const bool live0 = swiglu ? on < a.N : rows[0] < nrows_total;
+    const bool live1 = swiglu ? on < a.N : rows[1] < nrows_total;
+    const TW* w0 = static_cast<const TW*>(a.w) + (int64_t)(live0 ? rows[0] : 0) * a.ldw;
+    const TW* w1 = static_cast<const TW*>(a.w) + (int64_t)(live1 ? rows[1] : 0) * a.ldw;
+    const int nch = K / 8;
+    Chunk8<TW> pf0[kPrefetch], pf1[kPrefetch];
+#pragma unroll
+    for (int j = 0; j < kPrefetch; ++j) {
+        const int c = lane + 32 * j;
+        if (c < nch) {
+            if (live0) load_raw8<TW>(w0 + c * 8, pf0[j]);
+            if (live1) load_raw8<TW>(w1 + c * 8, pf1[j]);
+        }
+    }
+    griddep_wait();
     // ---- prologue: the NB input vectors in shared memory (fp32)
     if (a.pro == PRO_NORM) {
         for (int b = 0; b < NB; ++b) {
@@ -144,30 +202,36 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvArgs a) {
     }
     __syncthreads();
 
-    // ---- the warp's two rows (SwiGLU: the gate row n and the up row N + n)
-    const int n0 = blockIdx.x * kRowsPerCta + warp * kRowsPerWarp;
-    int rows[2];
-    const bool swiglu = a.epi == EPI_SWIGLU;
-    const int on = swiglu ? (int)blockIdx.x * (kRowsPerCta / 2) + warp : -1;  // SwiGLU output of this warp
-    if (swiglu) {
-        rows[0] = on;
-        rows[1] = a.N + on;
-    } else {
-        rows[0] = n0;
-        rows[1] = n0 + 1;
-    }
-    const int nrows_total = swiglu ? 2 * a.N : a.N;
-    const bool live0 = swiglu ? on < a.N : rows[0] < nrows_total;
-    const bool live1 = swiglu ? on < a.N : rows[1] < nrows_total;
     float acc[2][NB];
 #pragma unroll
     for (int r = 0; r < 2; ++r)
 #pragma unroll
         for (int b = 0; b < NB; ++b) acc[r][b] = 0.f;
-    const TW* w0 = static_cast<const TW*>(a.w) + (int64_t)(live0 ? rows[0] : 0) * a.ldw;
-    const TW* w1 = static_cast<const TW*>(a.w) + (int64_t)(live1 ? rows[1] : 0) * a.ldw;
-    const int nch = K / 8;
-    for (int c = lane; c < nch; c += 32) {
+    auto fma_chunk = [&](int c, const float* v0, const float* v1) {
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+            const float4 h0 = *reinterpret_cast<const float4*>(hs + b * K + c * 8);
+            const float4 h1 = *reinterpret_cast<const float4*>(hs + b * K + c * 8 + 4);
+            const float hv[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+            if (live0)
+#pragma unroll
+                for (int i = 0; i < 8; ++i) acc[0][b] = fmaf(v0[i], hv[i], acc[0][b]);
+            if (live1)
+#pragma unroll
+                for (int i = 0; i < 8; ++i) acc[1][b] = fmaf(v1[i], hv[i], acc[1][b]);
+        }
+    };
+#pragma unroll
+    for (int j = 0; j < kPrefetch; ++j) {
+        const int c = lane + 32 * j;
+        if (c < nch) {
+            float v0[8], v1[8];
+            unpack8<TW>(pf0[j], v0);
+            unpack8<TW>(pf1[j], v1);
+            fma_chunk(c, v0, v1);
+        }
+    }
+    for (int c = lane + 32 * kPrefetch; c < nch; c += 32) {
         float v0[8], v1[8];
         if (live0) load_chunk8<TW>(w0 + c * 8, v0);
         if (live1) load_chunk8<TW>(w1 + c * 8, v1);
@@ -271,88 +335,107 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvArgs a) {
     }
 }
 
-// one recurrence step per (batch, head): k L2-norm, S' = a*S + k (w*v - (b*k)^T (a*S)), o = q^T S'
-constexpr int kStateThreads = 128;
+// One recurrence step: k L2-norm, S' = a*S + k (w*v - (b*k)^T (a*S)), o = q^T S'.
+// The columns of S evolve independently (delta_j and o_j only involve column j),
+// so one CTA owns a group of 16 columns of one (batch, head) for all dk rows:
+// thread (ty, tx) holds rows ty, ty+16, ... of column tx, and the two sums over
+// rows go through shared memory.
+constexpr int kStateCols = 16;
+constexpr int kStateThreads = 256;
 
-template <int VPL>  // dv / 32 columns per lane
 __global__ void __launch_bounds__(kStateThreads) dgda_state_kernel(const float* feats, int64_t ldf, float* state,
                                                                    float* o, int64_t ldo, int H, int dk, int dv,
                                                                    int off_q, int off_k, int off_v, int off_a,
                                                                    int off_b, int off_w, float eps) {
-    const int b = blockIdx.y, h = blockIdx.x;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    __shared__ float sq[256], sk[256], sa[256], sbk[256];
-    __shared__ float part[4][VPL * 32];
-    __shared__ float delta[VPL * 32];
+    griddep_launch_dependents();
+    const int h = blockIdx.x, j0 = blockIdx.y * kStateCols, b = blockIdx.z;
+    const int tid = threadIdx.x, tx = tid % kStateCols, ty = tid / kStateCols;
+    constexpr int RY = kStateThreads / kStateCols;  // 16 row groups
+    __shared__ float sq[64], sk[64], sa[64], sbk[64];
+    __shared__ float red[RY][kStateCols + 1];
     __shared__ float knorm;
-    const float* f = feats + b * ldf;
-    for (int i = tid; i < dk; i += kStateThreads) {
-        sq[i] = f[off_q + h * dk + i];
-        sk[i] = f[off_k + h * dk + i];
-        sa[i] = expf(f[off_a + h * dk + i]);
-    }
-    __syncthreads();
-    if (warp == 0) {
-        float ss = 0.f;
-        for (int i = lane; i < dk; i += 32) ss = fmaf(sk[i], sk[i], ss);
-        for (int o2 = 16; o2 > 0; o2 >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o2);
-        if (lane == 0) knorm = 1.f / (sqrtf(ss) + eps);
-    }
-    __syncthreads();
-    for (int i = tid; i < dk; i += kStateThreads) {
-        sk[i] *= knorm;
-        sbk[i] = f[off_b + h * dk + i] * sk[i];
-    }
-    __syncthreads();
     float* S = state + ((int64_t)b * H + h) * dk * dv;
-    // this warp's rows: i = warp, warp + 4, ...
-    float sd[16][VPL];
-    const int nrow = (dk - warp + 3) / 4;
-    float dp[VPL];
+    const int j = j0 + tx;
+    const bool colv = j < dv;
+    // the state does not depend on the previous kernel (only this kernel writes it)
+    float sd[64 / RY];
 #pragma unroll
-    for (int c = 0; c < VPL; ++c) dp[c] = 0.f;
+    for (int r = 0; r < 64 / RY; ++r) {
+        const int i = ty + RY * r;
+        sd[r] = (i < dk && colv) ? S[(int64_t)i * dv + j] : 0.f;
+    }
+    griddep_wait();
+    const float* f = feats + (int64_t)b * ldf;
+    if (tid < dk) {
+        sq[tid] = f[off_q + h * dk + tid];
+        sk[tid] = f[off_k + h * dk + tid];
+        sa[tid] = expf(f[off_a + h * dk + tid]);
+        sbk[tid] = f[off_b + h * dk + tid];
+    }
+    __syncthreads();
+    if (tid < 32) {
+        float ss = 0.f;
+        for (int i = tid; i < dk; i += 32) ss = fmaf(sk[i], sk[i], ss);
+        for (int o2 = 16; o2 > 0; o2 >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o2);
+        if (tid == 0) knorm = 1.f / (sqrtf(ss) + eps);
+    }
+    __syncthreads();
+    float dp = 0.f;
 #pragma unroll
-    for (int r = 0; r < 16; ++r) {
-        if (r >= nrow) continue;
-        const int i = warp + 4 * r;
-#pragma unroll
-        for (int c = 0; c < VPL; ++c) {
-            const int j = lane + 32 * c;
-            const float v = j < dv ? S[(int64_t)i * dv + j] * sa[i] : 0.f;
-            sd[r][c] = v;
-            dp[c] = fmaf(sbk[i], v, dp[c]);
+    for (int r = 0; r < 64 / RY; ++r) {
+        const int i = ty + RY * r;
+        if (i < dk) {
+            sd[r] *= sa[i];
+            dp = fmaf(sbk[i] * (sk[i] * knorm), sd[r], dp);
         }
     }
-#pragma unroll
-    for (int c = 0; c < VPL; ++c) part[warp][lane + 32 * c] = dp[c];
+    red[ty][tx] = dp;
     __syncthreads();
-    for (int j = tid; j < dv; j += kStateThreads) {
-        const float wv = f[off_w + h * dv + j] * f[off_v + h * dv + j];
-        delta[j] = wv - (part[0][j] + part[1][j] + part[2][j] + part[3][j]);
+    float delta = 0.f;
+    if (colv) {
+        float tot = 0.f;
+#pragma unroll
+        for (int y = 0; y < RY; ++y) tot += red[y][tx];
+        delta = f[off_w + h * dv + j] * f[off_v + h * dv + j] - tot;
     }
     __syncthreads();
-    float op[VPL];
+    float op = 0.f;
 #pragma unroll
-    for (int c = 0; c < VPL; ++c) op[c] = 0.f;
-#pragma unroll
-    for (int r = 0; r < 16; ++r) {
-        if (r >= nrow) continue;
-        const int i = warp + 4 * r;
-#pragma unroll
-        for (int c = 0; c < VPL; ++c) {
-            const int j = lane + 32 * c;
-            if (j >= dv) continue;
-            const float s2 = fmaf(sk[i], delta[j], sd[r][c]);
+    for (int r = 0; r < 64 / RY; ++r) {
+        const int i = ty + RY * r;
+        if (i < dk && colv) {
+            const float s2 = fmaf(sk[i] * knorm, delta, sd[r]);
             S[(int64_t)i * dv + j] = s2;
-            op[c] = fmaf(sq[i], s2, op[c]);
+            op = fmaf(sq[i], s2, op);
         }
     }
+    red[ty][tx] = op;
     __syncthreads();
+    if (ty == 0 && colv) {
+        float tot = 0.f;
 #pragma unroll
-    for (int c = 0; c < VPL; ++c) part[warp][lane + 32 * c] = op[c];
-    __syncthreads();
-    for (int j = tid; j < dv; j += kStateThreads)
-        o[b * ldo + h * dv + j] = part[0][j] + part[1][j] + part[2][j] + part[3][j];
+        for (int y = 0; y < RY; ++y) tot += red[y][tx];
+        o[(int64_t)b * ldo + h * dv + j] = tot;
+    }
+}
+
+// Launch with the programmatic-stream-serialization attribute (see griddep_wait).
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, args...);
+    if (e != cudaSuccess)
+        return set_error(MABA_ERR_CUDA, "launch: %s (%s)", cudaGetErrorName(e), cudaGetErrorString(e));
+    return MABA_OK;
 }
 
 // prefill: x += gate * y (optional), h = x * rsqrt(mean(x^2) + eps) * w; one warp per row
@@ -401,7 +484,7 @@ int launch_gemv(GemvArgs& a, cudaStream_t s) {
     if (smem > 200 * 1024) return set_error(MABA_ERR_UNSUPPORTED, "decode_gemv: B x K too large for shared memory");
     auto go = [&](auto kern) {
         if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        kern<<<grid, kGemvThreads, smem, s>>>(a);
+        MABA_TRY(launch_pdl(kern, dim3(grid), dim3(kGemvThreads), smem, s, a));
         return check_launch("decode_gemv");
     };
     switch (nb) {
@@ -631,8 +714,8 @@ extern "C" int maba_decode_dgda_state(const maba_tensor* feats, const maba_tenso
         return set_error(MABA_ERR_INVALID, "decode_dgda_state: feats / state shapes disagree");
     if (state->stride[3] != 1 || state->stride[2] != dv || state->stride[1] != dk * dv || state->stride[0] != H * dk * dv)
         return set_error(MABA_ERR_INVALID, "decode_dgda_state: state must be contiguous");
-    if (dk > 64 || dv > 128 || dk <= 0 || dv <= 0)
-        return set_error(MABA_ERR_UNSUPPORTED, "decode_dgda_state: dk <= 64, dv <= 128");
+    if (dk > 64 || dk <= 0 || dv <= 0)
+        return set_error(MABA_ERR_UNSUPPORTED, "decode_dgda_state: dk <= 64");
     const int64_t so[2] = {B, H * dv};
     MABA_TRY(expect_shape(o_out, "decode_dgda_state: o_out", 2, so));
     MABA_TRY(expect_dtype(o_out, "decode_dgda_state: o_out", MABA_F32));
@@ -640,18 +723,9 @@ extern "C" int maba_decode_dgda_state(const maba_tensor* feats, const maba_tenso
     const int cqk = (int)(H * dk), cv = (int)(H * dv);
     const int off_q = 0, off_k = cqk, off_v = 2 * cqk, off_a = 2 * cqk + cv, off_b = 3 * cqk + cv, off_w = 4 * cqk + cv;
     cudaStream_t s = as_stream(stream);
-    dim3 grid((unsigned)H, (unsigned)B);
-    const float* fp = static_cast<const float*>(feats->data);
-    float* sp = static_cast<float*>(state->data);
-    float* op = static_cast<float*>(o_out->data);
-    if (dv <= 32)
-        dgda_state_kernel<1><<<grid, kStateThreads, 0, s>>>(fp, feats->stride[0], sp, op, o_out->stride[0], (int)H,
-                                                            (int)dk, (int)dv, off_q, off_k, off_v, off_a, off_b, off_w, eps);
-    else if (dv <= 64)
-        dgda_state_kernel<2><<<grid, kStateThreads, 0, s>>>(fp, feats->stride[0], sp, op, o_out->stride[0], (int)H,
-                                                            (int)dk, (int)dv, off_q, off_k, off_v, off_a, off_b, off_w, eps);
-    else
-        dgda_state_kernel<4><<<grid, kStateThreads, 0, s>>>(fp, feats->stride[0], sp, op, o_out->stride[0], (int)H,
-                                                            (int)dk, (int)dv, off_q, off_k, off_v, off_a, off_b, off_w, eps);
+    const dim3 grid((unsigned)H, (unsigned)ceil_div(dv, kStateCols), (unsigned)B);
+    MABA_TRY(launch_pdl(dgda_state_kernel, grid, dim3(kStateThreads), 0, s, static_cast<const float*>(feats->data),
+                        feats->stride[0], static_cast<float*>(state->data), static_cast<float*>(o_out->data),
+                        o_out->stride[0], (int)H, (int)dk, (int)dv, off_q, off_k, off_v, off_a, off_b, off_w, eps));
     return check_launch("decode_dgda_state");
 }

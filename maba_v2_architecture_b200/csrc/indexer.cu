@@ -701,10 +701,85 @@ __global__ void __launch_bounds__(kTopkThreads) topk_decode_partial_kernel(TopkA
     }
 }
 
-__global__ void topk_decode_merge_kernel(TopkArgs a, const float* part_s, const int* part_i, int nsplit, int64_t B) {
-    const int lane = threadIdx.x & 31;
-    const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
-    if (row >= B * a.L) return;
+
+// Vectorised variant for 16-bit centroids with unit-stride, 16-byte-aligned rows
+// and d_idx = 8 * DV <= 64: each lane loads its candidate's whole row with DV
+// 16-byte loads (both of its candidates' rows issued before any use) and forms
+// the score with the same sequential FMA chain over d as the other kernels; the
+// eight warp lists are then merged as a tree (3 levels) instead of in sequence.
+template <typename T, int DV>
+__global__ void __launch_bounds__(kTopkThreads) topk_decode_vec_kernel(TopkArgs a, float* part_s, int* part_i,
+                                                                       int nsplit) {
+    constexpr int D = DV * 8;
+    __shared__ float qs[D];
+    __shared__ float lsm[kTopkThreads / 32][32];
+    __shared__ int lim[kTopkThreads / 32][32];
+    const int split = blockIdx.x;
+    const int64_t t = blockIdx.y, b = blockIdx.z;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    int64_t nb = a.nb;
+    if (a.pos_dev != nullptr) {
+        const int64_t v = *a.pos_dev / a.block + 1;
+        nb = v < a.nb ? v : a.nb;
+    }
+    if ((int64_t)split * kSplitCand >= nb) return;
+    const T* q = static_cast<const T*>(a.q);
+    const T* c = static_cast<const T*>(a.c) + b * a.sc[0];
+    for (int d = tid; d < D; d += kTopkThreads) qs[d] = load_as<float>(q + b * a.sq[0] + t * a.sq[1] + d * a.sq[2]) * a.scale_f;
+    const int64_t n0 = (int64_t)split * kSplitCand + warp * 64 + lane;
+    uint4 r0[DV], r1[DV];
+#pragma unroll
+    for (int k = 0; k < DV; ++k) {
+        r0[k] = n0 < nb ? *reinterpret_cast<const uint4*>(c + n0 * a.sc[1] + k * 8) : make_uint4(0u, 0u, 0u, 0u);
+        r1[k] = n0 + 32 < nb ? *reinterpret_cast<const uint4*>(c + (n0 + 32) * a.sc[1] + k * 8) : make_uint4(0u, 0u, 0u, 0u);
+    }
+    __syncthreads();
+    const int64_t qb = nb - 1;
+    float ls = -INFINITY;
+    int li = INT_MAX;
+#pragma unroll
+    for (int ch = 0; ch < 2; ++ch) {
+        const int64_t n = n0 + 32 * ch;
+        float sc = -INFINITY;
+        int ci = INT_MAX;
+        if (n < nb) {
+            float acc = 0.f;
+#pragma unroll
+            for (int k = 0; k < DV; ++k) {
+                const T* e = reinterpret_cast<const T*>(ch == 0 ? &r0[k] : &r1[k]);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) acc = fmaf(qs[k * 8 + i], Cvt<T>::to_f(e[i]), acc);
+            }
+            sc = acc - a.pen[qb - n];
+            ci = (int)n;
+        }
+        warp_offer(ls, li, sc, ci, a.keff, lane);
+    }
+    lsm[warp][lane] = ls;
+    lim[warp][lane] = li;
+    for (int half = kTopkThreads / 64; half > 0; half >>= 1) {
+        __syncthreads();
+        if (warp < half) {
+            warp_merge(ls, li, lsm[warp + half][lane], lim[warp + half][lane], lane);
+            lsm[warp][lane] = ls;
+            lim[warp][lane] = li;
+        }
+    }
+    if (warp == 0) {
+        const size_t o = ((size_t)(b * a.L + t) * nsplit + split) * 32 + lane;
+        part_s[o] = ls;
+        part_i[o] = li;
+    }
+}
+
+// Tree merge of the partial lists of one (batch, token) row: warp w first folds
+// lists w, w+32, ... in sequence, then the 32 warp lists meet in 5 levels.
+__global__ void __launch_bounds__(1024) topk_decode_merge_tree_kernel(TopkArgs a, const float* part_s,
+                                                                      const int* part_i, int nsplit, int64_t B) {
+    __shared__ float lsm[32][32];
+    __shared__ int lim[32][32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t row = blockIdx.x;
     const int64_t b = row / a.L, t = row - (row / a.L) * a.L;
     int64_t nb = a.nb;
     if (a.pos_dev != nullptr) {
@@ -713,11 +788,51 @@ __global__ void topk_decode_merge_kernel(TopkArgs a, const float* part_s, const 
     }
     const int used = (int)((nb + kSplitCand - 1) / kSplitCand);
     const size_t base = (size_t)row * nsplit * 32;
-    float ls = part_s[base + lane];
-    int li = part_i[base + lane];
-    for (int sp = 1; sp < used && sp < nsplit; ++sp)
+    float ls = -INFINITY;
+    int li = INT_MAX;
+    for (int sp = warp; sp < used && sp < nsplit; sp += 32)
         warp_merge(ls, li, part_s[base + sp * 32 + lane], part_i[base + sp * 32 + lane], lane);
-    write_topk_row(a, b, t, li, lane, nb - 1);
+    lsm[warp][lane] = ls;
+    lim[warp][lane] = li;
+    for (int half = 16; half > 0; half >>= 1) {
+        __syncthreads();
+        if (warp < half) {
+            warp_merge(ls, li, lsm[warp + half][lane], lim[warp + half][lane], lane);
+            lsm[warp][lane] = ls;
+            lim[warp][lane] = li;
+        }
+    }
+    if (warp == 0) write_topk_row(a, b, t, li, lane, nb - 1);
+    (void)B;
+}
+
+// Launches the split decode scan (vectorised partials where the layout allows)
+// and the tree merge.
+template <typename T>
+int launch_topk_decode_split(TopkArgs& a, int64_t B, int64_t L, int nsplit, float* ps, int* pi, cudaStream_t s) {
+    const bool vec = (sizeof(T) == 2) && a.D % 8 == 0 && a.D <= 64 && a.sc[2] == 1 && (a.sc[1] * 2) % 16 == 0 &&
+                     (a.sc[0] * 2) % 16 == 0 && (reinterpret_cast<uintptr_t>(a.c) & 15u) == 0;
+    const dim3 grid((unsigned)nsplit, (unsigned)L, (unsigned)B);
+    if (vec) {
+        switch (a.D / 8) {
+            case 1: topk_decode_vec_kernel<T, 1><<<grid, kTopkThreads, 0, s>>>(a, ps, pi, nsplit); break;
+            case 2: topk_decode_vec_kernel<T, 2><<<grid, kTopkThreads, 0, s>>>(a, ps, pi, nsplit); break;
+            case 3: topk_decode_vec_kernel<T, 3><<<grid, kTopkThreads, 0, s>>>(a, ps, pi, nsplit); break;
+            case 4: topk_decode_vec_kernel<T, 4><<<grid, kTopkThreads, 0, s>>>(a, ps, pi, nsplit); break;
+            case 5: topk_decode_vec_kernel<T, 5><<<grid, kTopkThreads, 0, s>>>(a, ps, pi, nsplit); break;
+            case 6: topk_decode_vec_kernel<T, 6><<<grid, kTopkThreads, 0, s>>>(a, ps, pi, nsplit); break;
+            case 7: topk_decode_vec_kernel<T, 7><<<grid, kTopkThreads, 0, s>>>(a, ps, pi, nsplit); break;
+            default: topk_decode_vec_kernel<T, 8><<<grid, kTopkThreads, 0, s>>>(a, ps, pi, nsplit); break;
+        }
+    } else {
+        const size_t smem = sizeof(float) * ((size_t)a.D + (size_t)8 * 32 * (a.D + 1) + 8 * 32) + sizeof(int) * 8 * 32;
+        auto kern = topk_decode_partial_kernel<T>;
+        if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        kern<<<grid, kTopkThreads, smem, s>>>(a, ps, pi, nsplit);
+    }
+    MABA_TRY(check_launch("index_topk(decode partial)"));
+    topk_decode_merge_tree_kernel<<<(unsigned)(B * L), 1024, 0, s>>>(a, ps, pi, nsplit, B);
+    return check_launch("index_topk(decode merge)");
 }
 
 int64_t decode_split_count(int64_t nb) { return (nb + kSplitCand - 1) / kSplitCand; }
@@ -897,15 +1012,7 @@ static int index_topk_impl(const maba_tensor* q_idx, const maba_tensor* centroid
                     if constexpr (sizeof(T) == 8) {
                         return launch_topk<T>(a, B, s);
                     } else {
-                        auto kern = topk_decode_partial_kernel<T>;
-                        if (smem > 48 * 1024)
-                            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-                        kern<<<dim3((unsigned)nsplit, (unsigned)L, (unsigned)B), kTopkThreads, smem, s>>>(a, ps, pi,
-                                                                                                        (int)nsplit);
-                        MABA_TRY(check_launch("index_topk(decode partial)"));
-                        const int64_t rows = B * L;
-                        topk_decode_merge_kernel<<<(unsigned)ceil_div(rows, 4), 128, 0, s>>>(a, ps, pi, (int)nsplit, B);
-                        return check_launch("index_topk(decode merge)");
+                        return launch_topk_decode_split<T>(a, B, L, (int)nsplit, ps, pi, s);
                     }
                 });
             }
@@ -1160,12 +1267,7 @@ extern "C" int maba_index_topk_decode_at(const maba_tensor* q_idx, const maba_te
         if constexpr (sizeof(T) == 8) {
             return set_error(MABA_ERR_UNSUPPORTED, "index_topk_decode_at: float64");
         } else {
-            auto kern = topk_decode_partial_kernel<T>;
-            if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            kern<<<dim3((unsigned)nsplit, 1, (unsigned)B), kTopkThreads, smem, s>>>(a, ps, pi, (int)nsplit);
-            MABA_TRY(check_launch("index_topk_decode_at(partial)"));
-            topk_decode_merge_kernel<<<(unsigned)ceil_div(B, 4), 128, 0, s>>>(a, ps, pi, (int)nsplit, B);
-            return check_launch("index_topk_decode_at(merge)");
+            return launch_topk_decode_split<T>(a, B, 1, (int)nsplit, ps, pi, s);
         }
     });
 }

@@ -12,12 +12,13 @@
 // by the heads), so the HBM traffic is the decode minimum: window + selected
 // blocks + pooled table.
 #include "sa_attention.cuh"
+#include "mma_util.cuh"
 
 namespace maba {
 namespace {
 
-constexpr int KT = 32;           // keys per smem tile
-constexpr int SPLIT_KEYS = 256;  // keys per split (HCA / sparse)
+constexpr int KT = 32;           // keys per smem tile (generic kernel)
+constexpr int SPLIT_KEYS = 128;  // keys per split (every stream)
 constexpr int MAXH = 16;
 constexpr int MAXDC = 256;
 
@@ -37,7 +38,9 @@ __host__ __device__ inline DecodePlan make_plan(const SaArgs& a, int64_t Lkv) {
     const int64_t nsink = a.n_sinks < Lkv ? a.n_sinks : Lkv;
     p.nsink_extra = nsink < p.lo ? nsink : p.lo;
     p.nlocal = p.nsink_extra + (pos - p.lo + 1);
-    p.n_local = 1;
+    // a fixed count (independent of the position), so that a capacity-sized launch and the
+    // combine agree on which splits hold which stream; splits past the stream's keys are empty
+    p.n_local = (int)((a.window + a.n_sinks + SPLIT_KEYS - 1) / SPLIT_KEYS);
     p.blocks_per_split = SPLIT_KEYS / a.block > 0 ? SPLIT_KEYS / a.block : 1;
     p.n_sparse = (a.K + p.blocks_per_split - 1) / p.blocks_per_split;
     p.nhca = 0;
@@ -80,7 +83,9 @@ __global__ void sa_decode_partial_kernel_t(SaArgs a, float* ws, int nsplit) {
     int stream;
     int64_t k0, k1;
     if (split < p.n_local) {
-        stream = 0; k0 = 0; k1 = p.nlocal;
+        stream = 0;
+        k0 = (int64_t)split * SPLIT_KEYS;
+        k1 = k0 + SPLIT_KEYS < p.nlocal ? k0 + SPLIT_KEYS : p.nlocal;
     } else if (split < p.n_local + p.n_sparse) {
         stream = 1;
         const int s = split - p.n_local;
@@ -255,6 +260,284 @@ __global__ void sa_decode_combine_kernel(SaArgs a, const float* ws, int nsplit) 
     }
 }
 
+// ---------------------------------------------------------------------------
+// 16-bit tensor-core split kernel: one split of up to SPLIT_KEYS keys per CTA,
+// 4 warps of 32 keys each.  The split's latent (or pooled) rows are gathered
+// into shared memory with 16-byte loads, all issued before the first use; the
+// heads are the 16 rows of the mma.sync tiles (zero rows past H):
+//   S = Qhat K^T (16 x 32 per warp, K = d_c), masked, softmax numerator in fp32,
+//   P (16-bit) -> shared, O = P V (16 x d_c per warp);
+// the four warps' (max, sum, O) are merged through shared memory into one
+// partial record per head.  Rows are padded by 8 elements, so the ldmatrix
+// reads of 8 rows hit 8 different bank groups.
+// ---------------------------------------------------------------------------
+constexpr int kMmaWarps = 4;
+constexpr int kMmaDC = 128;
+constexpr int kMmaLD = kMmaDC + 8;
+constexpr int kPLD = 32 + 8;
+
+template <typename T>
+__global__ void __launch_bounds__(32 * kMmaWarps) sa_decode_mma_kernel(SaArgs a, float* ws, int nsplit) {
+    constexpr int DC = kMmaDC, LD = kMmaLD, CPR = DC / 8;
+    constexpr int NTHR = 32 * kMmaWarps;
+    constexpr int MAXL = SPLIT_KEYS * CPR / NTHR;  // 16 chunks per thread
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    T* ks = reinterpret_cast<T*>(smem_raw);                           // [SPLIT_KEYS][LD]; later the O merge area
+    T* qs = ks + SPLIT_KEYS * LD;                                     // [16][LD]
+    T* ps = qs + 16 * LD;                                             // [warps][16][kPLD]
+    float* mw = reinterpret_cast<float*>(ps + kMmaWarps * 16 * kPLD);  // [warps][16]
+    float* lw = mw + kMmaWarps * 16;                                  // [warps][16]
+    int64_t* rows = reinterpret_cast<int64_t*>(lw + kMmaWarps * 16);  // [SPLIT_KEYS]
+    const int H = a.H;
+    const int split = blockIdx.x;
+    const int64_t b = blockIdx.y;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int64_t Lkv = visible_len(a);
+    const DecodePlan p = make_plan(a, Lkv);
+    if (split >= p.total()) return;
+    const int64_t pos = Lkv - 1;
+    const int64_t nb_kv = (Lkv + a.block - 1) / a.block;
+    int stream;
+    int64_t k0, k1;
+    if (split < p.n_local) {
+        stream = 0;
+        k0 = (int64_t)split * SPLIT_KEYS;
+        k1 = k0 + SPLIT_KEYS < p.nlocal ? k0 + SPLIT_KEYS : p.nlocal;
+    } else if (split < p.n_local + p.n_sparse) {
+        stream = 1;
+        k0 = (int64_t)(split - p.n_local) * p.blocks_per_split * a.block;
+        k1 = k0 + (int64_t)p.blocks_per_split * a.block;
+        const int64_t kmax = (int64_t)a.K * a.block;
+        if (k1 > kmax) k1 = kmax;
+    } else {
+        stream = 2;
+        k0 = (int64_t)(split - p.n_local - p.n_sparse) * SPLIT_KEYS;
+        k1 = k0 + SPLIT_KEYS < p.nhca ? k0 + SPLIT_KEYS : p.nhca;
+    }
+    const int nk = k1 > k0 ? (int)(k1 - k0) : 0;
+    for (int i = tid; i < SPLIT_KEYS; i += NTHR) {
+        const int64_t n = k0 + i;
+        int64_t row = -1;
+        if (i < nk) {
+            if (stream == 0) {
+                row = n < p.nsink_extra ? n : p.lo + (n - p.nsink_extra);
+            } else if (stream == 1) {
+                const int64_t slot = n / a.block, off = n - slot * a.block;
+                const int64_t blk = a.top_idx[b * a.st[0] + slot * a.st[2]];
+                const int64_t tok = blk * a.block + off;
+                if (blk >= 0 && blk < nb_kv && tok <= pos) row = tok;
+            } else {
+                row = n;
+            }
+        }
+        rows[i] = row;
+    }
+    // queries: 16 rows of 16-bit values (rows >= H zero)
+    const T* qh = static_cast<const T*>(a.qhat);
+    for (int e = tid; e < 16 * DC; e += NTHR) {
+        const int r = e / DC, d = e - r * DC;
+        qs[r * LD + d] = r < H ? qh[b * a.sq[0] + r * a.sq[2] + d * a.sq[3]] : Cvt<T>::from_f(0.f);
+    }
+    __syncthreads();
+    {
+        const T* base = stream == 2 ? static_cast<const T*>(a.hca) + b * a.sh[0] : static_cast<const T*>(a.ckv) + b * a.sc[0];
+        const int64_t rs = stream == 2 ? a.sh[1] : a.sc[1];
+        uint4 v[MAXL];
+#pragma unroll
+        for (int j = 0; j < MAXL; ++j) {
+            const int e = tid + j * NTHR;
+            const int64_t row = rows[e / CPR];
+            v[j] = row >= 0 ? *reinterpret_cast<const uint4*>(base + row * rs + (e % CPR) * 8) : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int j = 0; j < MAXL; ++j) {
+            const int e = tid + j * NTHR;
+            *reinterpret_cast<uint4*>(ks + (e / CPR) * LD + (e % CPR) * 8) = v[j];
+        }
+    }
+    __syncthreads();
+    // ---- scores of this warp's 32 keys
+    const T* kw = ks + warp * 32 * LD;
+    float sacc[4][4];
+#pragma unroll
+    for (int n = 0; n < 4; ++n)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) sacc[n][c] = 0.f;
+    warp_mma<T, false, false, 4>(sacc, qs, LD, kw, LD, DC, lane);
+    const int g = lane >> 2, t2 = (lane & 3) * 2;
+    float m0 = -INFINITY, m1 = -INFINITY;
+#pragma unroll
+    for (int n = 0; n < 4; ++n)
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+            const int key = warp * 32 + n * 8 + t2 + c;
+            const bool ok = key < nk && rows[key] >= 0;
+            if (!ok) {
+                sacc[n][c] = -INFINITY;
+                sacc[n][c + 2] = -INFINITY;
+            }
+            m0 = fmaxf(m0, sacc[n][c]);
+            m1 = fmaxf(m1, sacc[n][c + 2]);
+        }
+#pragma unroll
+    for (int o = 1; o < 4; o <<= 1) {
+        m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, o));
+        m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, o));
+    }
+    float l0 = 0.f, l1 = 0.f;
+#pragma unroll
+    for (int n = 0; n < 4; ++n)
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+            const float p0 = sacc[n][c] == -INFINITY ? 0.f : __expf(sacc[n][c] - m0);
+            const float p1 = sacc[n][c + 2] == -INFINITY ? 0.f : __expf(sacc[n][c + 2] - m1);
+            sacc[n][c] = p0;
+            sacc[n][c + 2] = p1;
+            l0 += p0;
+            l1 += p1;
+        }
+#pragma unroll
+    for (int o = 1; o < 4; o <<= 1) {
+        l0 += __shfl_xor_sync(0xffffffffu, l0, o);
+        l1 += __shfl_xor_sync(0xffffffffu, l1, o);
+    }
+    T* pw = ps + warp * 16 * kPLD;
+    store_acc16<T, 4>(pw, kPLD, sacc, lane);
+    if ((lane & 3) == 0) {
+        mw[warp * 16 + g] = m0;
+        mw[warp * 16 + g + 8] = m1;
+        lw[warp * 16 + g] = l0;
+        lw[warp * 16 + g + 8] = l1;
+    }
+    __syncwarp();
+    // ---- O = P V for this warp's keys
+    float oacc[DC / 8][4];
+#pragma unroll
+    for (int n = 0; n < DC / 8; ++n)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) oacc[n][c] = 0.f;
+    warp_mma<T, false, true, DC / 8>(oacc, pw, kPLD, kw, LD, 32, lane);
+    __syncthreads();  // every warp is done with the key tile: reuse it for the O merge
+    float* om = reinterpret_cast<float*>(ks);  // [warps][16][DC]
+#pragma unroll
+    for (int n = 0; n < DC / 8; ++n) {
+        float* r0 = om + (warp * 16 + g) * DC + n * 8 + t2;
+        float* r1 = om + (warp * 16 + g + 8) * DC + n * 8 + t2;
+        r0[0] = oacc[n][0];
+        r0[1] = oacc[n][1];
+        r1[0] = oacc[n][2];
+        r1[1] = oacc[n][3];
+    }
+    __syncthreads();
+    for (int e = tid; e < H * DC; e += NTHR) {
+        const int h = e / DC, d = e - h * DC;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kMmaWarps; ++w) M = fmaxf(M, mw[w * 16 + h]);
+        float L = 0.f, O = 0.f;
+        if (M != -INFINITY) {
+#pragma unroll
+            for (int w = 0; w < kMmaWarps; ++w) {
+                const float mwv = mw[w * 16 + h];
+                const float f = mwv == -INFINITY ? 0.f : __expf(mwv - M);
+                L = fmaf(f, lw[w * 16 + h], L);
+                O = fmaf(f, om[(w * 16 + h) * DC + d], O);
+            }
+        }
+        float* pp = part_ptr(ws, b, split, h, nsplit, H, DC);
+        if (d == 0) {
+            pp[0] = M;
+            pp[1] = L;
+        }
+        pp[2 + d] = O;
+    }
+}
+
+// Combine of the partial records: one CTA per (head, 32-dimension slice, batch
+// row), 8 warps, lane = dimension.  Per stream the maximum of the partial maxima
+// is found first (every warp reads all of them, 32 at a time), so the weighted
+// sums over the splits (warp w: splits w, w+8, ...) have no dependence between
+// iterations and their loads overlap; the warps' sums meet in shared memory and
+// the three streams are superposed with the gate softmax (and the HCA cumulative
+// mean for pos < r-1).
+constexpr int kCombWarps = 8;
+
+template <typename T>
+__global__ void __launch_bounds__(32 * kCombWarps) sa_decode_combine2_kernel(SaArgs a, const float* ws, int nsplit) {
+    const int DC = a.DC, H = a.H;
+    const int h = blockIdx.x;
+    const int d = blockIdx.y * 32 + (threadIdx.x & 31);
+    const int64_t b = blockIdx.z;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    __shared__ float wl[kCombWarps], wo[kCombWarps][32];
+    const int64_t Lkv = visible_len(a);
+    const DecodePlan p = make_plan(a, Lkv);
+    const int64_t pos = Lkv - 1;
+    const T* gp = static_cast<const T*>(a.gate);
+    const T* gr = a.gate4d ? gp + b * a.sg[0] + h * a.sg[1] : gp + b * a.sg[0];
+    const int64_t gs = a.gate4d ? a.sg[3] : a.sg[2];
+    const float g0 = load_as<float>(gr), g1 = load_as<float>(gr + gs), g2 = load_as<float>(gr + 2 * gs);
+    const float mg = fmaxf(g0, fmaxf(g1, g2));
+    const float e0 = expf(g0 - mg), e1 = expf(g1 - mg), e2 = expf(g2 - mg);
+    const float gsum = e0 + e1 + e2;
+    const float gate[3] = {e0 / gsum, e1 / gsum, e2 / gsum};
+    const int first[3] = {0, p.n_local, p.n_local + p.n_sparse};
+    const int cnt[3] = {p.n_local, p.n_sparse, p.n_hca};
+    const size_t rec = DC + 2;
+    const float* base = ws + ((size_t)b * nsplit * H + h) * rec;  // record of split k: base + k * H * rec
+    const size_t kstride = (size_t)H * rec;
+    float res = 0.f;
+    for (int s = 0; s < 3; ++s) {
+        if (s == 2 && pos < a.hca_r - 1) {
+            // cumulative mean of the latent prefix (sparse_attention.py:189-199)
+            if (warp == 0 && d < DC) {
+                const T* ckv = static_cast<const T*>(a.ckv) + b * a.sc[0];
+                float acc = 0.f;
+                for (int64_t j = 0; j <= pos; ++j) acc += load_as<float>(ckv + j * a.sc[1] + d * a.sc[2]);
+                res += gate[2] * (acc / float(pos + 1));
+            }
+            continue;
+        }
+        const float* sb = base + (size_t)first[s] * kstride;
+        float M = -INFINITY;
+        for (int k = lane; k < cnt[s]; k += 32) M = fmaxf(M, sb[k * kstride]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        if (M == -INFINITY) continue;  // the same in every warp
+        float L = 0.f, O = 0.f;
+#pragma unroll 8
+        for (int k = warp; k < cnt[s]; k += kCombWarps) {
+            const float* pp = sb + k * kstride;
+            const float mk = pp[0];
+            const float f = mk == -INFINITY ? 0.f : __expf(mk - M);
+            L = fmaf(f, pp[1], L);
+            if (d < DC) O = fmaf(f, pp[2 + d], O);
+        }
+        __syncthreads();
+        if (lane == 0) wl[warp] = L;
+        wo[warp][lane] = O;
+        __syncthreads();
+        if (warp == 0) {
+            float LL = 0.f, OO = 0.f;
+#pragma unroll
+            for (int w = 0; w < kCombWarps; ++w) {
+                LL += wl[w];
+                OO += wo[w][lane];
+            }
+            if (LL > 0.f) res += gate[s] * OO / LL;
+        }
+    }
+    if (warp == 0 && d < DC) store_from<T, float>(static_cast<T*>(a.out) + b * a.so[0] + h * a.so[2] + d * a.so[3], res);
+}
+
+bool tile_path_ok(const SaArgs& a, int es) {
+    if (es != 2 || a.DC != kMmaDC || a.H > 16) return false;
+    auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+    if (a.sc[2] != 1 || (a.sc[1] * es) % 16 || (a.sc[0] * es) % 16 || !al(a.ckv)) return false;
+    if (a.hca != nullptr && (a.sh[2] != 1 || (a.sh[1] * es) % 16 || (a.sh[0] * es) % 16 || !al(a.hca))) return false;
+    return true;
+}
+
 // Splits of the launch: exact for a host-known length, capacity-sized (every
 // split the largest visible table could need) for a device-held position.
 int decode_splits(const SaArgs& a) {
@@ -273,12 +556,26 @@ int launch_decode(SaArgs& a, int64_t B, cudaStream_t s) {
         return set_error(MABA_ERR_WORKSPACE, "sa_attention(decode): workspace of %zu bytes required, got %zu", need,
                          a.workspace_bytes);
     float* ws = static_cast<float*>(a.workspace);
-    const size_t smem = KT * (sizeof(int64_t) + sizeof(int)) + sizeof(float) * ((size_t)a.H * a.DC + (size_t)KT * (a.DC + 1));
-    auto k1 = sa_decode_partial_kernel_t<T>;
-    if (smem > 48 * 1024) cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    k1<<<dim3((unsigned)nsplit, (unsigned)B), 32 * a.H, smem, s>>>(a, ws, nsplit);
+    bool done = false;
+    if constexpr (sizeof(T) == 2) {
+        if (tile_path_ok(a, (int)sizeof(T))) {
+            const size_t smem = sizeof(T) * ((size_t)SPLIT_KEYS * kMmaLD + 16 * kMmaLD + kMmaWarps * 16 * kPLD) +
+                                sizeof(float) * 2 * kMmaWarps * 16 + sizeof(int64_t) * SPLIT_KEYS;
+            auto kern = sa_decode_mma_kernel<T>;
+            if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            kern<<<dim3((unsigned)nsplit, (unsigned)B), 32 * kMmaWarps, smem, s>>>(a, ws, nsplit);
+            done = true;
+        }
+    }
+    if (!done) {
+        const size_t smem = KT * (sizeof(int64_t) + sizeof(int)) + sizeof(float) * ((size_t)a.H * a.DC + (size_t)KT * (a.DC + 1));
+        auto k1 = sa_decode_partial_kernel_t<T>;
+        if (smem > 48 * 1024) cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        k1<<<dim3((unsigned)nsplit, (unsigned)B), 32 * a.H, smem, s>>>(a, ws, nsplit);
+    }
     MABA_TRY(check_launch("sa_attention(decode partial)"));
-    sa_decode_combine_kernel<T><<<(unsigned)B, 32 * a.H, 0, s>>>(a, ws, nsplit);
+    sa_decode_combine2_kernel<T><<<dim3((unsigned)a.H, (unsigned)ceil_div(a.DC, 32), (unsigned)B), 32 * kCombWarps, 0,
+                                   s>>>(a, ws, nsplit);
     return check_launch("sa_attention(decode combine)");
 }
 

@@ -206,6 +206,15 @@ def _lin(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
     return torch.matmul(x, w.t())
 
 
+def _lin_f32(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """x W^T with a float32 result (16-bit operands, float32 accumulation and output): the
+    products that feed the float32 residual stream and the logits skip a 16-bit rounding."""
+    if x.dtype == torch.float32:
+        return torch.matmul(x, w.t())
+    y = torch.mm(x.reshape(-1, x.shape[-1]), w.t(), out_dtype=torch.float32)
+    return y.view(*x.shape[:-1], w.shape[0])
+
+
 class MabaEngine:
     """The Maba v2 model on the sm_100a kernels, from a reference-format state dict.
 
@@ -251,21 +260,21 @@ class MabaEngine:
     @torch.no_grad()
     def forward(self, ids: torch.Tensor, last_only: bool = False, session: Optional["DecodeSession"] = None,
                 last_n: Optional[int] = None):
-        """Logits of every position ([B,T,V]; the last ``last_n`` positions only, or [B,1,V] with
-        ``last_only``) in float32 for a float32 engine and in the compute dtype otherwise;
+        """Float32 logits of every position ([B,T,V]; the last ``last_n`` positions only, or
+        [B,1,V] with ``last_only``);
         ``session`` also receives the decode caches (recurrent states, conv histories, latent /
         index-key caches and tables)."""
         s, dt = self.shape, self.dtype
         B, T = ids.shape
         Ntok = B * T
         ids = ids.to(self.device)
-        x = _lin(F.embedding(ids.reshape(-1), self.emb), self.w_emb_proj).float().contiguous()   # [N, D]
+        x = _lin_f32(F.embedding(ids.reshape(-1), self.emb), self.w_emb_proj).contiguous()   # [N, D] fp32
         h = torch.empty(Ntok, s.dim, dtype=dt, device=self.device)
         self._norm(x, None, None, self.layers[0].n1 if self.layers else self.final_norm, h)
         for li, L in enumerate(self.layers):
             y = self._sa_prefill(L, h, B, T, li, session) if L.attn else self._dgda_prefill(L, h, B, T, li, session)
             self._norm(x, y, L.g1, L.n2, h)
-            f = _lin(self._swiglu(_lin(h, L.w_gu)), L.w_down)
+            f = _lin_f32(self._swiglu(_lin(h, L.w_gu)), L.w_down)
             nxt = self.layers[li + 1].n1 if li + 1 < len(self.layers) else self.final_norm
             self._norm(x, f, L.g2, nxt, h)
         hv = h.view(B, T, s.dim)
@@ -273,8 +282,7 @@ class MabaEngine:
             hv = hv[:, -1:]
         elif last_n is not None:
             hv = hv[:, -last_n:]
-        logits = _lin(_lin(hv, self.w_head), self.emb)
-        return logits.float() if dt == torch.float32 else logits
+        return _lin_f32(_lin(hv, self.w_head), self.emb)
 
     def _dgda_prefill(self, L: _Layer, h, B, T, li, session):
         s, W = self.shape, L.mix
@@ -293,7 +301,7 @@ class MabaEngine:
         if session is not None:
             session.states[li].copy_(S)
             session.hists[li].copy_(torch.cat(nh, dim=1))
-        return _lin(o.transpose(1, 2).reshape(B * T, H * dv), W.w_o)
+        return _lin_f32(o.transpose(1, 2).reshape(B * T, H * dv), W.w_o)
 
     def _sa_prefill(self, L: _Layer, h, B, T, li, session):
         s, W = self.shape, L.mix
@@ -316,7 +324,7 @@ class MabaEngine:
             cache.cent[:, :cent.shape[1]] = cent
             if hca is not None:
                 cache.hca[:, :hca.shape[1]] = hca
-        return _lin(o_lat.reshape(B * T, H * dc), W.w_ov)
+        return _lin_f32(o_lat.reshape(B * T, H * dc), W.w_ov)
 
     # ------------------------------------------------------------------ decode
     def new_session(self, batch: int, max_len: int) -> "DecodeSession":
@@ -397,7 +405,7 @@ class DecodeSession:
         logits = self.engine.forward(ids, last_only=True, session=self)
         self.length = T
         self.pos_dev.fill_(T)
-        return logits.float()
+        return logits
 
     def _gemv(self, w, pro, x=None, aux=None, ids=None, epi=EPI_STORE, out=None, bias=None, gate=None, taps=None,
               hist=None, n_conv=0, alpha_end=0, ids_out=None, pos=None, ws=None):
