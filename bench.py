@@ -287,6 +287,10 @@ def config3_prefill(dev, steps: int = 3, warmup: int = 1, check_tokens: int = 25
                          "argmax_agree": float((got.argmax(-1) == want.argmax(-1)).double().mean()),
                          "tolerance": 2e-2}
         res["parity"]["ok"] = res["parity"]["max_rel"] <= 2e-2
+        # the reference's own bf16 run against its fp32 run: the noise floor of bf16 I/O
+        with torch.no_grad():
+            want16 = ref.to(torch.bfloat16)(ids[:1, :check_tokens].cpu()).logits.double()
+        res["parity"]["reference_bf16_vs_fp32_max_rel"] = float((want16 - want).abs().max() / want.abs().max())
     else:
         res["parity"] = {"unavailable": "no reference install under baseline/_ref"}
     del eng, out
@@ -544,8 +548,8 @@ SPLIT_TOKENS = 1 << 20
 def seq_split_prefill(torch, mb, dev, world, rank, barrier, total, reps=2):
     """The hot path (DGDA op + DG-Indexer + MABA-SA) over ONE sequence of `total` tokens cut
     into `world` contiguous segments, one per rank (maba_v2_architecture_b200.parallel),
-    sized by parallel.balanced_segments (later segments attend longer prefixes, so they are
-    shorter).  Every rank draws the whole sequence from one seed (config-2 distributions)
+    sized by parallel.split_bounds for equal work per rank (later segments attend longer
+    prefixes, the middle ranks also compute a DGDA transition).  Every rank draws the whole sequence from one seed (config-2 distributions)
     and keeps its segment.  DGDA exchanges the segment transitions (one all-gather of
     [1,H,64,128] fp32 payloads on its own communicator); MABA-SA sends each rank's latent
     rows, centroids and pooled rows to the later ranks only (parallel.exchange_prefix) into
@@ -560,7 +564,7 @@ def seq_split_prefill(torch, mb, dev, world, rank, barrier, total, reps=2):
     from maba_v2_architecture_b200 import parallel as par
     from maba_v2_architecture_b200.ops import absorb_queries
 
-    bounds = par.balanced_segments(total, world)
+    bounds = par.split_bounds(total, world)
     a0, a1 = bounds[rank], bounds[rank + 1]
     Ls = a1 - a0
     g = torch.Generator(device=dev).manual_seed(4000)   # the same sequence on every rank

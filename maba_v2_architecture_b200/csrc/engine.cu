@@ -26,6 +26,7 @@
 // loads (8 bf16), multiplying each chunk with all NB (<= 8) input vectors held
 // in shared memory; every CTA recomputes the input normalisation (a few KB).
 #include "common.cuh"
+#include "pdl.cuh"
 
 namespace maba {
 namespace {
@@ -99,13 +100,6 @@ __device__ __forceinline__ void unpack8(const Chunk8<T>& c, float* v) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) v[i] = Cvt<T>::to_f(e[i]);
 }
-
-// Programmatic dependent launch: the next kernel of the stream may start once every
-// CTA of this one has started, and runs its independent prologue (weight loads) while
-// this one finishes; griddep_wait() blocks until the previous kernel has completed and
-// its writes are visible.  Both are no-ops for a kernel launched without the attribute.
-__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
-__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.f + expf(-x)); }
 __device__ __forceinline__ float sigmoid_f(float x) { return 1.f / (1.f + expf(-x)); }
@@ -357,14 +351,15 @@ __global__ void __launch_bounds__(kStateThreads) dgda_state_kernel(const float* 
     float* S = state + ((int64_t)b * H + h) * dk * dv;
     const int j = j0 + tx;
     const bool colv = j < dv;
-    // the state does not depend on the previous kernel (only this kernel writes it)
+    // the state is read after the wait: its last writer (this layer's step before) is only
+    // known to be complete once every kernel before this one is
+    griddep_wait();
     float sd[64 / RY];
 #pragma unroll
     for (int r = 0; r < 64 / RY; ++r) {
         const int i = ty + RY * r;
         sd[r] = (i < dk && colv) ? S[(int64_t)i * dv + j] : 0.f;
     }
-    griddep_wait();
     const float* f = feats + (int64_t)b * ldf;
     if (tid < dk) {
         sq[tid] = f[off_q + h * dk + tid];
@@ -419,24 +414,7 @@ __global__ void __launch_bounds__(kStateThreads) dgda_state_kernel(const float* 
     }
 }
 
-// Launch with the programmatic-stream-serialization attribute (see griddep_wait).
-template <typename... KArgs, typename... Args>
-int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = grid;
-    cfg.blockDim = block;
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, args...);
-    if (e != cudaSuccess)
-        return set_error(MABA_ERR_CUDA, "launch: %s (%s)", cudaGetErrorName(e), cudaGetErrorString(e));
-    return MABA_OK;
-}
+
 
 // prefill: x += gate * y (optional), h = x * rsqrt(mean(x^2) + eps) * w; one warp per row
 template <typename TO, typename TY>

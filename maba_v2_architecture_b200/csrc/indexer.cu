@@ -1160,10 +1160,18 @@ __global__ void decode_append_kernel(AppendArgs a) {
         const bool padded = pos + 1 < start + a.block;
         for (int d = threadIdx.x; d < a.DI; d += blockDim.x) {
             float sum = 0.f, mx = padded ? 0.f : -INFINITY;
-            for (int64_t t = start; t <= pos; ++t) {
-                const float x = load_as<float>(kidx + b * a.s_k[0] + t * a.s_k[1] + d * a.s_k[2]);
-                sum += x;
-                mx = x > mx ? x : mx;
+            // rows in order (the pooling kernel's fp32 sum); eight loads in flight at a time
+            for (int64_t t0 = start; t0 <= pos; t0 += 8) {
+                float xs[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u)
+                    xs[u] = t0 + u <= pos ? load_as<float>(kidx + b * a.s_k[0] + (t0 + u) * a.s_k[1] + d * a.s_k[2]) : 0.f;
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    if (t0 + u > pos) break;
+                    sum += xs[u];
+                    mx = xs[u] > mx ? xs[u] : mx;
+                }
             }
             store_from<T, float>(cent + b * a.s_ce[0] + blk * a.s_ce[1] + d * a.s_ce[2],
                                  0.5f * (sum / float(a.block) + mx));
@@ -1175,7 +1183,15 @@ __global__ void decode_append_kernel(AppendArgs a) {
             T* hca = static_cast<T*>(a.hca);
             for (int d = threadIdx.x; d < a.DC; d += blockDim.x) {
                 float sum = 0.f;
-                for (int64_t t = pos + 1 - a.r; t <= pos; ++t) sum += load_as<float>(c + b * a.s_c[0] + t * a.s_c[1] + d * a.s_c[2]);
+                for (int64_t t0 = pos + 1 - a.r; t0 <= pos; t0 += 8) {
+                    float xs[8];
+#pragma unroll
+                    for (int u = 0; u < 8; ++u)
+                        xs[u] = t0 + u <= pos ? load_as<float>(c + b * a.s_c[0] + (t0 + u) * a.s_c[1] + d * a.s_c[2]) : 0.f;
+#pragma unroll
+                    for (int u = 0; u < 8; ++u)
+                        if (t0 + u <= pos) sum += xs[u];
+                }
                 store_from<T, float>(hca + b * a.s_h[0] + g * a.s_h[1] + d * a.s_h[2], sum / float(a.r));
             }
         }

@@ -103,6 +103,65 @@ def balanced_segments(total: int, world: int, unit: int = 64, flat: float = 67.0
     return bounds
 
 
+# measured per-token costs on one B200 (ms per 1,000 tokens, bf16, H = 10): the attention
+# of a query at position p (in thousands of tokens) costs ATTN_FLAT + ATTN_SLOPE * p (the
+# pooled-HCA stream grows with the prefix), the DGDA prefill DGDA_MS; a segment transition
+# costs about TRANSITION times its prefill
+ATTN_FLAT, ATTN_SLOPE, DGDA_MS, TRANSITION = 0.0159, 7.54e-5, 0.0092, 1.3
+
+
+def split_bounds(total: int, world: int, unit: int = 64, attn_flat: float = ATTN_FLAT,
+                 attn_slope: float = ATTN_SLOPE, dgda: float = DGDA_MS, transition: float = TRANSITION) -> List[int]:
+    """Segment boundaries [0, b_1, ..., total] (multiples of `unit`) that equalise each rank's
+    whole share of the split prefill: its queries' attention (flat + slope * position per
+    token) plus its DGDA role -- rank 0 one prefill of its segment, ranks 1..P-2 a transition
+    and a prefill, the last rank a prefill.  Found by bisection on the per-rank budget: each
+    rank takes the longest segment that fits it, and the last rank must fit too."""
+    if world == 1:
+        return [0, total]
+    k = 1e-3  # costs are per thousand tokens
+
+    def cost(r, a, b):
+        n = (b - a) * k
+        attn = attn_flat * n + 0.5 * attn_slope * ((b * k) ** 2 - (a * k) ** 2)
+        role = 1.0 if r in (0, world - 1) else 1.0 + transition
+        return attn + role * dgda * n
+
+    def assign(budget):
+        bounds, a = [0], 0
+        for r in range(world - 1):
+            lo, hi = a + unit, total - (world - 1 - r) * unit
+            if lo > hi:
+                return None
+            if cost(r, a, lo) > budget:
+                b = lo
+            else:
+                while hi - lo > unit:          # largest b with cost <= budget
+                    mid = (lo + hi) // (2 * unit) * unit
+                    if mid <= lo:
+                        break
+                    if cost(r, a, mid) <= budget:
+                        lo = mid
+                    else:
+                        hi = mid
+                b = hi if cost(r, a, hi) <= budget else lo
+            bounds.append(b)
+            a = b
+        bounds.append(total)
+        return bounds
+
+    lo_b, hi_b = 0.0, cost(0, 0, total) * 2.5
+    best = assign(hi_b)
+    for _ in range(60):
+        mid = 0.5 * (lo_b + hi_b)
+        bd = assign(mid)
+        if bd is not None and cost(world - 1, bd[-2], total) <= mid:
+            hi_b, best = mid, bd
+        else:
+            lo_b = mid
+    return best
+
+
 # ------------------------------------------------------------------ DGDA
 def dgda_segment_phase_a(q, k, v, b, w, la, backend=None):
     """Local: the segment's transition."""

@@ -138,6 +138,22 @@ def test_balanced_segments(world):
     assert bnd[1] - bnd[0] >= bnd[-1] - bnd[-2]  # later (longer-prefix) segments are shorter
 
 
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_split_bounds_equalise_rank_costs(world):
+    total = 1 << 20
+    bnd = par.split_bounds(total, world)
+    assert bnd[0] == 0 and bnd[-1] == total and len(bnd) == world + 1
+    assert all(b % 64 == 0 for b in bnd) and all(x < y for x, y in zip(bnd, bnd[1:]))
+    k = 1e-3
+
+    def cost(r, a, b):
+        n = (b - a) * k
+        role = 1.0 if r in (0, world - 1) else 1.0 + par.TRANSITION
+        return par.ATTN_FLAT * n + 0.5 * par.ATTN_SLOPE * ((b * k) ** 2 - (a * k) ** 2) + role * par.DGDA_MS * n
+    c = [cost(r, a, b) for r, (a, b) in enumerate(zip(bnd, bnd[1:]))]
+    assert max(c) / min(c) < 1.01
+
+
 def test_sa_split_rejects_ragged_segments():
     qhat, c, qi, ki, gate = _sa_inputs(4, T=96)
     with pytest.raises(ValueError, match="multiple of block"):
