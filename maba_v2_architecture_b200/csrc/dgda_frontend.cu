@@ -16,6 +16,7 @@
 // of k is a shuffle reduction over the d/8 lanes of a head (d/8 a power of two
 // <= 32, so a head never straddles a warp).
 #include "common.cuh"
+#include "activations.cuh"
 
 namespace maba {
 namespace {
@@ -91,13 +92,6 @@ __device__ __forceinline__ void store8<__nv_bfloat16>(__nv_bfloat16* p, int64_t 
     }
 }
 
-__device__ __forceinline__ float silu_f(float x) { return x / (1.f + expf(-x)); }
-__device__ __forceinline__ float sigmoid_f(float x) { return 1.f / (1.f + expf(-x)); }
-// -softplus(x) clamped at -14; softplus(x) = x above 20 (torch's threshold), log1p(e^x) below
-__device__ __forceinline__ float neg_softplus_clamped(float x) {
-    const float sp = x > 20.f ? x : log1pf(expf(x));
-    return fmaxf(-sp, -14.f);
-}
 
 template <typename T, int K>
 __global__ void __launch_bounds__(kFeThreads) dgda_frontend_kernel(FeArgs a, int64_t nruns) {
@@ -191,6 +185,114 @@ __global__ void __launch_bounds__(kFeThreads) dgda_frontend_kernel(FeArgs a, int
             for (int i = 0; i < kVec; ++i) y[i] *= inv;
         }
         if (ok) store8<T>(out + t * sec.so[1], sec.so[2], y);
+    }
+}
+
+// Tiled variant for sections of a multiple of 128 channels (heads of dk <= 128
+// lanes x 8 channels): one CTA owns 32 tokens x 128 channels of one section.  The
+// tile's input rows and the K-1 rows before it (or the conv history) are staged in
+// shared memory with 16-byte loads, all in flight at once, together with the 128
+// channels' taps; thread (token pair, channel group of 8) then forms its outputs
+// from shared memory, so the loads of a token's neighbours cost no extra DRAM
+// traffic and every thread has its whole input staged before it computes.
+constexpr int kTileTok = 32;
+constexpr int kTileCh = 128;
+
+template <typename T, int K>
+__global__ void __launch_bounds__(256) dgda_frontend_tile_kernel(FeArgs a, int64_t ntt, int nct) {
+    constexpr int ROWS = kTileTok + K - 1;
+    constexpr int LDS = kTileCh + 8;  // padded row (16-bit elements)
+    __shared__ __align__(16) T xs[ROWS][LDS];
+    __shared__ float taps[kTileCh][K];
+    const int tid = threadIdx.x;
+    int64_t blk = blockIdx.x;
+    const int ct = (int)(blk % nct);  // 128-channel chunk over the six sections
+    blk /= nct;
+    const int64_t tt = blk % ntt;
+    const int64_t b = blk / ntt;
+    // section of this chunk (sections are multiples of 128 channels)
+    int s = 0, cbase = ct * kTileCh;
+#pragma unroll
+    for (int i = 0; i < 5; ++i)
+        if (cbase >= a.C[s]) { cbase -= a.C[s]; ++s; }
+    const FeSection& sec = a.sec[s];
+    const T* x = static_cast<const T*>(sec.x) + b * sec.sx[0] + (int64_t)cbase * sec.sx[2];
+    const int64_t t0 = tt * kTileTok;
+    const bool conv = s < 3;
+    // stage rows t0-(K-1) .. t0+31: 16 chunks of 8 channels per row
+    for (int e = tid; e < ROWS * 16; e += 256) {
+        const int r = e >> 4, c8 = (e & 15) * 8;
+        const int64_t t = t0 - (K - 1) + r;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (t >= 0 && t < a.L) {
+            v = *reinterpret_cast<const uint4*>(x + t * sec.sx[1] + c8);
+        } else if (t < 0 && conv && a.hist[s] != nullptr) {
+            T* h8 = reinterpret_cast<T*>(&v);
+            const int64_t hj = (K - 1) + t;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int64_t off = b * a.sh[s][0] + (int64_t)(cbase + c8 + i) * a.sh[s][1] + hj * a.sh[s][2];
+                const float hv = a.hist_f32 ? static_cast<const float*>(a.hist[s])[off]
+                                            : Cvt<T>::to_f(static_cast<const T*>(a.hist[s])[off]);
+                h8[i] = Cvt<T>::from_f(hv);
+            }
+        }
+        *reinterpret_cast<uint4*>(&xs[r][c8]) = v;
+    }
+    if (conv) {
+        const T* cw = static_cast<const T*>(a.conv[s]);
+        for (int e = tid; e < kTileCh * K; e += 256) {
+            const int c = e / K, j = e - (e / K) * K;
+            taps[c][j] = Cvt<T>::to_f(cw[(int64_t)(cbase + c) * a.sconv[s][0] + j * a.sconv[s][1]]);
+        }
+    }
+    __syncthreads();
+    const int g = tid & 15;          // channel group (8 channels)
+    const int tp = tid >> 4;         // token pair 0..15
+    T* out = static_cast<T*>(sec.out) + b * sec.so[0] + (int64_t)(cbase + g * 8) * sec.so[2];
+    float w[kVec][K];
+    if (conv)
+#pragma unroll
+        for (int i = 0; i < kVec; ++i)
+#pragma unroll
+            for (int j = 0; j < K; ++j) w[i][j] = taps[g * 8 + i][j];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+        const int r = tp * 2 + u;    // token t0 + r, staged at row r + K - 1
+        const int64_t t = t0 + r;
+        float y[kVec];
+        if (conv) {
+            float acc[kVec];
+#pragma unroll
+            for (int i = 0; i < kVec; ++i) acc[i] = 0.f;
+#pragma unroll
+            for (int j = 0; j < K; ++j) {
+                const uint4 u = *reinterpret_cast<const uint4*>(&xs[r + j][g * 8]);
+                const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+                for (int i = 0; i < kVec; ++i) acc[i] = fmaf(w[i][j], Cvt<T>::to_f(e[i]), acc[i]);
+            }
+#pragma unroll
+            for (int i = 0; i < kVec; ++i) y[i] = silu_f(acc[i]);
+        } else {
+            const uint4 u = *reinterpret_cast<const uint4*>(&xs[r + K - 1][g * 8]);
+            const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+            for (int i = 0; i < kVec; ++i) {
+                const float v = Cvt<T>::to_f(e[i]);
+                y[i] = s == 3 ? neg_softplus_clamped(v) : sigmoid_f(v);
+            }
+        }
+        float ss = 0.f;
+#pragma unroll
+        for (int i = 0; i < kVec; ++i) ss = fmaf(y[i], y[i], ss);
+        for (int o = a.hw >> 1; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (s == 1) {
+            const float inv = 1.f / (sqrtf(ss) + a.eps);
+#pragma unroll
+            for (int i = 0; i < kVec; ++i) y[i] *= inv;
+        }
+        if (t < a.L) store8<T>(out + t * sec.so[1], sec.so[2], y);
     }
 }
 
@@ -301,9 +403,35 @@ extern "C" int maba_dgda_frontend(const maba_tensor* proj, const maba_tensor* co
     if (B == 0 || L == 0) return MABA_OK;
     cudaStream_t st = as_stream(stream);
     const int64_t nruns = ceil_div(L, kRun);
-    const int64_t threads = B * nruns * a.per_run;
+    bool tiled = dt != MABA_F32 && a.hw <= 16;
+    for (int sct = 0; sct < 6; ++sct)
+        tiled = tiled && a.C[sct] % kTileCh == 0 && proj[sct].stride[2] == 1 && proj[sct].stride[1] % 8 == 0 &&
+                proj[sct].stride[0] % 8 == 0 && (reinterpret_cast<uintptr_t>(proj[sct].data) & 15u) == 0;
+    if (tiled) {
+        const int64_t ntt = ceil_div(L, kTileTok);
+        const int nct = (a.C[0] + a.C[1] + a.C[2] + a.C[3] + a.C[4] + a.C[5]) / kTileCh;
+        const unsigned tgrid = (unsigned)(B * ntt * nct);
+        MABA_TRY(MABA_DISPATCH_FLOAT(dt, "dgda_frontend", [&] {
+            if constexpr (sizeof(T) != 2) {
+                return set_error(MABA_ERR_DTYPE, "dgda_frontend: tiled path is 16-bit");
+            } else {
+                switch (K) {
+                    case 1: dgda_frontend_tile_kernel<T, 1><<<tgrid, 256, 0, st>>>(a, ntt, nct); break;
+                    case 2: dgda_frontend_tile_kernel<T, 2><<<tgrid, 256, 0, st>>>(a, ntt, nct); break;
+                    case 3: dgda_frontend_tile_kernel<T, 3><<<tgrid, 256, 0, st>>>(a, ntt, nct); break;
+                    case 4: dgda_frontend_tile_kernel<T, 4><<<tgrid, 256, 0, st>>>(a, ntt, nct); break;
+                    case 5: dgda_frontend_tile_kernel<T, 5><<<tgrid, 256, 0, st>>>(a, ntt, nct); break;
+                    case 6: dgda_frontend_tile_kernel<T, 6><<<tgrid, 256, 0, st>>>(a, ntt, nct); break;
+                    case 7: dgda_frontend_tile_kernel<T, 7><<<tgrid, 256, 0, st>>>(a, ntt, nct); break;
+                    default: dgda_frontend_tile_kernel<T, 8><<<tgrid, 256, 0, st>>>(a, ntt, nct); break;
+                }
+                return check_launch("dgda_frontend(tile)");
+            }
+        }));
+    }
+    const int64_t threads = tiled ? 0 : B * nruns * a.per_run;
     const unsigned grid = (unsigned)ceil_div(threads, kFeThreads);
-    MABA_TRY(MABA_DISPATCH_FLOAT(dt, "dgda_frontend", [&] {
+    if (!tiled) MABA_TRY(MABA_DISPATCH_FLOAT(dt, "dgda_frontend", [&] {
         if constexpr (sizeof(T) == 8) {
             return set_error(MABA_ERR_DTYPE, "dgda_frontend: float64");
         } else {

@@ -26,6 +26,7 @@
 // loads (8 bf16), multiplying each chunk with all NB (<= 8) input vectors held
 // in shared memory; every CTA recomputes the input normalisation (a few KB).
 #include "common.cuh"
+#include "activations.cuh"
 #include "pdl.cuh"
 
 namespace maba {
@@ -101,12 +102,6 @@ __device__ __forceinline__ void unpack8(const Chunk8<T>& c, float* v) {
     for (int i = 0; i < 8; ++i) v[i] = Cvt<T>::to_f(e[i]);
 }
 
-__device__ __forceinline__ float silu_f(float x) { return x / (1.f + expf(-x)); }
-__device__ __forceinline__ float sigmoid_f(float x) { return 1.f / (1.f + expf(-x)); }
-__device__ __forceinline__ float neg_softplus_clamped(float x) {
-    const float sp = x > 20.f ? x : log1pf(expf(x));
-    return fmaxf(-sp, -14.f);
-}
 // (value desc, index asc) as one unsigned key: larger key = better
 __device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
     unsigned int u = __float_as_uint(v);
@@ -416,7 +411,88 @@ __global__ void __launch_bounds__(kStateThreads) dgda_state_kernel(const float* 
 
 
 
-// prefill: x += gate * y (optional), h = x * rsqrt(mean(x^2) + eps) * w; one warp per row
+// prefill: x += gate * y (optional), h = x * rsqrt(mean(x^2) + eps) * w; one warp per row.
+// Rows of D = 128 * NV elements (and unit column strides) take the vector path: every lane
+// holds 4 consecutive elements of NV 128-element slices, all loads issued at once.
+template <typename T> __device__ __forceinline__ void store4(T* p, float a, float b, float c, float d) {
+    p[0] = Cvt<T>::from_f(a);
+    p[1] = Cvt<T>::from_f(b);
+    p[2] = Cvt<T>::from_f(c);
+    p[3] = Cvt<T>::from_f(d);
+}
+template <> __device__ __forceinline__ void store4<float>(float* p, float a, float b, float c, float d) {
+    *reinterpret_cast<float4*>(p) = make_float4(a, b, c, d);
+}
+template <> __device__ __forceinline__ void store4<__nv_bfloat16>(__nv_bfloat16* p, float a, float b, float c, float d) {
+    __nv_bfloat162 lo = __floats2bfloat162_rn(a, b), hi = __floats2bfloat162_rn(c, d);
+    uint2 u;
+    u.x = *reinterpret_cast<uint32_t*>(&lo);
+    u.y = *reinterpret_cast<uint32_t*>(&hi);
+    *reinterpret_cast<uint2*>(p) = u;
+}
+template <> __device__ __forceinline__ void store4<__half>(__half* p, float a, float b, float c, float d) {
+    __half2 lo = __floats2half2_rn(a, b), hi = __floats2half2_rn(c, d);
+    uint2 u;
+    u.x = *reinterpret_cast<uint32_t*>(&lo);
+    u.y = *reinterpret_cast<uint32_t*>(&hi);
+    *reinterpret_cast<uint2*>(p) = u;
+}
+template <typename T> __device__ __forceinline__ float4 load4(const T* p) {
+    return make_float4(Cvt<T>::to_f(p[0]), Cvt<T>::to_f(p[1]), Cvt<T>::to_f(p[2]), Cvt<T>::to_f(p[3]));
+}
+template <> __device__ __forceinline__ float4 load4<float>(const float* p) { return *reinterpret_cast<const float4*>(p); }
+template <> __device__ __forceinline__ float4 load4<__nv_bfloat16>(const __nv_bfloat16* p) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+    const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+    return make_float4(a.x, a.y, b.x, b.y);
+}
+template <> __device__ __forceinline__ float4 load4<__half>(const __half* p) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+    return make_float4(a.x, a.y, b.x, b.y);
+}
+
+template <typename TO, typename TY, int NV>
+__global__ void rmsnorm_residual_vec_kernel(float* x, int64_t ldx, const TY* y, int64_t ldy, const float* gate,
+                                            const TO* w, float eps, TO* h, int64_t ldh, int64_t N) {
+    constexpr int D = 128 * NV;
+    const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= N) return;
+    float* xr = x + row * ldx;
+    float4 v[NV];
+#pragma unroll
+    for (int j = 0; j < NV; ++j) v[j] = *reinterpret_cast<const float4*>(xr + j * 128 + lane * 4);
+    if (y != nullptr) {
+        float4 yv[NV];
+#pragma unroll
+        for (int j = 0; j < NV; ++j) yv[j] = load4<TY>(y + row * ldy + j * 128 + lane * 4);
+#pragma unroll
+        for (int j = 0; j < NV; ++j) {
+            const float4 g = *reinterpret_cast<const float4*>(gate + j * 128 + lane * 4);
+            v[j].x = fmaf(g.x, yv[j].x, v[j].x);
+            v[j].y = fmaf(g.y, yv[j].y, v[j].y);
+            v[j].z = fmaf(g.z, yv[j].z, v[j].z);
+            v[j].w = fmaf(g.w, yv[j].w, v[j].w);
+            *reinterpret_cast<float4*>(xr + j * 128 + lane * 4) = v[j];
+        }
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) ss += v[j].x * v[j].x + v[j].y * v[j].y + v[j].z * v[j].z + v[j].w * v[j].w;
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float r = rsqrtf(ss / (float)D + eps);
+    if (h == nullptr) return;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+        const float4 wv = load4<TO>(w + j * 128 + lane * 4);
+        store4<TO>(h + row * ldh + j * 128 + lane * 4, v[j].x * r * wv.x, v[j].y * r * wv.y, v[j].z * r * wv.z,
+                   v[j].w * r * wv.w);
+    }
+}
+
 template <typename TO, typename TY>
 __global__ void rmsnorm_residual_kernel(float* x, int64_t ldx, const TY* y, int64_t ldy, const float* gate,
                                         const TO* w, float eps, TO* h, int64_t ldh, int64_t N, int D) {
@@ -439,6 +515,25 @@ __global__ void rmsnorm_residual_kernel(float* x, int64_t ldx, const TY* y, int6
     for (int k = lane; k < D; k += 32) h[row * ldh + k] = Cvt<TO>::from_f(xr[k] * r * Cvt<TO>::to_f(w[k]));
 }
 
+// silu(gate) * up, 8 outputs per thread (16-byte loads and stores where I % 8 == 0)
+template <typename T>
+__global__ void swiglu_vec_kernel(const T* u, int64_t ldu, T* out, int64_t ldo, int64_t N, int I) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int per_row = I / 8;
+    if (i >= N * per_row) return;
+    const int64_t row = i / per_row;
+    const int c = (int)(i - row * per_row) * 8;
+    const uint4 gu = *reinterpret_cast<const uint4*>(u + row * ldu + c);
+    const uint4 uu = *reinterpret_cast<const uint4*>(u + row * ldu + I + c);
+    const T* g8 = reinterpret_cast<const T*>(&gu);
+    const T* u8 = reinterpret_cast<const T*>(&uu);
+    uint4 o;
+    T* o8 = reinterpret_cast<T*>(&o);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) o8[k] = Cvt<T>::from_f(silu_f(Cvt<T>::to_f(g8[k])) * Cvt<T>::to_f(u8[k]));
+    *reinterpret_cast<uint4*>(out + row * ldo + c) = o;
+}
+
 template <typename T>
 __global__ void swiglu_kernel(const T* u, int64_t ldu, T* out, int64_t ldo, int64_t N, int I) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -448,6 +543,25 @@ __global__ void swiglu_kernel(const T* u, int64_t ldu, T* out, int64_t ldo, int6
     const float g = Cvt<T>::to_f(u[row * ldu + c]);
     const float v = Cvt<T>::to_f(u[row * ldu + I + c]);
     out[row * ldo + c] = Cvt<T>::from_f(silu_f(g) * v);
+}
+
+template <typename TO, typename TY>
+void launch_rmsnorm(bool vec, int nv, unsigned grid, cudaStream_t s, float* x, int64_t ldx, const TY* y, int64_t ldy,
+                    const float* gate, const TO* w, float eps, TO* h, int64_t ldh, int64_t N, int D) {
+    if (!vec) {
+        rmsnorm_residual_kernel<TO, TY><<<grid, 256, 0, s>>>(x, ldx, y, ldy, gate, w, eps, h, ldh, N, D);
+        return;
+    }
+    switch (nv) {
+        case 1: rmsnorm_residual_vec_kernel<TO, TY, 1><<<grid, 256, 0, s>>>(x, ldx, y, ldy, gate, w, eps, h, ldh, N); break;
+        case 2: rmsnorm_residual_vec_kernel<TO, TY, 2><<<grid, 256, 0, s>>>(x, ldx, y, ldy, gate, w, eps, h, ldh, N); break;
+        case 3: rmsnorm_residual_vec_kernel<TO, TY, 3><<<grid, 256, 0, s>>>(x, ldx, y, ldy, gate, w, eps, h, ldh, N); break;
+        case 4: rmsnorm_residual_vec_kernel<TO, TY, 4><<<grid, 256, 0, s>>>(x, ldx, y, ldy, gate, w, eps, h, ldh, N); break;
+        case 5: rmsnorm_residual_vec_kernel<TO, TY, 5><<<grid, 256, 0, s>>>(x, ldx, y, ldy, gate, w, eps, h, ldh, N); break;
+        case 6: rmsnorm_residual_vec_kernel<TO, TY, 6><<<grid, 256, 0, s>>>(x, ldx, y, ldy, gate, w, eps, h, ldh, N); break;
+        case 7: rmsnorm_residual_vec_kernel<TO, TY, 7><<<grid, 256, 0, s>>>(x, ldx, y, ldy, gate, w, eps, h, ldh, N); break;
+        default: rmsnorm_residual_vec_kernel<TO, TY, 8><<<grid, 256, 0, s>>>(x, ldx, y, ldy, gate, w, eps, h, ldh, N); break;
+    }
 }
 
 int wdtype_ok(int dt) { return dt == MABA_F32 || dt == MABA_BF16 || dt == MABA_F16; }
@@ -527,13 +641,17 @@ extern "C" int maba_rmsnorm_residual(const maba_tensor* x, const maba_tensor* y,
         } else {
             const T* wp = has_h ? static_cast<const T*>(weight->data) : nullptr;
             T* hp = has_h ? static_cast<T*>(h_out->data) : nullptr;
-            if (has_y && y->dtype == MABA_F32 && odt != MABA_F32)
-                rmsnorm_residual_kernel<T, float><<<grid, 256, 0, s>>>(
-                    xp, x->stride[0], static_cast<const float*>(y->data), ldy, gp, wp, eps, hp, ldh, N, (int)D);
-            else
-                rmsnorm_residual_kernel<T, T><<<grid, 256, 0, s>>>(
-                    xp, x->stride[0], has_y ? static_cast<const T*>(y->data) : nullptr, ldy, gp, wp, eps, hp, ldh, N,
-                    (int)D);
+            const bool yf = has_y && y->dtype == MABA_F32 && odt != MABA_F32;
+            const bool vec = D % 128 == 0 && D / 128 <= 8 && x->stride[0] % 4 == 0 && (!has_y || y->stride[0] % 4 == 0) &&
+                             (!has_h || h_out->stride[0] % 4 == 0) && (reinterpret_cast<uintptr_t>(xp) & 15u) == 0;
+            auto go = [&](auto ty_tag) {
+                using TY = decltype(ty_tag);
+                launch_rmsnorm<T, TY>(vec, (int)(D / 128), grid, s, xp, x->stride[0],
+                                      has_y ? static_cast<const TY*>(y->data) : nullptr, ldy, gp, wp, eps, hp, ldh, N,
+                                      (int)D);
+            };
+            if (yf) go(float{});
+            else go(T{});
             return check_launch("rmsnorm_residual");
         }
     });
@@ -553,8 +671,15 @@ extern "C" int maba_swiglu(const maba_tensor* u, const maba_tensor* out, void* s
         if constexpr (sizeof(T) == 8) {
             return set_error(MABA_ERR_DTYPE, "swiglu: float64");
         } else {
-            swiglu_kernel<T><<<(unsigned)ceil_div(N * I, 256), 256, 0, s>>>(
-                static_cast<const T*>(u->data), u->stride[0], static_cast<T*>(out->data), out->stride[0], N, (int)I);
+            const bool vec = sizeof(T) == 2 && I % 8 == 0 && u->stride[0] % 8 == 0 && out->stride[0] % 8 == 0 &&
+                             (reinterpret_cast<uintptr_t>(u->data) & 15u) == 0 &&
+                             (reinterpret_cast<uintptr_t>(out->data) & 15u) == 0;
+            if (vec)
+                swiglu_vec_kernel<T><<<(unsigned)ceil_div(N * (I / 8), 256), 256, 0, s>>>(
+                    static_cast<const T*>(u->data), u->stride[0], static_cast<T*>(out->data), out->stride[0], N, (int)I);
+            else
+                swiglu_kernel<T><<<(unsigned)ceil_div(N * I, 256), 256, 0, s>>>(
+                    static_cast<const T*>(u->data), u->stride[0], static_cast<T*>(out->data), out->stride[0], N, (int)I);
             return check_launch("swiglu");
         }
     });

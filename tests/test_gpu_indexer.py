@@ -76,8 +76,8 @@ def test_topk_cases(ci):
     oidx, osc = OI.index_topk(q.numpy(), cn, lambda_dist=lam, top_k=top_k, return_scores=True)
     np.testing.assert_array_equal(sc.cpu().numpy(), osc)          # bit-exact scores (incl. -inf)
     np.testing.assert_array_equal(idx.cpu().numpy(), oidx)        # bit-exact indices (incl. filler rule)
-    ties = check_topk_rule(g["idx"], osc, np.arange(L) // 64, top_k)
-    assert ties <= max(2, L * B // 200)
+    # against the reference's own indices: measured 0 tie-classified rows in every case
+    assert check_topk_rule(g["idx"], osc, np.arange(L) // 64, top_k) == 0
 
 
 def test_topk_monotone_and_clamp():
@@ -152,7 +152,7 @@ def test_config2_full_size():
                               rows=rows)
     got = idx[0, torch.as_tensor(rows, device=DEV)].cpu().numpy()
     np.testing.assert_array_equal(got, oidx[0])
-    assert check_topk_rule(g["idx"][None], osc, rows // 64, 32) <= 5
+    assert check_topk_rule(g["idx"][None], osc, rows // 64, 32) == 0  # measured: no tie rows
     # every row: first min(32, qb+1) entries are distinct causal blocks, fillers ascending after them
     qb = torch.arange(65536, device=DEV) // 64
     nvalid = torch.clamp(qb + 1, max=32)
