@@ -189,13 +189,14 @@ __global__ void __launch_bounds__(kFeThreads) dgda_frontend_kernel(FeArgs a, int
 }
 
 // Tiled variant for sections of a multiple of 128 channels (heads of dk <= 128
-// lanes x 8 channels): one CTA owns 32 tokens x 128 channels of one section.  The
+// lanes x 8 channels): one CTA owns 128 tokens x 128 channels of one section.  The
 // tile's input rows and the K-1 rows before it (or the conv history) are staged in
 // shared memory with 16-byte loads, all in flight at once, together with the 128
-// channels' taps; thread (token pair, channel group of 8) then forms its outputs
+// channels' taps; thread (token group, channel group of 8) then forms its outputs
 // from shared memory, so the loads of a token's neighbours cost no extra DRAM
-// traffic and every thread has its whole input staged before it computes.
-constexpr int kTileTok = 32;
+// traffic and every thread has its whole input staged before it computes (eight
+// 16-byte loads in flight per thread).
+constexpr int kTileTok = 128;
 constexpr int kTileCh = 128;
 
 template <typename T, int K>
@@ -248,7 +249,7 @@ __global__ void __launch_bounds__(256) dgda_frontend_tile_kernel(FeArgs a, int64
     }
     __syncthreads();
     const int g = tid & 15;          // channel group (8 channels)
-    const int tp = tid >> 4;         // token pair 0..15
+    const int tp = tid >> 4;         // token group 0..15 (kTileTok / 16 consecutive tokens)
     T* out = static_cast<T*>(sec.out) + b * sec.so[0] + (int64_t)(cbase + g * 8) * sec.so[2];
     float w[kVec][K];
     if (conv)
@@ -256,9 +257,10 @@ __global__ void __launch_bounds__(256) dgda_frontend_tile_kernel(FeArgs a, int64
         for (int i = 0; i < kVec; ++i)
 #pragma unroll
             for (int j = 0; j < K; ++j) w[i][j] = taps[g * 8 + i][j];
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
-        const int r = tp * 2 + u;    // token t0 + r, staged at row r + K - 1
+    constexpr int TPT = kTileTok / 16;  // tokens per thread
+#pragma unroll 2
+    for (int u = 0; u < TPT; ++u) {
+        const int r = tp * TPT + u;  // token t0 + r, staged at row r + K - 1
         const int64_t t = t0 + r;
         float y[kVec];
         if (conv) {

@@ -62,6 +62,7 @@ struct GemvArgs {
     unsigned long long* keys;                // EPI_LOGITS: per-b argmax keys (zero before the first call)
     unsigned int* ticket;                    // EPI_LOGITS: CTA counter (zero before the first call)
     int64_t* ids_out; int64_t* pos_dev;      // EPI_LOGITS: argmax ids [B]; position advanced by 1 (optional)
+    int nblocks;                             // CTA-blocks of the launch (or phase)
 };
 
 template <typename T>
@@ -111,20 +112,22 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
 
 constexpr int kPrefetch = 6;  // weight chunks per lane and row loaded before the dependency wait
 
-template <typename TW, int NB>
-__global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvArgs a) {
-    extern __shared__ float hs[];  // [NB][K] input vectors
+// One CTA-block of a decode GEMV: block `blk` of the launch's a.nblocks.  `wait` runs
+// between the weight prefetch and the first read of data an earlier kernel wrote
+// (the programmatic-dependency wait).
+template <typename TW, int NB, class Wait>
+__device__ __forceinline__ void gemv_body(const GemvArgs& a, int blk, float* hs, Wait wait) {
     __shared__ float red[kGemvWarps][NB];
     __shared__ unsigned long long best[kGemvWarps][NB];
-    griddep_launch_dependents();
+    __shared__ unsigned int last;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int K = a.K;
     // ---- the warp's two rows (SwiGLU: the gate row n and the up row N + n) and their
     // first weight chunks: the weights do not depend on the previous kernel
-    const int n0 = blockIdx.x * kRowsPerCta + warp * kRowsPerWarp;
+    const int n0 = blk * kRowsPerCta + warp * kRowsPerWarp;
     int rows[2];
     const bool swiglu = a.epi == EPI_SWIGLU;
-    const int on = swiglu ? (int)blockIdx.x * (kRowsPerCta / 2) + warp : -1;  // SwiGLU output of this warp
+    const int on = swiglu ? blk * (kRowsPerCta / 2) + warp : -1;  // SwiGLU output of this warp
     if (swiglu) {
         rows[0] = on;
         rows[1] = a.N + on;
@@ -147,7 +150,8 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvArgs a) {
             if (live1) load_raw8<TW>(w1 + c * 8, pf1[j]);
         }
     }
-    griddep_wait();
+    wait();
+    __syncthreads();  // a persistent CTA's previous block may still read hs
     // ---- prologue: the NB input vectors in shared memory (fp32)
     if (a.pro == PRO_NORM) {
         for (int b = 0; b < NB; ++b) {
@@ -309,8 +313,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvArgs a) {
     }
     __threadfence();
     __syncthreads();
-    __shared__ unsigned int last;
-    if (tid == 0) last = atomicAdd(a.ticket, 1u) == gridDim.x - 1 ? 1u : 0u;
+    if (tid == 0) last = atomicAdd(a.ticket, 1u) == (unsigned)a.nblocks - 1 ? 1u : 0u;
     __syncthreads();
     if (!last) return;
     __threadfence();
@@ -324,6 +327,13 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvArgs a) {
     }
 }
 
+template <typename TW, int NB>
+__global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvArgs a) {
+    extern __shared__ float hs[];  // [NB][K] input vectors
+    griddep_launch_dependents();
+    gemv_body<TW, NB>(a, blockIdx.x, hs, [] { griddep_wait(); });
+}
+
 // One recurrence step: k L2-norm, S' = a*S + k (w*v - (b*k)^T (a*S)), o = q^T S'.
 // The columns of S evolve independently (delta_j and o_j only involve column j),
 // so one CTA owns a group of 16 columns of one (batch, head) for all dk rows:
@@ -332,12 +342,28 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvArgs a) {
 constexpr int kStateCols = 16;
 constexpr int kStateThreads = 256;
 
-__global__ void __launch_bounds__(kStateThreads) dgda_state_kernel(const float* feats, int64_t ldf, float* state,
-                                                                   float* o, int64_t ldo, int H, int dk, int dv,
-                                                                   int off_q, int off_k, int off_v, int off_a,
-                                                                   int off_b, int off_w, float eps) {
-    griddep_launch_dependents();
-    const int h = blockIdx.x, j0 = blockIdx.y * kStateCols, b = blockIdx.z;
+struct StateArgs {
+    const float* feats; int64_t ldf;  // [B, 4*H*dk + 2*H*dv] decode features
+    float* state;                     // [B, H, dk, dv]
+    float* o; int64_t ldo;            // [B, H*dv]
+    int B, H, dk, dv;
+    int off_q, off_k, off_v, off_a, off_b, off_w;
+    float eps;
+    int nblocks;                      // H * ceil(dv / kStateCols) * B
+};
+
+template <class Wait>
+__device__ __forceinline__ void state_body(const StateArgs& a, int blk, Wait wait) {
+    const int ncg = (a.dv + kStateCols - 1) / kStateCols;
+    const int h = blk % a.H, j0 = (blk / a.H) % ncg * kStateCols, b = blk / (a.H * ncg);
+    const float* feats = a.feats;
+    const int64_t ldf = a.ldf;
+    float* state = a.state;
+    float* o = a.o;
+    const int64_t ldo = a.ldo;
+    const int H = a.H, dk = a.dk, dv = a.dv;
+    const int off_q = a.off_q, off_k = a.off_k, off_v = a.off_v, off_a = a.off_a, off_b = a.off_b, off_w = a.off_w;
+    const float eps = a.eps;
     const int tid = threadIdx.x, tx = tid % kStateCols, ty = tid / kStateCols;
     constexpr int RY = kStateThreads / kStateCols;  // 16 row groups
     __shared__ float sq[64], sk[64], sa[64], sbk[64];
@@ -348,7 +374,8 @@ __global__ void __launch_bounds__(kStateThreads) dgda_state_kernel(const float* 
     const bool colv = j < dv;
     // the state is read after the wait: its last writer (this layer's step before) is only
     // known to be complete once every kernel before this one is
-    griddep_wait();
+    wait();
+    __syncthreads();  // a persistent CTA's previous block may still read the shared arrays
     float sd[64 / RY];
 #pragma unroll
     for (int r = 0; r < 64 / RY; ++r) {
@@ -407,6 +434,12 @@ __global__ void __launch_bounds__(kStateThreads) dgda_state_kernel(const float* 
         for (int y = 0; y < RY; ++y) tot += red[y][tx];
         o[(int64_t)b * ldo + h * dv + j] = tot;
     }
+    __syncthreads();  // shared arrays are reused by the next body in a persistent launch
+}
+
+__global__ void __launch_bounds__(kStateThreads) dgda_state_kernel(StateArgs a) {
+    griddep_launch_dependents();
+    state_body(a, blockIdx.x, [] { griddep_wait(); });
 }
 
 
@@ -574,6 +607,7 @@ int launch_gemv(GemvArgs& a, cudaStream_t s) {
     int nb = a.B <= 1 ? 1 : a.B <= 2 ? 2 : a.B <= 4 ? 4 : 8;
     const size_t smem = sizeof(float) * (size_t)nb * a.K;
     if (smem > 200 * 1024) return set_error(MABA_ERR_UNSUPPORTED, "decode_gemv: B x K too large for shared memory");
+    a.nblocks = (int)grid;
     auto go = [&](auto kern) {
         if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         MABA_TRY(launch_pdl(kern, dim3(grid), dim3(kGemvThreads), smem, s, a));
@@ -690,20 +724,23 @@ extern "C" int maba_swiglu(const maba_tensor* u, const maba_tensor* out, void* s
 // ---------------------------------------------------------------------------
 extern "C" size_t maba_decode_gemv_workspace_size(int64_t B) { return (size_t)(B > 0 ? B : 1) * 8 + 16; }
 
-extern "C" int maba_decode_gemv(const maba_tensor* w, int32_t prologue, const maba_tensor* x,
-                                const maba_tensor* aux, float eps, const maba_tensor* ids, int32_t epilogue,
-                                const maba_tensor* out, const maba_tensor* bias, const maba_tensor* gate,
-                                const maba_tensor* taps, const maba_tensor* hist, int32_t n_conv, int32_t alpha_end,
-                                const maba_tensor* ids_out, int64_t* pos_dev, void* workspace,
-                                size_t workspace_bytes, void* stream) {
+namespace maba {
+namespace {
+// Validates one decode GEMV and fills its kernel arguments (nblocks included).
+int build_gemv(GemvArgs& a, int& dt_out, const maba_tensor* w, int32_t prologue, const maba_tensor* x,
+               const maba_tensor* aux, float eps, const maba_tensor* ids, int32_t epilogue, const maba_tensor* out,
+               const maba_tensor* bias, const maba_tensor* gate, const maba_tensor* taps, const maba_tensor* hist,
+               int32_t n_conv, int32_t alpha_end, const maba_tensor* ids_out, int64_t* pos_dev, void* workspace,
+               size_t workspace_bytes) {
     const maba_tensor* norm_w = aux;
     if (!present(w) || w->ndim != 2 || !wdtype_ok(w->dtype))
         return set_error(MABA_ERR_INVALID, "decode_gemv: w must be a [rows, K] float32 / float16 / bfloat16 weight");
     if (!row_vec_ok(w) || w->shape[1] % 8 != 0)
         return set_error(MABA_ERR_UNSUPPORTED, "decode_gemv: w rows must be contiguous, 16-byte aligned, K %% 8 == 0");
     const int dt = w->dtype;
+    dt_out = dt;
     const int64_t rows = w->shape[0], K = w->shape[1];
-    GemvArgs a{};
+    a = GemvArgs{};
     a.w = w->data; a.ldw = w->stride[0]; a.K = (int)K; a.pro = prologue; a.epi = epilogue;
     a.N = (int)(epilogue == EPI_SWIGLU ? rows / 2 : rows);
     if (epilogue == EPI_SWIGLU && rows % 2 != 0) return set_error(MABA_ERR_INVALID, "decode_gemv: SwiGLU needs 2I rows");
@@ -798,16 +835,13 @@ extern "C" int maba_decode_gemv(const maba_tensor* w, int32_t prologue, const ma
         default:
             return set_error(MABA_ERR_INVALID, "decode_gemv: unknown epilogue %d", epilogue);
     }
-    cudaStream_t s = as_stream(stream);
-    switch (dt) {
-        case MABA_F32: return launch_gemv<float>(a, s);
-        case MABA_F16: return launch_gemv<__half>(a, s);
-        default: return launch_gemv<__nv_bfloat16>(a, s);
-    }
+    const int per_cta = a.epi == EPI_SWIGLU ? kRowsPerCta / 2 : kRowsPerCta;
+    a.nblocks = (int)ceil_div(a.N, per_cta);
+    return MABA_OK;
 }
 
-extern "C" int maba_decode_dgda_state(const maba_tensor* feats, const maba_tensor* state, const maba_tensor* o_out,
-                                      int32_t n_heads, float eps, void* stream) {
+int build_state(StateArgs& sa, const maba_tensor* feats, const maba_tensor* state, const maba_tensor* o_out,
+                int32_t n_heads, float eps) {
     if (!present(feats) || feats->ndim != 2 || feats->dtype != MABA_F32 || feats->stride[1] != 1)
         return set_error(MABA_ERR_INVALID, "decode_dgda_state: feats must be float32 [B, 4*H*dk + 2*H*dv]");
     if (!present(state) || state->ndim != 4 || state->dtype != MABA_F32)
@@ -824,11 +858,41 @@ extern "C" int maba_decode_dgda_state(const maba_tensor* feats, const maba_tenso
     MABA_TRY(expect_dtype(o_out, "decode_dgda_state: o_out", MABA_F32));
     if (o_out->stride[1] != 1) return set_error(MABA_ERR_INVALID, "decode_dgda_state: o_out unit column stride");
     const int cqk = (int)(H * dk), cv = (int)(H * dv);
-    const int off_q = 0, off_k = cqk, off_v = 2 * cqk, off_a = 2 * cqk + cv, off_b = 3 * cqk + cv, off_w = 4 * cqk + cv;
+    sa = StateArgs{};
+    sa.feats = static_cast<const float*>(feats->data); sa.ldf = feats->stride[0];
+    sa.state = static_cast<float*>(state->data); sa.o = static_cast<float*>(o_out->data); sa.ldo = o_out->stride[0];
+    sa.B = (int)B; sa.H = (int)H; sa.dk = (int)dk; sa.dv = (int)dv;
+    sa.off_q = 0; sa.off_k = cqk; sa.off_v = 2 * cqk; sa.off_a = 2 * cqk + cv; sa.off_b = 3 * cqk + cv; sa.off_w = 4 * cqk + cv;
+    sa.eps = eps;
+    sa.nblocks = (int)(H * ceil_div(dv, kStateCols) * B);
+    return MABA_OK;
+}
+
+}  // namespace
+}  // namespace maba
+
+extern "C" int maba_decode_gemv(const maba_tensor* w, int32_t prologue, const maba_tensor* x,
+                                const maba_tensor* aux, float eps, const maba_tensor* ids, int32_t epilogue,
+                                const maba_tensor* out, const maba_tensor* bias, const maba_tensor* gate,
+                                const maba_tensor* taps, const maba_tensor* hist, int32_t n_conv, int32_t alpha_end,
+                                const maba_tensor* ids_out, int64_t* pos_dev, void* workspace,
+                                size_t workspace_bytes, void* stream) {
+    GemvArgs a;
+    int dt = 0;
+    MABA_TRY(build_gemv(a, dt, w, prologue, x, aux, eps, ids, epilogue, out, bias, gate, taps, hist, n_conv,
+                        alpha_end, ids_out, pos_dev, workspace, workspace_bytes));
     cudaStream_t s = as_stream(stream);
-    const dim3 grid((unsigned)H, (unsigned)ceil_div(dv, kStateCols), (unsigned)B);
-    MABA_TRY(launch_pdl(dgda_state_kernel, grid, dim3(kStateThreads), 0, s, static_cast<const float*>(feats->data),
-                        feats->stride[0], static_cast<float*>(state->data), static_cast<float*>(o_out->data),
-                        o_out->stride[0], (int)H, (int)dk, (int)dv, off_q, off_k, off_v, off_a, off_b, off_w, eps));
+    switch (dt) {
+        case MABA_F32: return launch_gemv<float>(a, s);
+        case MABA_F16: return launch_gemv<__half>(a, s);
+        default: return launch_gemv<__nv_bfloat16>(a, s);
+    }
+}
+
+extern "C" int maba_decode_dgda_state(const maba_tensor* feats, const maba_tensor* state, const maba_tensor* o_out,
+                                      int32_t n_heads, float eps, void* stream) {
+    StateArgs sa;
+    MABA_TRY(build_state(sa, feats, state, o_out, n_heads, eps));
+    MABA_TRY(launch_pdl(dgda_state_kernel, dim3((unsigned)sa.nblocks), dim3(kStateThreads), 0, as_stream(stream), sa));
     return check_launch("decode_dgda_state");
 }

@@ -407,84 +407,90 @@ class DecodeSession:
         self.pos_dev.fill_(T)
         return logits
 
-    def _gemv(self, w, pro, x=None, aux=None, ids=None, epi=EPI_STORE, out=None, bias=None, gate=None, taps=None,
-              hist=None, n_conv=0, alpha_end=0, ids_out=None, pos=None, ws=None):
-        rc = N.lib().maba_decode_gemv(
-            N.ref(N.desc(w)), pro, N.ref(N.desc(x)), N.ref(N.desc(aux)), float(self.engine.shape.rms_eps),
-            N.ref(N.desc(ids)), epi, N.ref(N.desc(out)), N.ref(N.desc(bias)), N.ref(N.desc(gate)),
-            N.ref(N.desc(taps)), N.ref(N.desc(hist)), int(n_conv), int(alpha_end), N.ref(N.desc(ids_out)),
-            pos.data_ptr() if pos is not None else None, ws.data_ptr() if ws is not None else None,
-            ws.numel() if ws is not None else 0, N.stream_of(w))
-        N.check(rc, "maba_decode_gemv")
+    @staticmethod
+    def _gemv_args(w, pro, x=None, aux=None, ids=None, epi=EPI_STORE, out=None, bias=None, gate=None, taps=None,
+                   hist=None, n_conv=0, alpha_end=0, ids_out=None, pos=None, ws=None):
+        return (w, pro, x, aux, ids, epi, out, bias, gate, taps, hist, n_conv, alpha_end, ids_out, pos, ws)
+
+    def _gemv_c_args(self, a):
+        w, pro, x, aux, ids, epi, out, bias, gate, taps, hist, n_conv, alpha_end, ids_out, pos, ws = a
+        return (N.ref(N.desc(w)), pro, N.ref(N.desc(x)), N.ref(N.desc(aux)), float(self.engine.shape.rms_eps),
+                N.ref(N.desc(ids)), epi, N.ref(N.desc(out)), N.ref(N.desc(bias)), N.ref(N.desc(gate)),
+                N.ref(N.desc(taps)), N.ref(N.desc(hist)), int(n_conv), int(alpha_end), N.ref(N.desc(ids_out)),
+                pos.data_ptr() if pos is not None else None, ws.data_ptr() if ws is not None else None,
+                ws.numel() if ws is not None else 0)
+
+    def _plan(self):
+        """One decode step as a list of pieces: ("gemv", args), ("state", layer) and ("sa", layer) -- the
+        cache append, split top-k and split-K attention of a MABA-SA layer."""
+        e, s = self.engine, self.engine.shape
+        B, H, dc = self.B, s.n_heads, s.d_c
+        g = self._gemv_args
+        plan = [("gemv", g(e.w_emb_proj, PRO_GATHER, aux=e.emb, ids=self.ids_buf, epi=EPI_STORE, out=self.x))]
+        for i, L in enumerate(e.layers):
+            W = L.mix
+            if L.attn:
+                plan.append(("gemv", g(W.w_in, PRO_NORM, x=self.x, aux=L.n1, epi=EPI_STORE, out=self.sa_out,
+                                       bias=W.bias)))
+                plan.append(("sa", i))
+                plan.append(("gemv", g(W.w_ov, PRO_VEC, x=self.sa[i].o_lat.view(B, H * dc), epi=EPI_RESIDUAL,
+                                       out=self.x, gate=L.g1)))
+            else:
+                plan.append(("gemv", g(W.w_in, PRO_NORM, x=self.x, aux=L.n1, epi=EPI_DGDA, out=self.feats,
+                                       taps=W.taps, hist=self.hists[i], n_conv=W.n_conv, alpha_end=W.alpha_end)))
+                plan.append(("state", i))
+                plan.append(("gemv", g(W.w_o, PRO_VEC, x=self.o, epi=EPI_RESIDUAL, out=self.x, gate=L.g1)))
+            plan.append(("gemv", g(L.w_gu, PRO_NORM, x=self.x, aux=L.n2, epi=EPI_SWIGLU, out=self.a)))
+            plan.append(("gemv", g(L.w_down, PRO_VEC, x=self.a, epi=EPI_RESIDUAL, out=self.x, gate=L.g2)))
+        plan.append(("gemv", g(e.w_head, PRO_NORM, x=self.x, aux=e.final_norm, epi=EPI_STORE, out=self.e)))
+        plan.append(("gemv", g(e.emb, PRO_VEC, x=self.e, epi=EPI_LOGITS, out=self.logits, ids_out=self.ids_buf,
+                               pos=self.pos_dev, ws=self.ws_head)))
+        return plan
+
+    def _sa_middle(self, i: int, st: int) -> None:
+        """Cache append, split decode top-k and split-K decode attention of MABA-SA layer i."""
+        e, s = self.engine, self.engine.shape
+        lib = N.lib()
+        W, cache = e.layers[i].mix, self.sa[i]
+        B, H, dc = self.B, s.n_heads, s.d_c
+        so = self.sa_out
+        c_new = so[:, W.off_c:W.off_c + dc].unsqueeze(1)
+        k_new = so[:, W.off_ki:W.off_ki + s.d_idx].unsqueeze(1)
+        q_idx = so[:, W.off_qi:W.off_qi + s.d_idx].unsqueeze(1)
+        qhat = so[:, W.off_q:W.off_q + H * dc].view(B, 1, H, dc)
+        gate = so[:, W.off_g:W.off_g + 3].unsqueeze(1)
+        N.check(lib.maba_decode_cache_append(
+            N.ref(N.desc(c_new)), N.ref(N.desc(k_new)), N.ref(N.desc(cache.c)), N.ref(N.desc(cache.kidx)),
+            N.ref(N.desc(cache.cent)), N.ref(N.desc(cache.hca)), self.pos_dev.data_ptr(), s.block, s.hca_r, st),
+            "maba_decode_cache_append")
+        wt = cache.ws_topk
+        N.check(lib.maba_index_topk_decode_at(
+            N.ref(N.desc(q_idx)), N.ref(N.desc(cache.cent)), float(s.lam), s.top_k, s.block, self.pos_dev.data_ptr(),
+            N.ref(N.desc(cache.idx)), wt.data_ptr() if wt is not None else None, wt.numel() if wt is not None else 0,
+            st), "maba_index_topk_decode_at")
+        wa = cache.ws_attn
+        N.check(lib.maba_sa_attention_decode_at(
+            N.ref(N.desc(qhat)), N.ref(N.desc(cache.c)), N.ref(N.desc(cache.hca)), N.ref(N.desc(cache.idx)),
+            N.ref(N.desc(gate)), N.ref(N.desc(cache.o_lat)), self.pos_dev.data_ptr(), s.window, s.sinks, s.block,
+            s.hca_r, wa.data_ptr() if wa is not None else None, wa.numel() if wa is not None else 0, st),
+            "maba_sa_attention_decode_at")
+
+    def _state(self, i: int, st: int) -> None:
+        N.check(N.lib().maba_decode_dgda_state(N.ref(N.desc(self.feats)), N.ref(N.desc(self.states[i])),
+                                               N.ref(N.desc(self.o)), self.engine.shape.n_heads,
+                                               float(self.engine.shape.k_eps), st), "maba_decode_dgda_state")
 
     def _step_device(self) -> None:
         """One decode step on the session's buffers: ids_buf -> logits, argmax -> ids_buf, position + 1."""
-        e, s = self.engine, self.engine.shape
         lib = N.lib()
         st = N.stream_of(self.x)
-        self._gemv(e.w_emb_proj, PRO_GATHER, aux=e.emb, ids=self.ids_buf, epi=EPI_STORE, out=self.x)
-        B, H, dc = self.B, s.n_heads, s.d_c
-        for i, L in enumerate(e.layers):
-            W = L.mix
-            if L.attn:
-                cache = self.sa[i]
-                self._gemv(W.w_in, PRO_NORM, x=self.x, aux=L.n1, epi=EPI_STORE, out=self.sa_out, bias=W.bias)
-                so = self.sa_out
-                c_new = so[:, W.off_c:W.off_c + dc].unsqueeze(1)
-                k_new = so[:, W.off_ki:W.off_ki + s.d_idx].unsqueeze(1)
-                q_idx = so[:, W.off_qi:W.off_qi + s.d_idx].unsqueeze(1)
-                qhat = so[:, W.off_q:W.off_q + H * dc].view(B, 1, H, dc)
-                gate = so[:, W.off_g:W.off_g + 3].unsqueeze(1)
-                N.check(lib.maba_decode_cache_append(
-                    N.ref(N.desc(c_new)), N.ref(N.desc(k_new)), N.ref(N.desc(cache.c)), N.ref(N.desc(cache.kidx)),
-                    N.ref(N.desc(cache.cent)), N.ref(N.desc(cache.hca)), self.pos_dev.data_ptr(), s.block, s.hca_r,
-                    st), "maba_decode_cache_append")
-                wt = cache.ws_topk
-                N.check(lib.maba_index_topk_decode_at(
-                    N.ref(N.desc(q_idx)), N.ref(N.desc(cache.cent)), float(s.lam), s.top_k, s.block,
-                    self.pos_dev.data_ptr(), N.ref(N.desc(cache.idx)), wt.data_ptr() if wt is not None else None,
-                    wt.numel() if wt is not None else 0, st), "maba_index_topk_decode_at")
-                wa = cache.ws_attn
-                N.check(lib.maba_sa_attention_decode_at(
-                    N.ref(N.desc(qhat)), N.ref(N.desc(cache.c)), N.ref(N.desc(cache.hca)), N.ref(N.desc(cache.idx)),
-                    N.ref(N.desc(gate)), N.ref(N.desc(cache.o_lat)), self.pos_dev.data_ptr(), s.window, s.sinks,
-                    s.block, s.hca_r, wa.data_ptr() if wa is not None else None, wa.numel() if wa is not None else 0,
-                    st), "maba_sa_attention_decode_at")
-                self._gemv(W.w_ov, PRO_VEC, x=cache.o_lat.view(B, H * dc), epi=EPI_RESIDUAL, out=self.x, gate=L.g1)
+        for kind, a in self._plan():
+            if kind == "gemv":
+                N.check(lib.maba_decode_gemv(*self._gemv_c_args(a), st), "maba_decode_gemv")
+            elif kind == "state":
+                self._state(a, st)
             else:
-                self._gemv(W.w_in, PRO_NORM, x=self.x, aux=L.n1, epi=EPI_DGDA, out=self.feats, taps=W.taps,
-                           hist=self.hists[i], n_conv=W.n_conv, alpha_end=W.alpha_end)
-                N.check(lib.maba_decode_dgda_state(N.ref(N.desc(self.feats)), N.ref(N.desc(self.states[i])),
-                                                   N.ref(N.desc(self.o)), H, float(s.k_eps), st),
-                        "maba_decode_dgda_state")
-                self._gemv(W.w_o, PRO_VEC, x=self.o, epi=EPI_RESIDUAL, out=self.x, gate=L.g1)
-            self._gemv(L.w_gu, PRO_NORM, x=self.x, aux=L.n2, epi=EPI_SWIGLU, out=self.a)
-            self._gemv(L.w_down, PRO_VEC, x=self.a, epi=EPI_RESIDUAL, out=self.x, gate=L.g2)
-        self._gemv(e.w_head, PRO_NORM, x=self.x, aux=e.final_norm, epi=EPI_STORE, out=self.e)
-        self._gemv(e.emb, PRO_VEC, x=self.e, epi=EPI_LOGITS, out=self.logits, ids_out=self.ids_buf, pos=self.pos_dev,
-                   ws=self.ws_head)
-
-    def bytes_per_step(self) -> int:
-        """HBM bytes one decode step must move at the current length: every weight it reads, the
-        recurrent states and conv histories read and written, and per MABA-SA layer the latent rows
-        of the window, sinks and selected blocks, the pooled rows and the centroid table it scans,
-        and the index keys of the tail block it re-pools."""
-        e, s = self.engine, self.engine.shape
-        nb = lambda t: t.numel() * t.element_size()
-        total = nb(e.w_emb_proj) + nb(e.w_head) + nb(e.emb) + nb(e.final_norm) + self.B * nb(e.emb[0])
-        pos = max(self.length, 1)
-        nblk = (pos + s.block - 1) // s.block
-        for i, L in enumerate(e.layers):
-            total += nb(L.n1) + nb(L.n2) + nb(L.w_gu) + nb(L.w_down) + nb(L.g1) + nb(L.g2)
-            W = L.mix
-            if L.attn:
-                el = e.emb.element_size()
-                rows = min(pos, s.window + s.sinks) + min(s.top_k, nblk) * s.block
-                total += nb(W.w_in) + nb(W.w_ov) + nb(W.bias)
-                total += self.B * el * (rows * s.d_c + (pos // s.hca_r) * s.d_c + nblk * s.d_idx + s.block * s.d_idx)
-            else:
-                total += nb(W.w_in) + nb(W.w_o) + nb(W.taps) + 2 * nb(self.states[i]) + 2 * nb(self.hists[i])
-        return int(total)
+                self._sa_middle(a, st)
 
     def launches_per_step(self) -> int:
         """Kernels of this library one decode step launches (the count the step's graph holds)."""
