@@ -200,7 +200,7 @@ constexpr int kTileTok = 128;
 constexpr int kTileCh = 128;
 
 template <typename T, int K>
-__global__ void __launch_bounds__(256) dgda_frontend_tile_kernel(FeArgs a, int64_t ntt, int nct) {
+__global__ void __launch_bounds__(256, 4) dgda_frontend_tile_kernel(FeArgs a, int64_t ntt, int nct) {
     constexpr int ROWS = kTileTok + K - 1;
     constexpr int LDS = kTileCh + 8;  // padded row (16-bit elements)
     __shared__ __align__(16) T xs[ROWS][LDS];

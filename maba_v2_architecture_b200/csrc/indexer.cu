@@ -222,6 +222,7 @@ struct TopkArgs {
     int64_t ntiles;
     int vecload;             // q and centroids: unit stride on d, 16-byte aligned rows (16-bit types)
     int D, block, keff, decode;
+    float lam_f;             // lambda (the vectorised decode kernel forms the penalty in place)
     float scale_f;
     double scale_d;
 };
@@ -750,7 +751,8 @@ __global__ void __launch_bounds__(kTopkThreads) topk_decode_vec_kernel(TopkArgs 
 #pragma unroll
                 for (int i = 0; i < 8; ++i) acc = fmaf(qs[k * 8 + i], Cvt<T>::to_f(e[i]), acc);
             }
-            sc = acc - a.pen[qb - n];
+            // the penalty table's value, computed in place (penalty_table_kernel's arithmetic)
+            sc = acc - __fmul_rn(a.lam_f, (float)log1p((double)(qb - n)));
             ci = (int)n;
         }
         warp_offer(ls, li, sc, ci, a.keff, lane);
@@ -808,10 +810,15 @@ __global__ void __launch_bounds__(1024) topk_decode_merge_tree_kernel(TopkArgs a
 
 // Launches the split decode scan (vectorised partials where the layout allows)
 // and the tree merge.
+// The vectorised decode kernel applies: 16-bit centroids, unit-stride 16-byte-aligned rows, d <= 64.
+bool decode_vec_ok(const TopkArgs& a, int elem_bytes) {
+    return elem_bytes == 2 && a.D % 8 == 0 && a.D <= 64 && a.sc[2] == 1 && (a.sc[1] * 2) % 16 == 0 &&
+           (a.sc[0] * 2) % 16 == 0 && (reinterpret_cast<uintptr_t>(a.c) & 15u) == 0;
+}
+
 template <typename T>
 int launch_topk_decode_split(TopkArgs& a, int64_t B, int64_t L, int nsplit, float* ps, int* pi, cudaStream_t s) {
-    const bool vec = (sizeof(T) == 2) && a.D % 8 == 0 && a.D <= 64 && a.sc[2] == 1 && (a.sc[1] * 2) % 16 == 0 &&
-                     (a.sc[0] * 2) % 16 == 0 && (reinterpret_cast<uintptr_t>(a.c) & 15u) == 0;
+    const bool vec = decode_vec_ok(a, (int)sizeof(T));
     const dim3 grid((unsigned)nsplit, (unsigned)L, (unsigned)B);
     if (vec) {
         switch (a.D / 8) {
@@ -999,6 +1006,7 @@ static int index_topk_impl(const maba_tensor* q_idx, const maba_tensor* centroid
     a.q_pos0 = decode ? 0 : q_pos0;
     a.scale_d = 1.0 / sqrt((double)D);
     a.scale_f = (float)a.scale_d;
+    a.lam_f = lambda_dist;
     if (decode_split_wanted(a, B, q_idx->dtype)) {
         const int64_t nsplit = decode_split_count(nb);
         const size_t off = (need + 255) / 256 * 256;
@@ -1265,8 +1273,6 @@ extern "C" int maba_index_topk_decode_at(const maba_tensor* q_idx, const maba_te
         return set_error(MABA_ERR_WORKSPACE, "index_topk_decode_at: workspace of %zu bytes required", need);
     cudaStream_t s = as_stream(stream);
     float* pen = static_cast<float*>(workspace);
-    penalty_table_kernel<<<(unsigned)ceil_div(nbcap, 256), 256, 0, s>>>(pen, nbcap, lambda_dist);
-    MABA_TRY(check_launch("index_topk_decode_at(penalty)"));
     const int64_t nsplit = decode_split_count(nbcap);
     const size_t off = (nbcap * sizeof(float) + 255) / 256 * 256;
     float* ps = reinterpret_cast<float*>(static_cast<char*>(workspace) + off);
@@ -1276,9 +1282,15 @@ extern "C" int maba_index_topk_decode_at(const maba_tensor* q_idx, const maba_te
     a.pen = pen;
     for (int i = 0; i < 3; ++i) { a.sq[i] = q_idx->stride[i]; a.sc[i] = cent_table->stride[i]; a.si[i] = idx_out->stride[i]; }
     a.L = 1; a.nb = nbcap; a.D = (int)D; a.block = block_size; a.keff = (int)kout; a.decode = 1;
-    a.scale_d = 1.0 / sqrt((double)D); a.scale_f = (float)a.scale_d; a.pos_dev = pos_dev;
+    a.scale_d = 1.0 / sqrt((double)D); a.scale_f = (float)a.scale_d;
+    a.lam_f = lambda_dist; a.pos_dev = pos_dev;
     const size_t smem = sizeof(float) * ((size_t)D + (size_t)8 * 32 * (D + 1) + 8 * 32) + sizeof(int) * 8 * 32;
     if (smem > 200 * 1024) return set_error(MABA_ERR_UNSUPPORTED, "index_topk_decode_at: d_idx too large");
+    // the vectorised kernel forms the penalties itself; the other one reads the table
+    if (!decode_vec_ok(a, q_idx->dtype == MABA_F32 ? 4 : 2)) {
+        penalty_table_kernel<<<(unsigned)ceil_div(nbcap, 256), 256, 0, s>>>(pen, nbcap, lambda_dist);
+        MABA_TRY(check_launch("index_topk_decode_at(penalty)"));
+    }
     return MABA_DISPATCH_FLOAT(q_idx->dtype, "index_topk_decode_at", [&] {
         if constexpr (sizeof(T) == 8) {
             return set_error(MABA_ERR_UNSUPPORTED, "index_topk_decode_at: float64");

@@ -15,7 +15,7 @@ the GPU, and runs
   indexer, the fused three-stream attention in latent space, and one output GEMM
   whose weight folds the value up-projection into o_proj (W_o W_uv); residual
   adds and RMSNorms fused into one kernel; the residual stream in float32;
-* **decode** one token per step in 5 launches per DGDA block and 10 per MABA-SA
+* **decode** one token per step in 5 launches per DGDA block and 9 per MABA-SA
   block: GEMVs with the RMSNorm in their prologue and the conv/gates, SwiGLU,
   gated residual add or logits-with-argmax in their epilogue, the recurrence
   kernel, and the O(1)-append latent / index-key caches with the split decode
@@ -497,7 +497,7 @@ class DecodeSession:
         n = 3  # embedding, head projection, logits
         for L in self.engine.layers:
             n += 2  # SwiGLU in, down + residual
-            n += 8 if L.attn else 3  # SA: in, append, penalty, top-k partial + merge, attention partial + combine, out
+            n += 7 if L.attn else 3  # SA: in, append, top-k partial + merge, attention partial + combine, out
         return n
 
     @torch.no_grad()
