@@ -492,6 +492,28 @@ class DecodeSession:
             else:
                 self._sa_middle(a, st)
 
+    def bytes_per_step(self) -> int:
+        """HBM bytes one decode step must move at the current length: every weight it reads, the
+        recurrent states and conv histories read and written, and per MABA-SA layer the latent rows
+        of the window, sinks and selected blocks, the pooled rows and the centroid table it scans,
+        and the index keys of the tail block it re-pools."""
+        e, s = self.engine, self.engine.shape
+        nb = lambda t: t.numel() * t.element_size()
+        total = nb(e.w_emb_proj) + nb(e.w_head) + nb(e.emb) + nb(e.final_norm) + self.B * nb(e.emb[0])
+        pos = max(self.length, 1)
+        nblk = (pos + s.block - 1) // s.block
+        for i, L in enumerate(e.layers):
+            total += nb(L.n1) + nb(L.n2) + nb(L.w_gu) + nb(L.w_down) + nb(L.g1) + nb(L.g2)
+            W = L.mix
+            if L.attn:
+                el = e.emb.element_size()
+                rows = min(pos, s.window + s.sinks) + min(s.top_k, nblk) * s.block
+                total += nb(W.w_in) + nb(W.w_ov) + nb(W.bias)
+                total += self.B * el * (rows * s.d_c + (pos // s.hca_r) * s.d_c + nblk * s.d_idx + s.block * s.d_idx)
+            else:
+                total += nb(W.w_in) + nb(W.w_o) + nb(W.taps) + 2 * nb(self.states[i]) + 2 * nb(self.hists[i])
+        return int(total)
+
     def launches_per_step(self) -> int:
         """Kernels of this library one decode step launches (the count the step's graph holds)."""
         n = 3  # embedding, head projection, logits

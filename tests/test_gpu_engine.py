@@ -87,6 +87,10 @@ def test_graph_replay_matches_eager_steps():
         assert torch.equal(lg, le), "graph vs eager logits"
         assert torch.equal(graph.ids_buf, tok), "device argmax"
     assert int(graph.pos_dev) == 70 + 60 == graph.length
+    # the bench's per-step accounting: every weight is read once per step
+    weights = sum(t.numel() * t.element_size() for L in eng.layers for t in (L.w_gu, L.w_down, L.mix.w_in))
+    assert graph.bytes_per_step() > weights
+    assert graph.launches_per_step() == 3 + sum(2 + (7 if L.attn else 3) for L in eng.layers)
 
 
 def _reference_dir():
