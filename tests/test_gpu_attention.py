@@ -57,6 +57,7 @@ def test_kernel_vs_oracle(B, Lq, Lkv, H, DC, K, window, block, r, gate4d):
     (1, 64, 64, 2, 1, 1, 0, False, torch.bfloat16),        # window 1, no sinks, one selected block
     (1, 300, 300, 2, 32, 4096, 4, False, torch.float16),   # window covering everything, top-32, fp16
     (1, 1024, 1024, 10, 32, 128, 4, False, torch.bfloat16),  # config-2 shape, longer HCA stream
+    (1, 128, 40000, 2, 32, 128, 4, False, torch.bfloat16),  # unions of ~600 blocks: running-maximum kernel
 ])
 def test_tc_kernel_vs_oracle(B, Lq, Lkv, H, K, window, sinks, gate4d, dt):
     """The tcgen05 path (block 64, d_c 128, even H): every stream, mask and tile edge vs the oracle."""
