@@ -345,6 +345,21 @@ MABA_API size_t maba_decode_gemv_workspace_size(int64_t B);
 MABA_API int maba_decode_dgda_state(const maba_tensor* feats, const maba_tensor* state, const maba_tensor* o_out,
                                     int32_t n_heads, float eps, void* stream);
 
+/* maba_decode_dgda_mix: the DGDA mixer of one decode step up to its output projection,
+ *   in one launch: the stacked input projection (w [4*H*dk + 2*H*dv, D], rows q|k|v|alpha|
+ *   erase|write) of h = RMSNorm(x) * norm_w, the dgda epilogue of maba_decode_gemv (feats,
+ *   taps and hist as there), then maba_decode_dgda_state's recurrence step for each head,
+ *   run by the last CTA to finish that head's rows.  dk, dv multiples of 16, at most 64.
+ *   workspace: maba_decode_dgda_mix_workspace_size(H) bytes, zeroed before the first call
+ *   (every call leaves it zeroed).  Replaces, per DGDA block of MabaBlock.step (model.py:
+ *   111-129), the layer's feature path (layers/dgda.py:238-270) and the recurrence step
+ *   (common.py:271-309). */
+MABA_API int maba_decode_dgda_mix(const maba_tensor* w, const maba_tensor* x, const maba_tensor* norm_w, float eps,
+                                  const maba_tensor* taps, const maba_tensor* hist, const maba_tensor* feats,
+                                  const maba_tensor* state, const maba_tensor* o_out, int32_t n_heads, float k_eps,
+                                  void* workspace, size_t workspace_bytes, void* stream);
+MABA_API size_t maba_decode_dgda_mix_workspace_size(int32_t n_heads);
+
 #ifdef __cplusplus
 }
 #endif

@@ -61,6 +61,8 @@ SIGNATURES = {
                                         T_P, _vp, _vp, _sz, _vp]),
     "maba_decode_gemv_workspace_size": (_sz, [_i64]),
     "maba_decode_dgda_state": (ctypes.c_int, [T_P, T_P, T_P, _i32, _f32, _vp]),
+    "maba_decode_dgda_mix": (ctypes.c_int, [T_P, T_P, T_P, _f32, T_P, T_P, T_P, T_P, T_P, _i32, _f32, _vp, _sz, _vp]),
+    "maba_decode_dgda_mix_workspace_size": (ctypes.c_size_t, [_i32]),
     "maba_dgda_transition_workspace_size": (_sz, [_i32, _i64, _i64, _i64]),
     "maba_compute_centroids": (ctypes.c_int, [T_P, T_P, _i32, _vp]),
     "maba_index_topk": (ctypes.c_int, [T_P, T_P, _f32, _i32, _i32, _i32, T_P, T_P, _vp, _sz, _vp]),

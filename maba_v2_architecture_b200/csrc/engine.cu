@@ -22,9 +22,12 @@
 // before waiting for it, so in a captured decode step the weight streams of
 // consecutive kernels overlap.
 //
-// A GEMV warp owns R = 2 output rows and streams their weights with 16-byte
-// loads (8 bf16), multiplying each chunk with all NB (<= 8) input vectors held
-// in shared memory; every CTA recomputes the input normalisation (a few KB).
+// A GEMV CTA owns 16 weight rows (a warp two of them).  It copies the rows into
+// shared memory with cp.async before the programmatic-dependency wait, together
+// with the rows' epilogue weights (bias, residual gate, conv taps); after the wait
+// it issues the epilogue's dependent loads (residual row, conv history), builds
+// the NB (<= 8) input vectors in shared memory (every CTA recomputes the input
+// normalisation, a few KB), and multiplies 16-byte weight chunks with them.
 #include "common.cuh"
 #include "activations.cuh"
 #include "pdl.cuh"
@@ -39,6 +42,24 @@ constexpr int kRowsPerCta = kGemvWarps * kRowsPerWarp;
 
 enum Prologue { PRO_NORM = 0, PRO_GATHER = 1, PRO_VEC = 2 };
 enum Epilogue { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_DGDA = 2, EPI_SWIGLU = 3, EPI_LOGITS = 4 };
+
+// One recurrence step: k L2-norm, S' = a*S + k (w*v - (b*k)^T (a*S)), o = q^T S'.
+// The columns of S evolve independently (delta_j and o_j only involve column j),
+// so one CTA owns a group of 16 columns of one (batch, head) for all dk rows:
+// thread (ty, tx) holds rows ty, ty+16, ... of column tx, and the two sums over
+// rows go through shared memory.
+constexpr int kStateCols = 16;
+constexpr int kStateThreads = 256;
+
+struct StateArgs {
+    const float* feats; int64_t ldf;  // [B, 4*H*dk + 2*H*dv] decode features
+    float* state;                     // [B, H, dk, dv]
+    float* o; int64_t ldo;            // [B, H*dv]
+    int B, H, dk, dv;
+    int off_q, off_k, off_v, off_a, off_b, off_w;
+    float eps;
+    int nblocks;                      // H * ceil(dv / kStateCols) * B
+};
 
 struct GemvArgs {
     const void* w;            // [rows, K] weight (dtype TW), row stride ldw
@@ -63,44 +84,48 @@ struct GemvArgs {
     unsigned int* ticket;                    // EPI_LOGITS: CTA counter (zero before the first call)
     int64_t* ids_out; int64_t* pos_dev;      // EPI_LOGITS: argmax ids [B]; position advanced by 1 (optional)
     int nblocks;                             // CTA-blocks of the launch (or phase)
+    // EPI_DGDA with st_tickets: the last CTA of each head's rows runs the head's recurrence step
+    StateArgs st;                            // st.feats = out
+    unsigned int* st_tickets;                // [H] CTA counters (zero before the first call; left zeroed)
+    int st_per_head;                         // CTAs whose rows belong to one head: (4 dk + 2 dv) / 16
 };
 
-template <typename T>
-__device__ __forceinline__ void load_chunk8(const T* p, float* v) {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = Cvt<T>::to_f(p[i]);
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+                 "l"(src));
 }
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;\n" ::: "memory"); }
+
+// 8 weights from shared memory (16 bytes for 16-bit types, 32 for float32)
+template <typename T>
+__device__ __forceinline__ void load_chunk8_smem(const T* p, float* v);
 template <>
-__device__ __forceinline__ void load_chunk8<__nv_bfloat16>(const __nv_bfloat16* p, float* v) {
-    const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
-    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+__device__ __forceinline__ void load_chunk8_smem<__nv_bfloat16>(const __nv_bfloat16* p, float* v) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-        const float2 f = __bfloat1622float2(h[i]);
-        v[2 * i] = f.x;
-        v[2 * i + 1] = f.y;
+        v[2 * i] = __uint_as_float(w[i] << 16);
+        v[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
     }
 }
 template <>
-__device__ __forceinline__ void load_chunk8<float>(const float* p, float* v) {
-    const float4 a = __ldg(reinterpret_cast<const float4*>(p));
-    const float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
-    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-}
-
-// 8 weights in their storage type (one 16-byte load for 16-bit types, two for float32)
-template <typename T> struct Chunk8 { uint4 u[sizeof(T) == 4 ? 2 : 1]; };
-template <typename T>
-__device__ __forceinline__ void load_raw8(const T* p, Chunk8<T>& c) {
+__device__ __forceinline__ void load_chunk8_smem<__half>(const __half* p, float* v) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-    for (int i = 0; i < (sizeof(T) == 4 ? 2 : 1); ++i) c.u[i] = __ldg(reinterpret_cast<const uint4*>(p) + i);
+    for (int i = 0; i < 4; ++i) {
+        v[2 * i] = __half2float(__ushort_as_half((unsigned short)(w[i] & 0xffffu)));
+        v[2 * i + 1] = __half2float(__ushort_as_half((unsigned short)(w[i] >> 16)));
+    }
 }
-template <typename T>
-__device__ __forceinline__ void unpack8(const Chunk8<T>& c, float* v) {
-    const T* e = reinterpret_cast<const T*>(c.u);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = Cvt<T>::to_f(e[i]);
+template <>
+__device__ __forceinline__ void load_chunk8_smem<float>(const float* p, float* v) {
+    const float4 x = *reinterpret_cast<const float4*>(p);
+    const float4 y = *reinterpret_cast<const float4*>(p + 4);
+    v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
+    v[4] = y.x; v[5] = y.y; v[6] = y.z; v[7] = y.w;
 }
 
 // (value desc, index asc) as one unsigned key: larger key = better
@@ -110,48 +135,156 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
     return ((unsigned long long)u << 32) | (unsigned long long)(0xFFFFFFFFu - (unsigned int)idx);
 }
 
-constexpr int kPrefetch = 6;  // weight chunks per lane and row loaded before the dependency wait
+// Head of stacked DGDA row r (sections q | k | v | alpha | erase | write).
+__device__ __forceinline__ int dgda_head_of_row(const StateArgs& a, int r) {
+    const int cqk = a.H * a.dk, cv = a.H * a.dv;
+    if (r < 2 * cqk) return (r % cqk) / a.dk;
+    r -= 2 * cqk;
+    if (r < cv) return r / a.dv;
+    r -= cv;
+    if (r < 2 * cqk) return (r % cqk) / a.dk;
+    return (r - 2 * cqk) / a.dv;
+}
+
+// One recurrence step of (batch b, head h) by a whole 256-thread CTA (dk, dv <= 64):
+// k L2-norm, S' = a*S + k (w*v - (b*k)^T (a*S)), o = q^T S'.  Thread (rg, j) holds rows
+// rg, rg + 4, ... of column j; the two sums over rows go through shared memory.  The
+// features were written by other CTAs of this launch: they are read through L2.
+__device__ __forceinline__ void state_step_cta(const StateArgs& a, int b, int h) {
+    __shared__ float vq[64], vk[64], va[64], vb[64];
+    __shared__ float red4[4][64];
+    __shared__ float knorm_s;
+    const int tid = threadIdx.x, j = tid & 63, rg = tid >> 6;
+    const int dk = a.dk, dv = a.dv;
+    const bool colv = j < dv;
+    float* S = a.state + ((int64_t)b * a.H + h) * dk * dv;
+    const float* f = a.feats + (int64_t)b * a.ldf;
+    float sd[16];
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+        const int i = rg + 4 * r;
+        sd[r] = (i < dk && colv) ? S[(int64_t)i * dv + j] : 0.f;
+    }
+    if (tid < dk) {
+        vq[tid] = __ldcg(f + a.off_q + h * dk + tid);
+        vk[tid] = __ldcg(f + a.off_k + h * dk + tid);
+        va[tid] = expf(__ldcg(f + a.off_a + h * dk + tid));
+        vb[tid] = __ldcg(f + a.off_b + h * dk + tid);
+    }
+    const float wv = colv ? __ldcg(f + a.off_w + h * dv + j) * __ldcg(f + a.off_v + h * dv + j) : 0.f;
+    __syncthreads();
+    if (tid < 32) {
+        float ss = 0.f;
+        for (int i = tid; i < dk; i += 32) ss = fmaf(vk[i], vk[i], ss);
+        for (int o2 = 16; o2 > 0; o2 >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o2);
+        if (tid == 0) knorm_s = 1.f / (sqrtf(ss) + a.eps);
+    }
+    __syncthreads();
+    const float kn = knorm_s;
+    float dp = 0.f;
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+        const int i = rg + 4 * r;
+        if (i < dk) {
+            sd[r] *= va[i];
+            dp = fmaf(vb[i] * (vk[i] * kn), sd[r], dp);
+        }
+    }
+    red4[rg][j] = dp;
+    __syncthreads();
+    const float delta = wv - ((red4[0][j] + red4[1][j]) + (red4[2][j] + red4[3][j]));
+    __syncthreads();
+    float op = 0.f;
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+        const int i = rg + 4 * r;
+        if (i < dk && colv) {
+            const float s2 = fmaf(vk[i] * kn, delta, sd[r]);
+            S[(int64_t)i * dv + j] = s2;
+            op = fmaf(vq[i], s2, op);
+        }
+    }
+    red4[rg][j] = op;
+    __syncthreads();
+    if (rg == 0 && colv) a.o[(int64_t)b * a.ldo + h * dv + j] = (red4[0][j] + red4[1][j]) + (red4[2][j] + red4[3][j]);
+    __syncthreads();
+}
 
 // One CTA-block of a decode GEMV: block `blk` of the launch's a.nblocks.  `wait` runs
 // between the weight prefetch and the first read of data an earlier kernel wrote
 // (the programmatic-dependency wait).
-template <typename TW, int NB, class Wait>
+template <typename TW, int NB, bool MIX, class Wait>
 __device__ __forceinline__ void gemv_body(const GemvArgs& a, int blk, float* hs, Wait wait) {
     __shared__ float red[kGemvWarps][NB];
     __shared__ unsigned long long best[kGemvWarps][NB];
     __shared__ unsigned int last;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int K = a.K;
-    // ---- the warp's two rows (SwiGLU: the gate row n and the up row N + n) and their
-    // first weight chunks: the weights do not depend on the previous kernel
-    const int n0 = blk * kRowsPerCta + warp * kRowsPerWarp;
-    int rows[2];
     const bool swiglu = a.epi == EPI_SWIGLU;
-    const int on = swiglu ? blk * (kRowsPerCta / 2) + warp : -1;  // SwiGLU output of this warp
-    if (swiglu) {
-        rows[0] = on;
-        rows[1] = a.N + on;
-    } else {
-        rows[0] = n0;
-        rows[1] = n0 + 1;
+    // ---- the CTA's weight rows into shared memory by cp.async: the weights do not depend
+    // on the previous kernel, so the copies run under its tail.  Shared row rr belongs to
+    // warp rr >> 1: (SwiGLU) the gate row o and the up row N + o of output o; else two
+    // consecutive rows.
+    TW* wsm = reinterpret_cast<TW*>(hs + NB * K);  // [kRowsPerCta][K], after the input vectors
+    const int c16 = K * (int)sizeof(TW) / 16;       // 16-byte chunks per row
+    const int half = kRowsPerCta / 2;
+    for (int e = tid; e < kRowsPerCta * c16; e += kGemvThreads) {
+        const int rr = e / c16, c = e - rr * c16;
+        const int o = blk * half + (rr >> 1);
+        const int row = swiglu ? ((rr & 1) ? a.N + o : o) : blk * kRowsPerCta + rr;
+        const bool lv = swiglu ? o < a.N : row < a.N;
+        if (lv)
+            cp_async16(reinterpret_cast<char*>(wsm + (size_t)rr * K) + c * 16,
+                       reinterpret_cast<const char*>(static_cast<const TW*>(a.w) + (int64_t)row * a.ldw) + c * 16);
     }
-    const int nrows_total = swiglu ? 2 * a.N : a.N;
-    const bool live0 = swiglu ? on < a.N : rows[0] < nrows_total;
-    const bool live1 = swiglu ? on < a.N : rows[1] < nrows_total;
-    const TW* w0 = static_cast<const TW*>(a.w) + (int64_t)(live0 ? rows[0] : 0) * a.ldw;
-    const TW* w1 = static_cast<const TW*>(a.w) + (int64_t)(live1 ? rows[1] : 0) * a.ldw;
-    const int nch = K / 8;
-    Chunk8<TW> pf0[kPrefetch], pf1[kPrefetch];
+    cp_async_commit();
+    const int on = swiglu ? blk * half + warp : -1;  // SwiGLU output of this warp
+    int rows[2];
+    rows[0] = swiglu ? on : blk * kRowsPerCta + warp * kRowsPerWarp;
+    rows[1] = swiglu ? a.N + on : rows[0] + 1;
+    const bool live0 = swiglu ? on < a.N : rows[0] < a.N;
+    const bool live1 = swiglu ? on < a.N : rows[1] < a.N;
+    // ---- epilogue weights of the warp's rows (bias, residual gate or conv taps), also
+    // independent of the previous kernel
+    float ew[2][8];
 #pragma unroll
-    for (int j = 0; j < kPrefetch; ++j) {
-        const int c = lane + 32 * j;
-        if (c < nch) {
-            if (live0) load_raw8<TW>(w0 + c * 8, pf0[j]);
-            if (live1) load_raw8<TW>(w1 + c * 8, pf1[j]);
+    for (int r = 0; r < 2; ++r) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ew[r][j] = 0.f;
+        const bool lv = r == 0 ? live0 : live1;
+        const int n = rows[r];
+        if (!lv) continue;
+        if (a.epi == EPI_STORE && a.bias) ew[r][0] = a.bias[n];
+        else if (a.epi == EPI_RESIDUAL) ew[r][0] = a.gate[n];
+        else if (a.epi == EPI_DGDA && n < a.nconv) {
+            // history taps in slots 0..ktaps-2, the current token's tap in slot 7
+            const TW* tp = static_cast<const TW*>(a.taps) + (int64_t)n * a.ktaps;
+#pragma unroll
+            for (int j = 0; j < 7; ++j)
+                if (j < a.ktaps - 1) ew[r][j] = Cvt<TW>::to_f(tp[j]);
+            ew[r][7] = Cvt<TW>::to_f(tp[a.ktaps - 1]);
         }
     }
     wait();
-    __syncthreads();  // a persistent CTA's previous block may still read hs
+    __syncthreads();
+    // ---- the epilogue's inputs written by earlier kernels (lane b: batch row b), in flight
+    // during the prologue and the products
+    float ev[2][8];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ev[r][j] = 0.f;
+        const bool lv = r == 0 ? live0 : live1;
+        const int n = rows[r];
+        if (!lv || lane >= a.B) continue;
+        if (a.epi == EPI_RESIDUAL) ev[r][0] = a.xres[lane * a.ldr + n];
+        else if (a.epi == EPI_DGDA && n < a.nconv) {
+            const float* h = a.hist + lane * a.ldh + (int64_t)n * (a.ktaps - 1);
+#pragma unroll
+            for (int j = 0; j < 7; ++j)
+                if (j < a.ktaps - 1) ev[r][j] = h[j];
+        }
+    }
     // ---- prologue: the NB input vectors in shared memory (fp32)
     if (a.pro == PRO_NORM) {
         for (int b = 0; b < NB; ++b) {
@@ -193,6 +326,7 @@ __device__ __forceinline__ void gemv_body(const GemvArgs& a, int blk, float* hs,
                 hs[b * K + k] = v;
             }
     }
+    cp_async_wait_all();
     __syncthreads();
 
     float acc[2][NB];
@@ -200,34 +334,13 @@ __device__ __forceinline__ void gemv_body(const GemvArgs& a, int blk, float* hs,
     for (int r = 0; r < 2; ++r)
 #pragma unroll
         for (int b = 0; b < NB; ++b) acc[r][b] = 0.f;
-    auto fma_chunk = [&](int c, const float* v0, const float* v1) {
-#pragma unroll
-        for (int b = 0; b < NB; ++b) {
-            const float4 h0 = *reinterpret_cast<const float4*>(hs + b * K + c * 8);
-            const float4 h1 = *reinterpret_cast<const float4*>(hs + b * K + c * 8 + 4);
-            const float hv[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
-            if (live0)
-#pragma unroll
-                for (int i = 0; i < 8; ++i) acc[0][b] = fmaf(v0[i], hv[i], acc[0][b]);
-            if (live1)
-#pragma unroll
-                for (int i = 0; i < 8; ++i) acc[1][b] = fmaf(v1[i], hv[i], acc[1][b]);
-        }
-    };
-#pragma unroll
-    for (int j = 0; j < kPrefetch; ++j) {
-        const int c = lane + 32 * j;
-        if (c < nch) {
-            float v0[8], v1[8];
-            unpack8<TW>(pf0[j], v0);
-            unpack8<TW>(pf1[j], v1);
-            fma_chunk(c, v0, v1);
-        }
-    }
-    for (int c = lane + 32 * kPrefetch; c < nch; c += 32) {
+    const TW* w0 = wsm + (size_t)(2 * warp) * K;
+    const TW* w1 = w0 + K;
+    const int nch = K / 8;
+    for (int c = lane; c < nch; c += 32) {
         float v0[8], v1[8];
-        if (live0) load_chunk8<TW>(w0 + c * 8, v0);
-        if (live1) load_chunk8<TW>(w1 + c * 8, v1);
+        if (live0) load_chunk8_smem<TW>(w0 + c * 8, v0);
+        if (live1) load_chunk8_smem<TW>(w1 + c * 8, v1);
 #pragma unroll
         for (int b = 0; b < NB; ++b) {
             const float4 h0 = *reinterpret_cast<const float4*>(hs + b * K + c * 8);
@@ -262,26 +375,26 @@ __device__ __forceinline__ void gemv_body(const GemvArgs& a, int blk, float* hs,
             }
             continue;
         }
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            const bool lv = r == 0 ? live0 : live1;
-            if (!lv) continue;
-            const int n = rows[r];
-            float y = acc[r][b];
+        // one output row: n, its value y, its epilogue weights tw and dependent inputs hv
+        auto row_out = [&](int n, float y, const float (&tw)[8], const float (&hv)[8]) {
             if (a.epi == EPI_STORE) {
-                if (a.bias) y += a.bias[n];
+                if (a.bias) y += tw[0];
                 if (a.out_f32) static_cast<float*>(a.out)[b * a.ldo + n] = y;
                 else static_cast<TW*>(a.out)[b * a.ldo + n] = Cvt<TW>::from_f(y);
             } else if (a.epi == EPI_RESIDUAL) {
-                a.xres[b * a.ldr + n] += a.gate[n] * y;
+                a.xres[b * a.ldr + n] = fmaf(tw[0], y, hv[0]);
             } else if (a.epi == EPI_DGDA) {
                 float f;
                 if (n < a.nconv) {
-                    const TW* tp = static_cast<const TW*>(a.taps) + (int64_t)n * a.ktaps;
+                    // causal conv over the history (oldest first) and this token, then SiLU
                     float* h = a.hist + b * a.ldh + (int64_t)n * (a.ktaps - 1);
-                    float cv = Cvt<TW>::to_f(tp[a.ktaps - 1]) * y;
-                    for (int j = 0; j < a.ktaps - 1; ++j) cv = fmaf(Cvt<TW>::to_f(tp[j]), h[j], cv);
-                    for (int j = 0; j + 1 < a.ktaps - 1; ++j) h[j] = h[j + 1];
+                    float cv = tw[7] * y;
+#pragma unroll
+                    for (int j = 0; j < 7; ++j)
+                        if (j < a.ktaps - 1) cv = fmaf(tw[j], hv[j], cv);
+#pragma unroll
+                    for (int j = 0; j < 6; ++j)
+                        if (j + 1 < a.ktaps - 1) h[j] = hv[j + 1];
                     if (a.ktaps > 1) h[a.ktaps - 2] = y;
                     f = silu_f(cv);
                 } else if (n < a.a_end) {
@@ -295,7 +408,22 @@ __device__ __forceinline__ void gemv_body(const GemvArgs& a, int blk, float* hs,
                 const unsigned long long k = argmax_key(y, n);
                 mykey[b] = k > mykey[b] ? k : mykey[b];
             }
-        }
+        };
+        if (live0) row_out(rows[0], acc[0][b], ew[0], ev[0]);
+        if (live1) row_out(rows[1], acc[1][b], ew[1], ev[1]);
+    }
+    if constexpr (MIX) {
+        // the head's last CTA (its rows are one head's slice of one section) runs the step
+        const int h = dgda_head_of_row(a.st, blk * kRowsPerCta);
+        __threadfence();
+        __syncthreads();
+        if (tid == 0) last = atomicAdd(a.st_tickets + h, 1u) == (unsigned)a.st_per_head - 1 ? 1u : 0u;
+        __syncthreads();
+        if (!last) return;
+        __threadfence();
+        for (int b = 0; b < a.B; ++b) state_step_cta(a.st, b, h);
+        if (tid == 0) a.st_tickets[h] = 0u;
+        return;
     }
     if (a.epi != EPI_LOGITS) return;
     // ---- argmax: warp -> CTA -> global key, the last CTA publishes the ids
@@ -327,30 +455,13 @@ __device__ __forceinline__ void gemv_body(const GemvArgs& a, int blk, float* hs,
     }
 }
 
-template <typename TW, int NB>
+// MIX: the DGDA mixer form (EPI_DGDA with the recurrence step in each head's last CTA)
+template <typename TW, int NB, bool MIX>
 __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvArgs a) {
-    extern __shared__ float hs[];  // [NB][K] input vectors
+    extern __shared__ float hs[];  // [NB][K] input vectors, then the CTA's weight rows
     griddep_launch_dependents();
-    gemv_body<TW, NB>(a, blockIdx.x, hs, [] { griddep_wait(); });
+    gemv_body<TW, NB, MIX>(a, blockIdx.x, hs, [] { griddep_wait(); });
 }
-
-// One recurrence step: k L2-norm, S' = a*S + k (w*v - (b*k)^T (a*S)), o = q^T S'.
-// The columns of S evolve independently (delta_j and o_j only involve column j),
-// so one CTA owns a group of 16 columns of one (batch, head) for all dk rows:
-// thread (ty, tx) holds rows ty, ty+16, ... of column tx, and the two sums over
-// rows go through shared memory.
-constexpr int kStateCols = 16;
-constexpr int kStateThreads = 256;
-
-struct StateArgs {
-    const float* feats; int64_t ldf;  // [B, 4*H*dk + 2*H*dv] decode features
-    float* state;                     // [B, H, dk, dv]
-    float* o; int64_t ldo;            // [B, H*dv]
-    int B, H, dk, dv;
-    int off_q, off_k, off_v, off_a, off_b, off_w;
-    float eps;
-    int nblocks;                      // H * ceil(dv / kStateCols) * B
-};
 
 template <class Wait>
 __device__ __forceinline__ void state_body(const StateArgs& a, int blk, Wait wait) {
@@ -605,7 +716,8 @@ int launch_gemv(GemvArgs& a, cudaStream_t s) {
     const int per_cta = a.epi == EPI_SWIGLU ? kRowsPerCta / 2 : kRowsPerCta;
     const unsigned grid = (unsigned)ceil_div(outs, per_cta);
     int nb = a.B <= 1 ? 1 : a.B <= 2 ? 2 : a.B <= 4 ? 4 : 8;
-    const size_t smem = sizeof(float) * (size_t)nb * a.K;
+    // input vectors [nb][K] fp32, then the CTA's weight rows [kRowsPerCta][K]
+    const size_t smem = sizeof(float) * (size_t)nb * a.K + sizeof(TW) * (size_t)kRowsPerCta * a.K;
     if (smem > 200 * 1024) return set_error(MABA_ERR_UNSUPPORTED, "decode_gemv: B x K too large for shared memory");
     a.nblocks = (int)grid;
     auto go = [&](auto kern) {
@@ -613,11 +725,12 @@ int launch_gemv(GemvArgs& a, cudaStream_t s) {
         MABA_TRY(launch_pdl(kern, dim3(grid), dim3(kGemvThreads), smem, s, a));
         return check_launch("decode_gemv");
     };
+    const bool mix = a.st_tickets != nullptr;
     switch (nb) {
-        case 1: return go(gemv_kernel<TW, 1>);
-        case 2: return go(gemv_kernel<TW, 2>);
-        case 4: return go(gemv_kernel<TW, 4>);
-        default: return go(gemv_kernel<TW, 8>);
+        case 1: return mix ? go(gemv_kernel<TW, 1, true>) : go(gemv_kernel<TW, 1, false>);
+        case 2: return mix ? go(gemv_kernel<TW, 2, true>) : go(gemv_kernel<TW, 2, false>);
+        case 4: return mix ? go(gemv_kernel<TW, 4, true>) : go(gemv_kernel<TW, 4, false>);
+        default: return mix ? go(gemv_kernel<TW, 8, true>) : go(gemv_kernel<TW, 8, false>);
     }
 }
 
@@ -881,6 +994,43 @@ extern "C" int maba_decode_gemv(const maba_tensor* w, int32_t prologue, const ma
     int dt = 0;
     MABA_TRY(build_gemv(a, dt, w, prologue, x, aux, eps, ids, epilogue, out, bias, gate, taps, hist, n_conv,
                         alpha_end, ids_out, pos_dev, workspace, workspace_bytes));
+    cudaStream_t s = as_stream(stream);
+    switch (dt) {
+        case MABA_F32: return launch_gemv<float>(a, s);
+        case MABA_F16: return launch_gemv<__half>(a, s);
+        default: return launch_gemv<__nv_bfloat16>(a, s);
+    }
+}
+
+extern "C" size_t maba_decode_dgda_mix_workspace_size(int32_t n_heads) {
+    return (size_t)(n_heads > 0 ? n_heads : 1) * 4 + 16;
+}
+
+extern "C" int maba_decode_dgda_mix(const maba_tensor* w, const maba_tensor* x, const maba_tensor* norm_w, float eps,
+                                    const maba_tensor* taps, const maba_tensor* hist, const maba_tensor* feats,
+                                    const maba_tensor* state, const maba_tensor* o_out, int32_t n_heads, float k_eps,
+                                    void* workspace, size_t workspace_bytes, void* stream) {
+    using namespace maba;
+    if (!present(state) || state->ndim != 4)
+        return set_error(MABA_ERR_INVALID, "decode_dgda_mix: state must be float32 [B, H, dk, dv]");
+    const int64_t H = state->shape[1], dk = state->shape[2], dv = state->shape[3];
+    if (dk % 16 != 0 || dv % 16 != 0 || dk > 64 || dv > 64)
+        return set_error(MABA_ERR_UNSUPPORTED, "decode_dgda_mix: head dims must be multiples of 16, at most 64");
+    const int cqk = (int)(H * dk), cv = (int)(H * dv);
+    if (!present(w) || w->ndim != 2 || w->shape[0] != 4 * (int64_t)cqk + 2 * cv)
+        return set_error(MABA_ERR_INVALID, "decode_dgda_mix: w must hold the 4*H*dk + 2*H*dv stacked rows");
+    GemvArgs a;
+    int dt = 0;
+    MABA_TRY(build_gemv(a, dt, w, PRO_NORM, x, norm_w, eps, nullptr, EPI_DGDA, feats, nullptr, nullptr, taps, hist,
+                        2 * cqk + cv, 3 * cqk + cv, nullptr, nullptr, nullptr, 0));
+    MABA_TRY(build_state(a.st, feats, state, o_out, n_heads, k_eps));
+    if (a.st.B != a.B) return set_error(MABA_ERR_INVALID, "decode_dgda_mix: x and state batches differ");
+    if (workspace == nullptr || workspace_bytes < maba_decode_dgda_mix_workspace_size(n_heads) ||
+        (reinterpret_cast<uintptr_t>(workspace) & 3u))
+        return set_error(MABA_ERR_WORKSPACE, "decode_dgda_mix: zeroed, 4-byte aligned workspace of %zu bytes required",
+                         maba_decode_dgda_mix_workspace_size(n_heads));
+    a.st_tickets = static_cast<unsigned int*>(workspace);
+    a.st_per_head = (int)((4 * dk + 2 * dv) / kRowsPerCta);
     cudaStream_t s = as_stream(stream);
     switch (dt) {
         case MABA_F32: return launch_gemv<float>(a, s);

@@ -15,10 +15,11 @@ the GPU, and runs
   indexer, the fused three-stream attention in latent space, and one output GEMM
   whose weight folds the value up-projection into o_proj (W_o W_uv); residual
   adds and RMSNorms fused into one kernel; the residual stream in float32;
-* **decode** one token per step in 5 launches per DGDA block and 9 per MABA-SA
+* **decode** one token per step in 4 launches per DGDA block and 9 per MABA-SA
   block: GEMVs with the RMSNorm in their prologue and the conv/gates, SwiGLU,
-  gated residual add or logits-with-argmax in their epilogue, the recurrence
-  kernel, and the O(1)-append latent / index-key caches with the split decode
+  gated residual add or logits-with-argmax in their epilogue (a DGDA block's
+  input GEMV also runs each head's recurrence step in the CTA that finishes the
+  head's rows last), and the O(1)-append latent / index-key caches with the split decode
   top-k and split-K decode attention at a device-held position, so one step is
   captured once as a CUDA graph and replayed.
 
@@ -394,6 +395,10 @@ class DecodeSession:
         self.ids_buf = torch.zeros(batch, dtype=torch.long, device=dev)
         self.pos_dev = torch.zeros((), dtype=torch.long, device=dev)
         self.ws_head = torch.zeros(lib.maba_decode_gemv_workspace_size(batch), dtype=torch.uint8, device=dev)
+        # DGDA blocks: input projection, features and recurrence step in one launch when the head
+        # dims allow (maba_decode_dgda_mix), else a GEMV with the features epilogue + the step kernel
+        self.fuse_mix = s.d_k % 16 == 0 and s.d_v % 16 == 0 and s.d_k <= 64 and s.d_v <= 64
+        self.ws_mix = torch.zeros(lib.maba_decode_dgda_mix_workspace_size(H), dtype=torch.uint8, device=dev)
         self.graph = None
 
     # ------------------------------------------------------------------
@@ -421,8 +426,9 @@ class DecodeSession:
                 ws.numel() if ws is not None else 0)
 
     def _plan(self):
-        """One decode step as a list of pieces: ("gemv", args), ("state", layer) and ("sa", layer) -- the
-        cache append, split top-k and split-K attention of a MABA-SA layer."""
+        """One decode step as a list of pieces: ("gemv", args), ("mix", layer) -- a DGDA block's input
+        projection, features and recurrence step --, ("state", layer) and ("sa", layer) -- the cache
+        append, split top-k and split-K attention of a MABA-SA layer."""
         e, s = self.engine, self.engine.shape
         B, H, dc = self.B, s.n_heads, s.d_c
         g = self._gemv_args
@@ -436,9 +442,13 @@ class DecodeSession:
                 plan.append(("gemv", g(W.w_ov, PRO_VEC, x=self.sa[i].o_lat.view(B, H * dc), epi=EPI_RESIDUAL,
                                        out=self.x, gate=L.g1)))
             else:
-                plan.append(("gemv", g(W.w_in, PRO_NORM, x=self.x, aux=L.n1, epi=EPI_DGDA, out=self.feats,
-                                       taps=W.taps, hist=self.hists[i], n_conv=W.n_conv, alpha_end=W.alpha_end)))
-                plan.append(("state", i))
+                if self.fuse_mix:
+                    plan.append(("mix", i))
+                else:
+                    plan.append(("gemv", g(W.w_in, PRO_NORM, x=self.x, aux=L.n1, epi=EPI_DGDA, out=self.feats,
+                                           taps=W.taps, hist=self.hists[i], n_conv=W.n_conv,
+                                           alpha_end=W.alpha_end)))
+                    plan.append(("state", i))
                 plan.append(("gemv", g(W.w_o, PRO_VEC, x=self.o, epi=EPI_RESIDUAL, out=self.x, gate=L.g1)))
             plan.append(("gemv", g(L.w_gu, PRO_NORM, x=self.x, aux=L.n2, epi=EPI_SWIGLU, out=self.a)))
             plan.append(("gemv", g(L.w_down, PRO_VEC, x=self.a, epi=EPI_RESIDUAL, out=self.x, gate=L.g2)))
@@ -475,6 +485,15 @@ class DecodeSession:
             s.hca_r, wa.data_ptr() if wa is not None else None, wa.numel() if wa is not None else 0, st),
             "maba_sa_attention_decode_at")
 
+    def _mix(self, i: int, st: int) -> None:
+        e, L = self.engine, self.engine.layers[i]
+        W = L.mix
+        N.check(N.lib().maba_decode_dgda_mix(
+            N.ref(N.desc(W.w_in)), N.ref(N.desc(self.x)), N.ref(N.desc(L.n1)), float(e.shape.rms_eps),
+            N.ref(N.desc(W.taps)), N.ref(N.desc(self.hists[i])), N.ref(N.desc(self.feats)),
+            N.ref(N.desc(self.states[i])), N.ref(N.desc(self.o)), e.shape.n_heads, float(e.shape.k_eps),
+            self.ws_mix.data_ptr(), self.ws_mix.numel(), st), "maba_decode_dgda_mix")
+
     def _state(self, i: int, st: int) -> None:
         N.check(N.lib().maba_decode_dgda_state(N.ref(N.desc(self.feats)), N.ref(N.desc(self.states[i])),
                                                N.ref(N.desc(self.o)), self.engine.shape.n_heads,
@@ -487,6 +506,8 @@ class DecodeSession:
         for kind, a in self._plan():
             if kind == "gemv":
                 N.check(lib.maba_decode_gemv(*self._gemv_c_args(a), st), "maba_decode_gemv")
+            elif kind == "mix":
+                self._mix(a, st)
             elif kind == "state":
                 self._state(a, st)
             else:
@@ -515,12 +536,10 @@ class DecodeSession:
         return int(total)
 
     def launches_per_step(self) -> int:
-        """Kernels of this library one decode step launches (the count the step's graph holds)."""
-        n = 3  # embedding, head projection, logits
-        for L in self.engine.layers:
-            n += 2  # SwiGLU in, down + residual
-            n += 7 if L.attn else 3  # SA: in, append, top-k partial + merge, attention partial + combine, out
-        return n
+        """Kernels of this library one decode step launches (the count the step's graph holds): one
+        per GEMV, fused DGDA mixer or recurrence step; five per MABA-SA middle (cache append, top-k
+        partial + merge, attention partial + combine)."""
+        return sum(5 if kind == "sa" else 1 for kind, _ in self._plan())
 
     @torch.no_grad()
     def step(self, ids: torch.Tensor) -> torch.Tensor:

@@ -69,6 +69,26 @@ def test_decode_equals_prefill_fp32(B, T, steps):
     assert_rel(torch.stack(got, 1), full[:, T:T + steps], 5e-4, "decode vs prefill")
 
 
+@pytest.mark.parametrize("tiny", [False, True])
+def test_fused_dgda_mix_equals_two_launch_form(tiny):
+    """maba_decode_dgda_mix (input GEMV + features + each head's recurrence step in the head's last
+    CTA) against the two-launch form (GEMV with the features epilogue, then the state kernel); the
+    101M layer shapes (d_k = d_v = 64, 10 heads) and the tiny model's (32, 2 heads)."""
+    cfg = tiny_config() if tiny else small_101m_shape()
+    eng = MabaEngine(cfg, init_state_dict(ModelShape.from_config(cfg), seed=31), dtype=torch.float32)
+    ids = torch.randint(0, cfg.vocab_size, (3, 100), generator=torch.Generator().manual_seed(32)).to(DEV)
+    fused, split = eng.new_session(batch=3, max_len=128), eng.new_session(batch=3, max_len=128)
+    split.fuse_mix = False
+    assert fused.fuse_mix and fused.launches_per_step() < split.launches_per_step()
+    fused.prefill(ids[:, :70])
+    split.prefill(ids[:, :70])
+    for t in range(70, 100):
+        a, b = fused.step(ids[:, t]).clone(), split.step(ids[:, t]).clone()
+        assert_rel(a, b, 1e-5, f"fused vs split step {t}")
+    for i in fused.states:
+        assert_rel(fused.states[i], split.states[i], 1e-5, f"state {i}")
+
+
 def test_graph_replay_matches_eager_steps():
     cfg = small_101m_shape(n_layers=8)
     sd = init_state_dict(ModelShape.from_config(cfg), seed=21)
@@ -90,7 +110,8 @@ def test_graph_replay_matches_eager_steps():
     # the bench's per-step accounting: every weight is read once per step
     weights = sum(t.numel() * t.element_size() for L in eng.layers for t in (L.w_gu, L.w_down, L.mix.w_in))
     assert graph.bytes_per_step() > weights
-    assert graph.launches_per_step() == 3 + sum(2 + (7 if L.attn else 3) for L in eng.layers)
+    assert graph.fuse_mix
+    assert graph.launches_per_step() == 3 + sum(2 + (7 if L.attn else 2) for L in eng.layers)
 
 
 def _reference_dir():
