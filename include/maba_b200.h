@@ -311,7 +311,7 @@ MABA_API int maba_swiglu(const maba_tensor* u, const maba_tensor* out, void* str
 
 /* maba_decode_gemv: one decode-step GEMV, out = W h, for B <= 8 rows.
  *   w: [rows, K] float32 / float16 / bfloat16, contiguous 16-byte-aligned rows, K % 8 == 0.
- *   prologue 0 (norm):   h = RMSNorm(x) * aux, x [B,K] float32, aux [K] (w's dtype);
+ *   prologue 0 (norm):   h = RMSNorm(x) * aux, x [B,K] float32, aux [K] (w's dtype), K <= 2048;
  *            1 (gather): h = aux[ids[b]], aux [V,K] embedding table, ids int64 [B];
  *            2 (vector): h = x, x [B,K] float32 or w's dtype.
  *   epilogue 0 (store):    out [B,rows] (float32 or w's dtype) = W h + bias (bias float32 [rows], optional);

@@ -265,6 +265,14 @@ __device__ __forceinline__ void gemv_body(const GemvArgs& a, int blk, float* hs,
             ew[r][7] = Cvt<TW>::to_f(tp[a.ktaps - 1]);
         }
     }
+    // the RMSNorm weight (a weight: loaded before the wait as well), K <= 8 * kGemvThreads
+    constexpr int kNormPer = 8;
+    float nwv[kNormPer];
+#pragma unroll
+    for (int j = 0; j < kNormPer; ++j) {
+        const int k = tid + j * kGemvThreads;
+        nwv[j] = (a.pro == PRO_NORM && k < K) ? Cvt<TW>::to_f(static_cast<const TW*>(a.norm_w)[k]) : 0.f;
+    }
     wait();
     __syncthreads();
     // ---- the epilogue's inputs written by earlier kernels (lane b: batch row b), in flight
@@ -304,11 +312,11 @@ __device__ __forceinline__ void gemv_body(const GemvArgs& a, int blk, float* hs,
 #pragma unroll
             for (int w = 0; w < kGemvWarps; ++w) ss += red[w][b];
             const float r = rsqrtf(ss / (float)K + a.eps);
-            const TW* nw = static_cast<const TW*>(a.norm_w);
-            if (b < a.B)
-                for (int k = tid; k < K; k += kGemvThreads) hs[b * K + k] = hs[b * K + k] * r * Cvt<TW>::to_f(nw[k]);
-            else
-                for (int k = tid; k < K; k += kGemvThreads) hs[b * K + k] = 0.f;
+#pragma unroll
+            for (int j = 0; j < kNormPer; ++j) {
+                const int k = tid + j * kGemvThreads;
+                if (k < K) hs[b * K + k] = b < a.B ? hs[b * K + k] * r * nwv[j] : 0.f;
+            }
         }
     } else if (a.pro == PRO_GATHER) {
         const TW* e = static_cast<const TW*>(a.emb);
@@ -484,9 +492,12 @@ __device__ __forceinline__ void state_body(const StateArgs& a, int blk, Wait wai
     const int j = j0 + tx;
     const bool colv = j < dv;
     // the state is read after the wait: its last writer (this layer's step before) is only
-    // known to be complete once every kernel before this one is
+    // known to be complete once every kernel before this one is.  Before the wait its lines
+    // are only asked into L2 (a prefetch moves no data into this SM, so it cannot be stale).
+    if (tx == 0)
+        for (int r = ty; r < dk; r += RY) asm volatile("prefetch.global.L2 [%0];" ::"l"(S + (int64_t)r * dv + j0));
     wait();
-    __syncthreads();  // a persistent CTA's previous block may still read the shared arrays
+    __syncthreads();
     float sd[64 / RY];
 #pragma unroll
     for (int r = 0; r < 64 / RY; ++r) {
@@ -863,6 +874,7 @@ int build_gemv(GemvArgs& a, int& dt_out, const maba_tensor* w, int32_t prologue,
             return set_error(MABA_ERR_INVALID, "decode_gemv: x must be [B, K] with unit column stride");
         B = x->shape[0];
         if (prologue == PRO_NORM) {
+            if (K > 8 * kGemvThreads) return set_error(MABA_ERR_UNSUPPORTED, "decode_gemv: RMSNorm prologue K <= 2048");
             MABA_TRY(expect_dtype(x, "decode_gemv: x", MABA_F32));
             const int64_t sn[1] = {K};
             MABA_TRY(expect_shape(norm_w, "decode_gemv: norm_w", 1, sn));

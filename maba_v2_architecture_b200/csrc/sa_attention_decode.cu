@@ -315,30 +315,21 @@ __global__ void __launch_bounds__(32 * kMmaWarps) sa_decode_mma_kernel(SaArgs a,
         k1 = k0 + SPLIT_KEYS < p.nhca ? k0 + SPLIT_KEYS : p.nhca;
     }
     const int nk = k1 > k0 ? (int)(k1 - k0) : 0;
-    for (int i = tid; i < SPLIT_KEYS; i += NTHR) {
+    // key row of split key i (-1: none); the sparse stream reads its block from the top-k list
+    auto row_of = [&](int i) -> int64_t {
+        if (i >= nk) return -1;
         const int64_t n = k0 + i;
-        int64_t row = -1;
-        if (i < nk) {
-            if (stream == 0) {
-                row = n < p.nsink_extra ? n : p.lo + (n - p.nsink_extra);
-            } else if (stream == 1) {
-                const int64_t slot = n / a.block, off = n - slot * a.block;
-                const int64_t blk = a.top_idx[b * a.st[0] + slot * a.st[2]];
-                const int64_t tok = blk * a.block + off;
-                if (blk >= 0 && blk < nb_kv && tok <= pos) row = tok;
-            } else {
-                row = n;
-            }
+        if (stream == 0) return n < p.nsink_extra ? n : p.lo + (n - p.nsink_extra);
+        if (stream == 1) {
+            const int64_t slot = n / a.block, off = n - slot * a.block;
+            const int64_t blk = a.top_idx[b * a.st[0] + slot * a.st[2]];
+            const int64_t tok = blk * a.block + off;
+            return (blk >= 0 && blk < nb_kv && tok <= pos) ? tok : -1;
         }
-        rows[i] = row;
-    }
-    // queries: 16 rows of 16-bit values (rows >= H zero)
-    const T* qh = static_cast<const T*>(a.qhat);
-    for (int e = tid; e < 16 * DC; e += NTHR) {
-        const int r = e / DC, d = e - r * DC;
-        qs[r * LD + d] = r < H ? qh[b * a.sq[0] + r * a.sq[2] + d * a.sq[3]] : Cvt<T>::from_f(0.f);
-    }
-    __syncthreads();
+        return n;
+    };
+    // keys and queries in one round of loads: this thread's 16-byte key chunks (chunk e of
+    // the tile is key e / CPR, columns (e % CPR) * 8) and its query elements
     {
         const T* base = stream == 2 ? static_cast<const T*>(a.hca) + b * a.sh[0] : static_cast<const T*>(a.ckv) + b * a.sc[0];
         const int64_t rs = stream == 2 ? a.sh[1] : a.sc[1];
@@ -346,8 +337,25 @@ __global__ void __launch_bounds__(32 * kMmaWarps) sa_decode_mma_kernel(SaArgs a,
 #pragma unroll
         for (int j = 0; j < MAXL; ++j) {
             const int e = tid + j * NTHR;
-            const int64_t row = rows[e / CPR];
+            const int64_t row = row_of(e / CPR);
+            if ((e % CPR) == 0) rows[e / CPR] = row;
             v[j] = row >= 0 ? *reinterpret_cast<const uint4*>(base + row * rs + (e % CPR) * 8) : make_uint4(0u, 0u, 0u, 0u);
+        }
+        const T* qh = static_cast<const T*>(a.qhat);
+        const bool qvec = a.sq[3] == 1 && (a.sq[2] % 8) == 0 && (a.sq[0] % 8) == 0 &&
+                          (reinterpret_cast<uintptr_t>(qh) & 15u) == 0;
+        if (qvec) {
+            for (int e = tid; e < 16 * CPR; e += NTHR) {
+                const int r = e / CPR, c = e - r * CPR;
+                const uint4 q = r < H ? *reinterpret_cast<const uint4*>(qh + b * a.sq[0] + r * a.sq[2] + c * 8)
+                                      : make_uint4(0u, 0u, 0u, 0u);
+                *reinterpret_cast<uint4*>(qs + r * LD + c * 8) = q;
+            }
+        } else {
+            for (int e = tid; e < 16 * DC; e += NTHR) {
+                const int r = e / DC, d = e - r * DC;
+                qs[r * LD + d] = r < H ? qh[b * a.sq[0] + r * a.sq[2] + d * a.sq[3]] : Cvt<T>::from_f(0.f);
+            }
         }
 #pragma unroll
         for (int j = 0; j < MAXL; ++j) {

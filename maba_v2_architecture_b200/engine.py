@@ -15,11 +15,11 @@ the GPU, and runs
   indexer, the fused three-stream attention in latent space, and one output GEMM
   whose weight folds the value up-projection into o_proj (W_o W_uv); residual
   adds and RMSNorms fused into one kernel; the residual stream in float32;
-* **decode** one token per step in 4 launches per DGDA block and 9 per MABA-SA
+* **decode** one token per step in 5 launches per DGDA block and 9 per MABA-SA
   block: GEMVs with the RMSNorm in their prologue and the conv/gates, SwiGLU,
-  gated residual add or logits-with-argmax in their epilogue (a DGDA block's
-  input GEMV also runs each head's recurrence step in the CTA that finishes the
-  head's rows last), and the O(1)-append latent / index-key caches with the split decode
+  gated residual add or logits-with-argmax in their epilogue, the recurrence
+  kernel (or, with ``fuse_mix``, the recurrence run by each head's last CTA of the
+  DGDA input GEMV), and the O(1)-append latent / index-key caches with the split decode
   top-k and split-K decode attention at a device-held position, so one step is
   captured once as a CUDA graph and replayed.
 
@@ -395,9 +395,10 @@ class DecodeSession:
         self.ids_buf = torch.zeros(batch, dtype=torch.long, device=dev)
         self.pos_dev = torch.zeros((), dtype=torch.long, device=dev)
         self.ws_head = torch.zeros(lib.maba_decode_gemv_workspace_size(batch), dtype=torch.uint8, device=dev)
-        # DGDA blocks: input projection, features and recurrence step in one launch when the head
-        # dims allow (maba_decode_dgda_mix), else a GEMV with the features epilogue + the step kernel
-        self.fuse_mix = s.d_k % 16 == 0 and s.d_v % 16 == 0 and s.d_k <= 64 and s.d_v <= 64
+        # DGDA blocks: a GEMV with the features epilogue, then the recurrence-step kernel; with
+        # fuse_mix, one launch (maba_decode_dgda_mix: the step runs in each head's last CTA of the
+        # GEMV), which measured 2-3 % slower per token on the 101M model, so it is off by default
+        self.fuse_mix = False
         self.ws_mix = torch.zeros(lib.maba_decode_dgda_mix_workspace_size(H), dtype=torch.uint8, device=dev)
         self.graph = None
 

