@@ -248,7 +248,7 @@ def _reference_model_101m(sd16, n_layers=None):
     return m
 
 
-def config3_prefill(dev, steps: int = 3, warmup: int = 1, check_tokens: int = 256):
+def config3_prefill(dev, steps: int = 5, warmup: int = 3, check_tokens: int = 256):
     """Config 3: the 101M model (random N(0,0.02) weights, seed 2) on the engine, bf16, forward
     over B=8 x T=8,192 uniform ids; prefill tokens/s.  Parity: the logits of the first
     `check_tokens` positions of sequence 0 against the unmodified reference model on the CPU
@@ -266,16 +266,20 @@ def config3_prefill(dev, steps: int = 3, warmup: int = 1, check_tokens: int = 25
     for _ in range(warmup):
         out = eng.forward(ids)  # outputs kept alive as in the timed loop
     torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(steps):
+    # per-step device time (events around each step); the median step is reported, so that a
+    # host-side enqueue stall in one step (the GPU idles while the host launches) does not count
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+    ev[0].record()
+    for i in range(steps):
         out = eng.forward(ids)
-    e1.record()
+        ev[i + 1].record()
     torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / steps
+    per = sorted(ev[i].elapsed_time(ev[i + 1]) for i in range(steps))
+    ms = per[len(per) // 2]
     res = {"workload": "config3: 101M model (101,282,319 params) bf16, B=8 T=8192, random-init weights, "
                        "MabaEngine prefill (all logits)",
            "value": 8 * 8192 / (ms * 1e-3), "unit": "tok/s", "ms_per_step": ms, "steps": steps,
+           "step_ms_min_max": [per[0], per[-1]], "timing": "median of per-step CUDA-event times",
            "logits_finite": bool(torch.isfinite(out[:, -1].float()).all())}
     ref = _reference_model_101m({k: v.float() for k, v in sd.items()})
     if ref is not None:
