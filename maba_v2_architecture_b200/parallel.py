@@ -250,7 +250,7 @@ def sa_segment_phase_b(qhat_local, q_idx_local, gate_local, c_all: Sequence[torc
 
 
 def exchange_prefix(bufs: Sequence[torch.Tensor], bounds: Sequence[int], units: Sequence[int], rank: int,
-                    group=None) -> None:
+                    group=None, wait: bool = True):
     """Prefix exchange of per-token tables between the ranks of a sequence split.
 
     ``bufs[i]`` is a [B, bounds[-1] // units[i], d] table (one row per ``units[i]``
@@ -260,7 +260,9 @@ def exchange_prefix(bufs: Sequence[torch.Tensor], bounds: Sequence[int], units: 
     batch), since no query attends a later segment.  Rows of later ranks are left as they
     were.  Every rank issues its sends and receives in the same order, so the batch pairs
     up; the exchange is asynchronous to the host (NCCL runs it on its own stream and the
-    current stream waits for it)."""
+    current stream waits for it).  With ``wait=False`` the requests are returned instead and
+    the caller waits on them later (work queued on the current stream meanwhile overlaps the
+    transfers)."""
     world = len(bounds) - 1
     ops = []
     for buf, u in zip(bufs, units):
@@ -272,9 +274,12 @@ def exchange_prefix(bufs: Sequence[torch.Tensor], bounds: Sequence[int], units: 
                 lo, hi = bounds[seg] // u, bounds[seg + 1] // u
                 if hi > lo:
                     ops.append(dist.P2POp(dist.irecv if j < rank else dist.isend, buf[bi, lo:hi], j, group))
-    if ops:
-        for req in dist.batch_isend_irecv(ops):
-            req.wait()
+    reqs = dist.batch_isend_irecv(ops) if ops else []
+    if not wait:
+        return reqs
+    for req in reqs:
+        req.wait()
+    return None
 
 
 def sa_segment_tables(c_buf: torch.Tensor, cent_buf: torch.Tensor, hca_buf: torch.Tensor, k_idx_local: torch.Tensor,
