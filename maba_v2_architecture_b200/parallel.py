@@ -106,8 +106,9 @@ def balanced_segments(total: int, world: int, unit: int = 64, flat: float = 67.0
 # measured per-token costs on one B200 (ms per 1,000 tokens, bf16, H = 10): the attention
 # of a query at position p (in thousands of tokens) costs ATTN_FLAT + ATTN_SLOPE * p (the
 # pooled-HCA stream grows with the prefix), the DGDA prefill DGDA_MS; a segment transition
-# costs about TRANSITION times its prefill
-ATTN_FLAT, ATTN_SLOPE, DGDA_MS, TRANSITION = 0.0159, 7.54e-5, 0.0092, 1.3
+# costs about TRANSITION times its prefill (measured on eight B200s at 1,048,576 tokens: a
+# middle rank's transition 1.8-1.9x its output pass)
+ATTN_FLAT, ATTN_SLOPE, DGDA_MS, TRANSITION = 0.0159, 7.54e-5, 0.0092, 1.9
 
 
 def split_bounds(total: int, world: int, unit: int = 64, attn_flat: float = ATTN_FLAT,
