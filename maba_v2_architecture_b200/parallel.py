@@ -107,26 +107,37 @@ def balanced_segments(total: int, world: int, unit: int = 64, flat: float = 67.0
 # of a query at position p (in thousands of tokens) costs ATTN_FLAT + ATTN_SLOPE * p (the
 # pooled-HCA stream grows with the prefix), the DGDA prefill DGDA_MS; a segment transition
 # costs about TRANSITION times its prefill (measured on eight B200s at 1,048,576 tokens: a
-# middle rank's transition 1.8-1.9x its output pass)
-ATTN_FLAT, ATTN_SLOPE, DGDA_MS, TRANSITION = 0.0159, 7.54e-5, 0.0092, 1.9
+# middle rank's transition 1.8-1.9x its output pass); receiving the MABA-SA prefix tables
+# costs XFER_MS per thousand prefix tokens and runs under the rank's DGDA payload work
+ATTN_FLAT, ATTN_SLOPE, DGDA_MS, TRANSITION, XFER_MS = 0.0159, 7.54e-5, 0.0092, 1.9, 0.0021
+
+
+def split_cost(r: int, world: int, a: int, b: int, attn_flat: float = ATTN_FLAT, attn_slope: float = ATTN_SLOPE,
+               dgda: float = DGDA_MS, transition: float = TRANSITION, xfer: float = XFER_MS) -> float:
+    """Modelled device time (ms) of rank r holding tokens [a, b) of a split: its queries'
+    attention (flat + slope * position per token), its DGDA role (rank 0 one prefill; ranks
+    1..P-2 a transition, then an output pass; the last rank an output pass) and the receipt
+    of the prefix tables, which overlaps the transition."""
+    k = 1e-3  # costs are per thousand tokens
+    n = (b - a) * k
+    attn = attn_flat * n + 0.5 * attn_slope * ((b * k) ** 2 - (a * k) ** 2)
+    if r == 0:
+        return attn + dgda * n
+    payload = transition * dgda * n if r < world - 1 else 0.0
+    return attn + dgda * n + max(payload, xfer * a * k)
 
 
 def split_bounds(total: int, world: int, unit: int = 64, attn_flat: float = ATTN_FLAT,
-                 attn_slope: float = ATTN_SLOPE, dgda: float = DGDA_MS, transition: float = TRANSITION) -> List[int]:
+                 attn_slope: float = ATTN_SLOPE, dgda: float = DGDA_MS, transition: float = TRANSITION,
+                 xfer: float = XFER_MS) -> List[int]:
     """Segment boundaries [0, b_1, ..., total] (multiples of `unit`) that equalise each rank's
-    whole share of the split prefill: its queries' attention (flat + slope * position per
-    token) plus its DGDA role -- rank 0 one prefill of its segment, ranks 1..P-2 a transition
-    and a prefill, the last rank a prefill.  Found by bisection on the per-rank budget: each
-    rank takes the longest segment that fits it, and the last rank must fit too."""
+    modelled share of the split prefill (split_cost).  Found by bisection on the per-rank
+    budget: each rank takes the longest segment that fits it, and the last rank must fit too."""
     if world == 1:
         return [0, total]
-    k = 1e-3  # costs are per thousand tokens
 
     def cost(r, a, b):
-        n = (b - a) * k
-        attn = attn_flat * n + 0.5 * attn_slope * ((b * k) ** 2 - (a * k) ** 2)
-        role = 1.0 if r in (0, world - 1) else 1.0 + transition
-        return attn + role * dgda * n
+        return split_cost(r, world, a, b, attn_flat, attn_slope, dgda, transition, xfer)
 
     def assign(budget):
         bounds, a = [0], 0

@@ -146,12 +146,16 @@ def test_split_bounds_equalise_rank_costs(world):
     assert all(b % 64 == 0 for b in bnd) and all(x < y for x, y in zip(bnd, bnd[1:]))
     k = 1e-3
 
-    def cost(r, a, b):
+    def cost(r, a, b):  # the model restated: attention + DGDA role + prefix receipt under the payload
         n = (b - a) * k
-        role = 1.0 if r in (0, world - 1) else 1.0 + par.TRANSITION
-        return par.ATTN_FLAT * n + 0.5 * par.ATTN_SLOPE * ((b * k) ** 2 - (a * k) ** 2) + role * par.DGDA_MS * n
+        attn = par.ATTN_FLAT * n + 0.5 * par.ATTN_SLOPE * ((b * k) ** 2 - (a * k) ** 2)
+        if r == 0:
+            return attn + par.DGDA_MS * n
+        payload = par.TRANSITION * par.DGDA_MS * n if r < world - 1 else 0.0
+        return attn + par.DGDA_MS * n + max(payload, par.XFER_MS * a * k)
     c = [cost(r, a, b) for r, (a, b) in enumerate(zip(bnd, bnd[1:]))]
     assert max(c) / min(c) < 1.01
+    assert c == pytest.approx([par.split_cost(r, world, a, b) for r, (a, b) in enumerate(zip(bnd, bnd[1:]))])
 
 
 def test_sa_split_rejects_ragged_segments():
