@@ -107,9 +107,10 @@ def balanced_segments(total: int, world: int, unit: int = 64, flat: float = 67.0
 # of a query at position p (in thousands of tokens) costs ATTN_FLAT + ATTN_SLOPE * p (the
 # pooled-HCA stream grows with the prefix), the DGDA prefill DGDA_MS; a segment transition
 # costs about TRANSITION times its prefill (measured on eight B200s at 1,048,576 tokens: a
-# middle rank's transition 1.8-1.9x its output pass); receiving the MABA-SA prefix tables
-# costs XFER_MS per thousand prefix tokens and runs under the rank's DGDA payload work
-ATTN_FLAT, ATTN_SLOPE, DGDA_MS, TRANSITION, XFER_MS = 0.0159, 7.54e-5, 0.0092, 1.9, 0.0021
+# middle rank's transition 1.8-1.9x its output pass).  The MABA-SA prefix exchange took 1-2 ms
+# on every rank alike (senders and receivers), so by default it does not move the bounds;
+# XFER_MS per thousand received prefix tokens models an exchange that overlaps the transition.
+ATTN_FLAT, ATTN_SLOPE, DGDA_MS, TRANSITION, XFER_MS = 0.0159, 7.54e-5, 0.0092, 1.9, 0.0
 
 
 def split_cost(r: int, world: int, a: int, b: int, attn_flat: float = ATTN_FLAT, attn_slope: float = ATTN_SLOPE,
