@@ -199,6 +199,36 @@ __global__ void __launch_bounds__(kFeThreads) dgda_frontend_kernel(FeArgs a, int
 constexpr int kTileTok = 128;
 constexpr int kTileCh = 128;
 
+// 8 16-bit values <-> a 16-byte word, in registers (no addressable temporaries)
+template <typename T> __device__ __forceinline__ void unpack8_bits(const uint4& u, float* v);
+template <> __device__ __forceinline__ void unpack8_bits<__nv_bfloat16>(const uint4& u, float* v) {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        v[2 * i] = __uint_as_float(w[i] << 16);
+        v[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    }
+}
+template <> __device__ __forceinline__ void unpack8_bits<__half>(const uint4& u, float* v) {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        v[2 * i] = __half2float(__ushort_as_half((unsigned short)(w[i] & 0xffffu)));
+        v[2 * i + 1] = __half2float(__ushort_as_half((unsigned short)(w[i] >> 16)));
+    }
+}
+template <typename T> __device__ __forceinline__ uint32_t pack2_bits(float lo, float hi);
+template <> __device__ __forceinline__ uint32_t pack2_bits<__nv_bfloat16>(float lo, float hi) {
+    uint32_t d;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+    return d;
+}
+template <> __device__ __forceinline__ uint32_t pack2_bits<__half>(float lo, float hi) {
+    uint32_t d;
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+    return d;
+}
+
 template <typename T, int K>
 __global__ void __launch_bounds__(256, 4) dgda_frontend_tile_kernel(FeArgs a, int64_t ntt, int nct) {
     constexpr int ROWS = kTileTok + K - 1;
@@ -269,32 +299,36 @@ __global__ void __launch_bounds__(256, 4) dgda_frontend_tile_kernel(FeArgs a, in
             for (int i = 0; i < kVec; ++i) acc[i] = 0.f;
 #pragma unroll
             for (int j = 0; j < K; ++j) {
-                const uint4 u = *reinterpret_cast<const uint4*>(&xs[r + j][g * 8]);
-                const T* e = reinterpret_cast<const T*>(&u);
+                float e[kVec];
+                unpack8_bits<T>(*reinterpret_cast<const uint4*>(&xs[r + j][g * 8]), e);
 #pragma unroll
-                for (int i = 0; i < kVec; ++i) acc[i] = fmaf(w[i][j], Cvt<T>::to_f(e[i]), acc[i]);
+                for (int i = 0; i < kVec; ++i) acc[i] = fmaf(w[i][j], e[i], acc[i]);
             }
 #pragma unroll
             for (int i = 0; i < kVec; ++i) y[i] = silu_f(acc[i]);
         } else {
-            const uint4 u = *reinterpret_cast<const uint4*>(&xs[r + K - 1][g * 8]);
-            const T* e = reinterpret_cast<const T*>(&u);
+            float e[kVec];
+            unpack8_bits<T>(*reinterpret_cast<const uint4*>(&xs[r + K - 1][g * 8]), e);
 #pragma unroll
-            for (int i = 0; i < kVec; ++i) {
-                const float v = Cvt<T>::to_f(e[i]);
-                y[i] = s == 3 ? neg_softplus_clamped(v) : sigmoid_f(v);
-            }
+            for (int i = 0; i < kVec; ++i) y[i] = s == 3 ? neg_softplus_clamped(e[i]) : sigmoid_f(e[i]);
         }
-        float ss = 0.f;
+        if (s == 1) {  // per-head L2 norm of k (the section is the same for the whole CTA)
+            float ss = 0.f;
 #pragma unroll
-        for (int i = 0; i < kVec; ++i) ss = fmaf(y[i], y[i], ss);
-        for (int o = a.hw >> 1; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-        if (s == 1) {
+            for (int i = 0; i < kVec; ++i) ss = fmaf(y[i], y[i], ss);
+            for (int o = a.hw >> 1; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
             const float inv = 1.f / (sqrtf(ss) + a.eps);
 #pragma unroll
             for (int i = 0; i < kVec; ++i) y[i] *= inv;
         }
-        if (t < a.L) store8<T>(out + t * sec.so[1], sec.so[2], y);
+        if (t < a.L) {
+            T* op = out + t * sec.so[1];
+            if (sec.so[2] == 1 && (reinterpret_cast<uintptr_t>(op) & 15u) == 0)
+                *reinterpret_cast<uint4*>(op) = make_uint4(pack2_bits<T>(y[0], y[1]), pack2_bits<T>(y[2], y[3]),
+                                                           pack2_bits<T>(y[4], y[5]), pack2_bits<T>(y[6], y[7]));
+            else
+                store8<T>(op, sec.so[2], y);
+        }
     }
 }
 
