@@ -157,7 +157,7 @@ template <> __device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi
 }
 
 // EXACT = false: bound-referenced softmax (16-bit bf16 only); a CTA any of whose
-// head pairs misses the range condition appends its unit to redo_list.
+// rows shows underflow in a stream's sum appends its unit to redo_list.
 // EXACT = true: running-maximum softmax; with redo_list the grid covers the
 // listed units only (blocks past *redo_count return at once).
 template <typename T, bool EXACT>
@@ -176,6 +176,7 @@ __global__ void __launch_bounds__(NTHR, 1)
     uint64_t* bars = reinterpret_cast<uint64_t*>(base + LY.bars);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + LY.misc);
     volatile int* abort_f = reinterpret_cast<volatile int*>(base + LY.misc + 4);
+    volatile int* redo_f = reinterpret_cast<volatile int*>(base + LY.misc + 8);  // some row failed the bound check
     unsigned long long* umask = reinterpret_cast<unsigned long long*>(base + LY.umask);
     int* ulist = reinterpret_cast<int*>(base + LY.ulist);
     unsigned* bitmap = reinterpret_cast<unsigned*>(base + LY.bitmap);
@@ -206,6 +207,7 @@ __global__ void __launch_bounds__(NTHR, 1)
             mbar_init(&bars[i], cnt);
         }
         *abort_f = 0;
+        *redo_f = 0;
         fence_barrier_init();
     }
     if (warp == 0 && lane == 0) {
@@ -450,19 +452,17 @@ __global__ void __launch_bounds__(NTHR, 1)
         //
         // Reference maxima.  Softmax is invariant to the reference m subtracted from
         // the scores; it only has to keep every exponent in range.  Before a head
-        // pair's tiles, each row gets per stream an upper bound of its scores,
-        // |q| * (max key norm of the stream's tiles), and one exact score of a key it
-        // attends to (a probe).  With m = min(bound, probe + 60) every score s of the
-        // stream has s - m <= 60 and the stream maximum has max - m >= -60 (natural
-        // log units), whenever bound - probe <= 120: then P = exp(s - m) needs no
-        // running maximum, no rescale of O and no exchange between the two warps.
-        // When some row of the CTA misses that condition (or no key norms were
-        // given), the head pair runs the exact running-maximum form instead: the
-        // pair publishes its tiles' maxima to each other (named barriers used as
-        // producer -> consumer pairs) and replays the partner's, so both hold the
-        // same lazily rescaled reference at every tile.  Every named-barrier call is
-        // unconditional (a wait that ran out only skips TMEM work), so the two warps
-        // always make the same calls.
+        // pair's tiles, each row gets per stream the upper bound of its scores
+        // m = |q| * (max key norm of the stream's tiles): every score s has s - m <= 0,
+        // so P = exp(s - m) needs no running maximum, no rescale of O and no exchange
+        // between the two warps.  Underflow is checked afterwards: a stream whose row
+        // sum is below e^-60 (its maximum lies more than ~60 below the bound, where
+        // exponentials start to flush) sends the CTA to the running-maximum kernel, as
+        // do missing key norms.  In that kernel (EXACT) the pair publishes its tiles'
+        // maxima to each other (named barriers used as producer -> consumer pairs) and
+        // replays the partner's, so both hold the same lazily rescaled reference at
+        // every tile.  Every named-barrier call is unconditional (a wait that ran out
+        // only skips TMEM work), so the two warps always make the same calls.
         const int wg = warp >> 2;
         const int q4 = warp & 3;
         const int rid = q4 * 32 + lane;
@@ -579,46 +579,22 @@ __global__ void __launch_bounds__(NTHR, 1)
             const int qb = hq & 1;
             const bool okq = mbar_wait_warp(&bars[B_QFULL + qb], (hq >> 1) & 1, abort_f);
             okw = okw && okq;
-            float v0 = 0.f, v1 = 0.f;
-            if (!EXACT && okq && rvalid && tnc != nullptr) {
-                if (wg == 0) {
-                    v0 = qdot(qb, nullptr);
-                    v1 = qdot(qb, ckv + (int64_t)pos * a.sc[1]);
-                } else {
-                    if (probe_u >= 0) v0 = qdot(qb, ckv + (int64_t)probe_u * a.sc[1]);
-                    if (nv_hca > 0) v1 = qdot(qb, hcab);
-                }
-            }
+            float qq = 0.f;
+            if (!EXACT && okq && rvalid && tnc != nullptr) qq = qdot(qb, nullptr);
             __syncwarp();
             if (lane == 0) mbar_arrive(&bars[B_QEMPTY + qb]);  // Q read; the QK warp commits its last QK
             if constexpr (EXACT) {
                 r0 = r1 = r2 = 0.f;
                 return false;
             } else {
-                xref[(wg * 2 + 0) * 128 + rid] = v0;
-                xref[(wg * 2 + 1) * 128 + rid] = v1;
-                pair_sync(bar_pair);
-                const float qn = sqrtf(wg == 0 ? v0 : xref[0 * 128 + rid]) * 1.0001f;
-                const float pl = wg == 0 ? v1 : xref[1 * 128 + rid];
-                const float pu = wg == 1 ? v0 : xref[2 * 128 + rid];
-                const float ph = wg == 1 ? v1 : xref[3 * 128 + rid];
-                // the partner has read this warp's slots before either writes them again
-                pair_sync(bar_pair);
-                constexpr float RANGE = 60.f;
-                const float ul = qn * Mloc, uu = qn * Muni, uh = qn * Mhca;
-                r0 = fminf(ul, pl + RANGE) * LOG2E;
-                r1 = fminf(uu, pu + RANGE) * LOG2E;
-                r2 = fminf(uh, ph + RANGE) * LOG2E;
-                // streams without a key for this row take no reference
-                const bool rowok = !rvalid || ((ul - pl <= 2.f * RANGE) && (probe_u < 0 || uu - pu <= 2.f * RANGE) &&
-                                               (nv_hca == 0 || uh - ph <= 2.f * RANGE));
-                int all_ok;
-                asm volatile("{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
-                             "bar.red.and.pred q, 13, 256, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
-                             : "=r"(all_ok)
-                             : "r"((uint32_t)(rowok && tnc != nullptr))
-                             : "memory");
-                return all_ok != 0;
+                // the reference of each stream is the row's score bound |q| * (largest key norm
+                // of the stream's tiles): no exponent can overflow, and the epilogue sends the
+                // CTA to the running-maximum pass if some row's sum shows underflow
+                const float qn = sqrtf(qq) * 1.0001f;
+                r0 = qn * Mloc * LOG2E;
+                r1 = qn * Muni * LOG2E;
+                r2 = qn * Mhca * LOG2E;
+                return tnc != nullptr;
             }
         };
         float rl0, rl1, rl2;
@@ -858,6 +834,13 @@ __global__ void __launch_bounds__(NTHR, 1)
             const float L0 = l0 + xls[((wg ^ 1) * 3 + 0) * 128 + rid];
             const float L1 = l1 + xls[((wg ^ 1) * 3 + 1) * 128 + rid];
             const float L2 = l2 + xls[((wg ^ 1) * 3 + 2) * 128 + rid];
+            if constexpr (!EXACT) {
+                // a stream whose row sum fell below e^-60 (its largest score more than about 60
+                // below the bound) may have lost terms to the flush of small exponentials
+                constexpr float kMinL = 8.7e-27f;
+                if (rvalid && (L0 < kMinL || (probe_u >= 0 && L1 < kMinL) || (nv_hca > 0 && L2 < kMinL)))
+                    redo = true;
+            }
             if (okw) {
                 tc_fence_after();
                 const int h = hp * HPG + hh;
@@ -921,7 +904,7 @@ __global__ void __launch_bounds__(NTHR, 1)
             rl2 = nl2;
             fast = nfast;
         }
-        if (!EXACT && redo && warp == 0 && lane == 0 && redo_list != nullptr) redo_list[atomicAdd(redo_count, 1)] = unit;
+        if (!EXACT && redo) *redo_f = 1;
     }
     tc_fence_before();
     __syncthreads();
@@ -929,6 +912,7 @@ __global__ void __launch_bounds__(NTHR, 1)
         tc_fence_after();
         tmem_dealloc<TMEM_COLS>(tmem);
     }
+    if (!EXACT && tid == 0 && *redo_f && redo_list != nullptr) redo_list[atomicAdd(redo_count, 1)] = unit;
     if (tid == 0 && *abort_f) atomicExch(&g_device_error, 1);
 }
 
