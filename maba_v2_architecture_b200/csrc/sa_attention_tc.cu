@@ -80,8 +80,8 @@ constexpr uint32_t KV_BYTES = 2 * KV_HALF;
 constexpr uint32_t P_BYTES = ROWS * 128;    // 16 KB: P of one tile, 128 rows x 64 keys (16-bit)
 
 enum { B_QFULL = 0, B_QEMPTY = 2, B_KVFULL = 4, B_KVEMPTY = B_KVFULL + NS, B_SFULL = B_KVEMPTY + NS,
-       B_PFULL = B_SFULL + 2, B_ODONE = B_PFULL + 2, B_SFREE = B_ODONE + 4, B_DRAIN = B_SFREE + 2,
-       N_BARS = B_DRAIN + 2 };
+       B_PFULL = B_SFULL + 2, B_ODONE = B_PFULL + 4, B_SFREE = B_ODONE + 4, B_DRAIN = B_SFREE + 2,
+       B_OFREE = B_DRAIN + 2, N_BARS = B_OFREE + 1 };
 static_assert(N_BARS <= 32, "barrier area holds 32 mbarriers");
 
 struct TcLayout {
@@ -202,7 +202,8 @@ __global__ void __launch_bounds__(NTHR, 1)
     if (tid == 0) {
         for (int i = 0; i < N_BARS; ++i) {
             uint32_t cnt = 1;
-            if (i == B_PFULL || i == B_PFULL + 1 || i == B_SFREE || i == B_SFREE + 1) cnt = 128;
+            if ((i >= B_PFULL && i < B_PFULL + 4) || i == B_SFREE || i == B_SFREE + 1) cnt = 128;
+            if (i == B_OFREE) cnt = 8;  // the softmax warps, once they have read a head pair's O
             if (i == B_QEMPTY || i == B_QEMPTY + 1) cnt = 1 + 8;  // the last QK's commit + 8 softmax warps
             mbar_init(&bars[i], cnt);
         }
@@ -418,8 +419,14 @@ __global__ void __launch_bounds__(NTHR, 1)
             const uint64_t pd0 = sdesc_sw128(smem_addr(Ps), 16, 1024);
             int ij = 0;
             for (int i = 0; i < G; ++i) {
-                const int st = i % NS, sb = i & 1;
-                if (!mbar_wait_warp(&bars[B_PFULL + sb], (i >> 1) & 1, abort_f)) break;
+                const int st = i % NS;
+                // (bound-referenced kernel) a head pair's first PV overwrites O: every softmax
+                // warp has read the previous head pair's O
+                if (!EXACT && ij == 0 && i > 0 && !mbar_wait_warp(&bars[B_OFREE], ((i / n_tiles) - 1) & 1, abort_f))
+                    break;
+                // P(i) completes phase i >> 2 of barrier i & 3: consecutive phases of one barrier
+                // are four tiles apart, and P(i + 4) needs PV(i) done, so no phase is skipped
+                if (!mbar_wait_warp(&bars[B_PFULL + (i & 3)], (i >> 2) & 1, abort_f)) break;
                 tc_fence_after();
                 const int stream = ij < n_local ? 0 : (ij < n_local + U ? 1 : 2);
                 const bool first = ij == 0 || ij == n_local || ij == n_local + U;
@@ -684,7 +691,7 @@ __global__ void __launch_bounds__(NTHR, 1)
                             fence_proxy_async_smem();
                         }
                     }
-                    mbar_arrive(&bars[B_PFULL + wg]);
+                    mbar_arrive(&bars[B_PFULL + (gg & 3)]);
                 }
             } else {
             float m_cur = -INFINITY, l_cur = 0.f;
@@ -807,7 +814,7 @@ __global__ void __launch_bounds__(NTHR, 1)
                     }
                     tmem_wait_st();
                     tc_fence_before();
-                    mbar_arrive(&bars[B_PFULL + wg]);
+                    mbar_arrive(&bars[B_PFULL + (gg & 3)]);
                 }
                 // the partner's last tile, if it owns it
                 if (((gend - 1) & 1) != wg) {
@@ -895,10 +902,16 @@ __global__ void __launch_bounds__(NTHR, 1)
                     }
                 }
             }
-            // both warps have read O before either arrives for the next head pair's
-            // first tile (whose PV overwrites O)
+            // O has been read before the next head pair's first PV overwrites it: in the
+            // running-maximum kernel both warps meet here (its named-barrier exchanges
+            // stay in step), in the bound-referenced one the PV warp waits for O_FREE
             tc_fence_before();
-            pair_sync(bar_pair);
+            if constexpr (EXACT) {
+                pair_sync(bar_pair);
+            } else {
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bars[B_OFREE]);
+            }
             rl0 = nl0;
             rl1 = nl1;
             rl2 = nl2;
