@@ -193,7 +193,7 @@ MY_LAUNCHES_PER_STEP = None  # filled from the op list below
 # DRAM bytes per launch of the two candidate dominant kernels, from the ncu captures
 # summarised under profiles/ (read + write of one launch on this workload)
 # (attention: the T=32,768 capture scaled by 2, the units of a T=65,536 launch)
-TRAFFIC = {"sa_attention": 2 * (101.41e6 + 41.49e6), "dgda_prefill": 503.6e6 + 299.2e6}
+TRAFFIC = {"sa_attention": 2 * (101.19e6 + 41.92e6), "dgda_prefill": 503.6e6 + 299.2e6}
 TRAFFIC_FILE = {"sa_attention": "sa_attention_tc_config2.md", "dgda_prefill": "dgda_prep_config2.md"}
 
 
