@@ -332,6 +332,150 @@ __global__ void __launch_bounds__(256, 4) dgda_frontend_tile_kernel(FeArgs a, in
     }
 }
 
+// Persistent double-buffered form of the tiled kernel: each CTA walks the tiles
+// blockIdx.x, blockIdx.x + gridDim.x, ... and copies the next tile's input rows (and
+// its conv taps) into the other shared-memory stage with cp.async while it computes
+// the current one, so the loads of one tile run under the conv and gates of the
+// previous.  Rows before token 0 are zero-filled by the copy and then overwritten
+// from the conv history; rows past the end are zero-filled.  Needs 16-byte aligned
+// contiguous taps ([C, K] rows of K 16-bit values) and K <= 8.
+__device__ __forceinline__ void fe_cp16(void* dst, const void* src, bool valid) {
+    // cp.async with a source size of 0 writes zeros (the source is not read)
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+                 "l"(src), "r"(valid ? 16 : 0));
+}
+__device__ __forceinline__ void fe_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N> __device__ __forceinline__ void fe_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
+
+template <typename T, int K>
+__global__ void __launch_bounds__(256, 3) dgda_frontend_pipe_kernel(FeArgs a, int64_t ntt, int nct, int64_t ntiles) {
+    constexpr int ROWS = kTileTok + K - 1;
+    constexpr int LDS = kTileCh + 8;  // padded row (16-bit elements)
+    constexpr int TAPB = kTileCh * K * 2;  // bytes of one tile's taps (multiple of 16: K even or 128 channels)
+    extern __shared__ __align__(16) unsigned char fe_sm[];
+    T* xs0 = reinterpret_cast<T*>(fe_sm);                                  // [2][ROWS][LDS]
+    T* tp0 = reinterpret_cast<T*>(fe_sm + 2 * (size_t)ROWS * LDS * 2);     // [2][kTileCh * K]
+    const int tid = threadIdx.x;
+    const int g = tid & 15;   // channel group (8 channels)
+    const int tp = tid >> 4;  // token group
+    constexpr int TPT = kTileTok / 16;
+
+    struct Tile { int64_t b, t0; int s, cbase; };
+    auto decode = [&](int64_t blk) {
+        Tile tl;
+        const int ct = (int)(blk % nct);
+        blk /= nct;
+        tl.t0 = (blk % ntt) * kTileTok;
+        tl.b = blk / ntt;
+        tl.s = 0;
+        tl.cbase = ct * kTileCh;
+#pragma unroll
+        for (int i = 0; i < 5; ++i)
+            if (tl.cbase >= a.C[tl.s]) { tl.cbase -= a.C[tl.s]; ++tl.s; }
+        return tl;
+    };
+    auto issue = [&](int64_t blk, int stage) {
+        const Tile tl = decode(blk);
+        const FeSection& sec = a.sec[tl.s];
+        const T* x = static_cast<const T*>(sec.x) + tl.b * sec.sx[0] + (int64_t)tl.cbase * sec.sx[2];
+        T* xs = xs0 + (size_t)stage * ROWS * LDS;
+        for (int e = tid; e < ROWS * 16; e += 256) {
+            const int r = e >> 4, c8 = (e & 15) * 8;
+            const int64_t t = tl.t0 - (K - 1) + r;
+            const bool ok = t >= 0 && t < a.L;
+            fe_cp16(xs + r * LDS + c8, ok ? static_cast<const void*>(x + t * sec.sx[1] + c8) : static_cast<const void*>(x), ok);
+        }
+        if (tl.s < 3 && tid < TAPB / 16) {
+            const T* cw = static_cast<const T*>(a.conv[tl.s]) + (int64_t)tl.cbase * K;
+            fe_cp16(reinterpret_cast<unsigned char*>(tp0 + (size_t)stage * kTileCh * K) + tid * 16,
+                    reinterpret_cast<const unsigned char*>(cw) + tid * 16, true);
+        }
+        fe_commit();
+    };
+
+    int64_t blk = blockIdx.x;
+    if (blk < ntiles) issue(blk, 0);
+    for (int k = 0; blk < ntiles; ++k, blk += gridDim.x) {
+        const int stage = k & 1;
+        const int64_t nxt = blk + gridDim.x;
+        if (nxt < ntiles) {
+            issue(nxt, stage ^ 1);
+            fe_wait<1>();
+        } else {
+            fe_wait<0>();
+        }
+        __syncthreads();
+        const Tile tl = decode(blk);
+        const FeSection& sec = a.sec[tl.s];
+        const bool conv = tl.s < 3;
+        T* xs = xs0 + (size_t)stage * ROWS * LDS;
+        if (conv && tl.t0 == 0 && a.hist[tl.s] != nullptr) {
+            // the K-1 rows before token 0 come from the conv history
+            for (int e = tid; e < (K - 1) * kTileCh; e += 256) {
+                const int r = e / kTileCh, c = e - r * kTileCh;
+                const int64_t hj = r;  // history column (oldest first) = staged row r
+                const int64_t off = tl.b * a.sh[tl.s][0] + (int64_t)(tl.cbase + c) * a.sh[tl.s][1] + hj * a.sh[tl.s][2];
+                const float hv = a.hist_f32 ? static_cast<const float*>(a.hist[tl.s])[off]
+                                            : Cvt<T>::to_f(static_cast<const T*>(a.hist[tl.s])[off]);
+                xs[r * LDS + c] = Cvt<T>::from_f(hv);
+            }
+            __syncthreads();
+        }
+        T* out = static_cast<T*>(sec.out) + tl.b * sec.so[0] + (int64_t)(tl.cbase + g * 8) * sec.so[2];
+        float w[kVec][K];
+        if (conv) {
+            const T* tps = tp0 + (size_t)stage * kTileCh * K;
+#pragma unroll
+            for (int i = 0; i < kVec; ++i)
+#pragma unroll
+                for (int j = 0; j < K; ++j) w[i][j] = Cvt<T>::to_f(tps[(g * 8 + i) * K + j]);
+        }
+#pragma unroll 2
+        for (int u = 0; u < TPT; ++u) {
+            const int r = tp * TPT + u;  // token t0 + r, staged at row r + K - 1
+            const int64_t t = tl.t0 + r;
+            float y[kVec];
+            if (conv) {
+                float acc[kVec];
+#pragma unroll
+                for (int i = 0; i < kVec; ++i) acc[i] = 0.f;
+#pragma unroll
+                for (int j = 0; j < K; ++j) {
+                    float e[kVec];
+                    unpack8_bits<T>(*reinterpret_cast<const uint4*>(xs + (r + j) * LDS + g * 8), e);
+#pragma unroll
+                    for (int i = 0; i < kVec; ++i) acc[i] = fmaf(w[i][j], e[i], acc[i]);
+                }
+#pragma unroll
+                for (int i = 0; i < kVec; ++i) y[i] = silu_f(acc[i]);
+            } else {
+                float e[kVec];
+                unpack8_bits<T>(*reinterpret_cast<const uint4*>(xs + (r + K - 1) * LDS + g * 8), e);
+#pragma unroll
+                for (int i = 0; i < kVec; ++i) y[i] = tl.s == 3 ? neg_softplus_clamped(e[i]) : sigmoid_f(e[i]);
+            }
+            if (tl.s == 1) {  // per-head L2 norm of k
+                float ss = 0.f;
+#pragma unroll
+                for (int i = 0; i < kVec; ++i) ss = fmaf(y[i], y[i], ss);
+                for (int o = a.hw >> 1; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+                const float inv = 1.f / (sqrtf(ss) + a.eps);
+#pragma unroll
+                for (int i = 0; i < kVec; ++i) y[i] *= inv;
+            }
+            if (t < a.L) {
+                T* op = out + t * sec.so[1];
+                if (sec.so[2] == 1 && (reinterpret_cast<uintptr_t>(op) & 15u) == 0)
+                    *reinterpret_cast<uint4*>(op) = make_uint4(pack2_bits<T>(y[0], y[1]), pack2_bits<T>(y[2], y[3]),
+                                                               pack2_bits<T>(y[4], y[5]), pack2_bits<T>(y[6], y[7]));
+                else
+                    store8<T>(op, sec.so[2], y);
+            }
+        }
+        __syncthreads();  // every read of this stage is done before the next copy into it
+    }
+}
+
 // new conv history [B, C, K-1]: the last K-1 inputs of [history | x]
 template <typename T, typename TH>
 __global__ void dgda_frontend_hist_kernel(FeArgs a, void* nq, void* nk, void* nv, int64_t snh0, int64_t snh1,
@@ -443,7 +587,39 @@ extern "C" int maba_dgda_frontend(const maba_tensor* proj, const maba_tensor* co
     for (int sct = 0; sct < 6; ++sct)
         tiled = tiled && a.C[sct] % kTileCh == 0 && proj[sct].stride[2] == 1 && proj[sct].stride[1] % 8 == 0 &&
                 proj[sct].stride[0] % 8 == 0 && (reinterpret_cast<uintptr_t>(proj[sct].data) & 15u) == 0;
-    if (tiled) {
+    bool piped = tiled && K >= 1 && K <= 8;
+    for (int sct = 0; sct < 3; ++sct)
+        piped = piped && a.sconv[sct][1] == 1 && a.sconv[sct][0] == K &&
+                (reinterpret_cast<uintptr_t>(a.conv[sct]) & 15u) == 0;
+    if (piped) {
+        const int64_t ntt = ceil_div(L, kTileTok);
+        const int nct = (a.C[0] + a.C[1] + a.C[2] + a.C[3] + a.C[4] + a.C[5]) / kTileCh;
+        const int64_t ntiles = B * ntt * nct;
+        const size_t smem = 2 * (size_t)(kTileTok + K - 1) * (kTileCh + 8) * 2 + 2 * (size_t)kTileCh * K * 2;
+        const int64_t cap = (int64_t)sm_count() * 3;
+        const unsigned pgrid = (unsigned)(ntiles < cap ? ntiles : cap);
+        MABA_TRY(MABA_DISPATCH_FLOAT(dt, "dgda_frontend", [&] {
+            if constexpr (sizeof(T) != 2) {
+                return set_error(MABA_ERR_DTYPE, "dgda_frontend: tiled path is 16-bit");
+            } else {
+                auto go = [&](auto kern) {
+                    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+                    kern<<<pgrid, 256, smem, st>>>(a, ntt, nct, ntiles);
+                    return check_launch("dgda_frontend(pipe)");
+                };
+                switch (K) {
+                    case 1: return go(dgda_frontend_pipe_kernel<T, 1>);
+                    case 2: return go(dgda_frontend_pipe_kernel<T, 2>);
+                    case 3: return go(dgda_frontend_pipe_kernel<T, 3>);
+                    case 4: return go(dgda_frontend_pipe_kernel<T, 4>);
+                    case 5: return go(dgda_frontend_pipe_kernel<T, 5>);
+                    case 6: return go(dgda_frontend_pipe_kernel<T, 6>);
+                    case 7: return go(dgda_frontend_pipe_kernel<T, 7>);
+                    default: return go(dgda_frontend_pipe_kernel<T, 8>);
+                }
+            }
+        }));
+    } else if (tiled) {
         const int64_t ntt = ceil_div(L, kTileTok);
         const int nct = (a.C[0] + a.C[1] + a.C[2] + a.C[3] + a.C[4] + a.C[5]) / kTileCh;
         const unsigned tgrid = (unsigned)(B * ntt * nct);
