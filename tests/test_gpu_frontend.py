@@ -38,6 +38,7 @@ def expected(P, taps, hist, H, eps):
     (1, 7, 10, 64, False),
     (2, 200, 10, 64, True),   # not a multiple of the token run
     (1, 64, 4, 16, True),
+    (2, 3000, 10, 64, True),  # 16-bit: 1,440 tiles, more than the persistent grid holds (several per CTA)
 ])
 @pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16])
 def test_frontend_vs_oracle(B, L, H, d, with_hist, dt):
