@@ -481,19 +481,51 @@ def run_ours(args):
     timers = OpTimers(torch)
     gc.collect()
     gc.disable()
+    # the step as one CUDA graph (its launches enqueued once at capture), so the timed steps do
+    # not depend on how fast each rank's host enqueues ~26 launches per step; any failure to
+    # capture falls back to eager steps
+    graph, gout, graph_note = None, None, None
+    if not args.no_graph:
+        try:
+            cap = torch.cuda.Stream(dev)
+            cap.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(cap):
+                hot_path_step(mb, d, weights)  # warm the side stream's library state before capture
+            torch.cuda.current_stream(dev).wait_stream(cap)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                gout = hot_path_step(mb, d, weights)
+            torch.cuda.synchronize()
+        except Exception as ex:  # noqa: BLE001 -- any capture problem means eager timing
+            graph, gout, graph_note = None, None, f"eager steps: capture failed ({type(ex).__name__})"
     barrier()
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     wall0 = time.time()
     start.record()
     for _ in range(args.steps):
-        out = hot_path_step(mb, d, weights, timers)
+        if graph is not None:
+            graph.replay()
+        else:
+            out = hot_path_step(mb, d, weights, timers)
     end.record()
     torch.cuda.synchronize()
     wall1 = time.time()
     barrier()
     clocks.window(wall0, wall1)
     clk = clocks.stop()
+    if graph is not None:
+        # the per-op breakdown and the results from eager steps after the timed region; the
+        # graph's outputs must equal them
+        for _ in range(args.steps):
+            out = hot_path_step(mb, d, weights, timers)
+        torch.cuda.synchronize()
+        same = all(torch.equal(a_, b_) for a_, b_ in zip(gout, out))
+        graph_note = "one CUDA graph per step" + ("" if same else " (OUTPUTS DIFFER FROM EAGER)")
+        del graph, gout  # the graph's memory pool goes back before the end-to-end loop
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
     gc.enable()
     ms = start.elapsed_time(end) / args.steps
     if world > 1:
@@ -558,6 +590,7 @@ def run_ours(args):
             "per_op_ms": {k: round(v, 4) for k, v in per_op.items()},
             "seq_split_1m": split,
             "gpu_launches": count_launches(mb, T_TOK, H) * args.steps,
+            "timed_steps": graph_note or "eager steps",
             "clocks": clk,
         }
         if world == 1 and not args.no_cpu_baseline:
@@ -961,6 +994,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="skip the config-3 prefill and config-4 decode fields")
     ap.add_argument("--no-seq-split", action="store_true", help="skip the 1M-token sequence-split field")
+    ap.add_argument("--no-graph", action="store_true", help="time eager steps instead of one CUDA graph per step")
     ap.add_argument("--decode-ctx", type=int, default=1048576)
     ap.add_argument("--decode-steps", type=int, default=256)
     ap.add_argument("--only", default=None, choices=["sa_attention", "dgda_prefill", "index_topk", "dgda_step", "decode"],
