@@ -263,7 +263,7 @@ def sa_segment_phase_b(qhat_local, q_idx_local, gate_local, c_all: Sequence[torc
 
 
 def exchange_prefix(bufs: Sequence[torch.Tensor], bounds: Sequence[int], units: Sequence[int], rank: int,
-                    group=None, wait: bool = True):
+                    group=None, wait: bool = True, how: str = "broadcast"):
     """Prefix exchange of per-token tables between the ranks of a sequence split.
 
     ``bufs[i]`` is a [B, bounds[-1] // units[i], d] table (one row per ``units[i]``
@@ -275,8 +275,26 @@ def exchange_prefix(bufs: Sequence[torch.Tensor], bounds: Sequence[int], units: 
     up; the exchange is asynchronous to the host (NCCL runs it on its own stream and the
     current stream waits for it).  With ``wait=False`` the requests are returned instead and
     the caller waits on them later (work queued on the current stream meanwhile overlaps the
-    transfers)."""
+    transfers).
+
+    ``how="broadcast"`` (the default) sends each rank's rows to every rank with one broadcast
+    per table and source instead: more bytes arrive (later ranks' rows too, which no query
+    reads), but each transfer runs as one collective at the interconnect's broadcast rate,
+    where the point-to-point batch reached a fraction of it on eight B200s."""
     world = len(bounds) - 1
+    if how == "broadcast":
+        reqs = []
+        for buf, u in zip(bufs, units):
+            for bi in range(buf.shape[0]):
+                for j in range(world - 1):  # the last rank's rows precede no query
+                    lo, hi = bounds[j] // u, bounds[j + 1] // u
+                    if hi > lo:
+                        reqs.append(dist.broadcast(buf[bi, lo:hi], src=j, group=group, async_op=True))
+        if not wait:
+            return reqs
+        for req in reqs:
+            req.wait()
+        return None
     ops = []
     for buf, u in zip(bufs, units):
         for bi in range(buf.shape[0]):
