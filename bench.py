@@ -516,8 +516,12 @@ def run_ours(args):
     clocks.window(wall0, wall1)
     clk = clocks.stop()
     if graph is not None:
-        # the per-op breakdown and the results from eager steps after the timed region; the
-        # graph's outputs must equal them
+        # the per-op breakdown and the results from eager steps after the timed region (after
+        # warm-up steps of their own: the graph's pool holds the captured step's buffers, so the
+        # first eager steps allocate afresh); the graph's outputs must equal them
+        for _ in range(max(3, args.warmup)):
+            out = hot_path_step(mb, d, weights)
+        torch.cuda.synchronize()
         for _ in range(args.steps):
             out = hot_path_step(mb, d, weights, timers)
         torch.cuda.synchronize()
