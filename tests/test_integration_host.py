@@ -1,15 +1,17 @@
 """install() wires the B200 ops into a loaded reference package (host logic only).
 
-The reference checkout is only present where the golden fixtures were made; the
-test skips elsewhere.  It checks the registry entries, the method patches, the
-strict-mode environment and that uninstall() restores the reference."""
+The reference package comes from MABA_REFERENCE (a directory holding maba_sparse) or
+the offline install under baseline/_ref; the test skips where neither exists.  It
+checks the registry entries, the method patches, the strict-mode environment and that
+uninstall() restores the reference."""
 import os
 import sys
 
 import pytest
 import torch
 
-REF = os.environ.get("MABA_REFERENCE", "/root/reference")
+_REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+REF = os.environ.get("MABA_REFERENCE") or os.path.join(_REPO, "baseline", "_ref")
 
 
 @pytest.fixture
