@@ -401,6 +401,22 @@ def run_only(args):
         torch.cuda.synchronize()
         print(f"ran decode x{args.steps} at context {args.decode_ctx}")
         return
+    if args.only == "dgda_frontend":
+        # the fused DGDA front end of one config-3 DGDA layer: B=8 sequences (--batch 8 by default
+        # here) of --tokens (8,192) tokens, the six 640-channel sections of one projection output
+        B = args.batch if args.batch != 512 else 8
+        L = args.tokens or 8192
+        C = H * DH
+        g = torch.Generator(device=dev).manual_seed(6)
+        proj = torch.randn(B, L, 6 * C, device=dev, generator=g).to(torch.bfloat16)
+        cols = [proj[:, :, i * C:(i + 1) * C] for i in range(6)]
+        taps = [(torch.randn(C, 4, device=dev, generator=g) * 0.5).to(torch.bfloat16) for _ in range(3)]
+        torch.cuda.synchronize()
+        for _ in range(args.warmup_only + args.steps):
+            mb.ops.b200_dgda_frontend(cols, taps, None, n_heads=H, new_hist=False)
+        torch.cuda.synchronize()
+        print(f"ran dgda_frontend B={B} L={L} x{args.warmup_only + args.steps}")
+        return
     if args.only == "dgda_step":
         # one decode step of every head of a batch: fp32 state [B, H, 64, 64], bf16 vectors
         g = torch.Generator(device=dev).manual_seed(5)
@@ -1001,7 +1017,8 @@ def main():
     ap.add_argument("--no-graph", action="store_true", help="time eager steps instead of one CUDA graph per step")
     ap.add_argument("--decode-ctx", type=int, default=1048576)
     ap.add_argument("--decode-steps", type=int, default=256)
-    ap.add_argument("--only", default=None, choices=["sa_attention", "dgda_prefill", "index_topk", "dgda_step", "decode"],
+    ap.add_argument("--only", default=None, choices=["sa_attention", "dgda_prefill", "index_topk", "dgda_step", "decode",
+                                                      "dgda_frontend"],
                     help="profile helper: run one op of the step, print no JSON")
     ap.add_argument("--tokens", type=int, default=None,
                     help="profile helper: sequence length of the --only workload (default: the bench's)")
