@@ -463,9 +463,12 @@ __device__ __forceinline__ void gemv_body(const GemvArgs& a, int blk, float* hs,
     }
 }
 
-// MIX: the DGDA mixer form (EPI_DGDA with the recurrence step in each head's last CTA)
+// MIX: the DGDA mixer form (EPI_DGDA with the recurrence step in each head's last CTA).
+// The plain 16-bit form for up to two batch rows is held to 64 registers, so four CTAs fit
+// per SM and the CTAs of the next GEMVs in the chain find room to start their weight copies
+// early (2.8 % per decode step at B = 1); wider batches keep three, float32 weights two.
 template <typename TW, int NB, bool MIX>
-__global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvArgs a) {
+__global__ void __launch_bounds__(kGemvThreads, (MIX || sizeof(TW) == 4) ? 2 : (NB <= 2 ? 4 : 3)) gemv_kernel(GemvArgs a) {
     extern __shared__ float hs[];  // [NB][K] input vectors, then the CTA's weight rows
     griddep_launch_dependents();
     gemv_body<TW, NB, MIX>(a, blockIdx.x, hs, [] { griddep_wait(); });
